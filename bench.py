@@ -1,0 +1,301 @@
+#!/usr/bin/env python
+"""Headline benchmark: train tokens/s (all GPUs, max-over-ranks device time) of the dense GQA
+decoder of the benchmark configuration, at a global batch of 524,288 tokens per update.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1)
+
+Model: depth 20, width 1280, 10 query heads / 5 KV heads of dim 128, RoPE, RMSNorm, ReLU^2 MLP
+4x, vocab 65536, sequence 2048, on the shared shell (value embeddings, smear, backout, soft-cap
+15) - the reference's own shell class with these dimensions, so both arms train the same network.
+Optimizer: Muon + AdamW (the shell recipe), one update per step.  Data: iid uniform synthetic
+tokens, random-init weights.  Strong scaling: the global batch is fixed and every GPU runs
+global / N tokens per update (gradient accumulation below 8 GPUs).
+
+Two numbers are reported: ``value`` times the update on device-resident inputs (CUDA events,
+barrier + synchronize on both sides, max over ranks); ``e2e.value`` times the public
+``Trainer.step`` call, which copies every micro-batch host->device from pinned memory and
+reads the loss back.  The working set (activations of 32 x 2048 tokens) is far larger than
+L2, so no explicit flush is needed between timed steps.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BASELINE_TOKS = None  # BASELINE.md publishes no number for this configuration
+MODEL = dict(sequence_len=2048, vocab_size=65536, n_layer=20, n_head=10, n_kv_head=5, n_embd=1280,
+             window_pattern="L")
+GLOBAL_BATCH = 524288
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--micro-batch", type=int, default=0, help="rows per micro-batch (default 32 ours / 16 reference)")
+    p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
+    p.add_argument("--no-e2e", action="store_true", help=argparse.SUPPRESS)
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region (local rank 0 only)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled):
+        self.proc = None
+        self.enabled = enabled
+
+    def __enter__(self):
+        if self.enabled:
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                              "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                             text=True)
+            except OSError:
+                self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self, gpus):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx not in gpus:
+                continue
+            rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        seen = set()
+        mhz = []
+        for r in rows:
+            try:
+                mhz.append(float(r[1]))
+            except ValueError:
+                pass
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    seen.add(name)
+        try:
+            mx = float(rows[0][2])
+        except ValueError:
+            mx = None
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx, "reasons": sorted(seen),
+                "samples": len(rows)}
+
+
+def synthetic_batches(n_micro, rows, T, vocab, seed, device=None, pinned=False):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    xs, ys = [], []
+    for _ in range(n_micro):
+        tok = torch.randint(0, vocab, (rows, T + 1), generator=g)
+        x, y = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+        if pinned:
+            x, y = x.pin_memory(), y.pin_memory()
+        if device is not None:
+            x, y = x.to(device), y.to(device)
+        xs.append(x)
+        ys.append(y)
+    return xs, ys
+
+
+def count_own_kernels(step_fn):
+    """Launches of this repository's kernels in one step (torch profiler, outside the timed region)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        name = ev.name or ""
+        if ev.device_type == torch.autograd.DeviceType.CUDA and (name.startswith("void nt::") or "nt::" in name[:40]):
+            n += 1
+    return n
+
+
+def main():
+    args = parse()
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun for N > 1")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        ref = ROOT / "baseline" / "_ref"
+        if not (ref / "nanochat").is_dir():
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}))
+            return
+        sys.path.append(str(ref))
+
+    from nexttransformer_b200.runtime.process import initialize, shutdown
+    rank, world, device = initialize(seed=42, timeout_s=900)
+    if device.type != "cuda":
+        raise SystemExit("bench.py needs a CUDA device")
+    micro = args.micro_batch or (32 if args.impl == "ours" else 16)
+    T = MODEL["sequence_len"]
+    per_rank = GLOBAL_BATCH // world
+    if per_rank % (micro * T):
+        micro = max(1, per_rank // T)
+    accum = per_rank // (micro * T)
+    cfg = dict(MODEL, n_layer=args.layers)
+
+    if args.impl == "ours":
+        from nexttransformer_b200.models.shell import ShellConfig, build_shell
+        from nexttransformer_b200.optim.groups import shell_groups
+        from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+        from nexttransformer_b200.training.engine import Trainer
+        model = build_shell(ShellConfig(**cfg), device, seed=42)
+        st = model.fused_state()
+        opt = MuonAdamW(shell_groups(model), shadows={p: s for p, s in st.casts})
+        trainer = Trainer(model, opt, accumulation=accum)
+
+        def step_device(xs, ys):
+            return trainer.step_device(xs, ys)
+
+        def step_e2e(xs, ys):
+            return trainer.step(xs, ys)
+        flops_per_token = model.estimate_flops()
+    else:
+        from nexttransformer.models.backbone import GPT, GPTConfig
+        with torch.device("meta"):
+            model = GPT(GPTConfig(**cfg))
+        model.to_empty(device=device)
+        model.init_weights()
+        opt = model.setup_optimizer()
+
+        def step_device(xs, ys):
+            tot = torch.zeros((), device=device)
+            for x, y in zip(xs, ys):
+                loss = model(x, y)
+                (loss / accum).backward()
+                tot += loss.detach()
+            opt.step()
+            model.zero_grad(set_to_none=True)
+            return tot / accum
+
+        def step_e2e(xs, ys):
+            return float(step_device([x.to(device, non_blocking=True) for x in xs],
+                                     [y.to(device, non_blocking=True) for y in ys]))
+        flops_per_token = model.estimate_flops()
+
+    vocab = MODEL["vocab_size"]
+    dev_x, dev_y = synthetic_batches(accum, micro, T, vocab, seed=1000 + rank, device=device)
+    host_x, host_y = synthetic_batches(accum, micro, T, vocab, seed=2000 + rank, pinned=True)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[device.index])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step_device(dev_x, dev_y)
+    barrier()
+
+    # ---- device-timed region
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local == 0)
+    with sampler:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            loss = step_device(dev_x, dev_y)
+        end.record()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    final_loss = float(loss)
+
+    # ---- end-to-end through the public step call (H2D of inputs, D2H of the loss)
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(1):
+            step_e2e(host_x, host_y)
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(args.steps):
+            step_e2e(host_x, host_y)
+        e2.record()
+        barrier()
+        ms2 = s2.elapsed_time(e2) / args.steps
+        t2 = torch.tensor([ms2], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        ms2 = float(t2.item())
+        h2d = sum(x.numel() * x.element_size() + y.numel() * y.element_size() for x, y in zip(host_x, host_y))
+        e2e = {"value": GLOBAL_BATCH / (ms2 / 1000.0), "unit": "tokens/s", "ms_per_step": ms2,
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4}
+
+    launches = None
+    if args.impl == "ours":
+        try:
+            launches = count_own_kernels(lambda: step_device(dev_x, dev_y)) * args.steps
+        except Exception as exc:  # profiler unavailable: report as unknown
+            launches = None
+            if rank == 0:
+                print(f"launch count unavailable: {exc}", file=sys.stderr)
+
+    value = GLOBAL_BATCH / (ms_max / 1000.0)
+    gpus = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(world))).split(",")
+            if x.strip().isdigit()] or list(range(world))
+    clocks = sampler.summary(set(gpus[:world]) if local == 0 else set())
+    if rank == 0:
+        out = {"metric": "train tokens/sec on 8xB200 (max over ranks) per method at matched FLOPs/token",
+               "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+               "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",
+               "data": "synthetic uniform tokens, random-init weights",
+               "config": {"model": "dense GQA d20 w1280 h10/kv5 hd128 vocab65536 (shell: VE, smear, backout, softcap)",
+                          "global_batch": GLOBAL_BATCH, "seq_len": T, "parallelism": f"dp{world}",
+                          "micro_batch": micro, "grad_accum": accum, "l2": "working set >> L2 (no flush needed)",
+                          "flops_per_token": flops_per_token},
+               "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": final_loss}
+        if args.impl == "reference":
+            out["impl"] = "reference"
+            out.pop("gpu_launches")
+        print(json.dumps(out), flush=True)
+    del opt, model
+    shutdown()
+
+
+if __name__ == "__main__":
+    main()

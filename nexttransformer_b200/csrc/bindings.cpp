@@ -1,0 +1,320 @@
+// Python bindings of the sm_100a kernels.  Only this file includes torch headers; the .cu
+// files export plain C++ launchers so that they compile quickly and stay independent of torch.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "attention_sm100.h"
+#include "elementwise.h"
+#include "gemm_sm100.h"
+#include "optim.h"
+
+namespace {
+
+using torch::Tensor;
+using OptT = c10::optional<Tensor>;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_rows(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+const void* ptr_or_null(const OptT& t) { return t.has_value() && t->defined() ? t->data_ptr() : nullptr; }
+void* mptr_or_null(const OptT& t) { return t.has_value() && t->defined() ? t->data_ptr() : nullptr; }
+void ok(int rc, const char* what) { TORCH_CHECK(rc == 0, what, ": unsupported shape"); }
+
+int num_sms(const Tensor& t) {
+  static int cached[64] = {0};
+  const int dev = t.get_device();
+  if (!cached[dev]) cached[dev] = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
+  return cached[dev];
+}
+
+// ------------------------------------------------------------------ GEMM
+// A logical [M,K] (stored [M,K] or, with a_mn, [K,M]); B logical [N,K] (stored [N,K] or, with
+// b_mn, [K,N]); C [M,N].  2-D or 3-D (batched) tensors; the last dimension must be contiguous.
+void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const Tensor& C, int64_t epi, const OptT& R,
+          const OptT& P, double s_acc, double s_res, const OptT& s_dev) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  TORCH_CHECK(A.dim() == B.dim() && A.dim() == C.dim() && (A.dim() == 2 || A.dim() == 3), "gemm rank mismatch");
+  TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1 && C.stride(-1) == 1, "gemm needs unit inner stride");
+  const bool batched = A.dim() == 3;
+  GemmArgs g;
+  g.batch = batched ? static_cast<int>(A.size(0)) : 1;
+  g.M = static_cast<int>(C.size(-2));
+  g.N = static_cast<int>(C.size(-1));
+  g.K = static_cast<int>(a_mn ? A.size(-2) : A.size(-1));
+  TORCH_CHECK((a_mn ? A.size(-1) : A.size(-2)) == g.M, "A rows != C rows");
+  TORCH_CHECK((b_mn ? B.size(-1) : B.size(-2)) == g.N, "B rows != C cols");
+  TORCH_CHECK((b_mn ? B.size(-2) : B.size(-1)) == g.K, "A/B reduction mismatch");
+  g.A = A.data_ptr();
+  g.lda = A.stride(-2);
+  g.strideA = batched ? A.stride(0) : 0;
+  g.a_mn = a_mn;
+  g.B = B.data_ptr();
+  g.ldb = B.stride(-2);
+  g.strideB = batched ? B.stride(0) : 0;
+  g.b_mn = b_mn;
+  g.C = C.data_ptr();
+  g.ldc = C.stride(-2);
+  g.strideC = batched ? C.stride(0) : 0;
+  const bool f32_out = epi == EPI_F32 || epi == EPI_F32_ACC;
+  TORCH_CHECK(C.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm output dtype does not match epilogue");
+  if (epi == EPI_BF16_AXPBY || epi == EPI_RELU2_BWD) {
+    TORCH_CHECK(R.has_value() && R->defined(), "epilogue needs R");
+    TORCH_CHECK(R->scalar_type() == at::kBFloat16 && R->stride(-1) == 1 && R->size(-1) == g.N && R->size(-2) == g.M,
+                "R must be bf16 [.., M, N]");
+    g.R = R->data_ptr();
+    g.ldr = R->stride(-2);
+    g.strideR = batched ? R->stride(0) : 0;
+  }
+  if (epi == EPI_RELU2) {
+    TORCH_CHECK(P.has_value() && P->defined(), "relu2 epilogue needs P");
+    TORCH_CHECK(P->scalar_type() == at::kBFloat16 && P->stride(-1) == 1 && P->size(-1) == g.N && P->size(-2) == g.M,
+                "P must be bf16 [.., M, N]");
+    g.P = P->data_ptr();
+    g.ldp = P->stride(-2);
+    g.strideP = batched ? P->stride(0) : 0;
+  }
+  g.s_acc = static_cast<float>(s_acc);
+  g.s_res = static_cast<float>(s_res);
+  if (s_dev.has_value() && s_dev->defined()) {
+    TORCH_CHECK(s_dev->is_cuda() && s_dev->scalar_type() == at::kFloat && s_dev->numel() == 1, "s_dev: one fp32 value");
+    g.s_ptr = s_dev->data_ptr<float>();
+  }
+  g.epi = static_cast<int>(epi);
+  g.num_sms = num_sms(C);
+  const c10::cuda::CUDAGuard guard(C.device());
+  nt_gemm_launch(g, stream());
+}
+
+// ------------------------------------------------------------------ norms
+void mix_norm_fwd(const Tensor& x, const OptT& x0, const OptT& ab, const OptT& xm, const Tensor& h,
+                  const OptT& rstd, double out_scale) {
+  check_rows(x, "x");
+  check_rows(h, "h");
+  const int d = static_cast<int>(x.size(-1));
+  const int M = static_cast<int>(x.numel() / d);
+  if (x0.has_value() && x0->defined()) {
+    check_rows(*x0, "x0");
+    TORCH_CHECK(ab.has_value() && xm.has_value(), "mix needs ab and xm");
+    check_rows(*xm, "xm");
+  }
+  ok(nt_mix_norm_fwd(x.data_ptr(), ptr_or_null(x0), ab.has_value() ? ab->data_ptr<float>() : nullptr, mptr_or_null(xm),
+                     h.data_ptr(), rstd.has_value() ? rstd->data_ptr<float>() : nullptr, M, d,
+                     static_cast<float>(out_scale), stream()),
+     "mix_norm_fwd");
+}
+
+void norm_bwd(const Tensor& x, const Tensor& dy, const OptT& dres, const Tensor& dx) {
+  check_rows(x, "x");
+  check_rows(dy, "dy");
+  check_rows(dx, "dx");
+  if (dres.has_value() && dres->defined()) check_rows(*dres, "dres");
+  const int d = static_cast<int>(x.size(-1));
+  ok(nt_norm_bwd(x.data_ptr(), dy.data_ptr(), ptr_or_null(dres), dx.data_ptr(), static_cast<int>(x.numel() / d), d,
+                 stream()),
+     "norm_bwd");
+}
+
+void mix_norm_bwd(const Tensor& x, const Tensor& x0, const Tensor& xm, const Tensor& dh, const Tensor& dres,
+                  const Tensor& ab, const Tensor& dx, const Tensor& dx0_acc, const Tensor& part) {
+  for (auto* t : {&x, &x0, &xm, &dh, &dres, &dx, &dx0_acc}) check_rows(*t, "mix_norm_bwd operand");
+  const int d = static_cast<int>(x.size(-1));
+  ok(nt_mix_norm_bwd(x.data_ptr(), x0.data_ptr(), xm.data_ptr(), dh.data_ptr(), dres.data_ptr(), ab.data_ptr<float>(),
+                     dx.data_ptr(), dx0_acc.data_ptr<float>(), part.data_ptr<float>(),
+                     static_cast<int>(x.numel() / d), d, stream()),
+     "mix_norm_bwd");
+}
+
+void rope_norm_fwd(const Tensor& qkv, const Tensor& cosb, const Tensor& sinb, const Tensor& rstd, int64_t T, int64_t H,
+                   int64_t Hk, int64_t D, double scale, const OptT& ve_table, const OptT& idx, const OptT& hrow,
+                   const OptT& wg, const OptT& gate_out) {
+  check_rows(qkv, "qkv");
+  const int M = static_cast<int>(qkv.numel() / ((H + 2 * Hk) * D));
+  const bool ve = ve_table.has_value() && ve_table->defined();
+  ok(nt_rope_norm_fwd(qkv.data_ptr(), cosb.data_ptr(), sinb.data_ptr(), rstd.data_ptr<float>(), M,
+                      static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hk), static_cast<int>(D),
+                      static_cast<float>(scale), ve ? ve_table->data_ptr() : nullptr,
+                      ve ? idx->data_ptr<int64_t>() : nullptr, ve ? hrow->data_ptr() : nullptr,
+                      ve ? static_cast<int>(hrow->stride(-2)) : 0, ve ? wg->data_ptr() : nullptr,
+                      ve ? static_cast<int>(wg->size(-1)) : 0, ve ? gate_out->data_ptr<float>() : nullptr, stream()),
+     "rope_norm_fwd");
+}
+
+void rope_norm_bwd(const Tensor& dqkv, const Tensor& qkv, const Tensor& cosb, const Tensor& sinb, const Tensor& rstd,
+                   int64_t T, int64_t H, int64_t Hk, int64_t D, double scale, const OptT& ve_table, const OptT& idx,
+                   const OptT& gate, const OptT& dz, const OptT& ve_grad) {
+  check_rows(dqkv, "dqkv");
+  const int M = static_cast<int>(qkv.numel() / ((H + 2 * Hk) * D));
+  const bool ve = ve_table.has_value() && ve_table->defined();
+  ok(nt_rope_norm_bwd(dqkv.data_ptr(), qkv.data_ptr(), cosb.data_ptr(), sinb.data_ptr(), rstd.data_ptr<float>(), M,
+                      static_cast<int>(T), static_cast<int>(H), static_cast<int>(Hk), static_cast<int>(D),
+                      static_cast<float>(scale), ve ? ve_table->data_ptr() : nullptr,
+                      ve ? idx->data_ptr<int64_t>() : nullptr, ve ? gate->data_ptr<float>() : nullptr,
+                      ve ? dz->data_ptr<float>() : nullptr, ve ? ve_grad->data_ptr<float>() : nullptr, stream()),
+     "rope_norm_bwd");
+}
+
+void softcap_ce(const Tensor& logits, const Tensor& tgt, const Tensor& loss, const OptT& lse, int64_t V, double cap) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.stride(-1) == 1 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "logits layout");
+  ok(nt_softcap_ce(logits.data_ptr(), logits.stride(-2), tgt.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                   lse.has_value() ? lse->data_ptr<float>() : nullptr, static_cast<int>(logits.size(-2)),
+                   static_cast<int>(V), static_cast<int>(logits.size(-1)), static_cast<float>(cap), stream()),
+     "softcap_ce");
+}
+
+void embed_smear(const Tensor& wte, const Tensor& idx, const Tensor& wsm, const Tensor& lam, const Tensor& n_out,
+                 const Tensor& x_out, const Tensor& gate_out, int64_t T) {
+  check_rows(wte, "wte");
+  check_rows(n_out, "n_out");
+  check_rows(x_out, "x_out");
+  const int d = static_cast<int>(wte.size(-1));
+  ok(nt_embed_smear(wte.data_ptr(), idx.data_ptr<int64_t>(), wsm.data_ptr(), lam.data_ptr<float>(), n_out.data_ptr(),
+                    x_out.data_ptr(), gate_out.data_ptr<float>(), static_cast<int>(idx.numel()), static_cast<int>(T), d,
+                    static_cast<int>(wsm.numel()), stream()),
+     "embed_smear");
+}
+
+void embed_scatter(const Tensor& dy, const Tensor& idx, const Tensor& grad) {
+  check_cuda(dy, "dy");
+  TORCH_CHECK(dy.is_contiguous() && grad.is_contiguous(), "embed_scatter layout");
+  ok(nt_embed_scatter(dy.data_ptr(), dy.scalar_type() == at::kFloat, idx.data_ptr<int64_t>(), grad.data_ptr<float>(),
+                      static_cast<int>(idx.numel()), static_cast<int>(grad.size(-1)), stream()),
+     "embed_scatter");
+}
+
+void cast_bf16(const Tensor& src, const Tensor& dst) {
+  TORCH_CHECK(src.is_contiguous() && dst.is_contiguous() && src.numel() == dst.numel(), "cast layout");
+  ok(nt_cast_bf16(src.data_ptr<float>(), dst.data_ptr(), src.numel(), stream()), "cast_bf16");
+}
+
+// ------------------------------------------------------------------ optimizer
+void adamw(const Tensor& p, const Tensor& g, const Tensor& m, const Tensor& v, const OptT& shadow, double lr,
+           double b1, double b2, double eps, double wd, int64_t step) {
+  TORCH_CHECK(p.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "adamw layout");
+  TORCH_CHECK(g.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat, "adamw grad/state must be fp32");
+  AdamWHyper h;
+  h.lr = static_cast<float>(lr);
+  h.beta1 = static_cast<float>(b1);
+  h.beta2 = static_cast<float>(b2);
+  h.eps = static_cast<float>(eps);
+  h.wd = static_cast<float>(wd);
+  h.bias1 = static_cast<float>(1.0 - std::pow(b1, static_cast<double>(step)));
+  h.bias2 = static_cast<float>(1.0 - std::pow(b2, static_cast<double>(step)));
+  ok(nt_adamw(p.data_ptr(), p.scalar_type() == at::kBFloat16, g.data_ptr<float>(), m.data_ptr<float>(),
+              v.data_ptr<float>(), mptr_or_null(shadow), p.numel(), h, stream()),
+     "adamw");
+}
+
+void muon_prep(const Tensor& grad_ptrs, const Tensor& mom_ptrs, const Tensor& X, const Tensor& rowss, double mu) {
+  const int K = static_cast<int>(X.size(0)), m = static_cast<int>(X.size(1)), n = static_cast<int>(X.size(2));
+  ok(nt_muon_prep(reinterpret_cast<float* const*>(grad_ptrs.data_ptr<int64_t>()),
+                  reinterpret_cast<float* const*>(mom_ptrs.data_ptr<int64_t>()), X.data_ptr(), rowss.data_ptr<float>(), K,
+                  m, n, static_cast<float>(mu), stream()),
+     "muon_prep");
+}
+
+void muon_normalize(const Tensor& X, const Tensor& rowss, const Tensor& tot) {
+  const int K = static_cast<int>(X.size(0)), m = static_cast<int>(X.size(1)), n = static_cast<int>(X.size(2));
+  ok(nt_muon_normalize(X.data_ptr(), rowss.data_ptr<float>(), tot.data_ptr<float>(), K, m, n, stream()),
+     "muon_normalize");
+}
+
+void muon_finish(const Tensor& X, const Tensor& red, const Tensor& tot, const Tensor& smb_ptrs, const Tensor& fscale,
+                 const Tensor& param_ptrs, const OptT& shadow_ptrs, double beta2, double lr, double wd) {
+  const int K = static_cast<int>(X.size(0)), m = static_cast<int>(X.size(1)), n = static_cast<int>(X.size(2));
+  ok(nt_muon_finish(X.data_ptr(), red.data_ptr<float>(), tot.data_ptr<float>(),
+                    reinterpret_cast<float* const*>(smb_ptrs.data_ptr<int64_t>()), fscale.data_ptr<float>(),
+                    reinterpret_cast<float* const*>(param_ptrs.data_ptr<int64_t>()),
+                    shadow_ptrs.has_value() ? reinterpret_cast<void* const*>(shadow_ptrs->data_ptr<int64_t>()) : nullptr,
+                    K, m, n, static_cast<float>(beta2), static_cast<float>(lr), static_cast<float>(wd), stream()),
+     "muon_finish");
+}
+
+// ------------------------------------------------------------------ attention
+AttnArgs attn_args(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse, int64_t B,
+                   int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window, double scale) {
+  for (auto* t : {&q, &k, &v, &o}) {
+    check_cuda(*t, "attention operand");
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "attention operands: bf16, unit stride");
+  }
+  AttnArgs a;
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.ldq = q.stride(-2); a.ldk = k.stride(-2); a.ldv = v.stride(-2); a.ldo = o.stride(-2);
+  a.B = static_cast<int>(B); a.T = static_cast<int>(T); a.H = static_cast<int>(H); a.Hk = static_cast<int>(Hk);
+  a.D = static_cast<int>(D);
+  a.window = static_cast<int>(window);
+  a.scale = static_cast<float>(scale);
+  a.num_sms = num_sms(q);
+  return a;
+}
+
+// q [B*T, >=H*D] (row stride ldq), k/v [B*T, >=Hk*D], o [B*T, H*D], lse [B, H, T]
+void attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse, int64_t B,
+              int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window, double scale) {
+  AttnArgs a = attn_args(q, k, v, o, lse, B, T, H, Hk, D, window, scale);
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_attention_fwd(a, stream()), "attention_fwd");
+}
+
+void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
+              const Tensor& dout, const Tensor& dq, const Tensor& dk, const Tensor& dv, const Tensor& dq_acc,
+              const Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window,
+              double scale) {
+  AttnArgs a = attn_args(q, k, v, o, lse, B, T, H, Hk, D, window, scale);
+  a.dout = dout.data_ptr(); a.lddo = dout.stride(-2);
+  a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
+  a.lddq = dq.stride(-2); a.lddk = dk.stride(-2); a.lddv = dv.stride(-2);
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_attention_bwd(a, stream()), "attention_bwd");
+}
+
+std::vector<int64_t> read_errors() {
+  unsigned w = 0;
+  const int g = nt_gemm_read_error(&w);
+  unsigned wa = 0;
+  const int a = nt_attention_read_error(&wa);
+  return {g, static_cast<int64_t>(w), a, static_cast<int64_t>(wa)};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nexttransformer_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "bf16 tcgen05 GEMM with fused epilogue");
+  m.def("mix_norm_fwd", &mix_norm_fwd);
+  m.def("norm_bwd", &norm_bwd);
+  m.def("mix_norm_bwd", &mix_norm_bwd);
+  m.def("rope_norm_fwd", &rope_norm_fwd);
+  m.def("rope_norm_bwd", &rope_norm_bwd);
+  m.def("softcap_ce", &softcap_ce);
+  m.def("embed_smear", &embed_smear);
+  m.def("embed_scatter", &embed_scatter);
+  m.def("cast_bf16", &cast_bf16);
+  m.def("adamw", &adamw);
+  m.def("muon_prep", &muon_prep);
+  m.def("muon_normalize", &muon_normalize);
+  m.def("muon_finish", &muon_finish);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("read_errors", &read_errors);
+  m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
+  m.attr("EPI_F32") = static_cast<int>(EPI_F32);
+  m.attr("EPI_F32_ACC") = static_cast<int>(EPI_F32_ACC);
+  m.attr("EPI_BF16_AXPBY") = static_cast<int>(EPI_BF16_AXPBY);
+  m.attr("EPI_RELU2") = static_cast<int>(EPI_RELU2);
+  m.attr("EPI_RELU2_BWD") = static_cast<int>(EPI_RELU2_BWD);
+}

@@ -1,0 +1,436 @@
+// K0: persistent warp-specialized bf16 GEMM engine for sm_100a.
+//
+//   D[b, m, n] = epilogue( sum_k A[b, m, k] * B[b, n, k] )
+//
+// A is stored K-major ([M, K], K contiguous) or M-major ([K, M], M contiguous); B is stored
+// K-major ([N, K]) or N-major ([K, N]).  Those four storage orders cover a Linear layer's
+// forward (A K-major, B K-major), input gradient (B N-major) and weight gradient (both
+// MN-major), and the Newton-Schulz chain of the Muon optimizer.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x64 A tiles and BNx64 B tiles, 128-byte swizzle, into a
+//               STAGES-deep shared-memory ring guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM (2 x BN fp32 columns = double-buffered accumulator) and issues
+//               tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees ring
+//               slots and publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one accumulator row per thread),
+//               apply the fused epilogue, store to global memory.  While they drain one
+//               accumulator, warp 1 fills the other.
+// Tiles are visited in a grouped raster (GROUP_M row-blocks at a time) so that A and B tiles
+// are re-read from L2.  No TMA load here uses cluster multicast.
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace nt {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int GROUP_M = 16;
+constexpr int NUM_THREADS = 192;
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], tmem holder, abort flag
+  static constexpr int BAR_BYTES = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
+};
+
+struct Params {
+  int M, N, K, batch;
+  int tiles_m, tiles_n;
+  int epi;
+  void* C;
+  int64_t ldc, strideC;  // elements
+  const void* R;         // residual / pre-activation input (bf16)
+  int64_t ldr, strideR;
+  void* P;               // second output (bf16 pre-activation)
+  int64_t ldp, strideP;
+  float s_acc, s_res;
+  const float* s_ptr;
+};
+
+NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  int r = t - b * per_batch;
+  const int group_span = GROUP_M * p.tiles_n;
+  const int g = r / group_span;
+  const int first_m = g * GROUP_M;
+  const int rows_in_group = min(GROUP_M, p.tiles_m - first_m);
+  const int in_g = r - g * group_span;
+  mb = first_m + in_g % rows_in_group;
+  nb = in_g / rows_in_group;
+}
+
+// Epilogue for 32 consecutive columns of one row.
+template <int EPI>
+NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int row, int col0, const uint32_t (&acc)[32]) {
+  if (row >= p.M) return;
+  const int ncols = min(32, p.N - col0);
+  if (ncols <= 0) return;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
+  const bool full = (ncols == 32);
+
+  if constexpr (EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+    float* c = reinterpret_cast<float*>(p.C) + b * p.strideC + static_cast<int64_t>(row) * p.ldc + col0;
+    if (full && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 o = make_float4(v[i] * sacc, v[i + 1] * sacc, v[i + 2] * sacc, v[i + 3] * sacc);
+        if constexpr (EPI == EPI_F32_ACC) {
+          float4 old = *reinterpret_cast<float4*>(c + i);
+          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+        }
+        *reinterpret_cast<float4*>(c + i) = o;
+      }
+    } else {
+      for (int i = 0; i < ncols; ++i) {
+        float o = v[i] * sacc;
+        if constexpr (EPI == EPI_F32_ACC) o += c[i];
+        c[i] = o;
+      }
+    }
+    return;
+  } else {
+    __nv_bfloat16* c =
+        reinterpret_cast<__nv_bfloat16*>(p.C) + b * p.strideC + static_cast<int64_t>(row) * p.ldc + col0;
+    const __nv_bfloat16* r = nullptr;
+    if constexpr (EPI == EPI_BF16_AXPBY || EPI == EPI_RELU2_BWD) {
+      r = reinterpret_cast<const __nv_bfloat16*>(p.R) + b * p.strideR + static_cast<int64_t>(row) * p.ldr + col0;
+    }
+    __nv_bfloat16* pp = nullptr;
+    if constexpr (EPI == EPI_RELU2) {
+      pp = reinterpret_cast<__nv_bfloat16*>(p.P) + b * p.strideP + static_cast<int64_t>(row) * p.ldp + col0;
+    }
+    uint32_t out[16];
+    uint32_t pre[16];
+    float rv[32];
+    if constexpr (EPI == EPI_BF16_AXPBY || EPI == EPI_RELU2_BWD) {
+      if (full && ((reinterpret_cast<uintptr_t>(r) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 q = *reinterpret_cast<const uint4*>(r + 8 * i);
+          float2 f0 = unpack_bf16x2(q.x), f1 = unpack_bf16x2(q.y), f2 = unpack_bf16x2(q.z), f3 = unpack_bf16x2(q.w);
+          rv[8 * i + 0] = f0.x; rv[8 * i + 1] = f0.y; rv[8 * i + 2] = f1.x; rv[8 * i + 3] = f1.y;
+          rv[8 * i + 4] = f2.x; rv[8 * i + 5] = f2.y; rv[8 * i + 6] = f3.x; rv[8 * i + 7] = f3.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rv[i] = (i < ncols) ? bf2f(r[i]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float o0, o1;
+      if constexpr (EPI == EPI_BF16) {
+        o0 = v[i] * sacc;
+        o1 = v[i + 1] * sacc;
+      } else if constexpr (EPI == EPI_BF16_AXPBY) {
+        // Round the product first, as a bf16 matmul followed by a bf16 add would.
+        o0 = bf2f(f2bf(v[i] * sacc)) + p.s_res * rv[i];
+        o1 = bf2f(f2bf(v[i + 1] * sacc)) + p.s_res * rv[i + 1];
+      } else if constexpr (EPI == EPI_RELU2) {
+        const float h0 = bf2f(f2bf(v[i])), h1 = bf2f(f2bf(v[i + 1]));
+        pre[i / 2] = pack_bf16x2(h0, h1);
+        const float r0 = fmaxf(h0, 0.f), r1 = fmaxf(h1, 0.f);
+        o0 = r0 * r0;
+        o1 = r1 * r1;
+      } else {  // EPI_RELU2_BWD: d(relu(h)^2)/dh = 2 relu(h)
+        const float g0 = bf2f(f2bf(v[i])), g1 = bf2f(f2bf(v[i + 1]));
+        o0 = g0 * 2.f * fmaxf(rv[i], 0.f);
+        o1 = g1 * 2.f * fmaxf(rv[i + 1], 0.f);
+      }
+      out[i / 2] = pack_bf16x2(o0, o1);
+    }
+    if (full && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(c + 8 * i) = make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+      if constexpr (EPI == EPI_RELU2) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(pp + 8 * i) = make_uint4(pre[4 * i], pre[4 * i + 1], pre[4 * i + 2], pre[4 * i + 3]);
+      }
+    } else {
+      for (int i = 0; i < ncols; ++i) {
+        const uint32_t w = out[i / 2];
+        c[i] = __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xFFFFu)));
+        if constexpr (EPI == EPI_RELU2) {
+          const uint32_t q = pre[i / 2];
+          pp[i] = __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (q >> 16) : (q & 0xFFFFu)));
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int A_MN, int B_MN, int EPI, int STAGES>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFFSET);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int b, mb, nb;
+        tile_coords(t, p, b, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, 0x100u + stage, abort_flag)) { ok = false; break; }
+          uint8_t* sA = smem + stage * S::STAGE_BYTES;
+          uint8_t* sB = sA + S::A_BYTES;
+          mbar_expect_tx(&full[stage], S::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if constexpr (A_MN == 0) {
+            tma_load_3d(sA, &tmA, &full[stage], k0, m0, b);
+          } else {
+            tma_load_3d(sA, &tmA, &full[stage], m0, k0, b);
+            tma_load_3d(sA + 8192, &tmA, &full[stage], m0 + 64, k0, b);
+          }
+          if constexpr (B_MN == 0) {
+            tma_load_3d(sB, &tmB, &full[stage], k0, n0, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, b);
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: wait (bounded) until the copies of the last issued stages have landed.
+      const int outstanding = issued < STAGES ? issued : STAGES;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < outstanding; ++i) {
+        if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+        mbar_wait(&full[s], ph, 0x180u + s, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, 0x200u + acc, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, 0x300u + stage, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            // K-major: step 32 bytes along the swizzled 128-byte row.
+            // MN-major: step 16 rows of 128 bytes (two 8-row swizzle atoms).
+            const uint64_t ad = A_MN ? smem_desc(a_addr + j * 2048, 8192, 1024) : smem_desc(a_addr + j * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(b_addr + j * 2048, 8192, 1024) : smem_desc(b_addr + j * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    const float sacc = p.s_ptr ? p.s_acc * *p.s_ptr : p.s_acc;
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
+      tc_fence_after();
+      int b, mb, nb;
+      tile_coords(t, p, b, mb, nb);
+      const int row = mb * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_wait_ld();
+        epilogue32<EPI>(p, sacc, b, row, nb * BN + c * 32, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// 3-D bf16 tensor map: dims {inner, outer, batch}, box {64, box_outer, 1}, 128-byte swizzle.
+static CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
+                            int64_t batch_stride, int box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16) throw std::runtime_error("gemm operand is not 16-byte aligned");
+  if ((ld * 2) % 16 || (batch > 1 && (batch_stride * 2) % 16))
+    throw std::runtime_error("gemm operand strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2),
+                           static_cast<cuuint64_t>((batch > 1 ? batch_stride : ld * outer) * 2)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_outer), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return map;
+}
+
+template <int BN, int A_MN, int B_MN, int EPI>
+static void launch_t(const GemmArgs& g, cudaStream_t stream) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  using S = Smem<BN, STAGES>;
+  // A: logical [M, K].  K-major storage [M rows, K cols] (inner = K); M-major [K rows, M cols].
+  CUtensorMap ta = A_MN == 0 ? make_map(g.A, g.K, g.M, g.lda, g.batch, g.strideA, BM)
+                             : make_map(g.A, g.M, g.K, g.lda, g.batch, g.strideA, BK);
+  CUtensorMap tb = B_MN == 0 ? make_map(g.B, g.K, g.N, g.ldb, g.batch, g.strideB, BN)
+                             : make_map(g.B, g.N, g.K, g.ldb, g.batch, g.strideB, BK);
+  Params p;
+  p.M = g.M; p.N = g.N; p.K = g.K; p.batch = g.batch;
+  p.tiles_m = (g.M + BM - 1) / BM;
+  p.tiles_n = (g.N + BN - 1) / BN;
+  p.epi = EPI;
+  p.C = g.C; p.ldc = g.ldc; p.strideC = g.strideC;
+  p.R = g.R; p.ldr = g.ldr; p.strideR = g.strideR;
+  p.P = g.P; p.ldp = g.ldp; p.strideP = g.strideP;
+  p.s_acc = g.s_acc; p.s_res = g.s_res; p.s_ptr = g.s_ptr;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    configured = true;
+  }
+  const int tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+  kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, p);
+}
+
+template <int BN, int A_MN, int B_MN>
+static void dispatch_epi(const GemmArgs& g, cudaStream_t s) {
+  switch (g.epi) {
+    case EPI_BF16: return launch_t<BN, A_MN, B_MN, EPI_BF16>(g, s);
+    case EPI_F32: return launch_t<BN, A_MN, B_MN, EPI_F32>(g, s);
+    case EPI_F32_ACC: return launch_t<BN, A_MN, B_MN, EPI_F32_ACC>(g, s);
+    case EPI_BF16_AXPBY: return launch_t<BN, A_MN, B_MN, EPI_BF16_AXPBY>(g, s);
+    case EPI_RELU2: return launch_t<BN, A_MN, B_MN, EPI_RELU2>(g, s);
+    case EPI_RELU2_BWD: return launch_t<BN, A_MN, B_MN, EPI_RELU2_BWD>(g, s);
+    default: throw std::runtime_error("unknown gemm epilogue");
+  }
+}
+
+template <int BN>
+static void dispatch_major(const GemmArgs& g, cudaStream_t s) {
+  if (!g.a_mn && !g.b_mn) return dispatch_epi<BN, 0, 0>(g, s);
+  if (!g.a_mn && g.b_mn) return dispatch_epi<BN, 0, 1>(g, s);
+  if (g.a_mn && !g.b_mn) return dispatch_epi<BN, 1, 0>(g, s);
+  return dispatch_epi<BN, 1, 1>(g, s);
+}
+
+}  // namespace gemm
+}  // namespace nt
+
+void nt_gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+  using namespace nt::gemm;
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return;
+  // BN = 256 halves B-operand shared-memory traffic per MMA; N = 128 tiles keep more CTAs busy
+  // when the 256-wide grid would leave most SMs idle.
+  const long tiles256 = static_cast<long>(g.batch) * ((g.M + 127) / 128) * ((g.N + 255) / 256);
+  const bool wide = g.N >= 256 && tiles256 >= 2L * g.num_sms;
+  if (wide) dispatch_major<256>(g, stream);
+  else dispatch_major<128>(g, stream);
+}
+
+int nt_gemm_read_error(unsigned* where) {
+  nt::ErrorWord w{0, 0};
+  cudaMemcpyFromSymbol(&w, nt::g_nt_error, sizeof(w));
+  if (where) *where = w.where;
+  return static_cast<int>(w.code);
+}

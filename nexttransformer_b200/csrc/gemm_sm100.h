@@ -1,0 +1,41 @@
+// Host interface of the sm_100a GEMM engine (gemm_sm100.cu).
+#pragma once
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+// Fused epilogues.  acc is the fp32 accumulator of sum_k A[m,k] B[n,k].
+enum NtGemmEpilogue : int {
+  EPI_BF16 = 0,        // C(bf16) = s_acc * acc
+  EPI_F32 = 1,         // C(f32)  = s_acc * acc
+  EPI_F32_ACC = 2,     // C(f32) += s_acc * acc              (weight-gradient accumulation)
+  EPI_BF16_AXPBY = 3,  // C(bf16) = bf16(s_acc * acc) + s_res * R   (residual add, Newton-Schulz)
+  EPI_RELU2 = 4,       // P(bf16) = acc ; C(bf16) = relu(P)^2        (MLP up-projection)
+  EPI_RELU2_BWD = 5,   // C(bf16) = bf16(acc) * 2 relu(R)            (R = saved pre-activation)
+};
+
+struct GemmArgs {
+  int M = 0, N = 0, K = 0, batch = 1;
+  // A is logical [M, K]: a_mn = 0 -> stored [M, K] with row stride lda (elements);
+  //                      a_mn = 1 -> stored [K, M] with row stride lda.
+  const void* A = nullptr;
+  int64_t lda = 0, strideA = 0;
+  int a_mn = 0;
+  // B is logical [N, K]: b_mn = 0 -> stored [N, K]; b_mn = 1 -> stored [K, N].
+  const void* B = nullptr;
+  int64_t ldb = 0, strideB = 0;
+  int b_mn = 0;
+  void* C = nullptr;
+  int64_t ldc = 0, strideC = 0;
+  const void* R = nullptr;
+  int64_t ldr = 0, strideR = 0;
+  void* P = nullptr;
+  int64_t ldp = 0, strideP = 0;
+  float s_acc = 1.f, s_res = 1.f;
+  const float* s_ptr = nullptr;  // optional device scalar multiplying s_acc
+  int epi = EPI_BF16;
+  int num_sms = 148;
+};
+
+void nt_gemm_launch(const GemmArgs& args, cudaStream_t stream);
+// Returns the first error code recorded by a bounded wait in a GEMM kernel (0 = none).
+int nt_gemm_read_error(unsigned* where);

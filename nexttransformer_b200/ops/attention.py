@@ -1,0 +1,83 @@
+"""Causal (optionally sliding-window, GQA) attention on the packed q|k|v projection.
+
+``attention_fn(qkv, B, T, H, Hk, D, window)`` takes the ``[B*T, (H + 2 Hk) D]`` output of the
+QKV GEMM (after RoPE / QK-norm) and returns ``y [B*T, H D]``; its backward returns ``dqkv`` in
+the same packed layout, which the QKV input-gradient GEMM consumes directly.
+
+On CUDA the forward and backward run the sm_100a flash-attention kernels of
+``csrc/attention_sm100.cu``.  ``window`` is the reference's left window: a query at position t
+sees keys t - window .. t; a window >= T - 1 is plain causal attention.
+"""
+import math
+
+import torch
+from torch.autograd import Function
+
+from nexttransformer_b200.ops._ext import ext
+from nexttransformer_b200.models.shell import sdpa
+
+# Set by the kernel module once the tcgen05 path is validated for a (D, dtype) pair.
+KERNEL_HEAD_DIMS = (128,)
+
+
+def _use_kernel(qkv, D):
+    return qkv.is_cuda and D in KERNEL_HEAD_DIMS and getattr(ext(), "attn_fwd", None) is not None and _kernel_enabled
+
+
+_kernel_enabled = False  # flipped on once the tcgen05 kernels are validated on B200
+
+
+class _KernelAttn(Function):
+    @staticmethod
+    def forward(ctx, qkv, B, T, H, Hk, D, window):
+        lib = ext()
+        M = B * T
+        q = qkv[:, :H * D]
+        k = qkv[:, H * D:(H + Hk) * D]
+        v = qkv[:, (H + Hk) * D:]
+        o = torch.empty(M, H * D, device=qkv.device, dtype=torch.bfloat16)
+        lse = torch.empty(B, H, T, device=qkv.device, dtype=torch.float32)
+        w = window if 0 <= window < T - 1 else -1
+        lib.attn_fwd(q, k, v, o, lse, B, T, H, Hk, D, w, 1.0 / math.sqrt(D))
+        ctx.save_for_backward(qkv, o, lse)
+        ctx.shape = (B, T, H, Hk, D, w)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse = ctx.saved_tensors
+        B, T, H, Hk, D, w = ctx.shape
+        lib = ext()
+        M = B * T
+        dqkv = torch.empty_like(qkv)
+        dq_acc = torch.zeros(M, H * D, device=qkv.device, dtype=torch.float32)
+        delta = torch.empty(B, H, T, device=qkv.device, dtype=torch.float32)
+        lib.attn_bwd(qkv[:, :H * D], qkv[:, H * D:(H + Hk) * D], qkv[:, (H + Hk) * D:], o, lse, do.contiguous(),
+                     dqkv[:, :H * D], dqkv[:, H * D:(H + Hk) * D], dqkv[:, (H + Hk) * D:], dq_acc, delta,
+                     B, T, H, Hk, D, w, 1.0 / math.sqrt(D))
+        return dqkv, None, None, None, None, None, None
+
+
+class _LibraryAttn(Function):
+    """PyTorch SDPA inside a private autograd graph (oracle, CPU, unsupported head dims)."""
+
+    @staticmethod
+    def forward(ctx, qkv, B, T, H, Hk, D, window):
+        with torch.enable_grad():
+            leaf = qkv.detach().requires_grad_()
+            v4 = leaf.view(B, T, H + 2 * Hk, D)
+            y = sdpa(v4[:, :, :H], v4[:, :, H:H + Hk], v4[:, :, H + Hk:], window).reshape(B * T, H * D)
+        ctx.leaf, ctx.y = leaf, y
+        return y.detach()
+
+    @staticmethod
+    def backward(ctx, dy):
+        (dqkv,) = torch.autograd.grad(ctx.y, ctx.leaf, dy)
+        ctx.leaf = ctx.y = None
+        return dqkv, None, None, None, None, None, None
+
+
+def attention_fn(qkv, B, T, H, Hk, D, window):
+    if _use_kernel(qkv, D):
+        return _KernelAttn.apply(qkv, B, T, H, Hk, D, window)
+    return _LibraryAttn.apply(qkv, B, T, H, Hk, D, window)

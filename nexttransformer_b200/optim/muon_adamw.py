@@ -1,0 +1,291 @@
+"""Muon + AdamW with ZeRO-style ownership, on the sm_100a kernels.
+
+The update rules are the reference's (``nanochat/optim.py``):
+  * AdamW: decoupled decay ``p *= 1 - lr wd``, moments by lerp, bias correction, ``eps`` outside
+    the square root.  Moments are kept in fp32 (the reference keeps them in the parameter's
+    dtype, bf16 for embeddings).
+  * Muon: Nesterov momentum by lerp -> bf16 -> MuonEq row equilibration -> Frobenius normalise
+    (x 1.01) -> 5 Polar-Express quintic iterations with per-step coefficients (tall/wide
+    forms) -> Muon+ renormalisation to sqrt(min(m, n)) -> NorMuon factored second moment
+    (beta2) -> cautious weight decay; learning rate scaled by sqrt(max(1, m / n)).
+
+Distribution (world > 1): each rank owns whole Muon matrices (``ceil(K / world)`` of every
+same-shape group, in group order) and row slices of the large AdamW tensors.  Gradients are
+reduced to their owner (averaged), the owner updates, and updated parameters are sent back
+to every rank - reduce-scatter + all-gather volume, never a full all-reduce of gradients.
+
+Gradients are read from ``p.main_grad`` when a fused path produced one, else ``p.grad``.
+"""
+import math
+
+import torch
+import torch.distributed as dist
+
+POLAR_EXPRESS = (
+    (8.156554524902461, -22.48329292557795, 15.878769915207462),
+    (4.042929935166739, -2.808917465908714, 0.5000178451051316),
+    (3.8916678022926607, -2.772484153217685, 0.5060648178503393),
+    (3.285753657755655, -2.3681294933425376, 0.46449024233003106),
+    (2.3465413258596377, -1.7097828382687081, 0.42323551169305323),
+)
+
+
+def grad_of(p):
+    g = getattr(p, "main_grad", None)
+    return g if g is not None else p.grad
+
+
+# ------------------------------------------------------------------ reference math (any device)
+@torch.no_grad()
+def adamw_reference(p, g, m, v, step, lr, b1, b2, eps, wd):
+    p32 = p.float()
+    p32.mul_(1 - lr * wd)
+    m.lerp_(g.float(), 1 - b1)
+    v.lerp_(g.float().square(), 1 - b2)
+    denom = (v / (1 - b2 ** step)).sqrt() + eps
+    p32.add_(m / denom, alpha=-lr / (1 - b1 ** step))
+    p.copy_(p32)
+
+
+@torch.no_grad()
+def muon_reference(grads, params, mom, smb, momentum, lr, wd, beta2, ns_steps, compute_dtype=torch.bfloat16):
+    """One Muon step on stacked [K, m, n] tensors (grads are consumed)."""
+    mom.lerp_(grads, 1 - momentum)
+    g = grads.lerp_(mom, momentum)
+    X = g.to(compute_dtype)
+    target = X.float().norm(dim=(-2, -1), keepdim=True) / X.size(-2) ** 0.5
+    rown = X.float().norm(dim=-1, keepdim=True).clamp_min(1e-6)
+    X = X * (target / rown).to(X.dtype)
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) * 1.01 + 1e-6)
+    tall = g.size(-2) > g.size(-1)
+    for a, b, c in POLAR_EXPRESS[:ns_steps]:
+        if tall:
+            A = X.mT @ X
+            X = a * X + X @ (b * A + c * (A @ A))
+        else:
+            A = X @ X.mT
+            X = a * X + (b * A + c * (A @ A)) @ X
+    g = X.to(params.dtype)
+    g = g * (min(g.size(-2), g.size(-1)) ** 0.5 / g.float().norm(dim=(-2, -1), keepdim=True).clamp_min(1e-6)).to(g.dtype)
+    red = -1 if g.size(-2) >= g.size(-1) else -2
+    vmean = g.float().square().mean(dim=red, keepdim=True)
+    rsize = g.size(red)
+    vnorm = (vmean.sum(dim=(-2, -1), keepdim=True) * rsize).sqrt()
+    smb.lerp_(vmean.to(smb.dtype), 1 - beta2)
+    step = smb.clamp_min(1e-10).rsqrt()
+    vnew = ((vmean * rsize) * step.float().square()).sum(dim=(-2, -1), keepdim=True).sqrt()
+    g = g * (step * (vnorm / vnew.clamp_min(1e-10))).to(g.dtype)
+    mask = (g * params) >= 0
+    params.sub_(lr * g + lr * wd * params * mask)
+
+
+# ------------------------------------------------------------------ optimizer
+class MuonAdamW(torch.optim.Optimizer):
+    """param_groups: dicts with ``kind`` 'adamw' (lr, betas, eps, weight_decay) or 'muon'
+    (lr, momentum, ns_steps, beta2, weight_decay); every Muon group holds same-shape matrices."""
+
+    def __init__(self, param_groups, shadows=None):
+        super().__init__(param_groups, defaults={})
+        # fp32 master -> bf16 shadow written by the update (the fused forward reads shadows)
+        self.shadows = shadows or {}
+        self._work = {}
+
+    # -------------------------------------------------------------- helpers
+    @staticmethod
+    def _dist():
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            return dist.get_rank(), dist.get_world_size()
+        return 0, 1
+
+    def _adamw_state(self, p, rows):
+        st = self.state[p]
+        if not st:
+            st["step"] = 0
+            st["rows"] = rows
+            shape = (rows.stop - rows.start, *p.shape[1:]) if rows is not None else p.shape
+            st["exp_avg"] = torch.zeros(shape, device=p.device, dtype=torch.float32)
+            st["exp_avg_sq"] = torch.zeros(shape, device=p.device, dtype=torch.float32)
+        return st
+
+    # -------------------------------------------------------------- AdamW
+    def _adamw_plan(self, group, rank, world):
+        """(param, row slice or None, reduce work handle, reduced grad slice) per parameter."""
+        plans = []
+        for p in group["params"]:
+            g = grad_of(p)
+            if g is None:
+                raise RuntimeError("missing gradient in the fixed training graph")
+            if world == 1:
+                plans.append((p, None, None, g))
+            elif p.numel() < 1024 or p.shape[0] % world:
+                work = dist.all_reduce(g, op=dist.ReduceOp.AVG, async_op=True)
+                plans.append((p, None, work, g))
+            else:
+                n = p.shape[0] // world
+                out = torch.empty((n, *g.shape[1:]), device=g.device, dtype=g.dtype)
+                work = dist.reduce_scatter_tensor(out, g.contiguous(), op=dist.ReduceOp.AVG, async_op=True)
+                plans.append((p, slice(rank * n, (rank + 1) * n), work, out))
+        return plans
+
+    def _adamw_apply(self, group, plans, world, gathers):
+        b1, b2 = group["betas"]
+        for p, rows, work, g in plans:
+            if work is not None:
+                work.wait()
+            st = self._adamw_state(p, rows)
+            st["step"] += 1
+            pv = p.data if rows is None else p.data[rows]
+            gv = g if g.dtype == torch.float32 else g.float()
+            shadow = self.shadows.get(p)
+            if pv.is_cuda:
+                from nexttransformer_b200.ops._ext import ext
+                sh = None
+                if shadow is not None and rows is None and shadow.is_contiguous():
+                    sh = shadow
+                ext().adamw(pv, gv.contiguous(), st["exp_avg"], st["exp_avg_sq"], sh, group["lr"], b1, b2,
+                            group["eps"], group["weight_decay"], st["step"])
+                if shadow is not None and sh is None:
+                    gathers.append(("shadow", p, shadow))
+            else:
+                adamw_reference(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], b1, b2,
+                                group["eps"], group["weight_decay"])
+            if rows is not None:
+                gathers.append(("adamw", p, dist.all_gather_into_tensor(p.data, p.data[rows].contiguous(),
+                                                                          async_op=True)))
+
+    # -------------------------------------------------------------- Muon
+    def _muon_owned(self, group, rank, world):
+        params = group["params"]
+        chunk = math.ceil(len(params) / world)
+        lo = rank * chunk
+        return params, chunk, list(range(lo, min(lo + chunk, len(params))))
+
+    def _muon_reduce(self, group, rank, world):
+        params, chunk, _ = self._muon_owned(group, rank, world)
+        if world == 1:
+            return []
+        works = []
+        for i, p in enumerate(params):
+            works.append(dist.reduce(grad_of(p), dst=min(i // chunk, world - 1), op=dist.ReduceOp.SUM,
+                                     async_op=True))
+        return works
+
+    def _muon_apply(self, group, rank, world, works, gathers):
+        for w in works:
+            w.wait()
+        params, chunk, owned = self._muon_owned(group, rank, world)
+        shape = params[0].shape
+        m, n = shape[-2], shape[-1]
+        lr = group["lr"] * max(1.0, m / n) ** 0.5
+        if owned:
+            mine = [params[i] for i in owned]
+            for p in mine:
+                st = self.state[p]
+                if "momentum_buffer" not in st:
+                    st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.float32)
+                    st["second_momentum_buffer"] = torch.zeros((m, 1) if m >= n else (1, n), device=p.device,
+                                                               dtype=torch.float32)
+            if world > 1:
+                for p in mine:
+                    grad_of(p).div_(world)
+            if mine[0].is_cuda:
+                self._muon_cuda(group, mine, m, n, lr)
+            else:
+                grads = torch.stack([grad_of(p).float() for p in mine])
+                stack = torch.stack([p.data for p in mine])
+                mom = torch.stack([self.state[p]["momentum_buffer"] for p in mine])
+                smb = torch.stack([self.state[p]["second_momentum_buffer"] for p in mine])
+                muon_reference(grads, stack, mom, smb, group["momentum"], lr, group["weight_decay"], group["beta2"],
+                               group["ns_steps"], torch.bfloat16)
+                for j, p in enumerate(mine):
+                    p.data.copy_(stack[j])
+                    self.state[p]["momentum_buffer"].copy_(mom[j])
+                    self.state[p]["second_momentum_buffer"].copy_(smb[j])
+                    if p in self.shadows:
+                        self.shadows[p].copy_(p.data)
+        if world > 1:
+            for i, p in enumerate(params):
+                src = min(i // chunk, world - 1)
+                gathers.append(("muon", p, dist.broadcast(p.data, src=src, async_op=True)))
+                if p in self.shadows:
+                    gathers.append(("shadow", p, self.shadows[p]))
+
+    def _ptrs(self, tensors):
+        return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64).to(tensors[0].device,
+                                                                                   non_blocking=True)
+
+    def _muon_cuda(self, group, mine, m, n, lr):
+        from nexttransformer_b200.ops._ext import ext
+        from nexttransformer_b200.ops import gemm as G
+        lib = ext()
+        K = len(mine)
+        dev = mine[0].device
+        key = (m, n, K)
+        if key not in self._work:
+            s = min(m, n)
+            L = m if m >= n else n
+            self._work[key] = dict(
+                X=torch.empty(K, m, n, device=dev, dtype=torch.bfloat16),
+                X2=torch.empty(K, m, n, device=dev, dtype=torch.bfloat16),
+                A=torch.empty(K, s, s, device=dev, dtype=torch.bfloat16),
+                Bm=torch.empty(K, s, s, device=dev, dtype=torch.bfloat16),
+                rowss=torch.empty(K, m, device=dev, dtype=torch.float32),
+                tot=torch.empty(K, device=dev, dtype=torch.float32),
+                red=torch.empty(K, L, device=dev, dtype=torch.float32),
+                fscale=torch.empty(K, L, device=dev, dtype=torch.float32))
+        w = self._work[key]
+        grads = [grad_of(p) for p in mine]
+        if any(g.dtype != torch.float32 or not g.is_contiguous() for g in grads):
+            grads = [g.float().contiguous() for g in grads]
+        g_ptr = self._ptrs(grads)
+        m_ptr = self._ptrs([self.state[p]["momentum_buffer"] for p in mine])
+        s_ptr = self._ptrs([self.state[p]["second_momentum_buffer"] for p in mine])
+        p_ptr = self._ptrs([p.data for p in mine])
+        shadows = [self.shadows.get(p) for p in mine]
+        sh_ptr = self._ptrs(shadows) if all(s is not None and s.is_contiguous() for s in shadows) else None
+        X, X2, A, Bm = w["X"], w["X2"], w["A"], w["Bm"]
+        lib.muon_prep(g_ptr, m_ptr, X, w["rowss"], group["momentum"])
+        lib.muon_normalize(X, w["rowss"], w["tot"])
+        tall = m > n
+        for a, b, c in POLAR_EXPRESS[:group["ns_steps"]]:
+            if tall:
+                G.gemm(X, X, A, a_mn=True, b_mn=True)
+                G.gemm(A, A, Bm, b_mn=True, epi=G.EPI_BF16_AXPBY, r=A, s_acc=c, s_res=b)
+                G.gemm(X, Bm, X2, b_mn=True, epi=G.EPI_BF16_AXPBY, r=X, s_acc=1.0, s_res=a)
+            else:
+                G.gemm(X, X, A)
+                G.gemm(A, A, Bm, b_mn=True, epi=G.EPI_BF16_AXPBY, r=A, s_acc=c, s_res=b)
+                G.gemm(Bm, X, X2, b_mn=True, epi=G.EPI_BF16_AXPBY, r=X, s_acc=1.0, s_res=a)
+            X, X2 = X2, X
+        lib.muon_finish(X, w["red"], w["tot"], s_ptr, w["fscale"], p_ptr, sh_ptr, group["beta2"], lr,
+                        group["weight_decay"])
+        if sh_ptr is None:
+            for p, s in zip(mine, shadows):
+                if s is not None:
+                    s.copy_(p.data)
+
+    # -------------------------------------------------------------- step
+    @torch.no_grad()
+    def step(self):
+        rank, world = self._dist()
+        plans = []
+        for group in self.param_groups:
+            if group["kind"] == "adamw":
+                plans.append(self._adamw_plan(group, rank, world))
+            elif group["kind"] == "muon":
+                plans.append(self._muon_reduce(group, rank, world))
+            else:
+                raise ValueError(f"unknown optimizer kind {group['kind']!r}")
+        gathers = []
+        for group, plan in zip(self.param_groups, plans):
+            if group["kind"] == "adamw":
+                self._adamw_apply(group, plan, world, gathers)
+            else:
+                self._muon_apply(group, rank, world, plan, gathers)
+        for kind, p, item in gathers:
+            if kind == "shadow":
+                continue
+            item.wait()
+        for kind, p, item in gathers:
+            if kind == "shadow":
+                item.copy_(p.data)

@@ -1,0 +1,49 @@
+"""Training-step engine: the public per-update call of the framework.
+
+``Trainer(model, optimizer, accumulation).step(inputs, targets)`` runs one optimizer update:
+micro-batches are copied host->device (pinned, non-blocking), forward/backward through the
+model (the fused sm_100a path on CUDA), gradients reduced to their owners and the Muon/AdamW
+update applied by the optimizer, then the mean loss is read back to the host.
+"""
+import torch
+
+from nexttransformer_b200.optim.groups import set_schedule
+
+
+class Trainer:
+    def __init__(self, model, optimizer, accumulation=1, train_config=None, schedule=True):
+        self.model = model
+        self.optimizer = optimizer
+        self.accumulation = accumulation
+        self.train_config = train_config
+        self.schedule = schedule and train_config is not None
+        self.step_index = 0
+        self.device = model.get_device()
+
+    def zero_grad(self):
+        m = self.model
+        if hasattr(m, "zero_main_grads") and getattr(m, "_fused", None) is not None:
+            m.zero_main_grads()
+        for p in m.parameters():
+            p.grad = None
+
+    def step_device(self, inputs, targets):
+        """One update on device-resident micro-batches ``inputs[i], targets[i]``; returns the loss tensor."""
+        if self.schedule:
+            set_schedule(self.optimizer, self.step_index, self.train_config)
+        self.zero_grad()
+        total = torch.zeros((), device=self.device, dtype=torch.float32)
+        for x, y in zip(inputs, targets):
+            loss = self.model(x, y)
+            (loss / self.accumulation).backward()
+            total += loss.detach().float()
+        self.optimizer.step()
+        self.step_index += 1
+        return total / self.accumulation
+
+    def step(self, inputs, targets):
+        """One update from host (pinned) micro-batches; returns the mean loss as a Python float."""
+        dev = self.device
+        xs = [x.to(dev, non_blocking=True) for x in inputs]
+        ys = [y.to(dev, non_blocking=True) for y in targets]
+        return float(self.step_device(xs, ys))

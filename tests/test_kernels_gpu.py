@@ -1,0 +1,249 @@
+"""Numerics of the sm_100a kernels against plain-PyTorch fp32 references (CUDA only)."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from nexttransformer_b200.ops._ext import ext
+    return ext()
+
+
+def _close(a, b, rtol, atol=1e-3):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    ref = b.abs().max().item()
+    assert err <= atol + rtol * ref, f"max err {err} vs scale {ref}"
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (300, 200, 136), (1024, 768, 1280), (4096, 2560, 1280)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_storage_orders(M, N, K, a_mn, b_mn):
+    from nexttransformer_b200.ops import gemm as G
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(N, K, device="cuda").bfloat16()
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    G.gemm(a, b, C, a_mn=a_mn, b_mn=b_mn)
+    torch.cuda.synchronize()
+    _close(C, A.float() @ B.float().t(), rtol=1e-2, atol=1e-1)
+    from nexttransformer_b200.ops._ext import check_errors
+    check_errors()
+
+
+def test_gemm_epilogues():
+    from nexttransformer_b200.ops import gemm as G
+    torch.manual_seed(1)
+    M, N, K = 512, 384, 256
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") / 16).bfloat16()
+    ref = A.float() @ B.float().t()
+    R = torch.randn(M, N, device="cuda").bfloat16()
+    # f32 + accumulate
+    C = torch.ones(M, N, device="cuda")
+    G.gemm(A, B, C, epi=G.EPI_F32_ACC, s_acc=0.5)
+    _close(C, 1 + 0.5 * ref, rtol=1e-3, atol=1e-2)
+    G.gemm(A, B, C, epi=G.EPI_F32)
+    _close(C, ref, rtol=1e-3, atol=1e-2)
+    # device scale
+    s = torch.tensor([0.25], device="cuda")
+    G.gemm(A, B, C, epi=G.EPI_F32, s_dev=s, s_acc=2.0)
+    _close(C, 0.5 * ref, rtol=1e-3, atol=1e-2)
+    # axpby
+    Cb = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    G.gemm(A, B, Cb, epi=G.EPI_BF16_AXPBY, r=R, s_acc=2.0, s_res=-0.5)
+    _close(Cb, 2 * ref - 0.5 * R.float(), rtol=2e-2, atol=5e-2)
+    # relu^2 with pre-activation
+    P = torch.empty_like(Cb)
+    G.gemm(A, B, Cb, epi=G.EPI_RELU2, p=P)
+    _close(P, ref, rtol=1e-2, atol=5e-2)
+    _close(Cb, F.relu(P.float()).square(), rtol=1e-2, atol=5e-2)
+    # relu^2 backward
+    G.gemm(A, B, Cb, epi=G.EPI_RELU2_BWD, r=R)
+    _close(Cb, ref * 2 * F.relu(R.float()), rtol=2e-2, atol=1e-1)
+
+
+def test_gemm_batched():
+    from nexttransformer_b200.ops import gemm as G
+    torch.manual_seed(2)
+    X = torch.randn(3, 320, 640, device="cuda").bfloat16()
+    A = torch.empty(3, 320, 320, device="cuda", dtype=torch.bfloat16)
+    G.gemm(X, X, A)
+    _close(A, X.float() @ X.float().mT, rtol=1e-2, atol=5e-1)
+    At = torch.empty(3, 640, 640, device="cuda", dtype=torch.bfloat16)
+    G.gemm(X, X, At, a_mn=True, b_mn=True)
+    _close(At, X.float().mT @ X.float(), rtol=1e-2, atol=5e-1)
+    Y = torch.empty_like(X)
+    G.gemm(A, X, Y, b_mn=True)
+    _close(Y, A.float() @ X.float(), rtol=1e-2, atol=5e-1)
+
+
+def test_norms():
+    lib = _lib()
+    torch.manual_seed(3)
+    M, d = 1000, 1280
+    x = torch.randn(M, d, device="cuda").bfloat16()
+    x0 = torch.randn(M, d, device="cuda").bfloat16()
+    ab = torch.tensor([1.1, 0.15], device="cuda")
+    xm, h = torch.empty_like(x), torch.empty_like(x)
+    lib.mix_norm_fwd(x, x0, ab, xm, h, None, 1.0)
+    ref_xm = (ab[0].bfloat16() * x) + (ab[1].bfloat16() * x0)
+    _close(xm, ref_xm, rtol=1e-2, atol=2e-2)
+    _close(h, F.rms_norm(xm.float(), (d,)), rtol=1e-2, atol=2e-2)
+    # backward
+    xr = xm.float().requires_grad_()
+    y = F.rms_norm(xr, (d,))
+    dy = torch.randn(M, d, device="cuda").bfloat16()
+    dres = torch.randn(M, d, device="cuda").bfloat16()
+    y.backward(dy.float())
+    dx = torch.empty_like(x)
+    lib.norm_bwd(xm, dy, dres, dx)
+    _close(dx, xr.grad + dres.float(), rtol=2e-2, atol=2e-2)
+    # mix backward
+    acc = torch.zeros(M, d, device="cuda")
+    part = torch.empty(M, 2, device="cuda")
+    lib.mix_norm_bwd(x, x0, xm, dy, dres, ab, dx, acc, part)
+    g = xr.grad + dres.float()
+    a, b = ab[0].bfloat16().float(), ab[1].bfloat16().float()
+    _close(dx, a * g, rtol=2e-2, atol=2e-2)
+    _close(acc, b * g, rtol=1e-2, atol=1e-2)
+    _close(part.sum(0), torch.stack(((g * x.float()).sum(), (g * x0.float()).sum())), rtol=1e-2, atol=1.0)
+
+
+def test_rope_norm_ve_roundtrip():
+    from nexttransformer_b200.models.shell import apply_rotary_emb
+    lib = _lib()
+    torch.manual_seed(4)
+    B, T, H, Hk, D = 2, 256, 4, 2, 128
+    M = B * T
+    qkv = torch.randn(M, (H + 2 * Hk) * D, device="cuda").bfloat16()
+    t = torch.arange(T, device="cuda", dtype=torch.float32)
+    inv = 1.0 / (100000 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    f = torch.outer(t, inv)
+    cos, sin = f.cos().bfloat16().contiguous(), f.sin().bfloat16().contiguous()
+    V = 50
+    ve_table = torch.randn(V, Hk * D, device="cuda").bfloat16()
+    idx = torch.randint(0, V, (M,), device="cuda")
+    h = torch.randn(M, 512, device="cuda").bfloat16()
+    wg = (torch.rand(Hk, 12, device="cuda") * 0.02).bfloat16()
+    out = qkv.clone()
+    rstd = torch.empty(M, H + Hk, device="cuda")
+    gate = torch.empty(M, Hk, device="cuda")
+    lib.rope_norm_fwd(out, cos, sin, rstd, T, H, Hk, D, 1.2, ve_table, idx, h, wg, gate)
+    # reference
+    v4 = qkv.float().view(B, T, H + 2 * Hk, D).requires_grad_()
+    c4, s4 = cos.float()[None, :, None, :], sin.float()[None, :, None, :]
+    q = F.rms_norm(apply_rotary_emb(v4[:, :, :H], c4, s4), (D,)) * 1.2
+    k = F.rms_norm(apply_rotary_emb(v4[:, :, H:H + Hk], c4, s4), (D,)) * 1.2
+    z = h[:, :12].float() @ wg.float().t()
+    g = 3 * torch.sigmoid(z)
+    v = v4[:, :, H + Hk:] + g.view(B, T, Hk, 1) * ve_table.float()[idx].view(B, T, Hk, D)
+    ref = torch.cat((q, k, v), 2).reshape(M, -1)
+    _close(out, ref, rtol=2e-2, atol=3e-2)
+    _close(gate, g, rtol=1e-2, atol=1e-2)
+    dout = torch.randn_like(ref)
+    ref.backward(dout)
+    d = dout.bfloat16().contiguous()
+    dz = torch.empty(M, Hk, device="cuda")
+    vg = torch.zeros(V, Hk * D, device="cuda")
+    lib.rope_norm_bwd(d, out, cos, sin, rstd, T, H, Hk, D, 1.2, ve_table, idx, gate, dz, vg)
+    _close(d, v4.grad.reshape(M, -1), rtol=3e-2, atol=5e-2)
+
+
+def test_softcap_ce():
+    lib = _lib()
+    torch.manual_seed(5)
+    rows, V, Vp = 64, 1000, 1024
+    logits = (torch.randn(rows, Vp, device="cuda") * 20).bfloat16()
+    tgt = torch.randint(0, V, (rows,), device="cuda")
+    tgt[3] = -1
+    lf = logits.float()[:, :V].requires_grad_()
+    z = 15 * torch.tanh(lf / 15)
+    ref = F.cross_entropy(z, tgt, ignore_index=-1, reduction="none")
+    ref.sum().backward()
+    loss = torch.empty(rows, device="cuda")
+    work = logits.clone()
+    lib.softcap_ce(work, tgt, loss, None, V, 15.0)
+    _close(loss, ref, rtol=1e-3, atol=1e-3)
+    _close(work[:, :V], lf.grad, rtol=2e-2, atol=2e-3)
+    assert work[:, V:].abs().max().item() == 0
+
+
+def test_adamw_kernel():
+    from nexttransformer_b200.optim.muon_adamw import adamw_reference
+    lib = _lib()
+    torch.manual_seed(6)
+    p = torch.randn(3000, device="cuda")
+    g = torch.randn(3000, device="cuda")
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    p2, m2, v2 = p.clone(), m.clone(), v.clone()
+    for step in (1, 2, 3):
+        lib.adamw(p, g, m, v, None, 0.01, 0.8, 0.95, 1e-10, 0.1, step)
+        adamw_reference(p2, g, m2, v2, step, 0.01, 0.8, 0.95, 1e-10, 0.1)
+    _close(p, p2, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("shape", [(256, 512), (512, 256), (384, 384)])
+def test_muon_kernels_match_reference(shape):
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW, muon_reference
+    torch.manual_seed(7)
+    K = 3
+    ps = [torch.nn.Parameter(torch.randn(*shape, device="cuda") * 0.02) for _ in range(K)]
+    ref = [p.detach().clone() for p in ps]
+    grads = [torch.randn(*shape, device="cuda") for _ in range(K)]
+    for p, g in zip(ps, grads):
+        p.grad = g.clone()
+    opt = MuonAdamW([dict(kind="muon", params=ps, lr=0.02, momentum=0.95, ns_steps=5, beta2=0.9,
+                          weight_decay=0.1)])
+    opt.step()
+    stack = torch.stack(ref)
+    m, n = shape
+    smb = torch.zeros(K, *((m, 1) if m >= n else (1, n)), device="cuda")
+    muon_reference(torch.stack(grads), stack, torch.zeros_like(stack), smb, 0.95,
+                   0.02 * max(1.0, m / n) ** 0.5, 0.1, 0.9, 5)
+    upd = torch.stack([p.detach() for p in ps]) - torch.stack(ref)
+    rupd = stack - torch.stack(ref)
+    cos = F.cosine_similarity(upd.flatten(), rupd.flatten(), dim=0).item()
+    assert cos > 0.99, cos
+    assert abs(upd.norm().item() / rupd.norm().item() - 1) < 0.05
+
+
+def test_fused_model_matches_eager():
+    from nexttransformer_b200.models.shell import ShellConfig, build_shell
+    torch.manual_seed(8)
+    cfg = ShellConfig(sequence_len=256, vocab_size=1000, n_layer=4, n_head=4, n_kv_head=2, n_embd=512,
+                      window_pattern="SSSL")
+    model = build_shell(cfg, "cuda", seed=3)
+    # give the zero-initialised projections some signal
+    with torch.no_grad():
+        for blk in model.transformer.h:
+            blk.attn.c_proj.weight.normal_(0, 0.02)
+            blk.mlp.c_proj.weight.normal_(0, 0.02)
+        model.smear_lambda.fill_(0.5)
+    idx = torch.randint(0, 1000, (2, 256), device="cuda")
+    tgt = torch.randint(0, 1000, (2, 256), device="cuda")
+    loss_e = model.forward_eager(idx, tgt)
+    loss_e.backward()
+    eager = {n: p.grad.detach().float().clone() for n, p in model.named_parameters()}
+    for p in model.parameters():
+        p.grad = None
+    st = model.fused_state()
+    st.refresh_shadows()
+    model.zero_main_grads()
+    loss_f = model(idx, tgt)
+    loss_f.backward()
+    torch.cuda.synchronize()
+    assert abs(loss_f.item() - loss_e.item()) < 2e-2 * abs(loss_e.item())
+    for n, p in model.named_parameters():
+        g = p.main_grad
+        e = eager[n]
+        if e.abs().max() == 0:
+            continue
+        cos = F.cosine_similarity(g.flatten().float(), e.flatten(), dim=0).item()
+        assert cos > 0.97, (n, cos)
