@@ -1,9 +1,690 @@
-// K1: flash attention for sm_100a (forward and backward) -- see attention_sm100.h.
+// K1: flash attention for sm_100a (causal, optional left window, GQA, head dim 128).
+//
+// Forward (one CTA per (query tile of 128, head, batch); 192 threads):
+//   warp 0      TMA: the Q tile once, then K/V tiles (128 keys) into a 2-stage ring.
+//   warp 1      TMEM owner and MMA issuer: S_t = Q K_t^T into one of two TMEM S buffers
+//               (issued one tile ahead), then O += P_{t-1} V_{t-1} into the TMEM O accumulator.
+//   warps 2..5  softmax, one query row per thread: tcgen05.ld of the S row, online softmax in
+//               the log2 domain, lazy rescaling of O in TMEM (only when the running max grows by
+//               more than 2^8), P written to shared memory in the 128-byte-swizzled K-major
+//               layout the next MMA reads; at the end O / l and the log-sum-exp are stored.
+// Backward (one CTA per (key tile of 128, KV head, batch)), loops over the query heads of the
+// KV group and the query tiles that see the key tile:
+//   S^T = K Q^T and dP^T = V dO^T in TMEM; one thread per key row forms P^T and
+//   dS^T = P^T (dP^T - delta) in shared memory; dV += P^T dO and dK += dS^T Q accumulate in
+//   TMEM over the whole loop; dQ = dS K lands in TMEM and is added to an fp32 buffer with
+//   vector atomics.  Small kernels compute delta = rowsum(dO * O) and convert dQ to bf16.
+// Every mbarrier wait is bounded (see common.cuh).  No TMA load uses cluster multicast.
 #include "attention_sm100.h"
 #include "common.cuh"
 
-int nt_attention_fwd(const AttnArgs&, cudaStream_t) { return -1; }
-int nt_attention_bwd(const AttnArgs&, cudaStream_t) { return -1; }
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace nt {
+namespace attn {
+
+constexpr int TILE = 128;
+constexpr int HD = 128;
+constexpr int BOX_BYTES = TILE * 64 * 2;      // [128 rows x 64 bf16] = 16 KB
+constexpr int TILE_BYTES = 2 * BOX_BYTES;     // [128 rows x 128 bf16] = 32 KB
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct Params {
+  int B, T, H, Hk;
+  int window;
+  float scale_log2;  // softmax scale * log2(e)
+  float scale;
+  __nv_bfloat16* o;
+  int64_t ldo;
+  float* lse;
+  // backward
+  const __nv_bfloat16* dout;
+  int64_t lddo;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t lddk, lddv;
+  float* dq_acc;
+  const float* delta;
+};
+
+// K-major operand made of two [128 rows x 64] swizzled boxes; k-step j covers 16 columns.
+NT_DEVICE uint64_t kmajor_desc(uint32_t base, int j) {
+  return smem_desc(base + (j >> 2) * BOX_BYTES + (j & 3) * 32, 16, 1024);
+}
+// MN-major operand: rows are the reduction index (128 rows), two 64-wide MN boxes.
+NT_DEVICE uint64_t mnmajor_desc(uint32_t base, int j) {
+  return smem_desc(base + j * 2048, BOX_BYTES, 1024);
+}
+
+// Byte offset of 16-byte chunk `c` (0..15) of row `r` in a two-box 128B-swizzled tile.
+NT_DEVICE uint32_t swz_off(int r, int c) {
+  return (c >> 3) * BOX_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+NT_DEVICE float fast_exp2(float x) { return exp2f(x); }
+
+// ------------------------------------------------------------------------------ forward
+struct FwdSmem {
+  static constexpr int Q = 0;
+  static constexpr int K0 = Q + TILE_BYTES;
+  static constexpr int V0 = K0 + 2 * TILE_BYTES;
+  static constexpr int P = V0 + 2 * TILE_BYTES;
+  static constexpr int BAR = P + TILE_BYTES;
+  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, o_done
+  static constexpr int NBAR = 13;
+  static constexpr int TOTAL = BAR + NBAR * 8 + 16 + 1024;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* kv_empty = bars + 5;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_free = bars + 9;
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_done = bars + 12;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + FwdSmem::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.T + TILE - 1) / TILE;
+  const int qt = n_qt - 1 - blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qt * TILE;
+  int j_lo = 0;
+  if (p.window >= 0) j_lo = max(0, (q0 - p.window) / TILE);
+  const int j_hi = min(n_qt - 1, (q0 + TILE - 1) / TILE);
+  const int n_kv = j_hi - j_lo + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint32_t t_o = tbase;          // O accumulator: columns [0, 128)
+  const uint32_t t_s = tbase + 128;    // S buffers: [128, 256), [256, 384)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(sm + FwdSmem::Q, &tmQ, q_full, h * HD, q0, b);
+      tma_load_3d(sm + FwdSmem::Q + BOX_BYTES, &tmQ, q_full, h * HD + 64, q0, b);
+      int issued = 0;
+      for (int t = 0; t < n_kv; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, 0x10u + st, abort_flag)) break;
+        const int k0 = (j_lo + t) * TILE;
+        uint8_t* ks = sm + FwdSmem::K0 + st * TILE_BYTES;
+        uint8_t* vs = sm + FwdSmem::V0 + st * TILE_BYTES;
+        mbar_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_3d(ks, &tmK, &k_full[st], hk * HD, k0, b);
+        tma_load_3d(ks + BOX_BYTES, &tmK, &k_full[st], hk * HD + 64, k0, b);
+        mbar_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_3d(vs, &tmV, &v_full[st], hk * HD, k0, b);
+        tma_load_3d(vs + BOX_BYTES, &tmV, &v_full[st], hk * HD + 64, k0, b);
+        ++issued;
+      }
+      // drain copies still in flight
+      mbar_wait(q_full, 0, 0x1Fu, nullptr);
+      for (int t = max(0, issued - 2); t < issued; ++t) {
+        mbar_wait(&k_full[t & 1], (t >> 1) & 1, 0x1Du, nullptr);
+        mbar_wait(&v_full[t & 1], (t >> 1) & 1, 0x1Eu, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(TILE, TILE, 0, 0);      // S = Q K^T
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(TILE, HD, 0, 1);     // O += P V (V MN-major)
+      const uint32_t q_addr = smem_u32(sm + FwdSmem::Q);
+      const uint32_t p_addr = smem_u32(sm + FwdSmem::P);
+      bool ok = mbar_wait(q_full, 0, 0x20u, abort_flag);
+      for (int t = 0; ok && t <= n_kv; ++t) {
+        if (t < n_kv) {
+          const int st = t & 1;
+          if (!mbar_wait(&k_full[st], (t >> 1) & 1, 0x21u, abort_flag)) break;
+          if (!mbar_wait(&s_free[st], ((t >> 1) & 1) ^ 1u, 0x22u, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm + FwdSmem::K0 + st * TILE_BYTES);
+#pragma unroll
+          for (int j = 0; j < HD / 16; ++j)
+            umma_bf16(t_s + st * 128, kmajor_desc(q_addr, j), kmajor_desc(k_addr, j), idesc, j > 0);
+          umma_commit(&s_full[st]);
+        }
+        if (t > 0) {
+          const int u = t - 1, su = u & 1;
+          if (!mbar_wait(p_full, u & 1, 0x23u, abort_flag)) break;
+          if (!mbar_wait(&v_full[su], (u >> 1) & 1, 0x24u, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sm + FwdSmem::V0 + su * TILE_BYTES);
+#pragma unroll
+          for (int j = 0; j < TILE / 16; ++j)
+            umma_bf16(t_o, kmajor_desc(p_addr, j), mnmajor_desc(v_addr, j), idesc_pv, (u > 0 || j > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&kv_empty[su]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    uint8_t* pbuf = sm + FwdSmem::P;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int t = 0; t < n_kv; ++t) {
+      const int st = t & 1;
+      const int k0 = (j_lo + t) * TILE;
+      if (!mbar_wait(&s_full[st], (t >> 1) & 1, 0x30u, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      float s[TILE];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_s + st * 128 + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * p.scale_log2;
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+      const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
+                            (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
+      if (boundary) {
+#pragma unroll
+        for (int i = 0; i < TILE; ++i) {
+          const int kj = k0 + i;
+          const bool valid = kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+          if (!valid) s[i] = -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < TILE; ++i) mx = fmaxf(mx, s[i]);
+      // lazy rescale: keep the old reference max unless the row grew by more than 2^8
+      float m_new = m;
+      if (t == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
+      const float alpha = (t == 0 || m_new == m) ? 1.f : fast_exp2(m - m_new);
+      const float mref = (m_new == -INFINITY) ? 0.f : m_new;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < TILE; ++i) {
+        s[i] = fast_exp2(s[i] - mref);
+        sum += s[i];
+      }
+      l = l * alpha + sum;
+      if (t > 0) {
+        // PV of the previous tile must be complete before O is touched or P is overwritten
+        if (!mbar_wait(o_done, (t - 1) & 1, 0x31u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld32(t_o + lane_off + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st16(t_o + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+            tmem_st16(t_o + lane_off + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+          }
+          tmem_wait_st();
+        }
+      }
+      m = m_new;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 w = make_uint4(pack_bf16x2(s[8 * c + 0], s[8 * c + 1]), pack_bf16x2(s[8 * c + 2], s[8 * c + 3]),
+                             pack_bf16x2(s[8 * c + 4], s[8 * c + 5]), pack_bf16x2(s[8 * c + 6], s[8 * c + 7]));
+        *reinterpret_cast<uint4*>(pbuf + swz_off(r, c)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, 0x32u, abort_flag)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + (static_cast<int64_t>(b) * p.T + qi) * p.ldo + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_o + lane_off + c * 32, v);
+        tmem_wait_ld();
+        if (qi < p.T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w = make_uint4(pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
+                                 pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
+                                 pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
+                                 pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
+            *reinterpret_cast<uint4*>(orow + c * 32 + i) = w;
+          }
+        }
+      }
+      if (qi < p.T)
+        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + qi] = (m * 0.6931471805599453f) + logf(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------ backward
+struct BwdSmem {
+  static constexpr int K = 0;
+  static constexpr int V = K + TILE_BYTES;
+  static constexpr int Q = V + TILE_BYTES;     // Q tile (one stage)
+  static constexpr int DO = Q + TILE_BYTES;    // dO tile
+  static constexpr int PT = DO + TILE_BYTES;   // P^T  [keys x queries]
+  static constexpr int DST = PT + TILE_BYTES;  // dS^T [keys x queries]
+  static constexpr int LSE = DST + TILE_BYTES; // 128 floats
+  static constexpr int DEL = LSE + 512;        // 128 floats
+  static constexpr int BAR = DEL + 512;
+  // kv_full, qd_full, qd_empty, st_full, ps_full, dq_full, dq_free
+  static constexpr int NBAR = 7;
+  static constexpr int TOTAL = BAR + NBAR * 8 + 16 + 1024;
+};
+
+NT_DEVICE void bwd_q_range(const Params& p, int k0, int& i_lo, int& i_hi) {
+  const int n_qt = (p.T + TILE - 1) / TILE;
+  i_lo = k0 / TILE;  // causal: queries >= keys
+  i_hi = n_qt - 1;
+  if (p.window >= 0) i_hi = min(i_hi, (k0 + TILE - 1 + p.window) / TILE);
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = bars + 2;
+  uint64_t* st_full = bars + 3;
+  uint64_t* ps_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + BwdSmem::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* s_lse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
+  float* s_del = reinterpret_cast<float*>(sm + BwdSmem::DEL);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int group = p.H / p.Hk;
+  const int k0 = kt * TILE;
+  int i_lo, i_hi;
+  bwd_q_range(p, k0, i_lo, i_hi);
+  const int n_q = i_hi - i_lo + 1;
+  const int n_it = group * n_q;  // iterations: (head in group, query tile)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < BwdSmem::NBAR; ++i) mbar_init(&bars[i], 1);
+    mbar_init(ps_full, 128);
+    mbar_init(dq_free, 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint32_t t_st = tbase;         // S^T, later dQ
+  const uint32_t t_dp = tbase + 128;   // dP^T
+  const uint32_t t_dv = tbase + 256;   // dV accumulator
+  const uint32_t t_dk = tbase + 384;   // dK accumulator
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_3d(sm + BwdSmem::K, &tmK, kv_full, hk * HD, k0, b);
+      tma_load_3d(sm + BwdSmem::K + BOX_BYTES, &tmK, kv_full, hk * HD + 64, k0, b);
+      tma_load_3d(sm + BwdSmem::V, &tmV, kv_full, hk * HD, k0, b);
+      tma_load_3d(sm + BwdSmem::V + BOX_BYTES, &tmV, kv_full, hk * HD + 64, k0, b);
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int h = hk * group + it / n_q;
+        const int q0 = (i_lo + it % n_q) * TILE;
+        if (!mbar_wait(qd_empty, (it & 1) ^ 1u, 0x50u, abort_flag)) break;
+        mbar_expect_tx(qd_full, 2 * TILE_BYTES);
+        tma_load_3d(sm + BwdSmem::Q, &tmQ, qd_full, h * HD, q0, b);
+        tma_load_3d(sm + BwdSmem::Q + BOX_BYTES, &tmQ, qd_full, h * HD + 64, q0, b);
+        tma_load_3d(sm + BwdSmem::DO, &tmDO, qd_full, h * HD, q0, b);
+        tma_load_3d(sm + BwdSmem::DO + BOX_BYTES, &tmDO, qd_full, h * HD + 64, q0, b);
+        ++issued;
+      }
+      mbar_wait(kv_full, 0, 0x5Eu, nullptr);
+      if (issued > 0) mbar_wait(qd_full, (issued - 1) & 1, 0x5Fu, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(TILE, TILE, 0, 0);   // S^T = K Q^T ; dP^T = V dO^T
+      constexpr uint32_t id_kv = idesc_bf16_f32(TILE, HD, 0, 1);    // dV += P^T dO ; dK += dS^T Q
+      constexpr uint32_t id_q = idesc_bf16_f32(TILE, HD, 1, 1);     // dQ = dS K  (A = dS^T read M-major)
+      const uint32_t k_addr = smem_u32(sm + BwdSmem::K), v_addr = smem_u32(sm + BwdSmem::V);
+      const uint32_t q_addr = smem_u32(sm + BwdSmem::Q), do_addr = smem_u32(sm + BwdSmem::DO);
+      const uint32_t pt_addr = smem_u32(sm + BwdSmem::PT), ds_addr = smem_u32(sm + BwdSmem::DST);
+      bool ok = mbar_wait(kv_full, 0, 0x60u, abort_flag);
+      for (int it = 0; ok && it < n_it; ++it) {
+        if (!mbar_wait(qd_full, it & 1, 0x61u, abort_flag)) break;
+        if (!mbar_wait(dq_free, (it & 1) ^ 1u, 0x62u, abort_flag)) break;  // S^T/dQ columns free
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < HD / 16; ++j) umma_bf16(t_st, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
+#pragma unroll
+        for (int j = 0; j < HD / 16; ++j)
+          umma_bf16(t_dp, kmajor_desc(v_addr, j), kmajor_desc(do_addr, j), id_s, j > 0);
+        umma_commit(st_full);
+        if (!mbar_wait(ps_full, it & 1, 0x63u, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < TILE / 16; ++j)
+          umma_bf16(t_dv, kmajor_desc(pt_addr, j), mnmajor_desc(do_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < TILE / 16; ++j)
+          umma_bf16(t_dk, kmajor_desc(ds_addr, j), mnmajor_desc(q_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+        for (int j = 0; j < TILE / 16; ++j)
+          umma_bf16(t_st, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
+        umma_commit(dq_full);
+        umma_commit(qd_empty);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;   // key row (S^T phase) / query row (dQ phase)
+    const int kj = k0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    uint8_t* pt = sm + BwdSmem::PT;
+    uint8_t* ds = sm + BwdSmem::DST;
+    const int tid = threadIdx.x - 64;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * group + it / n_q;
+      const int q0 = (i_lo + it % n_q) * TILE;
+      // per-query statistics of this tile into shared memory
+      named_bar_sync(1, 128);
+      {
+        const int qi = q0 + tid;
+        const int64_t o = (static_cast<int64_t>(b) * p.H + h) * p.T + qi;
+        s_lse[tid] = qi < p.T ? p.lse[o] * LOG2E : INFINITY;
+        s_del[tid] = qi < p.T ? p.delta[o] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(st_full, it & 1, 0x70u, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const bool boundary = (k0 + TILE - 1 > q0) || (q0 + TILE > p.T) || (k0 + TILE > p.T) ||
+                            (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(t_st + lane_off + c * 32, sv);
+        tmem_ld32(t_dp + lane_off + c * 32, dv);
+        tmem_wait_ld();
+        float pv[32], dsv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int qi = q0 + c * 32 + i;
+          float pp = fast_exp2(__uint_as_float(sv[i]) * p.scale_log2 - s_lse[c * 32 + i]);
+          if (boundary) {
+            const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+            if (!valid) pp = 0.f;
+          }
+          pv[i] = pp;
+          dsv[i] = pp * (__uint_as_float(dv[i]) - s_del[c * 32 + i]);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int chunk = c * 4 + g;
+          uint4 w = make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
+                               pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]), pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7]));
+          *reinterpret_cast<uint4*>(pt + swz_off(r, chunk)) = w;
+          uint4 z = make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]), pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
+                               pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]), pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7]));
+          *reinterpret_cast<uint4*>(ds + swz_off(r, chunk)) = z;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ps_full);
+      // dQ tile (row = query q0 + r) -> fp32 atomics
+      if (!mbar_wait(dq_full, it & 1, 0x71u, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const int qi = q0 + r;
+      float* dst = p.dq_acc + (static_cast<int64_t>(b) * p.T + qi) * (static_cast<int64_t>(p.H) * HD) + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_st + lane_off + c * 32, v);
+        tmem_wait_ld();
+        if (qi < p.T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 a = make_float4(__uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale,
+                                   __uint_as_float(v[i + 2]) * p.scale, __uint_as_float(v[i + 3]) * p.scale);
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + i), a);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    // dV, dK of this key tile: all MMAs done once the last dq_full has fired
+    if (ok) {
+      tc_fence_after();
+      const bool live = kj < p.T;
+      __nv_bfloat16* dvr = p.dv + (static_cast<int64_t>(b) * p.T + kj) * p.lddv + hk * HD;
+      __nv_bfloat16* dkr = p.dk + (static_cast<int64_t>(b) * p.T + kj) * p.lddk + hk * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32], k[32];
+        tmem_ld32(t_dv + lane_off + c * 32, v);
+        tmem_ld32(t_dk + lane_off + c * 32, k);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 a = make_uint4(pack_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                 pack_bf16x2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])),
+                                 pack_bf16x2(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5])),
+                                 pack_bf16x2(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7])));
+            *reinterpret_cast<uint4*>(dvr + c * 32 + i) = a;
+            const float s = p.scale;
+            uint4 z = make_uint4(pack_bf16x2(__uint_as_float(k[i]) * s, __uint_as_float(k[i + 1]) * s),
+                                 pack_bf16x2(__uint_as_float(k[i + 2]) * s, __uint_as_float(k[i + 3]) * s),
+                                 pack_bf16x2(__uint_as_float(k[i + 4]) * s, __uint_as_float(k[i + 5]) * s),
+                                 pack_bf16x2(__uint_as_float(k[i + 6]) * s, __uint_as_float(k[i + 7]) * s));
+            *reinterpret_cast<uint4*>(dkr + c * 32 + i) = z;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// delta[b, h, t] = sum_d dO[b t, h d] * O[b t, h d]   (one warp per (row, head))
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo, const __nv_bfloat16* __restrict__ dout,
+                                  int64_t lddo, float* __restrict__ delta, int B, int T, int H) {
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= static_cast<int64_t>(B) * T * H) return;
+  const int h = static_cast<int>(gw % H);
+  const int64_t row = gw / H;
+  const __nv_bfloat16* a = o + row * ldo + h * HD + lane * 4;
+  const __nv_bfloat16* g = dout + row * lddo + h * HD + lane * 4;
+  const uint2 av = *reinterpret_cast<const uint2*>(a);
+  const uint2 gv = *reinterpret_cast<const uint2*>(g);
+  const float2 a0 = unpack_bf16x2(av.x), a1 = unpack_bf16x2(av.y), g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
+  float s = a0.x * g0.x + a0.y * g0.y + a1.x * g1.x + a1.y * g1.y;
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int b = static_cast<int>(row / T), t = static_cast<int>(row % T);
+    delta[(static_cast<int64_t>(b) * H + h) * T + t] = s;
+  }
+}
+
+// dq (bf16, strided rows) = dq_acc (fp32 [B*T, H*128])
+__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t lddq,
+                                       int64_t rows, int cols) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i >= rows * cols) return;
+  const int64_t r = i / cols;
+  const int c = static_cast<int>(i - r * cols);
+  const float4 v = *reinterpret_cast<const float4*>(acc + i);
+  uint2 w = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  *reinterpret_cast<uint2*>(dq + r * lddq + c) = w;
+}
+
+// ------------------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// dims {cols, T, B} over rows of stride ld (elements); box {64, 128, 1}; 128B swizzle.
+static CUtensorMap tile_map(const void* base, int64_t cols, int64_t ld, int T, int B) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * 2) % 16) throw std::runtime_error("attention operand alignment");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2), static_cast<cuuint64_t>(ld * 2 * T)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(TILE), 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+static Params make_params(const AttnArgs& a) {
+  Params p{};
+  p.B = a.B; p.T = a.T; p.H = a.H; p.Hk = a.Hk;
+  p.window = a.window;
+  p.scale = a.scale;
+  p.scale_log2 = a.scale * LOG2E;
+  p.o = reinterpret_cast<__nv_bfloat16*>(a.o);
+  p.ldo = a.ldo;
+  p.lse = a.lse;
+  return p;
+}
+
+}  // namespace attn
+}  // namespace nt
+
+using namespace nt::attn;
+
+static bool supported(const AttnArgs& a) {
+  return a.D == HD && a.B > 0 && a.T > 0 && a.H > 0 && a.Hk > 0 && a.H % a.Hk == 0;
+}
+
+int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
+  if (!supported(a)) return -1;
+  CUtensorMap tq = tile_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B);
+  CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
+  CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
+  Params p = make_params(a);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::TOTAL);
+    configured = true;
+  }
+  dim3 grid((a.T + TILE - 1) / TILE, a.H, a.B);
+  attn_fwd_kernel<<<grid, 192, FwdSmem::TOTAL, s>>>(tq, tk, tv, p);
+  return 0;
+}
+
+int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
+  if (!supported(a)) return -1;
+  if (reinterpret_cast<uintptr_t>(a.dq) % 8 || a.lddq % 4) return -1;
+  const int64_t rows = static_cast<int64_t>(a.B) * a.T;
+  const int64_t warps = rows * a.H;
+  attn_delta_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a.o), a.ldo, reinterpret_cast<const __nv_bfloat16*>(a.dout), a.lddo,
+      a.delta, a.B, a.T, a.H);
+  CUtensorMap tq = tile_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B);
+  CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
+  CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
+  CUtensorMap tdo = tile_map(a.dout, static_cast<int64_t>(a.H) * HD, a.lddo, a.T, a.B);
+  Params p = make_params(a);
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(a.dout);
+  p.lddo = a.lddo;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(a.dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(a.dv);
+  p.lddk = a.lddk;
+  p.lddv = a.lddv;
+  p.dq_acc = a.dq_acc;
+  p.delta = a.delta;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
+    configured = true;
+  }
+  dim3 grid((a.T + TILE - 1) / TILE, a.Hk, a.B);
+  attn_bwd_kernel<<<grid, 192, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, p);
+  const int cols = a.H * HD;
+  const int64_t n = rows * cols;
+  attn_dq_convert_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, s>>>(
+      a.dq_acc, reinterpret_cast<__nv_bfloat16*>(a.dq), a.lddq, rows, cols);
+  return 0;
+}
+
 int nt_attention_read_error(unsigned* where) {
   nt::ErrorWord w{0, 0};
   cudaMemcpyFromSymbol(&w, nt::g_nt_error, sizeof(w));

@@ -24,7 +24,7 @@ def _use_kernel(qkv, D):
     return qkv.is_cuda and D in KERNEL_HEAD_DIMS and getattr(ext(), "attn_fwd", None) is not None and _kernel_enabled
 
 
-_kernel_enabled = False  # flipped on once the tcgen05 kernels are validated on B200
+_kernel_enabled = True
 
 
 class _KernelAttn(Function):

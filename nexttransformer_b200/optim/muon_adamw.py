@@ -188,7 +188,7 @@ class MuonAdamW(torch.optim.Optimizer):
             if world > 1:
                 for p in mine:
                     grad_of(p).div_(world)
-            if mine[0].is_cuda:
+            if mine[0].is_cuda and self.gemm_shape_ok(m, n):
                 self._muon_cuda(group, mine, m, n, lr)
             else:
                 grads = torch.stack([grad_of(p).float() for p in mine])
@@ -209,6 +209,11 @@ class MuonAdamW(torch.optim.Optimizer):
                 gathers.append(("muon", p, dist.broadcast(p.data, src=src, async_op=True)))
                 if p in self.shadows:
                     gathers.append(("shadow", p, self.shadows[p]))
+
+    @staticmethod
+    def gemm_shape_ok(m, n):
+        """TMA needs 16-byte row strides; tiny matrices (e.g. value-embedding gates) use the plain path."""
+        return m % 8 == 0 and n % 8 == 0 and min(m, n) >= 64
 
     def _ptrs(self, tensors):
         return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64).to(tensors[0].device,
