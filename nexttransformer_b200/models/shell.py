@@ -304,7 +304,7 @@ class GPTShell(nn.Module):
         logits = self.readout(x, backout)
         if targets is None:
             return logits
-        return F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1,
+        return F.cross_entropy(logits.view(-1, logits.size(-1)), targets.reshape(-1), ignore_index=-1,
                                reduction=loss_reduction)
 
     def fused_supported(self):

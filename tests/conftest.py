@@ -39,7 +39,9 @@ def reference():
         pytest.skip("reference install (baseline/_ref) not present")
     if str(REF) not in sys.path:
         sys.path.append(str(REF))
-    os.environ.setdefault("NANOCHAT_DTYPE", "float32")
+    import torch
+    if not torch.cuda.is_available():
+        os.environ.setdefault("NANOCHAT_DTYPE", "float32")
     return REF
 
 
