@@ -93,6 +93,14 @@ void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const Tensor& 
   g.epi = static_cast<int>(epi);
   g.num_sms = num_sms(C);
   const c10::cuda::CUDAGuard guard(C.device());
+  Tensor ws;
+  const size_t ws_bytes = nt_gemm_splitk_bytes(g);
+  if (ws_bytes) {
+    // split-K partials live in a caching-allocator buffer for the duration of this call
+    ws = at::empty({static_cast<int64_t>(ws_bytes / sizeof(float))}, C.options().dtype(at::kFloat));
+    g.workspace = ws.data_ptr();
+    g.workspace_bytes = ws_bytes;
+  }
   nt_gemm_launch(g, stream());
 }
 

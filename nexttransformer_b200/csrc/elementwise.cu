@@ -33,6 +33,31 @@ NT_DEVICE void store8(__nv_bfloat16* p, const float (&v)[8]) {
 }
 NT_DEVICE float rbf(float v) { return bf2f(f2bf(v)); }
 
+// P consecutive bf16 values (P = 1, 2 or 4) as floats / from floats, vectorised.
+template <int P>
+NT_DEVICE void ldp(const __nv_bfloat16* p, float (&v)[P]) {
+  if constexpr (P == 1) {
+    v[0] = bf2f(*p);
+  } else if constexpr (P == 2) {
+    const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p));
+    v[0] = f.x; v[1] = f.y;
+  } else {
+    const uint2 q = *reinterpret_cast<const uint2*>(p);
+    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+}
+template <int P>
+NT_DEVICE void stp(__nv_bfloat16* p, const float (&v)[P]) {
+  if constexpr (P == 1) {
+    *p = f2bf(v[0]);
+  } else if constexpr (P == 2) {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(v[0], v[1]);
+  } else {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  }
+}
+
 // ------------------------------------------------------------------ mix + norm forward
 // xm = bf16(bf16(bf16(a) x) + bf16(bf16(b) x0))  (x0 == nullptr: xm = x, nothing written)
 // h = bf16(xm * rsqrt(mean(xm^2) + eps)); rstd saved per row.
@@ -215,16 +240,17 @@ __global__ void rope_norm_fwd_kernel(__nv_bfloat16* __restrict__ qkv, const __nv
   __nv_bfloat16* base = qkv + static_cast<int64_t>(row) * ld + head * D;
   if (head < H + Hk) {
     const int t = row % T;
-    float y1[P], y2[P];
+    float x1[P], x2[P], c[P], sn[P], y1[P], y2[P];
+    const int i0 = lane * P;
+    ldp<P>(base + i0, x1);
+    ldp<P>(base + i0 + D / 2, x2);
+    ldp<P>(cosb + static_cast<int64_t>(t) * (D / 2) + i0, c);
+    ldp<P>(sinb + static_cast<int64_t>(t) * (D / 2) + i0, sn);
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < P; ++j) {
-      const int i = lane * P + j;
-      const float x1 = bf2f(base[i]), x2 = bf2f(base[i + D / 2]);
-      const float c = bf2f(cosb[static_cast<int64_t>(t) * (D / 2) + i]);
-      const float s = bf2f(sinb[static_cast<int64_t>(t) * (D / 2) + i]);
-      y1[j] = rbf(rbf(x1 * c) + rbf(x2 * s));
-      y2[j] = rbf(rbf(x1 * -s) + rbf(x2 * c));
+      y1[j] = rbf(rbf(x1[j] * c[j]) + rbf(x2[j] * sn[j]));
+      y2[j] = rbf(rbf(x1[j] * -sn[j]) + rbf(x2[j] * c[j]));
       ss += y1[j] * y1[j] + y2[j] * y2[j];
     }
     ss = warp_sum(ss);
@@ -232,10 +258,11 @@ __global__ void rope_norm_fwd_kernel(__nv_bfloat16* __restrict__ qkv, const __nv
     if (lane == 0) rstd[static_cast<int64_t>(row) * (H + Hk) + head] = r;
 #pragma unroll
     for (int j = 0; j < P; ++j) {
-      const int i = lane * P + j;
-      base[i] = f2bf(rbf(y1[j] * r) * scale);
-      base[i + D / 2] = f2bf(rbf(y2[j] * r) * scale);
+      y1[j] = rbf(y1[j] * r) * scale;
+      y2[j] = rbf(y2[j] * r) * scale;
     }
+    stp<P>(base + i0, y1);
+    stp<P>(base + i0 + D / 2, y2);
   } else if (ve_table) {
     const int hk = head - H - Hk;
     float z = 0.f;
@@ -244,10 +271,26 @@ __global__ void rope_norm_fwd_kernel(__nv_bfloat16* __restrict__ qkv, const __nv
     const float gate = rbf(3.f * rbf(1.f / (1.f + __expf(-z))));
     if (lane == 0) gate_out[static_cast<int64_t>(row) * Hk + hk] = gate;
     const __nv_bfloat16* ve = ve_table + idx[row] * static_cast<int64_t>(Hk * D) + hk * D;
+    float a[2 * P], e[2 * P];
+    const int i0 = lane * 2 * P;
+    if constexpr (P == 1) {
+      ldp<2>(base + i0, a);
+      ldp<2>(ve + i0, e);
+    } else {
+      ldp<4>(base + i0, *reinterpret_cast<float(*)[4]>(&a[0]));
+      ldp<4>(ve + i0, *reinterpret_cast<float(*)[4]>(&e[0]));
+      if constexpr (P == 4) {
+        ldp<4>(base + i0 + 4, *reinterpret_cast<float(*)[4]>(&a[4]));
+        ldp<4>(ve + i0 + 4, *reinterpret_cast<float(*)[4]>(&e[4]));
+      }
+    }
 #pragma unroll
-    for (int j = 0; j < 2 * P; ++j) {
-      const int i = lane * 2 * P + j;
-      base[i] = f2bf(rbf(bf2f(base[i]) + rbf(gate * bf2f(ve[i]))));
+    for (int j = 0; j < 2 * P; ++j) a[j] = rbf(a[j] + rbf(gate * e[j]));
+    if constexpr (P == 1) {
+      stp<2>(base + i0, a);
+    } else {
+      stp<4>(base + i0, *reinterpret_cast<float(*)[4]>(&a[0]));
+      if constexpr (P == 4) stp<4>(base + i0 + 4, *reinterpret_cast<float(*)[4]>(&a[4]));
     }
   }
 }
@@ -273,28 +316,34 @@ __global__ void rope_norm_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __n
   if (head < H + Hk) {
     const int t = row % T;
     const float r = rstd[static_cast<int64_t>(row) * (H + Hk) + head];
-    float n1[P], n2[P], g1[P], g2[P];
+    float n1[P], n2[P], g1[P], g2[P], c[P], sn[P];
+    const int i0 = lane * P;
+    ldp<P>(qkv + o + i0, n1);
+    ldp<P>(qkv + o + i0 + D / 2, n2);
+    ldp<P>(dqkv + o + i0, g1);
+    ldp<P>(dqkv + o + i0 + D / 2, g2);
+    ldp<P>(cosb + static_cast<int64_t>(t) * (D / 2) + i0, c);
+    ldp<P>(sinb + static_cast<int64_t>(t) * (D / 2) + i0, sn);
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < P; ++j) {
-      const int i = lane * P + j;
-      n1[j] = bf2f(qkv[o + i]) / scale;
-      n2[j] = bf2f(qkv[o + i + D / 2]) / scale;
-      g1[j] = bf2f(dqkv[o + i]) * scale;
-      g2[j] = bf2f(dqkv[o + i + D / 2]) * scale;
+      n1[j] /= scale;
+      n2[j] /= scale;
+      g1[j] *= scale;
+      g2[j] *= scale;
       dot += g1[j] * n1[j] + g2[j] * n2[j];
     }
     dot = warp_sum(dot) / D;
+    float o1[P], o2[P];
 #pragma unroll
     for (int j = 0; j < P; ++j) {
-      const int i = lane * P + j;
       const float d1 = r * (g1[j] - n1[j] * dot), d2 = r * (g2[j] - n2[j] * dot);
-      const float c = bf2f(cosb[static_cast<int64_t>(t) * (D / 2) + i]);
-      const float s = bf2f(sinb[static_cast<int64_t>(t) * (D / 2) + i]);
       // forward: y1 = x1 c + x2 s ; y2 = -x1 s + x2 c  =>  dx1 = d1 c - d2 s ; dx2 = d1 s + d2 c
-      dqkv[o + i] = f2bf(d1 * c - d2 * s);
-      dqkv[o + i + D / 2] = f2bf(d1 * s + d2 * c);
+      o1[j] = d1 * c[j] - d2 * sn[j];
+      o2[j] = d1 * sn[j] + d2 * c[j];
     }
+    stp<P>(dqkv + o + i0, o1);
+    stp<P>(dqkv + o + i0 + D / 2, o2);
   } else if (ve_table) {
     const int hk = head - H - Hk;
     const float gate = gate_in[static_cast<int64_t>(row) * Hk + hk];
@@ -302,12 +351,13 @@ __global__ void rope_norm_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __n
     const __nv_bfloat16* ve = ve_table + tok * static_cast<int64_t>(Hk * D) + hk * D;
     float* vg = ve_grad + tok * static_cast<int64_t>(Hk * D) + hk * D;
     float dg = 0.f;
+    const int i0 = lane * 2 * P;
 #pragma unroll
-    for (int j = 0; j < 2 * P; ++j) {
-      const int i = lane * 2 * P + j;
-      const float g = bf2f(dqkv[o + i]);
-      dg += g * bf2f(ve[i]);
-      atomicAdd(vg + i, g * gate);
+    for (int j = 0; j < 2 * P; j += 2) {
+      const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dqkv + o + i0 + j));
+      const float2 e = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(ve + i0 + j));
+      dg += g.x * e.x + g.y * e.y;
+      atomicAdd(reinterpret_cast<float2*>(vg + i0 + j), make_float2(g.x * gate, g.y * gate));
     }
     dg = warp_sum(dg);
     // gate = 3 sigmoid(z): dgate/dz = gate * (1 - gate / 3)
@@ -406,6 +456,100 @@ __global__ void softcap_ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld
     else {
       for (int i = 0; i < 8 && c + i < Vp; ++i) l[c + i] = f2bf(o[i]);
     }
+  }
+}
+
+// Single-pass variant: the row stays in registers (VPT bf16 values per thread, 512 threads), and
+// the soft cap bounds z to [-cap, cap], so cap itself is a safe softmax shift.  With
+// u = 2^(2 x log2 e) (x = l / cap clamped to +-15, where tanh is saturated), r = 1 / (u + 1):
+//   tanh x = 1 - 2 r,   1 - tanh^2 x = 4 u r^2,   exp(z - cap) = 2^(-2 r cap log2 e)
+// which keeps the derivative of the cap accurate where tanh saturates.  Reads/writes each logit once.
+NT_DEVICE float exp2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+struct CapTerms {
+  float th, sech2, e;
+};
+NT_DEVICE CapTerms cap_terms(float l, float inv, float c2) {
+  const float x = fminf(fmaxf(l * inv, -15.f), 15.f);
+  const float u = exp2_fast(x * 2.8853900817779268f);  // 2 log2(e)
+  const float r = __frcp_rn(u + 1.f);
+  CapTerms t;
+  t.th = 1.f - 2.f * r;
+  t.sech2 = 4.f * u * r * r;
+  t.e = exp2_fast(-2.f * r * c2);
+  return t;
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(512) softcap_ce_reg_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
+                                                            const int64_t* __restrict__ tgt, float* __restrict__ loss,
+                                                            float* __restrict__ lse_out, int V, float cap) {
+  constexpr int NCHUNK = VPT / 8;
+  __shared__ float red[16];
+  __shared__ float zt_sh;
+  const int row = blockIdx.x;
+  __nv_bfloat16* l = logits + static_cast<int64_t>(row) * ld;
+  const int64_t target = tgt[row];
+  const float inv = 1.f / cap;
+  const float c2 = cap * 1.4426950408889634f;  // cap * log2(e)
+  uint4 raw[NCHUNK];
+#pragma unroll
+  for (int i = 0; i < NCHUNK; ++i) {
+    const int c = (i * 512 + threadIdx.x) * 8;
+    raw[i] = c < V ? *reinterpret_cast<const uint4*>(l + c) : make_uint4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) zt_sh = target >= 0 ? cap * cap_terms(bf2f(l[target]), inv, c2).th : 0.f;
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCHUNK; ++i) {
+    const int c = (i * 512 + threadIdx.x) * 8;
+    const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      if (c + 2 * j < V) sum += cap_terms(f.x, inv, c2).e;
+      if (c + 2 * j + 1 < V) sum += cap_terms(f.y, inv, c2).e;
+    }
+  }
+  sum = warp_sum(sum);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tot += red[i];
+  const float lse = cap + __logf(tot);
+  const float rinv = 1.f / tot;
+  if (threadIdx.x == 0) {
+    loss[row] = target >= 0 ? lse - zt_sh : 0.f;
+    if (lse_out) lse_out[row] = lse;
+  }
+#pragma unroll
+  for (int i = 0; i < NCHUNK; ++i) {
+    const int c = (i * 512 + threadIdx.x) * 8;
+    if (c >= V) continue;
+    const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      float g[2];
+      const float x2[2] = {f.x, f.y};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = c + 2 * j + h;
+        float gv = 0.f;
+        if (target >= 0 && col < V) {
+          const CapTerms ct = cap_terms(x2[h], inv, c2);
+          gv = (ct.e * rinv - (col == target ? 1.f : 0.f)) * ct.sech2;
+        }
+        g[h] = gv;
+      }
+      o[j] = pack_bf16x2(g[0], g[1]);
+    }
+    *reinterpret_cast<uint4*>(l + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -604,7 +748,19 @@ int nt_rope_norm_bwd(void* dqkv, const void* qkv, const void* cosb, const void* 
 int nt_softcap_ce(void* logits, int64_t ld, const int64_t* tgt, float* loss, float* lse, int rows, int V, int Vp,
                   float cap, cudaStream_t s) {
   if (ld % 8 || Vp % 8) return -1;
-  softcap_ce_kernel<<<rows, 1024, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, Vp, cap);
+  if (rows <= 0) return 0;
+  // padded columns (V..Vp) must end with zero gradient: the register kernel covers them when
+  // V is a multiple of 8 (they are written as 0); otherwise use the general two-pass kernel.
+  const bool reg = (V % 8 == 0) && Vp == V;
+  if (reg && Vp <= 512 * 8 * 4) {
+    softcap_ce_reg_kernel<32><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
+  } else if (reg && Vp <= 512 * 8 * 8) {
+    softcap_ce_reg_kernel<64><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
+  } else if (reg && Vp <= 512 * 8 * 16) {
+    softcap_ce_reg_kernel<128><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
+  } else {
+    softcap_ce_kernel<<<rows, 1024, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, Vp, cap);
+  }
   return 0;
 }
 

@@ -57,12 +57,18 @@ struct Params {
   int64_t ldp, strideP;
   float s_acc, s_res;
   const float* s_ptr;
+  int split;           // K slices (1 = no split-K)
+  int kb_per_split;    // k-blocks per slice
+  int64_t strideSplit; // elements between the partial-output slices of the workspace
 };
 
-NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb) {
-  const int per_batch = p.tiles_m * p.tiles_n;
+NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb, int& ks) {
+  const int per_slice = p.tiles_m * p.tiles_n;
+  const int per_batch = per_slice * p.split;
   b = t / per_batch;
   int r = t - b * per_batch;
+  ks = r / per_slice;
+  r -= ks * per_slice;
   const int group_span = GROUP_M * p.tiles_n;
   const int g = r / group_span;
   const int first_m = g * GROUP_M;
@@ -74,7 +80,7 @@ NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb) {
 
 // Epilogue for 32 consecutive columns of one row.
 template <int EPI>
-NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int row, int col0, const uint32_t (&acc)[32]) {
+NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int ks, int row, int col0, const uint32_t (&acc)[32]) {
   if (row >= p.M) return;
   const int ncols = min(32, p.N - col0);
   if (ncols <= 0) return;
@@ -84,12 +90,14 @@ NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int row, int col0,
   const bool full = (ncols == 32);
 
   if constexpr (EPI == EPI_F32 || EPI == EPI_F32_ACC) {
-    float* c = reinterpret_cast<float*>(p.C) + b * p.strideC + static_cast<int64_t>(row) * p.ldc + col0;
+    float* c = reinterpret_cast<float*>(p.C) + b * p.strideC + ks * p.strideSplit +
+               static_cast<int64_t>(row) * p.ldc + col0;
+    const bool acc_into = (EPI == EPI_F32_ACC) && p.split == 1;
     if (full && ((reinterpret_cast<uintptr_t>(c) & 15) == 0)) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
         float4 o = make_float4(v[i] * sacc, v[i + 1] * sacc, v[i + 2] * sacc, v[i + 3] * sacc);
-        if constexpr (EPI == EPI_F32_ACC) {
+        if (acc_into) {
           float4 old = *reinterpret_cast<float4*>(c + i);
           o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
         }
@@ -98,7 +106,7 @@ NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int row, int col0,
     } else {
       for (int i = 0; i < ncols; ++i) {
         float o = v[i] * sacc;
-        if constexpr (EPI == EPI_F32_ACC) o += c[i];
+        if (acc_into) o += c[i];
         c[i] = o;
       }
     }
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.K + BK - 1) / BK;
-  const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int total_tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -227,10 +235,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        int b, mb, nb;
-        tile_coords(t, p, b, mb, nb);
+        int b, mb, nb, ks;
+        tile_coords(t, p, b, mb, nb, ks);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb_lo = ks * p.kb_per_split, kb_hi = min(num_kb, kb_lo + p.kb_per_split);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, 0x100u + stage, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
           uint8_t* sB = sA + S::A_BYTES;
@@ -275,7 +284,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, 0x200u + acc, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        int tb, tmb, tnb, tks;
+        tile_coords(t, p, tb, tmb, tnb, tks);
+        const int kb_lo = tks * p.kb_per_split, kb_hi = min(num_kb, kb_lo + p.kb_per_split);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, 0x300u + stage, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * S::STAGE_BYTES);
@@ -286,7 +298,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // MN-major: step 16 rows of 128 bytes (two 8-row swizzle atoms).
             const uint64_t ad = A_MN ? smem_desc(a_addr + j * 2048, 8192, 1024) : smem_desc(a_addr + j * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc(b_addr + j * 2048, 8192, 1024) : smem_desc(b_addr + j * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb_lo || j != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -305,8 +317,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
       tc_fence_after();
-      int b, mb, nb;
-      tile_coords(t, p, b, mb, nb);
+      int b, mb, nb, ks;
+      tile_coords(t, p, b, mb, nb, ks);
       const int row = mb * BM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -314,7 +326,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
         tmem_ld32(t_row + c * 32, r);
         tmem_wait_ld();
-        epilogue32<EPI>(p, sacc, b, row, nb * BN + c * 32, r);
+        epilogue32<EPI>(p, sacc, b, ks, row, nb * BN + c * 32, r);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -327,6 +339,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
+}
+
+// C (+)= sum_s W[s]  in a fixed order (deterministic split-K reduction); n elements per slice.
+__global__ void splitk_reduce_kernel(const float* __restrict__ w, int split, int64_t n, float* __restrict__ c,
+                                     int64_t ldc, int cols, int accumulate) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i >= n) return;
+  float4 a = *reinterpret_cast<const float4*>(w + i);
+  for (int s = 1; s < split; ++s) {
+    const float4 b = *reinterpret_cast<const float4*>(w + s * n + i);
+    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+  }
+  const int64_t r = i / cols;
+  const int col = static_cast<int>(i - r * cols);
+  float4* dst = reinterpret_cast<float4*>(c + r * ldc + col);
+  if (accumulate) {
+    const float4 o = *dst;
+    a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
+  }
+  *dst = a;
 }
 
 // ---------------------------------------------------------------- host side
@@ -382,15 +414,30 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   p.R = g.R; p.ldr = g.ldr; p.strideR = g.strideR;
   p.P = g.P; p.ldp = g.ldp; p.strideP = g.strideP;
   p.s_acc = g.s_acc; p.s_res = g.s_res; p.s_ptr = g.s_ptr;
+  p.split = g.split_k > 1 ? g.split_k : 1;
+  const int num_kb = (g.K + BK - 1) / BK;
+  p.kb_per_split = (num_kb + p.split - 1) / p.split;
+  p.strideSplit = p.split > 1 ? static_cast<int64_t>(g.M) * g.N : 0;
+  if (p.split > 1) {
+    p.C = g.workspace;  // partial products: [split, M, N] fp32, contiguous
+    p.ldc = g.N;
+    p.strideC = 0;
+  }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     configured = true;
   }
-  const int tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
   kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, p);
+  if (p.split > 1) {
+    const int64_t n = static_cast<int64_t>(g.M) * g.N;
+    splitk_reduce_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const float*>(g.workspace), p.split, n, reinterpret_cast<float*>(g.C), g.ldc, g.N,
+        g.epi == EPI_F32_ACC ? 1 : 0);
+  }
 }
 
 template <int BN, int A_MN, int B_MN>
@@ -417,13 +464,40 @@ static void dispatch_major(const GemmArgs& g, cudaStream_t s) {
 }  // namespace gemm
 }  // namespace nt
 
-void nt_gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+namespace {
+// Split-K pays when an fp32-output problem has a long reduction but too few 128x256 tiles to fill
+// the machine (weight gradients reduce over all tokens).  Returns the slice count (1 = none).
+int choose_split(const GemmArgs& g) {
+  if (g.epi != EPI_F32 && g.epi != EPI_F32_ACC) return 1;
+  if (g.batch != 1 || g.N < 256 || g.M % 4 || g.N % 4 || g.ldc % 4) return 1;
+  const long tiles = static_cast<long>((g.M + 127) / 128) * ((g.N + 255) / 256);
+  const long want = 2L * g.num_sms;
+  if (tiles >= want) return 1;
+  const int num_kb = (g.K + 63) / 64;
+  int split = static_cast<int>((want + tiles - 1) / tiles);
+  split = split > 16 ? 16 : split;
+  while (split > 1 && num_kb / split < 16) --split;  // keep >= 16 k-blocks per slice
+  return split;
+}
+}  // namespace
+
+size_t nt_gemm_splitk_bytes(const GemmArgs& g) {
+  const int split = choose_split(g);
+  return split > 1 ? static_cast<size_t>(split) * g.M * g.N * sizeof(float) : 0;
+}
+
+void nt_gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
   using namespace nt::gemm;
+  GemmArgs g = g_in;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return;
-  // BN = 256 halves B-operand shared-memory traffic per MMA; N = 128 tiles keep more CTAs busy
-  // when the 256-wide grid would leave most SMs idle.
-  const long tiles256 = static_cast<long>(g.batch) * ((g.M + 127) / 128) * ((g.N + 255) / 256);
-  const bool wide = g.N >= 256 && tiles256 >= 2L * g.num_sms;
+  g.split_k = 1;
+  const int split = choose_split(g);
+  if (split > 1 && g.workspace && g.workspace_bytes >= static_cast<size_t>(split) * g.M * g.N * sizeof(float))
+    g.split_k = split;
+  // BN = 256 halves B-operand shared-memory traffic per MMA (128-wide tiles are bound by
+  // shared-memory bandwidth); 128-wide tiles are kept only when 256-wide ones cannot fill the GPU.
+  const long tiles256 = static_cast<long>(g.batch) * g.split_k * ((g.M + 127) / 128) * ((g.N + 255) / 256);
+  const bool wide = g.N >= 256 && tiles256 >= g.num_sms;
   if (wide) dispatch_major<256>(g, stream);
   else dispatch_major<128>(g, stream);
 }

@@ -34,7 +34,16 @@ struct GemmArgs {
   const float* s_ptr = nullptr;  // optional device scalar multiplying s_acc
   int epi = EPI_BF16;
   int num_sms = 148;
+  // Optional fp32 workspace for split-K (EPI_F32 / EPI_F32_ACC only): the reduction dimension
+  // is cut into slices whose partial products land in the workspace and are summed in a fixed
+  // order by a second kernel, so results are deterministic.
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  int split_k = 1;  // set by the launcher
 };
+
+// Bytes of workspace nt_gemm_launch would use for split-K on this problem (0 = no split).
+size_t nt_gemm_splitk_bytes(const GemmArgs& args);
 
 void nt_gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // Returns the first error code recorded by a bounded wait in a GEMM kernel (0 = none).

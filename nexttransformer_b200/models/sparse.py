@@ -300,10 +300,15 @@ class SparseMixer(nn.Module):
                 sc = torch.matmul(qq, ck.transpose(-2, -1)) * c.head_dim ** -.5
                 prob = safe_softmax(sc, complete[None, None])
                 compressed = torch.matmul(prob, cv)
-                sel_size = c.block_size
-                imp = self._selection_importance(prob, ends, sel_size, T)
-                nsel = (T + sel_size - 1) // sel_size
-                sel_complete = (torch.arange(nsel, device=x.device) + 1) * sel_size - 1 <= pos[:, None]
+                if c.compression_stride:
+                    # overlapping compression: pool block importance onto selection blocks of block_size
+                    sel_size = c.block_size
+                    imp = self._selection_importance(prob, ends, sel_size, T)
+                    nsel = (T + sel_size - 1) // sel_size
+                    sel_complete = (torch.arange(nsel, device=x.device) + 1) * sel_size - 1 <= pos[:, None]
+                else:
+                    # non-overlapping compression of the selection size: identity importance map
+                    sel_size, imp, sel_complete = size, prob, complete
                 idx, valid = block_indices(imp, sel_complete, pos, sel_size, T, max(1, c.sparse_topk // sel_size))
                 local = (pos[:, None] - torch.arange(c.local_window, device=x.device)[None, :]).flip(-1)
                 lv = (local >= 0)[None, None].expand(B, H, -1, -1)
