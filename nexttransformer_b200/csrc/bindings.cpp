@@ -172,12 +172,14 @@ void rope_norm_bwd(const Tensor& dqkv, const Tensor& qkv, const Tensor& cosb, co
      "rope_norm_bwd");
 }
 
-void softcap_ce(const Tensor& logits, const Tensor& tgt, const Tensor& loss, const OptT& lse, int64_t V, double cap) {
+void softcap_ce(const Tensor& logits, const Tensor& tgt, const Tensor& loss, const OptT& lse, int64_t V, double cap,
+                int64_t variant) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.stride(-1) == 1 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0, "logits layout");
   ok(nt_softcap_ce(logits.data_ptr(), logits.stride(-2), tgt.data_ptr<int64_t>(), loss.data_ptr<float>(),
                    lse.has_value() ? lse->data_ptr<float>() : nullptr, static_cast<int>(logits.size(-2)),
-                   static_cast<int>(V), static_cast<int>(logits.size(-1)), static_cast<float>(cap), stream()),
+                   static_cast<int>(V), static_cast<int>(logits.size(-1)), static_cast<float>(cap),
+                   static_cast<int>(variant), stream()),
      "softcap_ce");
 }
 
@@ -308,7 +310,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mix_norm_bwd", &mix_norm_bwd);
   m.def("rope_norm_fwd", &rope_norm_fwd);
   m.def("rope_norm_bwd", &rope_norm_bwd);
-  m.def("softcap_ce", &softcap_ce);
+  m.def("softcap_ce", &softcap_ce, py::arg("logits"), py::arg("tgt"), py::arg("loss"), py::arg("lse"), py::arg("V"),
+        py::arg("cap"), py::arg("variant") = 0);
   m.def("embed_smear", &embed_smear);
   m.def("embed_scatter", &embed_scatter);
   m.def("cast_bf16", &cast_bf16);

@@ -459,100 +459,6 @@ __global__ void softcap_ce_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld
   }
 }
 
-// Single-pass variant: the row stays in registers (VPT bf16 values per thread, 512 threads), and
-// the soft cap bounds z to [-cap, cap], so cap itself is a safe softmax shift.  With
-// u = 2^(2 x log2 e) (x = l / cap clamped to +-15, where tanh is saturated), r = 1 / (u + 1):
-//   tanh x = 1 - 2 r,   1 - tanh^2 x = 4 u r^2,   exp(z - cap) = 2^(-2 r cap log2 e)
-// which keeps the derivative of the cap accurate where tanh saturates.  Reads/writes each logit once.
-NT_DEVICE float exp2_fast(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-struct CapTerms {
-  float th, sech2, e;
-};
-NT_DEVICE CapTerms cap_terms(float l, float inv, float c2) {
-  const float x = fminf(fmaxf(l * inv, -15.f), 15.f);
-  const float u = exp2_fast(x * 2.8853900817779268f);  // 2 log2(e)
-  const float r = __frcp_rn(u + 1.f);
-  CapTerms t;
-  t.th = 1.f - 2.f * r;
-  t.sech2 = 4.f * u * r * r;
-  t.e = exp2_fast(-2.f * r * c2);
-  return t;
-}
-
-template <int VPT>
-__global__ void __launch_bounds__(512) softcap_ce_reg_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
-                                                            const int64_t* __restrict__ tgt, float* __restrict__ loss,
-                                                            float* __restrict__ lse_out, int V, float cap) {
-  constexpr int NCHUNK = VPT / 8;
-  __shared__ float red[16];
-  __shared__ float zt_sh;
-  const int row = blockIdx.x;
-  __nv_bfloat16* l = logits + static_cast<int64_t>(row) * ld;
-  const int64_t target = tgt[row];
-  const float inv = 1.f / cap;
-  const float c2 = cap * 1.4426950408889634f;  // cap * log2(e)
-  uint4 raw[NCHUNK];
-#pragma unroll
-  for (int i = 0; i < NCHUNK; ++i) {
-    const int c = (i * 512 + threadIdx.x) * 8;
-    raw[i] = c < V ? *reinterpret_cast<const uint4*>(l + c) : make_uint4(0, 0, 0, 0);
-  }
-  if (threadIdx.x == 0) zt_sh = target >= 0 ? cap * cap_terms(bf2f(l[target]), inv, c2).th : 0.f;
-  float sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < NCHUNK; ++i) {
-    const int c = (i * 512 + threadIdx.x) * 8;
-    const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(w[j]);
-      if (c + 2 * j < V) sum += cap_terms(f.x, inv, c2).e;
-      if (c + 2 * j + 1 < V) sum += cap_terms(f.y, inv, c2).e;
-    }
-  }
-  sum = warp_sum(sum);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) tot += red[i];
-  const float lse = cap + __logf(tot);
-  const float rinv = 1.f / tot;
-  if (threadIdx.x == 0) {
-    loss[row] = target >= 0 ? lse - zt_sh : 0.f;
-    if (lse_out) lse_out[row] = lse;
-  }
-#pragma unroll
-  for (int i = 0; i < NCHUNK; ++i) {
-    const int c = (i * 512 + threadIdx.x) * 8;
-    if (c >= V) continue;
-    const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(w[j]);
-      float g[2];
-      const float x2[2] = {f.x, f.y};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int col = c + 2 * j + h;
-        float gv = 0.f;
-        if (target >= 0 && col < V) {
-          const CapTerms ct = cap_terms(x2[h], inv, c2);
-          gv = (ct.e * rinv - (col == target ? 1.f : 0.f)) * ct.sech2;
-        }
-        g[h] = gv;
-      }
-      o[j] = pack_bf16x2(g[0], g[1]);
-    }
-    *reinterpret_cast<uint4*>(l + c) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
-}
-
 // ------------------------------------------------------------------ embedding + norm + smear
 // n[row] = norm(wte[idx[row]]);  x[row] = n[row] + gate[row] * n[row-1]  (t > 0 within a sequence)
 // gate = bf16(lambda) * sigmoid(dot(n[row, :24], w_smear)); the sigmoid is saved (0 at t == 0)
@@ -746,21 +652,11 @@ int nt_rope_norm_bwd(void* dqkv, const void* qkv, const void* cosb, const void* 
 }
 
 int nt_softcap_ce(void* logits, int64_t ld, const int64_t* tgt, float* loss, float* lse, int rows, int V, int Vp,
-                  float cap, cudaStream_t s) {
+                  float cap, int variant, cudaStream_t s) {
   if (ld % 8 || Vp % 8) return -1;
   if (rows <= 0) return 0;
-  // padded columns (V..Vp) must end with zero gradient: the register kernel covers them when
-  // V is a multiple of 8 (they are written as 0); otherwise use the general two-pass kernel.
-  const bool reg = (V % 8 == 0) && Vp == V;
-  if (reg && Vp <= 512 * 8 * 4) {
-    softcap_ce_reg_kernel<32><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
-  } else if (reg && Vp <= 512 * 8 * 8) {
-    softcap_ce_reg_kernel<64><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
-  } else if (reg && Vp <= 512 * 8 * 16) {
-    softcap_ce_reg_kernel<128><<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, cap);
-  } else {
-    softcap_ce_kernel<<<rows, 1024, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, Vp, cap);
-  }
+  (void)variant;
+  softcap_ce_kernel<<<rows, 1024, 0, s>>>((__nv_bfloat16*)logits, ld, tgt, loss, lse, V, Vp, cap);
   return 0;
 }
 

@@ -16,8 +16,9 @@ int nt_rope_norm_fwd(void* qkv, const void* cosb, const void* sinb, float* rstd,
 int nt_rope_norm_bwd(void* dqkv, const void* qkv, const void* cosb, const void* sinb, const float* rstd, int M,
                      int T, int H, int Hk, int D, float scale, const void* ve_table, const int64_t* idx,
                      const float* gate, float* dz, float* ve_grad, cudaStream_t s);
+// variant is reserved for alternative kernels (0 = default)
 int nt_softcap_ce(void* logits, int64_t ld, const int64_t* tgt, float* loss, float* lse, int rows, int V, int Vp,
-                  float cap, cudaStream_t s);
+                  float cap, int variant, cudaStream_t s);
 int nt_embed_smear(const void* wte, const int64_t* idx, const void* wsm, const float* lam, void* n_out, void* x_out,
                    float* gate_out, int M, int T, int d, int G, cudaStream_t s);
 int nt_embed_scatter(const void* dy, int dy_is_f32, const int64_t* idx, float* grad, int M, int d, cudaStream_t s);

@@ -18,6 +18,9 @@ from nexttransformer_b200.ops import gemm as G
 from nexttransformer_b200.ops._ext import ext
 from nexttransformer_b200.ops.attention import attention_fn
 
+# Cross-entropy kernel variant (0: automatic, 1: two-pass); kept selectable for numerics checks.
+CE_VARIANT = 0
+
 
 class GradSlot:
     """An fp32 gradient buffer that the next GEMM overwrites instead of accumulating into."""
@@ -282,7 +285,7 @@ class HeadLossFn(Function):
         lib.mix_norm_fwd(xo, None, None, None, hf, None, 1.0)
         logits = G.linear(hf, model.lm_head._w)
         rows = torch.empty(logits.shape[0], device=x.device, dtype=torch.float32)
-        lib.softcap_ce(logits, tgt, rows, None, cfg.vocab_size, cfg.softcap)
+        lib.softcap_ce(logits, tgt, rows, None, cfg.vocab_size, cfg.softcap, CE_VARIANT)
         total = rows.sum()
         if reduction == "mean":
             count = (tgt != -1).sum().clamp_min(1).float()
