@@ -401,6 +401,11 @@ class LanguageModel(GPTShell):
             self.last_lm_loss, self.last_aux_loss = loss.detach(), loss.new_zeros(())
             self.last_stats = {"fused_dense": True}
             return loss
+        if c.method == "dense":
+            # the SSSL anchor is the shell's own forward (same graph the cost anchor audits)
+            out = self.forward_eager(idx, targets, loss_reduction)
+            self.last_stats = {"native_dense_delegate": True}
+            return out
         special = None
         if c.method in ("ut_act", "huginn", "ouro"):
             logits, aux, special = self._loop_hidden(idx, targets)
@@ -431,14 +436,16 @@ class LanguageModel(GPTShell):
         return self.last_lm_loss + (aux if self.training else 0)
 
 
-def build_model(config: ModelConfig, device="cpu", seed=42):
-    """Meta construction -> materialise on `device` -> reference-order initialisation."""
-    torch.manual_seed(seed)
+def construct(config: ModelConfig):
+    """The model on the meta device (no storage)."""
     hooks = plug.load(config.method) if config.method in PLUGIN_METHODS else None
     with torch.device("meta"):
-        model = (hooks.model if hooks and hooks.model else LanguageModel)(config)
-    if str(device) == "meta":
-        return model
+        return (hooks.model if hooks and hooks.model else LanguageModel)(config)
+
+
+def materialize(model, device):
+    """Allocate a meta-constructed model on `device` and run the reference-order initialisation."""
+    config = model.config
     model.to_empty(device=device)
     from nexttransformer_b200.models.linear import CausalDepthwise
     for m in model.modules():
@@ -461,7 +468,16 @@ def build_model(config: ModelConfig, device="cpu", seed=42):
             m.expert_bias.zero_()
             m.load.zero_()
             nn.init.normal_(m.router.weight, std=0.02)
-    if hooks:
+    if config.method in PLUGIN_METHODS:
         plug.reset(model)
     model.init_weights()
     return model
+
+
+def build_model(config: ModelConfig, device="cpu", seed=42):
+    """Meta construction -> materialise on `device` -> reference-order initialisation."""
+    torch.manual_seed(seed)
+    model = construct(config)
+    if str(device) == "meta":
+        return model
+    return materialize(model, device)

@@ -8,9 +8,9 @@ reference (``nexttransformer/models/others.py``): c_q, q_up, c_k, c_v, c_proj.
 """
 import torch
 from torch import nn
-import torch.nn.functional as F
 
-from nexttransformer_b200.models.shell import Linear, apply_rotary_emb, norm, window_mask
+from nexttransformer_b200.models import shell as shell_mod
+from nexttransformer_b200.models.shell import Linear, apply_rotary_emb, norm
 
 
 class MLAAttention(nn.Module):
@@ -51,10 +51,5 @@ class MLAAttention(nn.Module):
             k = torch.cat((k_nope, k_rope.expand(B, T, H, self.rope)), -1)
         else:
             k = k_nope
-        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
-        w = window_size[0]
-        if w < 0 or w >= T - 1:
-            y = F.scaled_dot_product_attention(qt, kt, vt, is_causal=True)
-        else:
-            y = F.scaled_dot_product_attention(qt, kt, vt, attn_mask=window_mask(T, w, x.device))
-        return self.c_proj(y.transpose(1, 2).reshape(B, T, H * self.v_dim))
+        y = shell_mod.sdpa(q, k, v, window_size[0])
+        return self.c_proj(y.reshape(B, T, H * self.v_dim))

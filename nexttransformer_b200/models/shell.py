@@ -243,9 +243,9 @@ class GPTShell(nn.Module):
                 nn.init.uniform_(g.weight, 0.0, 0.02)
         self.cos, self.sin = self._rotary(self.rotary_seq_len, cfg.head_dim)
         if COMPUTE_DTYPE != torch.float16:
-            self.transformer.wte.to(dtype=COMPUTE_DTYPE)
-            for ve in self.value_embeds.values():
-                ve.to(dtype=COMPUTE_DTYPE)
+            for emb in (self.transformer.wte, *self.value_embeds.values()):
+                if emb.weight.dtype != COMPUTE_DTYPE:
+                    emb.to(dtype=COMPUTE_DTYPE)
 
     def get_device(self):
         return self.transformer.wte.weight.device
