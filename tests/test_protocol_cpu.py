@@ -40,18 +40,6 @@ def test_causal_edges():
     assert causal_edges(2048, 2048) == 2048 * 2049 // 2
 
 
-@pytest.mark.parametrize("method", ["dense", "dense_full", "gdn", "nsa", "moba", "dsa", "hc", "mhc", "attnres",
-                                    "ut_act", "ouro", "mla_nope", "gdn_hybrid_swa", "elu_norm", "retnet"])
-def test_ledger_matches_reference(reference, method):
-    from nexttransformer.models.config import debug_config as rdebug
-    from nexttransformer.protocol.compute import audit_graph as raudit
-    c, rc = debug_config(method), rdebug(method)
-    mine = audit_graph(c, batch=2)
-    ref = raudit(rc, batch=2)
-    assert not mine["unknown"], mine["unknown"]
-    assert mine["phases"] == ref["phases"], (mine["phases"], ref["phases"])
-
-
 def test_formal_dense_anchor():
     """The SSSL d24 anchor costs 4.672398325 GFLOPs per input token at the protocol batch."""
     c = candidate_config("dense")
