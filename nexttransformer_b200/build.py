@@ -1,4 +1,7 @@
-"""Build the sm_100a CUDA extension in place: ``python -m nexttransformer_b200.build``.
+"""Build the native extensions in place: ``python -m nexttransformer_b200.build``.
+
+``_C`` holds the sm_100a CUDA kernels; ``_native`` the host-side C++ runtime (best-fit data
+packing, BPE merge training).
 
 The kernels live in ``nexttransformer_b200/csrc``.  They are compiled only for Blackwell
 (``-gencode arch=compute_100a,code=sm_100a``) and linked into ``nexttransformer_b200/_C*.so``
@@ -23,7 +26,7 @@ NVCC_FLAGS = [
 def build(verbose=False):
     """Compile every CUDA source of the package into ``nexttransformer_b200/_C``."""
     from setuptools import setup
-    from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+    from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
     os.environ.setdefault("MAX_JOBS", str(max(1, os.cpu_count() or 1)))
     ext = CUDAExtension(
@@ -32,12 +35,17 @@ def build(verbose=False):
         include_dirs=[str(HERE / "csrc")],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
     )
+    host = CppExtension(
+        name="nexttransformer_b200._native",
+        sources=[str(HERE / "csrc" / "native_host.cpp")],
+        extra_compile_args={"cxx": ["-O3", "-std=c++17"]},
+    )
     build_temp = HERE.parent / "build" / "nt_ext"
     argv = ["build_ext", "--inplace", "--build-temp", str(build_temp)]
     cwd = os.getcwd()
     os.chdir(HERE.parent)
     try:
-        setup(name="nexttransformer_b200_ext", ext_modules=[ext],
+        setup(name="nexttransformer_b200_ext", ext_modules=[ext, host],
               cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
               script_args=argv if verbose else ["-q", *argv])
     finally:
