@@ -39,7 +39,8 @@ class MoEFFN(nn.Module):
         self.experts = nn.ModuleList(ExpertMLP(width, expert_width) for _ in range(num_experts))
         self.register_buffer("expert_bias", torch.zeros(num_experts), persistent=True)
         self.register_buffer("load", torch.zeros(num_experts), persistent=False)
-        self.ep_group = None       # set by parallel.expert.enable_expert_parallel
+        self.ep_group = None       # set by parallel.expert.enable_expert_parallel (None = world group)
+        self.ep_size = 1
         self.last_stats = {}
 
     def route(self, rows):
@@ -56,7 +57,7 @@ class MoEFFN(nn.Module):
         with torch.no_grad():
             self.load += torch.bincount(choice.flatten(), minlength=self.num_experts).float()
         out = self.shared(rows) if self.shared is not None else torch.zeros_like(rows)
-        if self.ep_group is not None:
+        if self.ep_size > 1:
             from nexttransformer_b200.parallel.expert import expert_parallel_combine
             routed = expert_parallel_combine(self, rows, choice, w)
         else:

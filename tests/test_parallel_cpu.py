@@ -1,0 +1,83 @@
+"""Expert- and tensor-parallel algorithms on gloo ranks (CPU) against single-process references."""
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests.conftest import free_port
+
+
+def _init(rank, world, port):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), CUDA_VISIBLE_DEVICES="")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    return dist
+
+
+def _ep_worker(rank, world, port, q):
+    dist = _init(rank, world, port)
+    from nexttransformer_b200.models.moe import MoEFFN
+    from nexttransformer_b200.parallel.expert import enable_expert_parallel
+    torch.manual_seed(0)
+    ref = MoEFFN(16, num_experts=4, top_k=2, expert_width=8)
+    with torch.no_grad():
+        for p in ref.parameters():
+            p.normal_(0, 0.3)
+    ep = MoEFFN(16, num_experts=4, top_k=2, expert_width=8)
+    ep.load_state_dict(ref.state_dict())
+    enable_expert_parallel(ep)
+    torch.manual_seed(1)
+    x_all = torch.randn(world, 12, 16)
+    x = x_all[rank].clone().requires_grad_()
+    y = ep(x)
+    xr = x_all[rank].clone().requires_grad_()
+    yr = ref(xr)
+    fwd = (y - yr).abs().max().item()
+    y.square().sum().backward()
+    yr.square().sum().backward()
+    dx = (x.grad - xr.grad).abs().max().item()
+    # expert weights: the owner's gradient equals the sum of the reference gradients over ranks
+    own = [i for i in range(4) if i // 2 == rank]
+    g_all = torch.stack([ref.experts[i].c_fc.weight.grad for i in range(4)])
+    dist.all_reduce(g_all)
+    g_ep = torch.cat([ep.experts[i].c_fc.weight.grad.flatten() for i in own])
+    g_ref = torch.cat([g_all[i].flatten() for i in own])
+    q.put((rank, fwd, dx, (g_ep - g_ref).abs().max().item()))
+    dist.destroy_process_group()
+
+
+def _tp_worker(rank, world, port, q):
+    dist = _init(rank, world, port)
+    from nexttransformer_b200.models.shell import MLP, ShellConfig
+    from nexttransformer_b200.parallel.tensor import MLPTP
+    torch.manual_seed(0)
+    dense = MLP(ShellConfig(n_embd=16, n_head=2, n_kv_head=2, mlp_width=32))
+    with torch.no_grad():
+        for p in dense.parameters():
+            p.normal_(0, .2)
+    tp = MLPTP.from_dense(dense)
+    torch.manual_seed(2)
+    x = torch.randn(8, 16)
+    rows = x.shape[0] // world
+    y_shard = tp(x[rank * rows:(rank + 1) * rows])
+    ref = dense(x)[rank * rows:(rank + 1) * rows]
+    q.put((rank, (y_shard - ref).abs().max().item()))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", ["ep", "tp"])
+def test_parallel_matches_reference(worker):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    fn = _ep_worker if worker == "ep" else _tp_worker
+    procs = [ctx.Process(target=fn, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    for _ in range(2):
+        vals = q.get()
+        assert max(vals[1:]) < 1e-4, vals
