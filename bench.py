@@ -34,6 +34,7 @@ BASELINE_TOKS = None  # BASELINE.md publishes no number for this configuration
 MODEL = dict(sequence_len=2048, vocab_size=65536, n_layer=20, n_head=10, n_kv_head=5, n_embd=1280,
              window_pattern="L")
 GLOBAL_BATCH = 524288
+METRIC = "train tokens/sec on 8\u00d7B200 (max over ranks) per method at matched FLOPs/token"
 
 
 def parse():
@@ -279,7 +280,7 @@ def main():
             if x.strip().isdigit()] or list(range(world))
     clocks = sampler.summary(set(gpus[:world]) if local == 0 else set())
     if rank == 0:
-        out = {"metric": "train tokens/sec on 8xB200 (max over ranks) per method at matched FLOPs/token",
+        out = {"metric": METRIC,
                "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
                "vs_baseline": (value / BASELINE_TOKS) if BASELINE_TOKS else None, "dtype": "bf16",

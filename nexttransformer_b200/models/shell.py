@@ -86,7 +86,15 @@ def window_mask(T, window, device):
 
 
 def sdpa(q, k, v, window):
-    """Causal attention on [B, T, H, D] tensors with an optional left window (GQA by repetition)."""
+    """Causal attention on [B, T, H, D] tensors with an optional left window (GQA by repetition).
+
+    CUDA bf16 tensors of a supported head dim run the sm_100a flash-attention kernels; everything else
+    (CPU, fp32 oracles, FakeTensor audits) runs PyTorch's SDPA.
+    """
+    if q.is_cuda:
+        from nexttransformer_b200.ops import attention as _attn
+        if _attn.kernel_supports(q, k, v):
+            return _attn.attention_bthd(q, k, v, window)
     B, T, H, D = q.shape
     q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     gqa = k.shape[1] != H

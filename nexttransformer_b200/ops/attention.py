@@ -77,6 +77,50 @@ class _LibraryAttn(Function):
         return dqkv, None, None, None, None, None, None
 
 
+class _KernelAttnBTHD(Function):
+    """The same kernels on separate ``[B, T, H, D]`` q / ``[B, T, Hk, D]`` k, v tensors (the layout
+    of the eager mixers); gradients come back in that layout."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, window):
+        B, T, H, D = q.shape
+        Hk = k.shape[2]
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o = torch.empty(B * T, H * D, device=q.device, dtype=torch.bfloat16)
+        lse = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
+        w = window if 0 <= window < T - 1 else -1
+        ext().attn_fwd(q.view(B * T, H * D), k.view(B * T, Hk * D), v.view(B * T, Hk * D), o, lse, B, T, H, Hk, D,
+                       w, 1.0 / math.sqrt(D))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.w = w
+        return o.view(B, T, H, D)
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        B, T, H, D = q.shape
+        Hk = k.shape[2]
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        dq_acc = torch.zeros(B * T, H * D, device=q.device, dtype=torch.float32)
+        delta = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
+        ext().attn_bwd(q.view(B * T, -1), k.view(B * T, -1), v.view(B * T, -1), o, lse,
+                       do.contiguous().view(B * T, -1), dq.view(B * T, -1), dk.view(B * T, -1), dv.view(B * T, -1),
+                       dq_acc, delta, B, T, H, Hk, D, ctx.w, 1.0 / math.sqrt(D))
+        return dq, dk, dv, None
+
+
+def kernel_supports(q, k, v):
+    """True when the sm_100a kernels take these ``[B, T, H, D]`` tensors."""
+    return (_kernel_enabled and q.is_cuda and q.dtype == k.dtype == v.dtype == torch.bfloat16
+            and q.shape[-1] in KERNEL_HEAD_DIMS and k.shape == v.shape and q.shape[2] % k.shape[2] == 0
+            and type(q) is torch.Tensor)
+
+
+def attention_bthd(q, k, v, window):
+    """Causal (windowed) GQA attention on ``[B, T, H, D]`` tensors through the sm_100a kernels."""
+    return _KernelAttnBTHD.apply(q, k, v, window)
+
+
 def attention_fn(qkv, B, T, H, Hk, D, window):
     if _use_kernel(qkv, D):
         return _KernelAttn.apply(qkv, B, T, H, Hk, D, window)

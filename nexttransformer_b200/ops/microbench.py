@@ -1,0 +1,211 @@
+"""Per-kernel timing harness for the sm_100a kernels (one GPU).
+
+    python -m nexttransformer_b200.ops.microbench <case> [--rows M] [--iters N] [--warmup W]
+
+Cases time one kernel family with CUDA events on the launching stream (warm-up first, a
+synchronize on both sides) and print one JSON line: milliseconds per launch, the algorithmic
+FLOPs or bytes, the achieved rate and its fraction of the measured peaks of this machine when
+``MEASURED_PEAKS.json`` sits at the repository root.  Operands are larger than L2 for the default
+sizes, so no flush is needed between launches.  The same command with small ``--rows`` and
+``--iters 1`` is the small case to capture under a profiler.
+
+Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, vocab 65536):
+  gemm_qkv, gemm_fc, gemm_proj, gemm_wgrad, gemm_head - the GEMM engine with its epilogues
+  attn_fwd, attn_bwd                                   - flash attention, rows = B*T (T 2048)
+  ce                                                   - soft-capped cross-entropy over 65536 logits
+  adamw                                                - AdamW over a [rows, 1280] table
+  muon                                                 - the Muon chain on 20 matrices [5120, 1280]
+  step                                                 - one fused training micro-step (all kernels)
+"""
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+WIDTH, HEADS, KV_HEADS, HEAD_DIM, FFN, VOCAB, SEQ = 1280, 10, 5, 128, 5120, 65536, 2048
+
+
+def peaks():
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if not path.is_file():
+        return {}
+    raw = json.loads(path.read_text())
+    flat = {}
+
+    def walk(d):
+        for k, v in d.items():
+            if isinstance(v, dict):
+                walk(v)
+            elif isinstance(v, (int, float)):
+                flat.setdefault(k, v)
+    walk(raw)
+    return flat
+
+
+def timed(fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def _bf16(*shape):
+    return torch.randn(*shape, device="cuda").to(torch.bfloat16)
+
+
+def case_gemm(kind, rows):
+    from nexttransformer_b200.ops import gemm as G
+    if kind == "gemm_qkv":
+        a, w = _bf16(rows, WIDTH), _bf16(WIDTH + 2 * KV_HEADS * HEAD_DIM, WIDTH)
+        out = torch.empty(rows, w.shape[0], device="cuda", dtype=torch.bfloat16)
+        return (lambda: G.gemm(a, w, out)), 2 * rows * w.shape[0] * WIDTH
+    if kind == "gemm_fc":
+        a, w = _bf16(rows, WIDTH), _bf16(FFN, WIDTH)
+        pre = torch.empty(rows, FFN, device="cuda", dtype=torch.bfloat16)
+        act = torch.empty_like(pre)
+        return (lambda: G.gemm(a, w, act, epi=G.EPI_RELU2, p=pre)), 2 * rows * FFN * WIDTH
+    if kind == "gemm_proj":
+        a, w, r = _bf16(rows, FFN), _bf16(WIDTH, FFN), _bf16(rows, WIDTH)
+        out = torch.empty(rows, WIDTH, device="cuda", dtype=torch.bfloat16)
+        return (lambda: G.gemm(a, w, out, epi=G.EPI_BF16_AXPBY, r=r)), 2 * rows * WIDTH * FFN
+    if kind == "gemm_wgrad":
+        dy, x = _bf16(rows, FFN), _bf16(rows, WIDTH)
+        grad = torch.zeros(FFN, WIDTH, device="cuda")
+        return (lambda: G.wgrad(dy, x, grad, accumulate=True)), 2 * rows * FFN * WIDTH
+    if kind == "gemm_head":
+        a, w = _bf16(rows, WIDTH), _bf16(VOCAB, WIDTH)
+        out = torch.empty(rows, VOCAB, device="cuda", dtype=torch.bfloat16)
+        return (lambda: G.gemm(a, w, out)), 2 * rows * VOCAB * WIDTH
+    raise ValueError(kind)
+
+
+def _attn_flops(B, causal_pairs, fwd):
+    per_pair = 4 * HEAD_DIM * HEADS      # QK^T and PV
+    return B * causal_pairs * per_pair * (1 if fwd else 2.5)
+
+
+def case_attn(kind, rows):
+    from nexttransformer_b200.ops.attention import attention_fn
+    B = max(1, rows // SEQ)
+    M = B * SEQ
+    qkv = _bf16(M, (HEADS + 2 * KV_HEADS) * HEAD_DIM).mul_(0.3).requires_grad_(kind == "attn_bwd")
+    pairs = SEQ * (SEQ + 1) // 2
+    if kind == "attn_fwd":
+        return (lambda: attention_fn(qkv, B, SEQ, HEADS, KV_HEADS, HEAD_DIM, -1)), _attn_flops(B, pairs, True)
+    y = attention_fn(qkv, B, SEQ, HEADS, KV_HEADS, HEAD_DIM, -1)
+    dy = torch.randn_like(y)
+
+    def bwd():
+        torch.autograd.grad(y, qkv, dy, retain_graph=True)
+    return bwd, _attn_flops(B, pairs, False)
+
+
+def case_ce(rows):
+    from nexttransformer_b200.ops._ext import ext
+    logits = _bf16(rows, VOCAB)
+    tgt = torch.randint(0, VOCAB, (rows,), device="cuda")
+    loss = torch.empty(rows, device="cuda")
+    lse = torch.empty(rows, device="cuda")
+    keep = logits.clone()
+
+    def run():
+        logits.copy_(keep)
+        ext().softcap_ce(logits, tgt, loss, lse, VOCAB, 15.0)
+    # the kernel reads the logits twice and writes the gradient once (the restore copy is extra)
+    return run, None, 3 * logits.numel() * 2
+
+
+def case_adamw(rows):
+    from nexttransformer_b200.ops._ext import ext
+    p = torch.randn(rows, WIDTH, device="cuda")
+    g, m, v = torch.randn_like(p), torch.zeros_like(p), torch.zeros_like(p)
+    sh = torch.empty(rows, WIDTH, device="cuda", dtype=torch.bfloat16)
+    step = [0]
+
+    def run():
+        step[0] += 1
+        ext().adamw(p, g, m, v, sh, 1e-3, 0.8, 0.95, 1e-10, 0.01, step[0])
+    # read p, g, m, v; write p, m, v (fp32) and the bf16 shadow
+    return run, None, p.numel() * (7 * 4 + 2)
+
+
+def case_muon(rows):
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+    params = [torch.nn.Parameter(torch.randn(FFN, WIDTH, device="cuda") * 0.02) for _ in range(20)]
+    for p in params:
+        p.grad = torch.randn_like(p)
+    opt = MuonAdamW([dict(kind="muon", params=params, lr=0.02, momentum=0.95, ns_steps=5, beta2=0.9,
+                          weight_decay=0.0)])
+    # 5 Polar-Express iterations x 3 GEMMs on tall [m, n] = [5120, 1280] matrices
+    m, n = FFN, WIDTH
+    flops = 20 * 5 * (2 * m * n * n + 2 * n * n * n + 2 * m * n * n)
+    return (lambda: opt.step()), flops
+
+
+def case_step(rows, layers):
+    from nexttransformer_b200.models.shell import ShellConfig, build_shell
+    B = max(1, rows // SEQ)
+    model = build_shell(ShellConfig(sequence_len=SEQ, vocab_size=VOCAB, n_layer=layers, n_head=HEADS,
+                                    n_kv_head=KV_HEADS, n_embd=WIDTH, window_pattern="L"), "cuda", seed=1)
+    model.fused_state()
+    model.train()
+    tok = torch.randint(0, VOCAB, (B, SEQ + 1), device="cuda")
+    x, y = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+
+    def run():
+        model(x, y).backward()
+    return run, model.estimate_flops() * B * SEQ
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("case")
+    ap.add_argument("--rows", type=int, default=65536)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=2)
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    byts = None
+    if a.case.startswith("gemm_"):
+        fn, flops = case_gemm(a.case, a.rows)
+    elif a.case.startswith("attn_"):
+        fn, flops = case_attn(a.case, a.rows)
+    elif a.case == "ce":
+        fn, flops, byts = case_ce(a.rows)
+    elif a.case == "adamw":
+        fn, flops, byts = case_adamw(a.rows)
+    elif a.case == "muon":
+        fn, flops = case_muon(a.rows)
+    elif a.case == "step":
+        fn, flops = case_step(a.rows, a.layers)
+    else:
+        raise SystemExit(f"unknown case {a.case}")
+    ms = timed(fn, a.iters, a.warmup)
+    from nexttransformer_b200.ops._ext import check_errors
+    check_errors()
+    pk = peaks()
+    out = {"case": a.case, "rows": a.rows, "ms": ms}
+    if flops:
+        tf = flops / ms / 1e9
+        out.update(tflops=tf)
+        if "bf16_tflops" in pk:
+            out.update(frac_of_measured_bf16=tf / pk["bf16_tflops"])
+    if byts:
+        gbs = byts / ms / 1e6
+        out.update(gbps=gbs)
+        if "hbm_gbs" in pk:
+            out.update(frac_of_measured_hbm=gbs / pk["hbm_gbs"])
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -6,9 +6,9 @@ interchangeable), parameter names/shapes match, and loss + every parameter gradi
 import pytest
 import torch
 
-from nexttransformer_b200.models.registry import BUILTIN_METHODS
+from nexttransformer_b200.models.registry import METHODS
 
-REFERENCE_METHODS = [m for m in BUILTIN_METHODS if m != "moe"]
+REFERENCE_METHODS = [m for m in METHODS if m != "moe"]
 
 
 @pytest.fixture(scope="module")

@@ -50,7 +50,8 @@ def test_formal_dense_anchor():
 
 GOLDEN_FAST = ["dense_full", "mha_no_ve", "hc", "attnres", "mla_nope", "fixed_recursive", "deeploop", "ouro",
                pytest.param("nsa", marks=pytest.mark.slow), pytest.param("gdn", marks=pytest.mark.slow),
-               pytest.param("kda", marks=pytest.mark.slow), "retnet"]
+               pytest.param("kda", marks=pytest.mark.slow), "retnet", "xsa", "gated_attention",
+               "gated_attention_headwise", "simplehc", "attnres_full_canon_abcd", "msar", "inkling_rel"]
 
 
 @pytest.mark.parametrize("method", GOLDEN_FAST)
@@ -67,5 +68,5 @@ def test_method_cost_matches_reference_record(method):
     c = ModelConfig(**{k: tuple(v) if isinstance(v, list) else v for k, v in ref_cfg.items() if k != "layer_mixers"})
     assert c.fingerprint == gold["model_hash"]
     per_token, _ = method_cost(c)
-    # 9 of these match to 1e-6; chunked linear and NSA differ by < 0.1 % (operator order), inside the 1 % rule
+    # most match to 1e-6; chunked linear and NSA differ by < 0.1 % (operator order), inside the 1 % rule
     assert abs(per_token / gold["flops_per_token"] - 1) < 5e-3, (per_token, gold["flops_per_token"])
