@@ -65,7 +65,12 @@ NT_DEVICE uint32_t swz_off(int r, int c) {
   return (c >> 3) * BOX_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
-NT_DEVICE float fast_exp2(float x) { return exp2f(x); }
+// 2^x with the SFU's approximate base-2 exponential (ex2.approx.ftz: inputs far below -126 give 0).
+NT_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // ------------------------------------------------------------------------------ forward
 struct FwdSmem {
@@ -208,6 +213,7 @@ __global__ void __launch_bounds__(192, 1)
       const int st = t & 1;
       const int k0 = (j_lo + t) * TILE;
       if (!mbar_wait(&s_full[st], (t >> 1) & 1, 0x30u, abort_flag)) { ok = false; break; }
+      __syncwarp();
       tc_fence_after();
       float s[TILE];
 #pragma unroll
@@ -248,6 +254,7 @@ __global__ void __launch_bounds__(192, 1)
       if (t > 0) {
         // PV of the previous tile must be complete before O is touched or P is overwritten
         if (!mbar_wait(o_done, (t - 1) & 1, 0x31u, abort_flag)) { ok = false; break; }
+        __syncwarp();
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -275,12 +282,14 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(p_full);
     }
     if (ok && mbar_wait(o_done, (n_kv - 1) & 1, 0x32u, abort_flag)) {
+      __syncwarp();
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + (static_cast<int64_t>(b) * p.T + qi) * p.ldo + h * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
+        __syncwarp();
         tmem_ld32(t_o + lane_off + c * 32, v);
         tmem_wait_ld();
         if (qi < p.T) {
@@ -307,20 +316,43 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ------------------------------------------------------------------------------ backward
+// One CTA per (key tile of 128, KV head, batch); 320 threads.  Key tiles are the fastest-varying
+// block index: CTAs running at the same time then share one (batch, KV head), so the fp32 dQ rows
+// they all add into stay resident in L2 (ordering heavy key tiles first across all heads instead
+// quadrupled the DRAM write traffic of dQ).
+//   warp 0      TMA: K and V once, then (Q, dO) tiles of every (query head, query tile) pair into
+//               a 2-stage ring.
+//   warp 1      TMEM owner and MMA issuer, per pair i:
+//                 S^T = K Q^T -> tS;  dP^T = V dO^T -> tDP (after dQ of pair i-1 left tDP);
+//                 dV += P^T dO with P^T read from tensor memory (tS, bf16);
+//                 dK += dS^T Q;  dQ = dS K -> tDP.
+//   warps 2..5  one key row per thread: P^T = exp2(S^T scale - lse) written back over tS as
+//               bf16, then dS^T = P^T (dP^T - delta) into shared memory (128B-swizzled).
+//   warps 6..9  drain dQ: tcgen05.ld of the 128 x 128 fp32 tile in two halves of 64 columns,
+//               release tDP, stage each half in the dS^T buffer (free once dK and dQ are done) and
+//               add it to the fp32 dQ buffer with one bulk tensor reduction (performed in L2), while
+//               the MMAs of the next pair go on; the softmax warps write the next dS^T once the
+//               last reduction has read the buffer.
+// Tensor-memory columns: tS [0,128) | tDP [128,256) | dV [256,384) | dK [384,512).
+// MMAs issued by one thread execute in order, so S^T of pair i+1 may be issued while the dV MMA
+// of pair i still reads P^T from the same columns.
 struct BwdSmem {
   static constexpr int K = 0;
   static constexpr int V = K + TILE_BYTES;
-  static constexpr int Q = V + TILE_BYTES;     // Q tile (one stage)
-  static constexpr int DO = Q + TILE_BYTES;    // dO tile
-  static constexpr int PT = DO + TILE_BYTES;   // P^T  [keys x queries]
-  static constexpr int DST = PT + TILE_BYTES;  // dS^T [keys x queries]
-  static constexpr int LSE = DST + TILE_BYTES; // 128 floats
-  static constexpr int DEL = LSE + 512;        // 128 floats
-  static constexpr int BAR = DEL + 512;
-  // kv_full, qd_full, qd_empty, st_full, ps_full, dq_full, dq_free
-  static constexpr int NBAR = 7;
+  static constexpr int Q = V + TILE_BYTES;        // 2 stages
+  static constexpr int DO = Q + 2 * TILE_BYTES;   // 2 stages
+  static constexpr int DST = DO + 2 * TILE_BYTES; // dS^T [keys x queries]
+  static constexpr int STAT = DST + TILE_BYTES;   // lse * log2(e) [128], delta [128] of the current pair
+  static constexpr int BAR = STAT + 1024;
+  // kv_full, qd_full[2], qd_empty[2], s_full, p_full, dp_full, ds_full, dq_full, dq_free,
+  // stg_full, stg_free, stg_done (the dS^T buffer doubles as the fp32 staging tile of the dQ
+  // reduction; stg_free completes per staged half, stg_done once per pair), stat_ready, stat_free
+  static constexpr int NBAR = 16;
   static constexpr int TOTAL = BAR + NBAR * 8 + 16 + 1024;
 };
+static_assert(BwdSmem::TOTAL <= 232448, "backward shared memory exceeds the sm_100 limit");
+
+constexpr int BWD_THREADS = 320;
 
 NT_DEVICE void bwd_q_range(const Params& p, int k0, int& i_lo, int& i_hi) {
   const int n_qt = (p.T + TILE - 1) / TILE;
@@ -329,23 +361,29 @@ NT_DEVICE void bwd_q_range(const Params& p, int k0, int& i_lo, int& i_hi) {
   if (p.window >= 0) i_hi = min(i_hi, (k0 + TILE - 1 + p.window) / TILE);
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, Params p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const __grid_constant__ CUtensorMap tmDQ, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 2;
-  uint64_t* st_full = bars + 3;
-  uint64_t* ps_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_free = bars + 6;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dp_full = bars + 7;
+  uint64_t* ds_full = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_free = bars + 10;
+  uint64_t* stg_full = bars + 11;
+  uint64_t* stg_free = bars + 12;
+  uint64_t* stg_done = bars + 13;
+  uint64_t* stat_ready = bars + 14;
+  uint64_t* stat_free = bars + 15;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + BwdSmem::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* s_lse = reinterpret_cast<float*>(sm + BwdSmem::LSE);
-  float* s_del = reinterpret_cast<float*>(sm + BwdSmem::DEL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -354,12 +392,25 @@ __global__ void __launch_bounds__(192, 1)
   int i_lo, i_hi;
   bwd_q_range(p, k0, i_lo, i_hi);
   const int n_q = i_hi - i_lo + 1;
-  const int n_it = group * n_q;  // iterations: (head in group, query tile)
+  const int n_it = group * n_q;  // (query head in the group, query tile) pairs
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < BwdSmem::NBAR; ++i) mbar_init(&bars[i], 1);
-    mbar_init(ps_full, 128);
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_full, 128);
+    mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
+    mbar_init(stg_full, 128);
+    mbar_init(stg_free, 1);
+    mbar_init(stg_done, 1);
+    mbar_init(stat_ready, 128);
+    mbar_init(stat_free, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -371,13 +422,15 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
-  const uint32_t t_st = tbase;         // S^T, later dQ
-  const uint32_t t_dp = tbase + 128;   // dP^T
-  const uint32_t t_dv = tbase + 256;   // dV accumulator
-  const uint32_t t_dk = tbase + 384;   // dK accumulator
+  const uint32_t t_s = tbase;          // S^T, then P^T (bf16, 64 columns)
+  const uint32_t t_dp = tbase + 128;   // dP^T, then dQ
+  const uint32_t t_dv = tbase + 256;
+  const uint32_t t_dk = tbase + 384;
 
   if (warp == 0) {
     if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDO);
       mbar_expect_tx(kv_full, 2 * TILE_BYTES);
       tma_load_3d(sm + BwdSmem::K, &tmK, kv_full, hk * HD, k0, b);
       tma_load_3d(sm + BwdSmem::K + BOX_BYTES, &tmK, kv_full, hk * HD + 64, k0, b);
@@ -385,18 +438,22 @@ __global__ void __launch_bounds__(192, 1)
       tma_load_3d(sm + BwdSmem::V + BOX_BYTES, &tmV, kv_full, hk * HD + 64, k0, b);
       int issued = 0;
       for (int it = 0; it < n_it; ++it) {
+        const int st = it & 1;
         const int h = hk * group + it / n_q;
         const int q0 = (i_lo + it % n_q) * TILE;
-        if (!mbar_wait(qd_empty, (it & 1) ^ 1u, 0x50u, abort_flag)) break;
-        mbar_expect_tx(qd_full, 2 * TILE_BYTES);
-        tma_load_3d(sm + BwdSmem::Q, &tmQ, qd_full, h * HD, q0, b);
-        tma_load_3d(sm + BwdSmem::Q + BOX_BYTES, &tmQ, qd_full, h * HD + 64, q0, b);
-        tma_load_3d(sm + BwdSmem::DO, &tmDO, qd_full, h * HD, q0, b);
-        tma_load_3d(sm + BwdSmem::DO + BOX_BYTES, &tmDO, qd_full, h * HD + 64, q0, b);
+        if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1u, 0x50u + st, abort_flag)) break;
+        uint8_t* qs = sm + BwdSmem::Q + st * TILE_BYTES;
+        uint8_t* ds = sm + BwdSmem::DO + st * TILE_BYTES;
+        mbar_expect_tx(&qd_full[st], 2 * TILE_BYTES);
+        tma_load_3d(qs, &tmQ, &qd_full[st], h * HD, q0, b);
+        tma_load_3d(qs + BOX_BYTES, &tmQ, &qd_full[st], h * HD + 64, q0, b);
+        tma_load_3d(ds, &tmDO, &qd_full[st], h * HD, q0, b);
+        tma_load_3d(ds + BOX_BYTES, &tmDO, &qd_full[st], h * HD + 64, q0, b);
         ++issued;
       }
+      // no copy may still be in flight when the CTA exits
       mbar_wait(kv_full, 0, 0x5Eu, nullptr);
-      if (issued > 0) mbar_wait(qd_full, (issued - 1) & 1, 0x5Fu, nullptr);
+      for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait(&qd_full[it & 1], (it >> 1) & 1, 0x5Fu, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -404,141 +461,231 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t id_kv = idesc_bf16_f32(TILE, HD, 0, 1);    // dV += P^T dO ; dK += dS^T Q
       constexpr uint32_t id_q = idesc_bf16_f32(TILE, HD, 1, 1);     // dQ = dS K  (A = dS^T read M-major)
       const uint32_t k_addr = smem_u32(sm + BwdSmem::K), v_addr = smem_u32(sm + BwdSmem::V);
-      const uint32_t q_addr = smem_u32(sm + BwdSmem::Q), do_addr = smem_u32(sm + BwdSmem::DO);
-      const uint32_t pt_addr = smem_u32(sm + BwdSmem::PT), ds_addr = smem_u32(sm + BwdSmem::DST);
+      const uint32_t ds_addr = smem_u32(sm + BwdSmem::DST);
       bool ok = mbar_wait(kv_full, 0, 0x60u, abort_flag);
       for (int it = 0; ok && it < n_it; ++it) {
-        if (!mbar_wait(qd_full, it & 1, 0x61u, abort_flag)) break;
-        if (!mbar_wait(dq_free, (it & 1) ^ 1u, 0x62u, abort_flag)) break;  // S^T/dQ columns free
+        const int st = it & 1;
+        const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + st * TILE_BYTES);
+        const uint32_t do_addr = smem_u32(sm + BwdSmem::DO + st * TILE_BYTES);
+        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, 0x61u, abort_flag)) break;
         tc_fence_after();
-#pragma unroll
-        for (int j = 0; j < HD / 16; ++j) umma_bf16(t_st, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
-#pragma unroll
+        // loops are kept rolled: fully unrolled, the descriptors of every k-step of every operand
+        // would be hoisted into registers that the other warp roles need
+#pragma unroll 1
+        for (int j = 0; j < HD / 16; ++j) umma_bf16(t_s, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
+        umma_commit(s_full);
+        if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x62u, abort_flag)) break;  // dQ of it-1 left tDP
+        tc_fence_after();
+#pragma unroll 1
         for (int j = 0; j < HD / 16; ++j)
           umma_bf16(t_dp, kmajor_desc(v_addr, j), kmajor_desc(do_addr, j), id_s, j > 0);
-        umma_commit(st_full);
-        if (!mbar_wait(ps_full, it & 1, 0x63u, abort_flag)) break;
+        umma_commit(dp_full);
+        if (!mbar_wait(p_full, it & 1, 0x63u, abort_flag)) break;
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16(t_dv, kmajor_desc(pt_addr, j), mnmajor_desc(do_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
-#pragma unroll
+          umma_bf16_tmem_a(t_dv, t_s + j * 8, mnmajor_desc(do_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
+        if (!mbar_wait(ds_full, it & 1, 0x64u, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
           umma_bf16(t_dk, kmajor_desc(ds_addr, j), mnmajor_desc(q_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16(t_st, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
+          umma_bf16(t_dp, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
         umma_commit(dq_full);
-        umma_commit(qd_empty);
+        umma_commit(&qd_empty[st]);
       }
     }
-  } else {
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ P^T and dS^T (one key row each)
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;   // key row (S^T phase) / query row (dQ phase)
+    const int r = quad * 32 + lane;
     const int kj = k0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* pt = sm + BwdSmem::PT;
-    uint8_t* ds = sm + BwdSmem::DST;
-    const int tid = threadIdx.x - 64;
-    bool ok = true;
+    uint8_t* dsb = sm + BwdSmem::DST;
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * group + it / n_q;
       const int q0 = (i_lo + it % n_q) * TILE;
-      // per-query statistics of this tile into shared memory
-      named_bar_sync(1, 128);
+      // per-query statistics of this pair into shared memory: every row reads all 128 of them.
+      // stat_free (all rows done with the previous pair) and stat_ready are mbarriers, so a row that
+      // leaves the loop after a timed-out wait cannot strand the others.
+      float* s_lse = reinterpret_cast<float*>(sm + BwdSmem::STAT);
+      float* s_del = s_lse + 128;
+      if (it > 0 && !mbar_wait(stat_free, (it - 1) & 1, 0x74u, abort_flag)) break;
       {
-        const int qi = q0 + tid;
-        const int64_t o = (static_cast<int64_t>(b) * p.H + h) * p.T + qi;
-        s_lse[tid] = qi < p.T ? p.lse[o] * LOG2E : INFINITY;
-        s_del[tid] = qi < p.T ? p.delta[o] : 0.f;
+        const int qi = q0 + r;
+        const int64_t o = (static_cast<int64_t>(b) * p.H + h) * p.T + min(qi, p.T - 1);
+        s_lse[r] = p.lse[o] * LOG2E;
+        s_del[r] = p.delta[o];
       }
-      named_bar_sync(1, 128);
-      if (!mbar_wait(st_full, it & 1, 0x70u, abort_flag)) { ok = false; break; }
-      tc_fence_after();
+      mbar_arrive(stat_ready);
+      if (!mbar_wait(stat_ready, it & 1, 0x75u, abort_flag)) break;
       const bool boundary = (k0 + TILE - 1 > q0) || (q0 + TILE > p.T) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
+      if (!mbar_wait(s_full, it & 1, 0x70u, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(t_st + lane_off + c * 32, sv);
-        tmem_ld32(t_dp + lane_off + c * 32, dv);
+        uint32_t sv[32];
+        tmem_ld32(t_s + lane_off + c * 32, sv);
         tmem_wait_ld();
-        float pv[32], dsv[32];
+        uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qi = q0 + c * 32 + i;
-          float pp = fast_exp2(__uint_as_float(sv[i]) * p.scale_log2 - s_lse[c * 32 + i]);
-          if (boundary) {
-            const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
-            if (!valid) pp = 0.f;
+        for (int i = 0; i < 32; i += 2) {
+          const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
+          float pp[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qi = q0 + c * 32 + i + e;
+            float v = fast_exp2(__uint_as_float(sv[i + e]) * p.scale_log2 - (e ? l2.y : l2.x));
+            if (boundary) {
+              const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+              if (!valid) v = 0.f;
+            }
+            pp[e] = v;
           }
-          pv[i] = pp;
-          dsv[i] = pp * (__uint_as_float(dv[i]) - s_del[c * 32 + i]);
+          pk[i / 2] = pack_bf16x2(pp[0], pp[1]);
         }
+        // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier chunk
+        tmem_st16(t_s + lane_off + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      if (!mbar_wait(dp_full, it & 1, 0x71u, abort_flag)) break;
+      // the dS^T buffer served as dQ staging for the previous pair: its second reduction read it last
+      if (it > 0 && !mbar_wait(stg_done, (it - 1) & 1, 0x73u, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dv[32], pk[16];
+        tmem_ld32(t_dp + lane_off + c * 32, dv);
+        tmem_ld16(t_s + lane_off + c * 16, pk);  // P^T back from tensor memory (read-only for the dV MMA)
+        tmem_wait_ld();
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const int chunk = c * 4 + g;
-          uint4 w = make_uint4(pack_bf16x2(pv[8 * g], pv[8 * g + 1]), pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]),
-                               pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]), pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7]));
-          *reinterpret_cast<uint4*>(pt + swz_off(r, chunk)) = w;
-          uint4 z = make_uint4(pack_bf16x2(dsv[8 * g], dsv[8 * g + 1]), pack_bf16x2(dsv[8 * g + 2], dsv[8 * g + 3]),
-                               pack_bf16x2(dsv[8 * g + 4], dsv[8 * g + 5]), pack_bf16x2(dsv[8 * g + 6], dsv[8 * g + 7]));
-          *reinterpret_cast<uint4*>(ds + swz_off(r, chunk)) = z;
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * g + 2 * e;
+            const float2 pp = unpack_bf16x2(pk[i / 2]);
+            const float2 dl = *reinterpret_cast<const float2*>(s_del + c * 32 + i);
+            w[e] = pack_bf16x2(pp.x * (__uint_as_float(dv[i]) - dl.x), pp.y * (__uint_as_float(dv[i + 1]) - dl.y));
+          }
+          *reinterpret_cast<uint4*>(dsb + swz_off(r, c * 4 + g)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ps_full);
-      // dQ tile (row = query q0 + r) -> fp32 atomics
-      if (!mbar_wait(dq_full, it & 1, 0x71u, abort_flag)) { ok = false; break; }
+      mbar_arrive(ds_full);
+      mbar_arrive(stat_free);
+    }
+    // dK of this key tile once every MMA has completed (the last dq_full)
+    if (!*abort_flag && mbar_wait(dq_full, (n_it - 1) & 1, 0x72u, abort_flag)) {
+      __syncwarp();
       tc_fence_after();
-      const int qi = q0 + r;
-      float* dst = p.dq_acc + (static_cast<int64_t>(b) * p.T + qi) * (static_cast<int64_t>(p.H) * HD) + h * HD;
+      // every lane takes part in the aligned TMEM loads; only rows inside the sequence store
+      const bool live = kj < p.T;
+      __nv_bfloat16* dkr = p.dk + (static_cast<int64_t>(b) * p.T + (live ? kj : 0)) * p.lddk + hk * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_st + lane_off + c * 32, v);
+        uint32_t k[32];
+        tmem_ld32(t_dk + lane_off + c * 32, k);
         tmem_wait_ld();
-        if (qi < p.T) {
+        const float sc = p.scale;
+        if (live) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float4 a = make_float4(__uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale,
-                                   __uint_as_float(v[i + 2]) * p.scale, __uint_as_float(v[i + 3]) * p.scale);
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + i), a);
+          for (int i = 0; i < 32; i += 8) {
+            uint4 z = make_uint4(pack_bf16x2(__uint_as_float(k[i]) * sc, __uint_as_float(k[i + 1]) * sc),
+                                 pack_bf16x2(__uint_as_float(k[i + 2]) * sc, __uint_as_float(k[i + 3]) * sc),
+                                 pack_bf16x2(__uint_as_float(k[i + 4]) * sc, __uint_as_float(k[i + 5]) * sc),
+                                 pack_bf16x2(__uint_as_float(k[i + 6]) * sc, __uint_as_float(k[i + 7]) * sc));
+            *reinterpret_cast<uint4*>(dkr + c * 32 + i) = z;
           }
         }
+        __syncwarp();
       }
-      tc_fence_before();
-      mbar_arrive(dq_free);
     }
-    // dV, dK of this key tile: all MMAs done once the last dq_full has fired
-    if (ok) {
+  } else {
+    // ------------------------------------------------------------ dQ drain (one query row each)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * group + it / n_q;
+      const int q0 = (i_lo + it % n_q) * TILE;
+      if (!mbar_wait(dq_full, it & 1, 0x78u, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+      const bool leader = threadIdx.x == 192;  // warp 6, lane 0: issues the bulk reductions
+      uint8_t* stg = sm + BwdSmem::DST;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[64];
+        tmem_ld32(t_dp + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(t_dp + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        if (half == 1) {
+          tc_fence_before();
+          mbar_arrive(dq_free);  // tDP may take the next dP^T
+        }
+        // staging must be free: read by the previous reduction (none before the first half of pair 0)
+        const int k = 2 * it + half - 1;
+        if (k >= 0 && !mbar_wait(stg_free, k & 1, 0x7Au, abort_flag)) { it = n_it; break; }
+        __syncwarp();
+        // two boxes of [128 rows x 32 fp32], 128-byte rows, 128-byte swizzle
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int i = bx * 32 + c * 4;
+            float4 w = make_float4(__uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale,
+                                   __uint_as_float(v[i + 2]) * p.scale, __uint_as_float(v[i + 3]) * p.scale);
+            *reinterpret_cast<float4*>(stg + bx * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) = w;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(stg_full);
+        if (leader) {
+          if (mbar_wait(stg_full, (2 * it + half) & 1, 0x7Bu, abort_flag)) {
+            tma_reduce_add_3d(&tmDQ, stg, h * HD + half * 64, q0, b);
+            tma_reduce_add_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, b);
+            tma_store_commit();
+            tma_store_wait_read0();
+          }
+          mbar_arrive(stg_free);
+          if (half == 1) mbar_arrive(stg_done);
+        }
+        __syncwarp();
+      }
+    }
+    if (threadIdx.x == 192) tma_store_wait0();  // every reduction has landed before the CTA retires
+    // dV of this key tile (every MMA has completed once the last dq_full fired)
+    const int kj = k0 + r;
+    if (!*abort_flag && mbar_wait(dq_full, (n_it - 1) & 1, 0x79u, abort_flag)) {
+      __syncwarp();
       tc_fence_after();
       const bool live = kj < p.T;
-      __nv_bfloat16* dvr = p.dv + (static_cast<int64_t>(b) * p.T + kj) * p.lddv + hk * HD;
-      __nv_bfloat16* dkr = p.dk + (static_cast<int64_t>(b) * p.T + kj) * p.lddk + hk * HD;
+      __nv_bfloat16* dvr = p.dv + (static_cast<int64_t>(b) * p.T + (live ? kj : 0)) * p.lddv + hk * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32], k[32];
-        tmem_ld32(t_dv + lane_off + c * 32, v);
-        tmem_ld32(t_dk + lane_off + c * 32, k);
+        uint32_t w[32];
+        tmem_ld32(t_dv + lane_off + c * 32, w);
         tmem_wait_ld();
         if (live) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
-            uint4 a = make_uint4(pack_bf16x2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
-                                 pack_bf16x2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])),
-                                 pack_bf16x2(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5])),
-                                 pack_bf16x2(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7])));
+            uint4 a = make_uint4(pack_bf16x2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])),
+                                 pack_bf16x2(__uint_as_float(w[i + 2]), __uint_as_float(w[i + 3])),
+                                 pack_bf16x2(__uint_as_float(w[i + 4]), __uint_as_float(w[i + 5])),
+                                 pack_bf16x2(__uint_as_float(w[i + 6]), __uint_as_float(w[i + 7])));
             *reinterpret_cast<uint4*>(dvr + c * 32 + i) = a;
-            const float s = p.scale;
-            uint4 z = make_uint4(pack_bf16x2(__uint_as_float(k[i]) * s, __uint_as_float(k[i + 1]) * s),
-                                 pack_bf16x2(__uint_as_float(k[i + 2]) * s, __uint_as_float(k[i + 3]) * s),
-                                 pack_bf16x2(__uint_as_float(k[i + 4]) * s, __uint_as_float(k[i + 5]) * s),
-                                 pack_bf16x2(__uint_as_float(k[i + 6]) * s, __uint_as_float(k[i + 7]) * s));
-            *reinterpret_cast<uint4*>(dkr + c * 32 + i) = z;
           }
         }
+        __syncwarp();
       }
     }
   }
@@ -613,6 +760,21 @@ static CUtensorMap tile_map(const void* base, int64_t cols, int64_t ld, int T, i
   return m;
 }
 
+// fp32 dQ accumulator [B, T, H*128]: dims {cols, T, B}, box {32, 128, 1} (128-byte rows), 128B swizzle.
+static CUtensorMap dq_map(float* base, int64_t cols, int T, int B) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || cols % 4) throw std::runtime_error("dQ buffer alignment");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 4), static_cast<cuuint64_t>(cols * 4 * T)};
+  cuuint32_t box[3] = {32u, static_cast<cuuint32_t>(TILE), 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (dQ) failed: " + std::to_string(int(r)));
+  return m;
+}
+
 static Params make_params(const AttnArgs& a) {
   Params p{};
   p.B = a.B; p.T = a.T; p.H = a.H; p.Hk = a.Hk;
@@ -662,6 +824,7 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
   CUtensorMap tdo = tile_map(a.dout, static_cast<int64_t>(a.H) * HD, a.lddo, a.T, a.B);
+  CUtensorMap tdq = dq_map(a.dq_acc, static_cast<int64_t>(a.H) * HD, a.T, a.B);
   Params p = make_params(a);
   p.dout = reinterpret_cast<const __nv_bfloat16*>(a.dout);
   p.lddo = a.lddo;
@@ -677,7 +840,7 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
     configured = true;
   }
   dim3 grid((a.T + TILE - 1) / TILE, a.Hk, a.B);
-  attn_bwd_kernel<<<grid, 192, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p);
   const int cols = a.H * HD;
   const int64_t n = rows * cols;
   attn_dq_convert_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, s>>>(

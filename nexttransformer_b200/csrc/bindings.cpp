@@ -292,6 +292,64 @@ void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o
   ok(nt_attention_bwd(a, stream()), "attention_bwd");
 }
 
+// LM head + soft-capped cross-entropy, forward: G = e (1 - t^2) for x = hf W^T (see EPI_CE_FWD),
+// per-row partial sums and target logits, then the row statistics.
+void gemm_ce_fwd(const Tensor& hf, const Tensor& w, const Tensor& G, const Tensor& tgt, const Tensor& part,
+                 const Tensor& ztgt, const Tensor& loss, const Tensor& rscale, const Tensor& rcorr, int64_t vocab,
+                 double cap) {
+  for (auto* t : {&hf, &w, &G}) check_rows(*t, "ce operand");
+  for (auto* t : {&tgt, &part, &ztgt, &loss, &rscale, &rcorr}) check_rows(*t, "ce row vector");
+  TORCH_CHECK(hf.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && G.scalar_type() == at::kBFloat16,
+              "ce operands must be bf16");
+  TORCH_CHECK(tgt.scalar_type() == at::kLong, "targets must be int64");
+  GemmArgs g;
+  g.M = static_cast<int>(hf.size(0));
+  g.N = static_cast<int>(w.size(0));
+  g.K = static_cast<int>(hf.size(1));
+  TORCH_CHECK(w.size(1) == g.K && G.size(0) == g.M && G.size(1) == g.N, "ce shapes");
+  const int nparts = (g.N + 127) / 128;
+  TORCH_CHECK(part.numel() == static_cast<int64_t>(g.M) * nparts, "ce part must be [rows, ceil(N/128)]");
+  g.A = hf.data_ptr(); g.lda = hf.stride(0);
+  g.B = w.data_ptr(); g.ldb = w.stride(0);
+  g.C = G.data_ptr(); g.ldc = G.stride(0);
+  g.epi = EPI_CE_FWD;
+  g.num_sms = num_sms(hf);
+  g.ce.tgt = tgt.data_ptr<int64_t>();
+  g.ce.part = part.data_ptr<float>();
+  g.ce.ztgt = ztgt.data_ptr<float>();
+  g.ce.vocab = static_cast<int>(vocab);
+  g.ce.cap = static_cast<float>(cap);
+  const c10::cuda::CUDAGuard guard(hf.device());
+  nt_gemm_launch(g, stream());
+  ok(nt_ce_finish(g.ce.part, nparts, g.ce.tgt, g.ce.ztgt, loss.data_ptr<float>(), rscale.data_ptr<float>(),
+                  rcorr.data_ptr<float>(), g.M, g.ce.cap, stream()),
+     "ce_finish");
+}
+
+// Input gradient of the head: dh = s (rscale G W - rcorr W[target]) (see EPI_CE_DGRAD).
+void gemm_ce_dgrad(const Tensor& G, const Tensor& w, const Tensor& dh, const Tensor& tgt, const Tensor& rscale,
+                   const Tensor& rcorr, const Tensor& s_dev) {
+  for (auto* t : {&G, &w, &dh}) check_rows(*t, "ce operand");
+  GemmArgs g;
+  g.M = static_cast<int>(G.size(0));
+  g.K = static_cast<int>(G.size(1));
+  g.N = static_cast<int>(w.size(1));
+  TORCH_CHECK(w.size(0) == g.K && dh.size(0) == g.M && dh.size(1) == g.N, "ce dgrad shapes");
+  g.A = G.data_ptr(); g.lda = G.stride(0);
+  g.B = w.data_ptr(); g.ldb = w.stride(0); g.b_mn = 1;
+  g.C = dh.data_ptr(); g.ldc = dh.stride(0);
+  g.epi = EPI_CE_DGRAD;
+  g.s_ptr = s_dev.data_ptr<float>();
+  g.num_sms = num_sms(G);
+  g.ce.tgt = tgt.data_ptr<int64_t>();
+  g.ce.rscale = rscale.data_ptr<float>();
+  g.ce.rcorr = rcorr.data_ptr<float>();
+  g.ce.w = w.data_ptr();
+  g.ce.ldw = w.stride(0);
+  const c10::cuda::CUDAGuard guard(G.device());
+  nt_gemm_launch(g, stream());
+}
+
 std::vector<int64_t> read_errors() {
   unsigned w = 0;
   const int g = nt_gemm_read_error(&w);
@@ -322,6 +380,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("read_errors", &read_errors);
+  m.def("gemm_ce_fwd", &gemm_ce_fwd);
+  m.def("gemm_ce_dgrad", &gemm_ce_dgrad);
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
   m.attr("EPI_F32") = static_cast<int>(EPI_F32);
   m.attr("EPI_F32_ACC") = static_cast<int>(EPI_F32_ACC);

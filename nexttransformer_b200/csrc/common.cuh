@@ -154,6 +154,25 @@ NT_DEVICE void tma_store_2d(const void* desc, const void* smem_src, int x, int y
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
                : "memory");
 }
+// Element-wise fp32 add of a shared-memory tile into global memory (reduction performed in L2).
+// Starting coordinates must be non-negative; the parts of the box outside the tensor are skipped.
+NT_DEVICE void tma_reduce_add_3d(const void* desc, const void* smem_src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+NT_DEVICE void tma_store_3d(const void* desc, const void* smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+// Wait until at most one committed bulk group still reads shared memory.
+NT_DEVICE void tma_store_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 NT_DEVICE void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 NT_DEVICE void tma_store_wait_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -194,6 +213,18 @@ NT_DEVICE void umma_bf16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Same MMA with the A operand (M x K, K-major) read from tensor memory: lane m holds row m,
+// column c holds elements 2c (low half) and 2c+1 (high half).
+NT_DEVICE void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t b_desc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

@@ -34,15 +34,23 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192;
 
+// Bulk-store epilogue: each epilogue warp stages [32 rows x 32 columns] bf16 boxes (2 KB, 64-byte
+// swizzle) in two alternating buffers; a second output (the ReLU^2 pre-activation) doubles them.
+constexpr int STG_BOX = 2048;
+constexpr int STG_WARP = 2 * 2 * STG_BOX;      // 2 buffers x (C box + P box)
+constexpr int STG_BYTES = 4 * STG_WARP;        // 4 epilogue warps = 32 KB
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = STG_OFFSET + STG_BYTES;
   // full[S], empty[S], tmem_full[2], tmem_empty[2], tmem holder, abort flag
   static constexpr int BAR_BYTES = (2 * STAGES + 4) * 8 + 16;
   static constexpr int TOTAL = BAR_OFFSET + BAR_BYTES + 1024;  // + alignment slack
+  static_assert(TOTAL <= 232448, "GEMM shared memory exceeds the sm_100 limit");
 };
 
 struct Params {
@@ -60,6 +68,8 @@ struct Params {
   int split;           // K slices (1 = no split-K)
   int kb_per_split;    // k-blocks per slice
   int64_t strideSplit; // elements between the partial-output slices of the workspace
+  CeArgs ce;           // cross-entropy epilogues only
+  int tma_out;         // 1: bf16 outputs leave through shared memory and bulk tensor stores
 };
 
 NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb, int& ks) {
@@ -78,12 +88,199 @@ NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb, int
   nb = in_g / rows_in_group;
 }
 
+// Soft-capped cross-entropy, forward: G = e (1 - t^2) over 32 columns of one row; returns the
+// sum of e over those columns and records z at the target column.
+NT_DEVICE float ce_fwd32(const Params& p, int row, int col0, const uint32_t (&acc)[32]) {
+  const CeArgs& ce = p.ce;
+  const float inv_cap = 1.f / ce.cap;
+  const int64_t tgt = ce.tgt[row];
+  const int ncols = min(32, p.N - col0);
+  float se = 0.f;
+  uint32_t out[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float g[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int col = col0 + i + e;
+      g[e] = 0.f;
+      if (col < ce.vocab) {
+        const float t = tanhf(__uint_as_float(acc[i + e]) * inv_cap);
+        const float z = ce.cap * t;
+        const float ex = __expf(z - ce.cap);
+        se += ex;
+        g[e] = ex * (1.f - t * t);
+        if (col == tgt) ce.ztgt[row] = z;
+      }
+    }
+    out[i / 2] = pack_bf16x2(g[0], g[1]);
+  }
+  __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(c) & 15) == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(c + 8 * i) = make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+  } else {
+    for (int i = 0; i < ncols; ++i) {
+      const uint32_t w = out[i / 2];
+      c[i] = __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xFFFFu)));
+    }
+  }
+  return se;
+}
+
+// Soft-capped cross-entropy, input gradient: s (rscale acc - rcorr W[target, col]) over 32 columns.
+NT_DEVICE void ce_dgrad32(const Params& p, float sacc, int row, int col0, const uint32_t (&acc)[32]) {
+  const CeArgs& ce = p.ce;
+  const int ncols = min(32, p.N - col0);
+  const int64_t tgt = ce.tgt[row];
+  const float rs = ce.rscale[row] * sacc;
+  const float rc = tgt >= 0 ? ce.rcorr[row] * sacc : 0.f;
+  const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(ce.w) + (tgt >= 0 ? tgt : 0) * ce.ldw + col0;
+  float wv[32];
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 q = *reinterpret_cast<const uint4*>(w + 8 * i);
+      float2 f0 = unpack_bf16x2(q.x), f1 = unpack_bf16x2(q.y), f2 = unpack_bf16x2(q.z), f3 = unpack_bf16x2(q.w);
+      wv[8 * i + 0] = f0.x; wv[8 * i + 1] = f0.y; wv[8 * i + 2] = f1.x; wv[8 * i + 3] = f1.y;
+      wv[8 * i + 4] = f2.x; wv[8 * i + 5] = f2.y; wv[8 * i + 6] = f3.x; wv[8 * i + 7] = f3.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) wv[i] = (i < ncols) ? bf2f(w[i]) : 0.f;
+  }
+  uint32_t out[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2)
+    out[i / 2] = pack_bf16x2(rs * __uint_as_float(acc[i]) - rc * wv[i], rs * __uint_as_float(acc[i + 1]) - rc * wv[i + 1]);
+  __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(c) & 15) == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(c + 8 * i) = make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+  } else {
+    for (int i = 0; i < ncols; ++i) {
+      const uint32_t v = out[i / 2];
+      c[i] = __ushort_as_bfloat16(static_cast<unsigned short>((i & 1) ? (v >> 16) : (v & 0xFFFFu)));
+    }
+  }
+}
+
+// bf16 epilogues: the 32 packed output values (and the ReLU^2 pre-activation) of one row chunk.
+// Rows past M and columns past N read no operand; the bulk store clips them.
+template <int EPI>
+NT_DEVICE void epi_pack(const Params& p, float sacc, int b, int row, int col0, const uint32_t (&acc)[32],
+                        uint32_t (&out)[16], uint32_t (&pre)[16], float& se) {
+  const bool live = row < p.M;
+  const int ncols = live ? max(0, min(32, p.N - col0)) : 0;
+  if constexpr (EPI == EPI_CE_FWD) {
+    const CeArgs& ce = p.ce;
+    const float inv_cap = 1.f / ce.cap;
+    const int64_t tgt = live ? ce.tgt[row] : -1;
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float g[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = col0 + i + e;
+        g[e] = 0.f;
+        if (i + e < ncols && col < ce.vocab) {
+          const float t = tanhf(__uint_as_float(acc[i + e]) * inv_cap);
+          const float z = ce.cap * t;
+          const float ex = __expf(z - ce.cap);
+          se += ex;
+          g[e] = ex * (1.f - t * t);
+          if (col == tgt) ce.ztgt[row] = z;
+        }
+      }
+      out[i / 2] = pack_bf16x2(g[0], g[1]);
+    }
+    return;
+  } else if constexpr (EPI == EPI_CE_DGRAD) {
+    const CeArgs& ce = p.ce;
+    const int64_t tgt = live ? ce.tgt[row] : -1;
+    const float rs = live ? ce.rscale[row] * sacc : 0.f;
+    const float rc = tgt >= 0 ? ce.rcorr[row] * sacc : 0.f;
+    const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(ce.w) + (tgt >= 0 ? tgt : 0) * ce.ldw + col0;
+    const bool vec = ncols == 32 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float wv[8];
+      if (vec) {
+        const uint4 u = *reinterpret_cast<const uint4*>(w + 8 * q);
+        const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y), f2 = unpack_bf16x2(u.z), f3 = unpack_bf16x2(u.w);
+        wv[0] = f0.x; wv[1] = f0.y; wv[2] = f1.x; wv[3] = f1.y; wv[4] = f2.x; wv[5] = f2.y; wv[6] = f3.x; wv[7] = f3.y;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = (8 * q + e < ncols) ? bf2f(w[8 * q + e]) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e += 2)
+        out[4 * q + e / 2] = pack_bf16x2(rs * __uint_as_float(acc[8 * q + e]) - rc * wv[e],
+                                         rs * __uint_as_float(acc[8 * q + e + 1]) - rc * wv[e + 1]);
+    }
+    return;
+  } else {
+    float rv[32];
+    if constexpr (EPI == EPI_BF16_AXPBY || EPI == EPI_RELU2_BWD) {
+      const __nv_bfloat16* r =
+          reinterpret_cast<const __nv_bfloat16*>(p.R) + b * p.strideR + static_cast<int64_t>(live ? row : 0) * p.ldr + col0;
+      if (ncols == 32 && ((reinterpret_cast<uintptr_t>(r) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 q = *reinterpret_cast<const uint4*>(r + 8 * i);
+          float2 f0 = unpack_bf16x2(q.x), f1 = unpack_bf16x2(q.y), f2 = unpack_bf16x2(q.z), f3 = unpack_bf16x2(q.w);
+          rv[8 * i + 0] = f0.x; rv[8 * i + 1] = f0.y; rv[8 * i + 2] = f1.x; rv[8 * i + 3] = f1.y;
+          rv[8 * i + 4] = f2.x; rv[8 * i + 5] = f2.y; rv[8 * i + 6] = f3.x; rv[8 * i + 7] = f3.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rv[i] = (i < ncols) ? bf2f(r[i]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const float v0 = __uint_as_float(acc[i]), v1 = __uint_as_float(acc[i + 1]);
+      float o0, o1;
+      if constexpr (EPI == EPI_BF16) {
+        o0 = v0 * sacc;
+        o1 = v1 * sacc;
+      } else if constexpr (EPI == EPI_BF16_AXPBY) {
+        o0 = bf2f(f2bf(v0 * sacc)) + p.s_res * rv[i];
+        o1 = bf2f(f2bf(v1 * sacc)) + p.s_res * rv[i + 1];
+      } else if constexpr (EPI == EPI_RELU2) {
+        const float h0 = bf2f(f2bf(v0)), h1 = bf2f(f2bf(v1));
+        pre[i / 2] = pack_bf16x2(h0, h1);
+        const float r0 = fmaxf(h0, 0.f), r1 = fmaxf(h1, 0.f);
+        o0 = r0 * r0;
+        o1 = r1 * r1;
+      } else {  // EPI_RELU2_BWD
+        const float g0 = bf2f(f2bf(v0)), g1 = bf2f(f2bf(v1));
+        o0 = g0 * 2.f * fmaxf(rv[i], 0.f);
+        o1 = g1 * 2.f * fmaxf(rv[i + 1], 0.f);
+      }
+      out[i / 2] = pack_bf16x2(o0, o1);
+    }
+  }
+}
+
+template <int EPI>
+__host__ __device__ constexpr bool bf16_out() {
+  return EPI == EPI_BF16 || EPI == EPI_BF16_AXPBY || EPI == EPI_RELU2 || EPI == EPI_RELU2_BWD || EPI == EPI_CE_FWD ||
+         EPI == EPI_CE_DGRAD;
+}
+
 // Epilogue for 32 consecutive columns of one row.
 template <int EPI>
 NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int ks, int row, int col0, const uint32_t (&acc)[32]) {
   if (row >= p.M) return;
   const int ncols = min(32, p.N - col0);
   if (ncols <= 0) return;
+  if constexpr (EPI == EPI_CE_DGRAD) {
+    ce_dgrad32(p, sacc, row, col0, acc);
+    return;
+  }
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(acc[i]);
@@ -186,7 +383,8 @@ NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int ks, int row, i
 
 template <int BN, int A_MN, int B_MN, int EPI, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmP, Params p) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -311,25 +509,115 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
     const float sacc = p.s_ptr ? p.s_acc * *p.s_ptr : p.s_acc;
-    int local = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
-      tc_fence_after();
-      int b, mb, nb, ks;
-      tile_coords(t, p, b, mb, nb, ks);
-      const int row = mb * BM + row_in_tile;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+    if constexpr (bf16_out<EPI>()) {
+      if (p.tma_out) {
+        // staged path: values -> swizzled shared-memory box -> bulk tensor store (no per-thread
+        // global stores, so the L1/LSU path stays free for the operand loads)
+        uint8_t* stg = smem + S::STG_OFFSET + (warp - 2) * STG_WARP;
+        const int nparts = (p.N + 127) / 128;
+        int g = 0;
+        int local = 0;
+        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+          const int acc = local & 1;
+          const uint32_t acc_phase = (local >> 1) & 1;
+          if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
+          __syncwarp();
+          tc_fence_after();
+          int b, mb, nb, ks;
+          tile_coords(t, p, b, mb, nb, ks);
+          const int row = mb * BM + row_in_tile;
+          const int row0 = mb * BM + quad * 32;
+          const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+          float se = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tmem_wait_ld();
-        epilogue32<EPI>(p, sacc, b, ks, row, nb * BN + c * 32, r);
+          for (int c = 0; c < BN / 32; ++c, ++g) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(t_row + c * 32, r);
+            tmem_wait_ld();
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&tempty[acc]);  // the accumulator is in registers: MMA may reuse it
+            }
+            const int col0 = nb * BN + c * 32;
+            uint32_t out[16], pre[16];
+            epi_pack<EPI>(p, sacc, b, row, col0, r, out, pre, se);
+            if constexpr (EPI == EPI_CE_FWD) {
+              const int group0 = nb * BN + (c & ~3) * 32;
+              if ((c & 3) == 3 && row < p.M && group0 < p.N) {
+                p.ce.part[static_cast<int64_t>(row) * nparts + group0 / 128] = se;
+                se = 0.f;
+              }
+            }
+            uint8_t* sc = stg + (g & 1) * (2 * STG_BOX);
+            if (lane == 0) tma_store_wait_read1();  // the store that used this buffer two chunks ago has read it
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int pos = lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4);
+              *reinterpret_cast<uint4*>(sc + pos) = make_uint4(out[4 * k], out[4 * k + 1], out[4 * k + 2], out[4 * k + 3]);
+              if constexpr (EPI == EPI_RELU2)
+                *reinterpret_cast<uint4*>(sc + STG_BOX + pos) =
+                    make_uint4(pre[4 * k], pre[4 * k + 1], pre[4 * k + 2], pre[4 * k + 3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row0 < p.M && col0 < p.N) {
+              tma_store_3d(&tmC, sc, col0, row0, b);
+              if constexpr (EPI == EPI_RELU2) tma_store_3d(&tmP, sc + STG_BOX, col0, row0, b);
+            }
+            if (lane == 0) tma_store_commit();
+          }
+          if constexpr (EPI == EPI_CE_FWD) {
+            if ((BN / 32) % 4 != 0 && row < p.M) p.ce.part[static_cast<int64_t>(row) * nparts + (nb * BN) / 128] = se;
+          }
+        }
+        if (lane == 0) tma_store_wait0();
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+    }
+    if (!bf16_out<EPI>() || !p.tma_out) {
+      int local = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
+        __syncwarp();
+        tc_fence_after();
+        int b, mb, nb, ks;
+        tile_coords(t, p, b, mb, nb, ks);
+        const int row = mb * BM + row_in_tile;
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+        if constexpr (EPI == EPI_CE_FWD) {
+          const int nparts = (p.N + 127) / 128;
+          float se = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            __syncwarp();  // the previous chunk's epilogue may have diverged (partial tiles)
+            tmem_ld32(t_row + c * 32, r);
+            tmem_wait_ld();
+            const int col0 = nb * BN + c * 32;
+            if (row < p.M && col0 < p.N) se += ce_fwd32(p, row, col0, r);
+            const int group0 = nb * BN + (c & ~3) * 32;  // first column of this 128-column part
+            if ((c & 3) == 3 && row < p.M && group0 < p.N) {
+              p.ce.part[static_cast<int64_t>(row) * nparts + group0 / 128] = se;
+              se = 0.f;
+            }
+          }
+          if ((BN / 32) % 4 != 0 && row < p.M) p.ce.part[static_cast<int64_t>(row) * nparts + (nb * BN) / 128] = se;
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            __syncwarp();  // the previous chunk's epilogue may have diverged (partial tiles)
+            tmem_ld32(t_row + c * 32, r);
+            tmem_wait_ld();
+            epilogue32<EPI>(p, sacc, b, ks, row, nb * BN + c * 32, r);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
     }
   }
 
@@ -359,6 +647,26 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ w, int split, int
     a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
   }
   *dst = a;
+}
+
+// Cross-entropy row statistics (one warp per row, fixed summation order).
+__global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, const int64_t* __restrict__ tgt,
+                                 const float* __restrict__ ztgt, float* __restrict__ loss, float* __restrict__ rscale,
+                                 float* __restrict__ rcorr, int rows, float cap) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float s = 0.f;
+  for (int i = lane; i < nparts; i += 32) s += part[static_cast<int64_t>(row) * nparts + i];
+  s = warp_sum(s);
+  if (lane == 0) {
+    const bool live = tgt[row] >= 0;
+    const float z = live ? ztgt[row] : 0.f;
+    loss[row] = live ? cap + logf(s) - z : 0.f;
+    rscale[row] = live ? 1.f / s : 0.f;
+    const float t = z / cap;
+    rcorr[row] = live ? 1.f - t * t : 0.f;
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -396,6 +704,22 @@ static CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int6
   return map;
 }
 
+// bf16 output map for the bulk-store epilogue: dims {N, M, batch}, box {32, 32, 1}, 64-byte swizzle.
+// Returns false (direct stores are used) when the layout does not allow bulk tensor stores.
+static bool out_map(CUtensorMap& map, const void* base, int64_t N, int64_t M, int64_t ld, int64_t batch,
+                    int64_t batch_stride) {
+  if (!base || reinterpret_cast<uintptr_t>(base) % 16 || (ld * 2) % 16 || (batch > 1 && (batch_stride * 2) % 16))
+    return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2),
+                           static_cast<cuuint64_t>((batch > 1 ? batch_stride : ld * M) * 2)};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int A_MN, int B_MN, int EPI>
 static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
@@ -414,6 +738,7 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   p.R = g.R; p.ldr = g.ldr; p.strideR = g.strideR;
   p.P = g.P; p.ldp = g.ldp; p.strideP = g.strideP;
   p.s_acc = g.s_acc; p.s_res = g.s_res; p.s_ptr = g.s_ptr;
+  p.ce = g.ce;
   p.split = g.split_k > 1 ? g.split_k : 1;
   const int num_kb = (g.K + BK - 1) / BK;
   p.kb_per_split = (num_kb + p.split - 1) / p.split;
@@ -423,6 +748,13 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
     p.ldc = g.N;
     p.strideC = 0;
   }
+  CUtensorMap tc = ta, tp = ta;  // placeholders when the direct epilogue runs
+  p.tma_out = 0;
+  if (bf16_out<EPI>() && p.split == 1 && g.tma_out_ok) {
+    bool ok = out_map(tc, g.C, g.N, g.M, g.ldc, g.batch, g.strideC);
+    if (EPI == EPI_RELU2) ok = ok && out_map(tp, g.P, g.N, g.M, g.ldp, g.batch, g.strideP);
+    p.tma_out = ok ? 1 : 0;
+  }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
   static bool configured = false;
   if (!configured) {
@@ -431,7 +763,7 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   }
   const int tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, p);
+  kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, tc, tp, p);
   if (p.split > 1) {
     const int64_t n = static_cast<int64_t>(g.M) * g.N;
     splitk_reduce_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, stream>>>(
@@ -449,6 +781,12 @@ static void dispatch_epi(const GemmArgs& g, cudaStream_t s) {
     case EPI_BF16_AXPBY: return launch_t<BN, A_MN, B_MN, EPI_BF16_AXPBY>(g, s);
     case EPI_RELU2: return launch_t<BN, A_MN, B_MN, EPI_RELU2>(g, s);
     case EPI_RELU2_BWD: return launch_t<BN, A_MN, B_MN, EPI_RELU2_BWD>(g, s);
+    case EPI_CE_FWD:
+      if constexpr (A_MN == 0 && B_MN == 0) return launch_t<BN, 0, 0, EPI_CE_FWD>(g, s);
+      throw std::runtime_error("cross-entropy forward epilogue needs K-major operands");
+    case EPI_CE_DGRAD:
+      if constexpr (A_MN == 0 && B_MN == 1) return launch_t<BN, 0, 1, EPI_CE_DGRAD>(g, s);
+      throw std::runtime_error("cross-entropy input-gradient epilogue needs A K-major, B N-major");
     default: throw std::runtime_error("unknown gemm epilogue");
   }
 }
@@ -507,4 +845,12 @@ int nt_gemm_read_error(unsigned* where) {
   cudaMemcpyFromSymbol(&w, nt::g_nt_error, sizeof(w));
   if (where) *where = w.where;
   return static_cast<int>(w.code);
+}
+
+int nt_ce_finish(const float* part, int nparts, const int64_t* tgt, const float* ztgt, float* loss, float* rscale,
+                 float* rcorr, int rows, float cap, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  nt::gemm::ce_finish_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(part, nparts, tgt, ztgt, loss, rscale, rcorr, rows,
+                                                                  cap);
+  return 0;
 }

@@ -11,6 +11,24 @@ enum NtGemmEpilogue : int {
   EPI_BF16_AXPBY = 3,  // C(bf16) = bf16(s_acc * acc) + s_res * R   (residual add, Newton-Schulz)
   EPI_RELU2 = 4,       // P(bf16) = acc ; C(bf16) = relu(P)^2        (MLP up-projection)
   EPI_RELU2_BWD = 5,   // C(bf16) = bf16(acc) * 2 relu(R)            (R = saved pre-activation)
+  // Soft-capped cross-entropy fused into the LM head (acc = logit x, t = tanh(x / cap),
+  // z = cap t, e = exp(z - cap); columns >= vocab are padding):
+  EPI_CE_FWD = 6,      // C(bf16) = e (1 - t^2); ce.part[row, col / 128] = sum of e over the 128
+                       // columns; ce.ztgt[row] = z at column ce.tgt[row]
+  EPI_CE_DGRAD = 7,    // C(bf16) = s_acc (ce.rscale[row] acc - ce.rcorr[row] ce.w[ce.tgt[row], col])
+};
+
+// Extra operands of the cross-entropy epilogues.
+struct CeArgs {
+  const int64_t* tgt = nullptr;   // [M] target ids (-1: ignored row)
+  float* part = nullptr;          // EPI_CE_FWD: [M, ceil(N / 128)] partial sums of e
+  float* ztgt = nullptr;          // EPI_CE_FWD: [M] soft-capped target logit (left as is for ignored rows)
+  int vocab = 0;
+  float cap = 15.f;
+  const float* rscale = nullptr;  // EPI_CE_DGRAD: [M] 1 / sum_e (0 for ignored rows)
+  const float* rcorr = nullptr;   // EPI_CE_DGRAD: [M] 1 - (z_target / cap)^2 (0 for ignored rows)
+  const void* w = nullptr;        // EPI_CE_DGRAD: head weight [vocab rows, N] (bf16)
+  int64_t ldw = 0;
 };
 
 struct GemmArgs {
@@ -40,11 +58,19 @@ struct GemmArgs {
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   int split_k = 1;  // set by the launcher
+  CeArgs ce;
+  // bf16 outputs leave through shared memory and bulk tensor stores when the layout allows it
+  // (16-byte aligned base and row stride); 0 forces per-thread global stores.
+  int tma_out_ok = 1;
 };
 
 // Bytes of workspace nt_gemm_launch would use for split-K on this problem (0 = no split).
 size_t nt_gemm_splitk_bytes(const GemmArgs& args);
 
 void nt_gemm_launch(const GemmArgs& args, cudaStream_t stream);
+// Cross-entropy row statistics from the EPI_CE_FWD partial sums: per row S = sum(part),
+// loss = cap + log S - ztgt, rscale = 1 / S, rcorr = 1 - (ztgt / cap)^2 (all 0 for ignored rows).
+int nt_ce_finish(const float* part, int nparts, const int64_t* tgt, const float* ztgt, float* loss, float* rscale,
+                 float* rcorr, int rows, float cap, cudaStream_t stream);
 // Returns the first error code recorded by a bounded wait in a GEMM kernel (0 = none).
 int nt_gemm_read_error(unsigned* where);

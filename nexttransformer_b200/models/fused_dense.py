@@ -4,8 +4,11 @@ Per layer the forward is five launches of our own kernels plus attention:
   mix+RMSNorm -> packed QKV GEMM -> RoPE+QK-norm+VE gate (in place) -> attention
   -> O-projection GEMM with residual-add epilogue -> RMSNorm -> c_fc GEMM with ReLU^2 epilogue
   -> c_proj GEMM with residual-add epilogue.
-The head is one GEMM into bf16 logits followed by a soft-capped cross-entropy kernel that
-replaces the logits by their gradient in place, so the backward needs no logits recompute.
+The head is one GEMM whose epilogue evaluates the soft-capped cross-entropy: it stores the
+unnormalised logit gradient G = exp(z - cap) (1 - tanh^2) instead of the logits, plus per-row partial
+sums of exp(z - cap) and the target's z; a row kernel turns those into loss, 1 / sum and the target
+correction.  The backward folds the row normalisation and the one-hot term into the input-gradient
+GEMM's epilogue and into a row-scaled weight-gradient operand, so no logits pass exists.
 
 Gradients of parameters never go through autograd: each Function writes (first micro-batch)
 or accumulates (later micro-batches) fp32 gradients straight into ``param.main_grad`` with
@@ -20,6 +23,8 @@ from nexttransformer_b200.ops.attention import attention_fn
 
 # Cross-entropy kernel variant (0: automatic, 1: two-pass); kept selectable for numerics checks.
 CE_VARIANT = 0
+# True: the cross-entropy runs in the head GEMM's epilogue; False: GEMM + separate CE kernel.
+FUSED_HEAD_CE = True
 
 
 class GradSlot:
@@ -283,9 +288,24 @@ class HeadLossFn(Function):
         xo = xo.contiguous()
         hf = torch.empty_like(xo)
         lib.mix_norm_fwd(xo, None, None, None, hf, None, 1.0)
-        logits = G.linear(hf, model.lm_head._w)
-        rows = torch.empty(logits.shape[0], device=x.device, dtype=torch.float32)
-        lib.softcap_ce(logits, tgt, rows, None, cfg.vocab_size, cfg.softcap, CE_VARIANT)
+        M = hf.shape[0]
+        if FUSED_HEAD_CE:
+            W = model.lm_head._w
+            Vp = W.shape[0]
+            Gm = torch.empty(M, Vp, device=x.device, dtype=torch.bfloat16)
+            part = torch.empty(M, (Vp + 127) // 128, device=x.device, dtype=torch.float32)
+            ztgt = torch.zeros(M, device=x.device, dtype=torch.float32)
+            rows = torch.empty(M, device=x.device, dtype=torch.float32)
+            rscale = torch.empty_like(rows)
+            rcorr = torch.empty_like(rows)
+            lib.gemm_ce_fwd(hf, W, Gm, tgt, part, ztgt, rows, rscale, rcorr, cfg.vocab_size, cfg.softcap)
+            del part
+            saved = (Gm, rscale, rcorr)
+        else:
+            logits = G.linear(hf, model.lm_head._w)
+            rows = torch.empty(M, device=x.device, dtype=torch.float32)
+            lib.softcap_ce(logits, tgt, rows, None, cfg.vocab_size, cfg.softcap, CE_VARIANT)
+            saved = (logits,)
         total = rows.sum()
         if reduction == "mean":
             count = (tgt != -1).sum().clamp_min(1).float()
@@ -294,19 +314,31 @@ class HeadLossFn(Function):
         else:
             loss = total
             inv = torch.ones(1, device=x.device, dtype=torch.float32)
-        ctx.save_for_backward(logits, hf, xo, xb if xb is not None else xo, inv)
-        ctx.model, ctx.has_xb = model, xb is not None
+        ctx.save_for_backward(hf, xo, xb if xb is not None else xo, inv, tgt, *saved)
+        ctx.model, ctx.has_xb, ctx.fused = model, xb is not None, FUSED_HEAD_CE
         return loss
 
     @staticmethod
     def backward(ctx, g):
-        dlogits, hf, xo, xb, inv = ctx.saved_tensors
+        hf, xo, xb, inv, tgt, *saved = ctx.saved_tensors
         model = ctx.model
         lib = ext()
         scale = (g.float().reshape(1) * inv).contiguous()
-        dh = G.dgrad(dlogits, model.lm_head._w, s_dev=scale)
+        W = model.lm_head._w
         buf, acc = model.lm_head._g.take()
-        G.wgrad(dlogits, hf, buf, accumulate=acc, s_dev=scale)
+        if ctx.fused:
+            Gm, rscale, rcorr = saved
+            # dlogits = scale (rscale G - rcorr onehot(target)); both terms go into the GEMMs
+            dh = torch.empty_like(hf)
+            lib.gemm_ce_dgrad(Gm, W, dh, tgt, rscale, rcorr, scale)
+            hf_s = (hf.float() * rscale[:, None]).to(torch.bfloat16)
+            G.wgrad(Gm, hf_s, buf, accumulate=acc, s_dev=scale)
+            corr = hf.float() * (-(scale * rcorr))[:, None]
+            lib.embed_scatter(corr, tgt.clamp_min(0), buf)
+        else:
+            (dlogits,) = saved
+            dh = G.dgrad(dlogits, W, s_dev=scale)
+            G.wgrad(dlogits, hf, buf, accumulate=acc, s_dev=scale)
         dxo = torch.empty_like(xo)
         lib.norm_bwd(xo, dh, None, dxo)
         dxb = None

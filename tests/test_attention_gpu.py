@@ -20,7 +20,8 @@ def _ref(qkv, B, T, H, Hk, D, window):
 
 
 @pytest.mark.parametrize("B,T,H,Hk,window", [(1, 128, 1, 1, -1), (2, 256, 2, 1, -1), (1, 384, 4, 2, -1),
-                                             (1, 512, 2, 2, 200), (1, 200, 2, 1, -1), (2, 1024, 4, 1, 300)])
+                                             (1, 512, 2, 2, 200), (1, 200, 2, 1, -1), (2, 1024, 4, 1, 300),
+                                             (1, 2048, 10, 5, -1)])
 def test_attention_forward_backward(B, T, H, Hk, window):
     from nexttransformer_b200.ops import attention as A
     from nexttransformer_b200.ops._ext import check_errors

@@ -256,3 +256,49 @@ def test_fused_model_matches_eager():
             continue
         cos = F.cosine_similarity(g.flatten().float(), e.flatten(), dim=0).item()
         assert cos > 0.97, (n, cos)
+
+
+@pytest.mark.parametrize("M,V,d", [(512, 4096, 256), (1000, 8192 + 64, 128), (256, 65536, 1280)])
+def test_fused_head_cross_entropy(M, V, d):
+    """LM head GEMM with the soft-capped cross-entropy in its epilogue, against fp32 PyTorch."""
+    import torch.nn.functional as F
+    from nexttransformer_b200.ops import gemm as G
+    from nexttransformer_b200.ops._ext import check_errors, ext
+    lib = ext()
+    torch.manual_seed(0)
+    cap = 15.0
+    vocab = V - 64 if V % 128 else V          # exercise padding columns
+    hf = torch.randn(M, d, device="cuda").bfloat16()
+    W = (torch.randn(V, d, device="cuda") * 0.2).bfloat16()
+    tgt = torch.randint(0, vocab, (M,), device="cuda")
+    tgt[::7] = -1
+    Gm = torch.empty(M, V, device="cuda", dtype=torch.bfloat16)
+    part = torch.empty(M, (V + 127) // 128, device="cuda")
+    ztgt = torch.zeros(M, device="cuda")
+    rows, rscale, rcorr = (torch.empty(M, device="cuda") for _ in range(3))
+    lib.gemm_ce_fwd(hf, W, Gm, tgt, part, ztgt, rows, rscale, rcorr, vocab, cap)
+    s = torch.tensor([0.37], device="cuda")
+    dh = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+    lib.gemm_ce_dgrad(Gm, W, dh, tgt, rscale, rcorr, s)
+    hf_s = (hf.float() * rscale[:, None]).bfloat16()
+    dW = torch.zeros(V, d, device="cuda")
+    G.wgrad(Gm, hf_s, dW, accumulate=False, s_dev=s)
+    lib.embed_scatter(hf.float() * (-(s * rcorr))[:, None], tgt.clamp_min(0), dW)
+    torch.cuda.synchronize()
+    check_errors()
+    # reference
+    x = hf.float() @ W.float().t()
+    z = cap * torch.tanh(x[:, :vocab] / cap)
+    valid = tgt >= 0
+    ref_rows = torch.where(valid, torch.logsumexp(z, -1) - z.gather(1, tgt.clamp_min(0)[:, None])[:, 0],
+                           torch.zeros_like(z[:, 0]))
+    assert torch.allclose(rows, ref_rows, rtol=1e-4, atol=2e-3), (rows - ref_rows).abs().max()
+    p = torch.softmax(z, -1)
+    p[valid, tgt[valid]] -= 1
+    dlog = torch.zeros(M, V, device="cuda")
+    dlog[:, :vocab] = p * (1 - (z / cap) ** 2) * valid[:, None] * 0.37
+    ref_dh = dlog @ W.float()
+    ref_dw = dlog.t() @ hf.float()
+    e1 = (dh.float() - ref_dh).abs().max().item() / ref_dh.abs().max().item()
+    e2 = (dW - ref_dw).abs().max().item() / ref_dw.abs().max().item()
+    assert e1 < 2e-2 and e2 < 2e-2, (e1, e2)
