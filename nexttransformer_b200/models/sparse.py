@@ -207,11 +207,17 @@ class SparseMixer(nn.Module):
         size = c.compression_size
         stride = c.compression_stride or size
         B, H, T, D = k.shape
-        n = max(1, (T - size) // stride + 1) if T >= size else 1
-        need = (n - 1) * stride + size
-        kp, vp = F.pad(k, (0, 0, 0, max(0, need - T))), F.pad(v, (0, 0, 0, max(0, need - T)))
-        kb = kp.unfold(2, size, stride).transpose(-1, -2)   # B,H,n,size,D
-        vb = vp.unfold(2, size, stride).transpose(-1, -2)
+        if stride == size:
+            # non-overlapping blocks: a padded reshape (the audited graph of the reference)
+            n = (T + size - 1) // size
+            kb = F.pad(k, (0, 0, 0, n * size - T)).reshape(B, H, n, size, D)
+            vb = F.pad(v, (0, 0, 0, n * size - T)).reshape_as(kb)
+        else:
+            n = max(1, (T - size) // stride + 1) if T >= size else 1
+            need = (n - 1) * stride + size
+            kp, vp = F.pad(k, (0, 0, 0, max(0, need - T))), F.pad(v, (0, 0, 0, max(0, need - T)))
+            kb = kp.unfold(2, size, stride).transpose(-1, -2)   # B,H,n,size,D
+            vb = vp.unfold(2, size, stride).transpose(-1, -2)
         ck = self.compress_k((kb + self.compress_position.to(kb)).flatten(-2))
         cv = self.compress_v(vb.flatten(-2))
         ends = torch.arange(kb.shape[2], device=k.device) * stride + size - 1   # last token of each block

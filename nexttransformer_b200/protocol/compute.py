@@ -135,6 +135,9 @@ class Ledger(TorchDispatchMode):
             return args[3].numel(), 0
         if name == "index_add":
             return args[3].numel(), 0
+        if name == "unfold_backward":
+            # overlapping windows (strided compression): one addition per gradient element
+            return args[0].numel(), 0
         if name == "native_layer_norm":
             return 7 * args[0].numel() + 5 * outs[1].numel(), 0
         if name == "native_layer_norm_backward":
