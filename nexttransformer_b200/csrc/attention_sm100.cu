@@ -49,7 +49,14 @@ struct Params {
   int64_t lddk, lddv;
   float* dq_acc;
   const float* delta;
+  long long* trace;
 };
+
+// Clock stamp of (role, pair, event) for the first CTA when a trace buffer is given.
+NT_DEVICE void stamp(const Params& p, int role, int it, int ev) {
+  if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && it < 64)
+    p.trace[(role * 64 + it) * 8 + ev] = clock64();
+}
 
 // K-major operand made of two [128 rows x 64] swizzled boxes; k-step j covers 16 columns.
 NT_DEVICE uint64_t kmajor_desc(uint32_t base, int j) {
@@ -442,6 +449,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const int h = hk * group + it / n_q;
         const int q0 = (i_lo + it % n_q) * TILE;
         if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1u, 0x50u + st, abort_flag)) break;
+        stamp(p, 0, it, 0);
         uint8_t* qs = sm + BwdSmem::Q + st * TILE_BYTES;
         uint8_t* ds = sm + BwdSmem::DO + st * TILE_BYTES;
         mbar_expect_tx(&qd_full[st], 2 * TILE_BYTES);
@@ -468,6 +476,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + st * TILE_BYTES);
         const uint32_t do_addr = smem_u32(sm + BwdSmem::DO + st * TILE_BYTES);
         if (!mbar_wait(&qd_full[st], (it >> 1) & 1, 0x61u, abort_flag)) break;
+        stamp(p, 1, it, 0);
         tc_fence_after();
         // loops are kept rolled: fully unrolled, the descriptors of every k-step of every operand
         // would be hoisted into registers that the other warp roles need
@@ -475,17 +484,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int j = 0; j < HD / 16; ++j) umma_bf16(t_s, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
         umma_commit(s_full);
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x62u, abort_flag)) break;  // dQ of it-1 left tDP
+        stamp(p, 1, it, 1);
         tc_fence_after();
 #pragma unroll 1
         for (int j = 0; j < HD / 16; ++j)
           umma_bf16(t_dp, kmajor_desc(v_addr, j), kmajor_desc(do_addr, j), id_s, j > 0);
         umma_commit(dp_full);
         if (!mbar_wait(p_full, it & 1, 0x63u, abort_flag)) break;
+        stamp(p, 1, it, 2);
         tc_fence_after();
 #pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
           umma_bf16_tmem_a(t_dv, t_s + j * 8, mnmajor_desc(do_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
         if (!mbar_wait(ds_full, it & 1, 0x64u, abort_flag)) break;
+        stamp(p, 1, it, 3);
         tc_fence_after();
 #pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
@@ -495,6 +507,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           umma_bf16(t_dp, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
         umma_commit(dq_full);
         umma_commit(&qd_empty[st]);
+        stamp(p, 1, it, 4);
       }
     }
   } else if (warp < 6) {
@@ -521,9 +534,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       mbar_arrive(stat_ready);
       if (!mbar_wait(stat_ready, it & 1, 0x75u, abort_flag)) break;
+      if (r == 0) stamp(p, 2, it, 0);
       const bool boundary = (k0 + TILE - 1 > q0) || (q0 + TILE > p.T) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
       if (!mbar_wait(s_full, it & 1, 0x70u, abort_flag)) break;
+      if (r == 0) stamp(p, 2, it, 1);
       __syncwarp();
       tc_fence_after();
 #pragma unroll 1
@@ -554,9 +569,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
+      if (r == 0) stamp(p, 2, it, 2);
       if (!mbar_wait(dp_full, it & 1, 0x71u, abort_flag)) break;
+      if (r == 0) stamp(p, 2, it, 3);
       // the dS^T buffer served as dQ staging for the previous pair: its second reduction read it last
       if (it > 0 && !mbar_wait(stg_done, (it - 1) & 1, 0x73u, abort_flag)) break;
+      if (r == 0) stamp(p, 2, it, 4);
       __syncwarp();
       tc_fence_after();
 #pragma unroll 1
@@ -582,6 +600,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       mbar_arrive(ds_full);
       mbar_arrive(stat_free);
+      if (r == 0) stamp(p, 2, it, 5);
     }
     // dK of this key tile once every MMA has completed (the last dq_full)
     if (!*abort_flag && mbar_wait(dq_full, (n_it - 1) & 1, 0x72u, abort_flag)) {
@@ -618,6 +637,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const int h = hk * group + it / n_q;
       const int q0 = (i_lo + it % n_q) * TILE;
       if (!mbar_wait(dq_full, it & 1, 0x78u, abort_flag)) break;
+      if (threadIdx.x == 192) stamp(p, 3, it, 0);
       __syncwarp();
       tc_fence_after();
       const bool leader = threadIdx.x == 192;  // warp 6, lane 0: issues the bulk reductions
@@ -635,6 +655,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         // staging must be free: read by the previous reduction (none before the first half of pair 0)
         const int k = 2 * it + half - 1;
         if (k >= 0 && !mbar_wait(stg_free, k & 1, 0x7Au, abort_flag)) { it = n_it; break; }
+        if (threadIdx.x == 192) stamp(p, 3, it, 1 + 2 * half);
         __syncwarp();
         // two boxes of [128 rows x 32 fp32], 128-byte rows, 128-byte swizzle
 #pragma unroll
@@ -655,6 +676,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             tma_reduce_add_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, b);
             tma_store_commit();
             tma_store_wait_read0();
+            stamp(p, 3, it, 2 + 2 * half);
           }
           mbar_arrive(stg_free);
           if (half == 1) mbar_arrive(stg_done);
@@ -834,6 +856,7 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   p.lddv = a.lddv;
   p.dq_acc = a.dq_acc;
   p.delta = a.delta;
+  p.trace = a.trace;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);

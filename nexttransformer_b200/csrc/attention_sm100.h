@@ -28,6 +28,9 @@ struct AttnArgs {
   int64_t lddq = 0, lddk = 0, lddv = 0;
   float* dq_acc = nullptr;  // fp32 [B*T, H*D] workspace
   float* delta = nullptr;   // fp32 [B, H, T] workspace
+  // Optional pipeline trace of the first CTA (int64 [4 roles][64 pairs][8 events] of SM clock
+  // stamps; zero-filled by the caller).  Diagnostics only.
+  long long* trace = nullptr;
 };
 
 // Return 0 on success, -1 when the shape is not supported by the kernels.

@@ -5,6 +5,7 @@
 #include <torch/extension.h>
 
 #include "attention_sm100.h"
+#include "comm.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
 #include "optim.h"
@@ -281,13 +282,14 @@ void attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o
 void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
               const Tensor& dout, const Tensor& dq, const Tensor& dk, const Tensor& dv, const Tensor& dq_acc,
               const Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window,
-              double scale) {
+              double scale, const OptT& trace) {
   AttnArgs a = attn_args(q, k, v, o, lse, B, T, H, Hk, D, window, scale);
   a.dout = dout.data_ptr(); a.lddo = dout.stride(-2);
   a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
   a.lddq = dq.stride(-2); a.lddk = dk.stride(-2); a.lddv = dv.stride(-2);
   a.dq_acc = dq_acc.data_ptr<float>();
   a.delta = delta.data_ptr<float>();
+  a.trace = trace.has_value() && trace->defined() ? reinterpret_cast<long long*>(trace->data_ptr<int64_t>()) : nullptr;
   const c10::cuda::CUDAGuard guard(q.device());
   ok(nt_attention_bwd(a, stream()), "attention_bwd");
 }
@@ -350,6 +352,29 @@ void gemm_ce_dgrad(const Tensor& G, const Tensor& w, const Tensor& dh, const Ten
   nt_gemm_launch(g, stream());
 }
 
+// Reduce-scatter over symmetric memory (see comm.h); pointer tables are int64 CUDA tensors.
+void p2p_reduce_scatter(const Tensor& peers, const Tensor& pads, const Tensor& seg_off, const Tensor& seg_len,
+                        int64_t rank, int64_t world, double scale, int64_t epoch, int64_t blocks, double timeout_s) {
+  for (auto* t : {&peers, &pads, &seg_off, &seg_len}) {
+    check_cuda(*t, "p2p table");
+    TORCH_CHECK(t->scalar_type() == at::kLong && t->is_contiguous(), "p2p tables must be contiguous int64");
+  }
+  TORCH_CHECK(peers.numel() == world && pads.numel() == world && seg_off.numel() == seg_len.numel(), "p2p table sizes");
+  const c10::cuda::CUDAGuard guard(peers.device());
+  ok(nt_p2p_reduce_scatter(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                           reinterpret_cast<const uint64_t*>(pads.data_ptr<int64_t>()), seg_off.data_ptr<int64_t>(),
+                           seg_len.data_ptr<int64_t>(), static_cast<int>(seg_off.numel()), static_cast<int>(rank),
+                           static_cast<int>(world), static_cast<float>(scale), static_cast<uint32_t>(epoch),
+                           static_cast<int>(blocks), static_cast<uint64_t>(timeout_s * 1e9), stream()),
+     "p2p_reduce_scatter");
+}
+
+std::vector<int64_t> read_comm_errors() {
+  unsigned w = 0;
+  const int c = nt_comm_read_error(&w);
+  return {c, static_cast<int64_t>(w)};
+}
+
 std::vector<int64_t> read_errors() {
   unsigned w = 0;
   const int g = nt_gemm_read_error(&w);
@@ -378,9 +403,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_normalize", &muon_normalize);
   m.def("muon_finish", &muon_finish);
   m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"), py::arg("delta"), py::arg("B"),
+        py::arg("T"), py::arg("H"), py::arg("Hk"), py::arg("D"), py::arg("window"), py::arg("scale"),
+        py::arg("trace") = py::none());
   m.def("read_errors", &read_errors);
   m.def("gemm_ce_fwd", &gemm_ce_fwd);
+  m.def("p2p_reduce_scatter", &p2p_reduce_scatter);
+  m.def("read_comm_errors", &read_comm_errors);
   m.def("gemm_ce_dgrad", &gemm_ce_dgrad);
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
   m.attr("EPI_F32") = static_cast<int>(EPI_F32);

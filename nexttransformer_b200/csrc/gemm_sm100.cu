@@ -509,6 +509,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
     const float sacc = p.s_ptr ? p.s_acc * *p.s_ptr : p.s_acc;
+    if constexpr (EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+      if (p.tma_out) {
+        // fp32 outputs: [32 rows x 32 fp32] boxes (128-byte rows, 128-byte swizzle) leave by bulk
+        // tensor store, or by bulk tensor add-reduction for the accumulating weight gradient (each
+        // output element receives exactly one addition, so the result stays deterministic)
+        uint8_t* stg = smem + S::STG_OFFSET + (warp - 2) * STG_WARP;
+        const bool reduce = EPI == EPI_F32_ACC && p.split == 1;
+        int g = 0;
+        int local = 0;
+        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+          const int acc = local & 1;
+          const uint32_t acc_phase = (local >> 1) & 1;
+          if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
+          __syncwarp();
+          tc_fence_after();
+          int b, mb, nb, ks;
+          tile_coords(t, p, b, mb, nb, ks);
+          const int row0 = mb * BM + quad * 32;
+          const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c, ++g) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(t_row + c * 32, r);
+            tmem_wait_ld();
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&tempty[acc]);
+            }
+            const int col0 = nb * BN + c * 32;
+            uint8_t* sc = stg + (g & 1) * (2 * STG_BOX);  // 4 KB box
+            if (lane == 0) tma_store_wait_read1();
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int pos = lane * 128 + ((k ^ (lane & 7)) << 4);
+              *reinterpret_cast<float4*>(sc + pos) =
+                  make_float4(__uint_as_float(r[4 * k]) * sacc, __uint_as_float(r[4 * k + 1]) * sacc,
+                              __uint_as_float(r[4 * k + 2]) * sacc, __uint_as_float(r[4 * k + 3]) * sacc);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row0 < p.M && col0 < p.N) {
+              // the split-K workspace is addressed as [split, M, N]: slice = z
+              const int z = p.split > 1 ? ks : b;
+              if (reduce) tma_reduce_add_3d(&tmC, sc, col0, row0, z);
+              else tma_store_3d(&tmC, sc, col0, row0, z);
+            }
+            if (lane == 0) tma_store_commit();
+          }
+        }
+        if (lane == 0) tma_store_wait0();
+      }
+    }
     if constexpr (bf16_out<EPI>()) {
       if (p.tma_out) {
         // staged path: values -> swizzled shared-memory box -> bulk tensor store (no per-thread
@@ -575,7 +629,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) tma_store_wait0();
       }
     }
-    if (!bf16_out<EPI>() || !p.tma_out) {
+    if (!(bf16_out<EPI>() || EPI == EPI_F32 || EPI == EPI_F32_ACC) || !p.tma_out) {
       int local = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
         const int acc = local & 1;
@@ -720,6 +774,21 @@ static bool out_map(CUtensorMap& map, const void* base, int64_t N, int64_t M, in
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 output map: dims {N, M, depth}, box {32, 32, 1}, 128-byte swizzle (depth = batch or split slices).
+static bool out_map_f32(CUtensorMap& map, const void* base, int64_t N, int64_t M, int64_t ld, int64_t depth,
+                        int64_t depth_stride) {
+  if (!base || reinterpret_cast<uintptr_t>(base) % 16 || (ld * 4) % 16 || (depth > 1 && (depth_stride * 4) % 16))
+    return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(depth)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 4),
+                           static_cast<cuuint64_t>((depth > 1 ? depth_stride : ld * M) * 4)};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return get_encode()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int A_MN, int B_MN, int EPI>
 static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
@@ -753,6 +822,11 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   if (bf16_out<EPI>() && p.split == 1 && g.tma_out_ok) {
     bool ok = out_map(tc, g.C, g.N, g.M, g.ldc, g.batch, g.strideC);
     if (EPI == EPI_RELU2) ok = ok && out_map(tp, g.P, g.N, g.M, g.ldp, g.batch, g.strideP);
+    p.tma_out = ok ? 1 : 0;
+  }
+  if ((EPI == EPI_F32 || EPI == EPI_F32_ACC) && g.tma_out_ok) {
+    const bool ok = p.split > 1 ? out_map_f32(tc, p.C, g.N, g.M, p.ldc, p.split, p.strideSplit)
+                                : out_map_f32(tc, g.C, g.N, g.M, g.ldc, g.batch, g.strideC);
     p.tma_out = ok ? 1 : 0;
   }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;

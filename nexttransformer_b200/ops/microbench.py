@@ -16,6 +16,7 @@ Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, v
   adamw                                                - AdamW over a [rows, 1280] table
   muon                                                 - the Muon chain on 20 matrices [5120, 1280]
   step                                                 - one fused training micro-step (all kernels)
+  attn_bwd_trace                                       - clock stamps of the first backward CTA per pair
 """
 import argparse
 import json
@@ -108,6 +109,42 @@ def case_attn(kind, rows):
     return bwd, _attn_flops(B, pairs, False)
 
 
+def attn_bwd_trace(rows):
+    """Pipeline stamps of the first backward CTA: per (role, pair) the SM-clock offsets of its events."""
+    from nexttransformer_b200.ops._ext import ext
+    lib = ext()
+    B = max(1, rows // SEQ)
+    M, H, Hk, D = B * SEQ, HEADS, KV_HEADS, HEAD_DIM
+    qkv = _bf16(M, (H + 2 * Hk) * D).mul_(0.3)
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:(H + Hk) * D], qkv[:, (H + Hk) * D:]
+    o = torch.empty(M, H * D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, H, SEQ, device="cuda")
+    sc = 1.0 / math.sqrt(D)
+    lib.attn_fwd(q, k, v, o, lse, B, SEQ, H, Hk, D, -1, sc)
+    do = torch.randn_like(o)
+    dqkv = torch.empty_like(qkv)
+    trace = torch.zeros(4, 64, 8, dtype=torch.int64, device="cuda")
+    for _ in range(2):
+        trace.zero_()
+        lib.attn_bwd(q, k, v, o, lse, do, dqkv[:, :H * D], dqkv[:, H * D:(H + Hk) * D], dqkv[:, (H + Hk) * D:],
+                     torch.zeros(M, H * D, device="cuda"), torch.empty(B, H, SEQ, device="cuda"), B, SEQ, H, Hk, D, -1,
+                     sc, trace)
+    torch.cuda.synchronize()
+    t = trace.cpu()
+    base = int(t[t > 0].min())
+    names = {0: "producer: qd_empty", 1: "mma: qd_full dq_free p_full ds_full issued",
+             2: "softmax: stat s_full p_arrive dp_full stg_done ds_arrive", 3: "drain: dq_full free0 read0 free1 read1"}
+    out = {}
+    for role in range(4):
+        rows_ = []
+        for it in range(16):
+            ev = [int(x) - base if int(x) else None for x in t[role, it]]
+            if any(e is not None for e in ev):
+                rows_.append(ev)
+        out[names[role]] = rows_
+    return out
+
+
 def case_ce(rows):
     from nexttransformer_b200.ops._ext import ext
     logits = _bf16(rows, VOCAB)
@@ -175,6 +212,9 @@ def main(argv=None):
     a = ap.parse_args(argv)
     torch.manual_seed(0)
     byts = None
+    if a.case == "attn_bwd_trace":
+        print(json.dumps(attn_bwd_trace(a.rows)), flush=True)
+        return
     if a.case.startswith("gemm_"):
         fn, flops = case_gemm(a.case, a.rows)
     elif a.case.startswith("attn_"):
