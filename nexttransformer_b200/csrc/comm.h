@@ -1,0 +1,13 @@
+// Host interface of the peer-memory collectives (comm.cu).
+#pragma once
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+// In-place reduce-scatter over symmetric memory: for every owned segment (element offset, length;
+// both multiples of 4) buf_me[seg] = scale * sum_w buf_w[seg].  `peers_dev` / `pads_dev` are device
+// arrays of the world's buffer and signal-pad pointers; `epoch` grows by one per call on every rank.
+// The signal pads need 2 * blocks * world 32-bit slots.
+int nt_p2p_reduce_scatter(const uint64_t* peers_dev, const uint64_t* pads_dev, const int64_t* seg_off,
+                          const int64_t* seg_len, int nseg, int rank, int world, float scale, uint32_t epoch,
+                          int blocks, uint64_t timeout_ns, cudaStream_t stream);
+int nt_comm_read_error(unsigned* where);
