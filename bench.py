@@ -44,6 +44,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--micro-batch", type=int, default=0, help="rows per micro-batch (default 32 ours / 16 reference)")
+    p.add_argument("--comm", choices=("nccl", "p2p"), default="p2p",
+                   help="gradient averaging of our arm on N > 1: NCCL collectives or the peer-memory kernel")
     p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
     p.add_argument("--no-e2e", action="store_true", help=argparse.SUPPRESS)
     return p.parse_args()
@@ -182,8 +184,23 @@ def main():
         from nexttransformer_b200.optim.muon_adamw import MuonAdamW
         from nexttransformer_b200.training.engine import Trainer
         model = build_shell(ShellConfig(**cfg), device, seed=42)
-        st = model.fused_state()
+        p2p = world > 1 and args.comm == "p2p"
+        if p2p:
+            from nexttransformer_b200.parallel.symmetric import (PeerReduceScatter, fused_state_with_arena,
+                                                                 ownership_segments)
+            try:
+                st = fused_state_with_arena(model, dist.group.WORLD)
+            except Exception as exc:  # symmetric memory unavailable: NCCL collectives instead
+                if rank == 0:
+                    print(f"peer-memory gradients unavailable ({exc}); using NCCL", file=sys.stderr)
+                p2p, args.comm = False, "nccl"
+                model._fused = None
+        if not p2p:
+            st = model.fused_state()
         opt = MuonAdamW(shell_groups(model), shadows={p: s for p, s in st.casts})
+        if p2p:
+            segs, covered = ownership_segments(opt, st.arena, world)
+            opt.use_peer_reduce_scatter(PeerReduceScatter(st.arena, segs, rank, world), covered)
         trainer = Trainer(model, opt, accumulation=accum)
 
         def step_device(xs, ys):
@@ -288,6 +305,7 @@ def main():
                "config": {"model": "dense GQA d20 w1280 h10/kv5 hd128 vocab65536 (shell: VE, smear, backout, softcap)",
                           "global_batch": GLOBAL_BATCH, "seq_len": T, "parallelism": f"dp{world}",
                           "micro_batch": micro, "grad_accum": accum, "l2": "working set >> L2 (no flush needed)",
+                          "grad_comm": (args.comm if world > 1 else "none") if args.impl == "ours" else "nccl",
                           "flops_per_token": flops_per_token},
                "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": final_loss}
         if args.impl == "reference":

@@ -50,13 +50,35 @@ class FusedState:
     gradient buffer; every parameter's ``main_grad`` is a view into these buffers.
     """
 
-    def __init__(self, model):
+    def __init__(self, model, grad_alloc=None, plan_only=False):
+        """``grad_alloc(shape)`` (optional) supplies the fp32 gradient buffers in a fixed order (a
+        flat arena, e.g. in symmetric memory); ``plan_only`` only walks that order so the caller
+        can size the arena, touching no parameter."""
         self.model = model
         dev = model.get_device()
         f32, bf = torch.float32, torch.bfloat16
         self.slots = []        # GEMM-written gradients (fresh / accumulate)
         self.zeroed = []       # gradients accumulated with atomics or torch ops
         self.casts = []        # (fp32 master, bf16 shadow)
+        self.arena = None
+
+        def grad(shape):
+            if grad_alloc is not None:
+                return grad_alloc(tuple(shape))
+            return torch.zeros(tuple(shape), device=dev, dtype=f32)
+
+        if plan_only:
+            for blk in model.transformer.h:
+                a = blk.attn
+                grad((a.c_q.weight.shape[0] + 2 * a.c_k.weight.shape[0], a.c_q.weight.shape[1]))
+                for lin in (a.c_proj, blk.mlp.c_fc, blk.mlp.c_proj):
+                    grad(lin.weight.shape)
+                if a.ve_gate is not None:
+                    grad(a.ve_gate.weight.shape)
+            grad(model.lm_head.weight.shape)
+            for p in self._loose(model):
+                grad(p.shape)
+            return
 
         def shadow(p, out=None):
             out = out if out is not None else torch.empty(p.shape, device=dev, dtype=bf)
@@ -67,7 +89,7 @@ class FusedState:
             a = blk.attn
             nq, nk, d = a.c_q.weight.shape[0], a.c_k.weight.shape[0], a.c_q.weight.shape[1]
             a._w_qkv = torch.empty(nq + 2 * nk, d, device=dev, dtype=bf)
-            g = torch.zeros(nq + 2 * nk, d, device=dev, dtype=f32)
+            g = grad((nq + 2 * nk, d))
             a._g_qkv = GradSlot(g)
             self.slots.append(a._g_qkv)
             for lin, lo, hi in ((a.c_q, 0, nq), (a.c_k, nq, nq + nk), (a.c_v, nq + nk, nq + 2 * nk)):
@@ -75,25 +97,30 @@ class FusedState:
                 shadow(lin.weight, a._w_qkv[lo:hi])
             for lin in (a.c_proj, blk.mlp.c_fc, blk.mlp.c_proj):
                 lin._w = shadow(lin.weight)
-                lin.weight.main_grad = torch.zeros_like(lin.weight)
+                lin.weight.main_grad = grad(lin.weight.shape)
                 lin._g = GradSlot(lin.weight.main_grad)
                 self.slots.append(lin._g)
             if a.ve_gate is not None:
                 a.ve_gate._w = shadow(a.ve_gate.weight)
-                a.ve_gate.weight.main_grad = torch.zeros_like(a.ve_gate.weight)
+                a.ve_gate.weight.main_grad = grad(a.ve_gate.weight.shape)
                 self.zeroed.append(a.ve_gate.weight.main_grad)
         head = model.lm_head
         head._w = shadow(head.weight)
-        head.weight.main_grad = torch.zeros_like(head.weight)
+        head.weight.main_grad = grad(head.weight.shape)
         head._g = GradSlot(head.weight.main_grad)
         self.slots.append(head._g)
         model.smear_gate._w = shadow(model.smear_gate.weight)
-        for p in (model.transformer.wte.weight, *[e.weight for e in model.value_embeds.values()],
-                  model.resid_lambdas, model.x0_lambdas, model.smear_gate.weight, model.smear_lambda,
-                  model.backout_lambda):
-            p.main_grad = torch.zeros(p.shape, device=dev, dtype=f32)
+        for p in self._loose(model):
+            p.main_grad = grad(p.shape)
             self.zeroed.append(p.main_grad)
         self.refresh_shadows()
+
+    @staticmethod
+    def _loose(model):
+        """Parameters whose gradients are accumulated by atomics or torch ops (zeroed per update)."""
+        return (model.transformer.wte.weight, *[e.weight for e in model.value_embeds.values()],
+                model.resid_lambdas, model.x0_lambdas, model.smear_gate.weight, model.smear_lambda,
+                model.backout_lambda)
 
     @torch.no_grad()
     def refresh_shadows(self):

@@ -89,6 +89,12 @@ class MuonAdamW(torch.optim.Optimizer):
         # fp32 master -> bf16 shadow written by the update (the fused forward reads shadows)
         self.shadows = shadows or {}
         self._work = {}
+        # Optional peer-memory reduce-scatter (parallel.symmetric.PeerReduceScatter) and the set of
+        # parameters whose gradients it averages in place; the others use NCCL collectives.
+        self.p2p, self.p2p_params = None, frozenset()
+
+    def use_peer_reduce_scatter(self, reducer, covered):
+        self.p2p, self.p2p_params = reducer, frozenset(covered)
 
     # -------------------------------------------------------------- helpers
     @staticmethod
@@ -117,6 +123,10 @@ class MuonAdamW(torch.optim.Optimizer):
                 raise RuntimeError("missing gradient in the fixed training graph")
             if world == 1:
                 plans.append((p, None, None, g))
+            elif p in self.p2p_params:
+                n = p.shape[0] // world   # this rank's rows were averaged in place by the peer kernel
+                rows = slice(rank * n, (rank + 1) * n)
+                plans.append((p, rows, None, g[rows]))
             elif p.numel() < 1024 or p.shape[0] % world:
                 work = dist.all_reduce(g, op=dist.ReduceOp.AVG, async_op=True)
                 plans.append((p, None, work, g))
@@ -166,6 +176,8 @@ class MuonAdamW(torch.optim.Optimizer):
             return []
         works = []
         for i, p in enumerate(params):
+            if p in self.p2p_params:
+                continue
             works.append(dist.reduce(grad_of(p), dst=min(i // chunk, world - 1), op=dist.ReduceOp.SUM,
                                      async_op=True))
         return works
@@ -187,7 +199,8 @@ class MuonAdamW(torch.optim.Optimizer):
                                                                dtype=torch.float32)
             if world > 1:
                 for p in mine:
-                    grad_of(p).div_(world)
+                    if p not in self.p2p_params:
+                        grad_of(p).div_(world)
             if mine[0].is_cuda and self.gemm_shape_ok(m, n):
                 self._muon_cuda(group, mine, m, n, lr)
             else:
@@ -273,6 +286,8 @@ class MuonAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def step(self):
         rank, world = self._dist()
+        if self.p2p is not None and world > 1:
+            self.p2p()
         plans = []
         for group in self.param_groups:
             if group["kind"] == "adamw":
