@@ -80,57 +80,81 @@ NT_DEVICE float fast_exp2(float x) {
 }
 
 // ------------------------------------------------------------------------------ forward
+// One CTA per pair of consecutive query tiles (A = 2c, B = 2c + 1) of one (head, batch); 320 threads.
+// The two tiles share every K/V tile load, and their softmax warpgroups alternate with the MMAs:
+//   warp 0      TMA: Q_A, Q_B once, then K/V tiles into a 2-stage ring.
+//   warp 1      TMEM owner and MMA issuer: S_A = Q_A K^T, S_B = Q_B K^T, O_A += P_A V (P from tensor
+//               memory), S_A of the next key tile, O_B += P_B V, S_B of the next key tile, ...
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per thread: row max
+//               over the S row (first pass), then P = exp2(S - m) written back over the first 64
+//               columns of S as bf16 (second pass), lazy rescaling of O only when the running max
+//               grows by more than 2^8; at the end O / l goes out through shared memory (the tile's Q
+//               buffer, whose last reader has finished) with a bulk tensor store, and the lse.
+// Tensor memory: O_A [0,128) | O_B [128,256) | S_A [256,384) | S_B [384,512).
+// Under the causal mask tile A has one key tile less than B (the diagonal tile of B).
 struct FwdSmem {
-  static constexpr int Q = 0;
-  static constexpr int K0 = Q + TILE_BYTES;
-  static constexpr int V0 = K0 + 2 * TILE_BYTES;
-  static constexpr int P = V0 + 2 * TILE_BYTES;
-  static constexpr int BAR = P + TILE_BYTES;
-  // q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full, o_done
-  static constexpr int NBAR = 13;
-  static constexpr int TOTAL = BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int QA = 0;
+  static constexpr int QB = QA + TILE_BYTES;
+  static constexpr int K0 = QB + TILE_BYTES;      // 2 stages
+  static constexpr int V0 = K0 + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int BAR = V0 + 2 * TILE_BYTES;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], o_done[2]
+  static constexpr int NBAR = 11;
+  static constexpr int TOTAL = BAR + NBAR * 8 + 32 + 1024;  // + tmem holder, abort and veto flags
 };
+static_assert(FwdSmem::TOTAL <= 232448, "forward shared memory exceeds the sm_100 limit");
+constexpr int FWD_THREADS = 320;
 
-__global__ void __launch_bounds__(192, 1)
+// Key-tile range [lo, hi] of query tile qt (causal, optional left window); empty when qt is past T.
+NT_DEVICE void fwd_kv_range(const Params& p, int qt, int& lo, int& hi) {
+  const int q0 = qt * TILE;
+  lo = 0;
+  if (p.window >= 0) lo = max(0, (q0 - p.window) / TILE);
+  hi = qt;
+}
+
+__global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, Params p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + FwdSmem::BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* kv_empty = bars + 5;
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_free = bars + 9;
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [A, B]
+  uint64_t* p_full = bars + 7;    // [A, B]
+  uint64_t* o_done = bars + 9;    // [A, B]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + FwdSmem::NBAR);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [abort, veto A, veto B]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + TILE - 1) / TILE;
-  const int qt = n_qt - 1 - blockIdx.x;  // longest rows first
+  const int n_pairs = (n_qt + 1) / 2;
+  const int pair = n_pairs - 1 - blockIdx.x;  // longest rows first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (p.H / p.Hk);
-  const int q0 = qt * TILE;
-  int j_lo = 0;
-  if (p.window >= 0) j_lo = max(0, (q0 - p.window) / TILE);
-  const int j_hi = min(n_qt - 1, (q0 + TILE - 1) / TILE);
+  const int qtA = 2 * pair, qtB = 2 * pair + 1;
+  const bool hasB = qtB < n_qt;
+  int loA, hiA, loB = 0, hiB = -1;
+  fwd_kv_range(p, qtA, loA, hiA);
+  if (hasB) fwd_kv_range(p, qtB, loB, hiB);
+  const int j_lo = loA, j_hi = hasB ? hiB : hiA;  // loA <= loB, hiA < hiB
   const int n_kv = j_hi - j_lo + 1;
+  const int nA = hiA - loA + 1, nB = hasB ? hiB - loB + 1 : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
-    *abort_flag = 0;
+    abort_flag[0] = 0;
+    abort_flag[1] = 0;
+    abort_flag[2] = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -141,17 +165,19 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
-  const uint32_t t_o = tbase;          // O accumulator: columns [0, 128)
-  const uint32_t t_s = tbase + 128;    // S buffers: [128, 256), [256, 384)
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sm + FwdSmem::Q, &tmQ, q_full, h * HD, q0, b);
-      tma_load_3d(sm + FwdSmem::Q + BOX_BYTES, &tmQ, q_full, h * HD + 64, q0, b);
+      mbar_expect_tx(q_full, (hasB ? 2 : 1) * TILE_BYTES);
+      tma_load_3d(sm + FwdSmem::QA, &tmQ, q_full, h * HD, qtA * TILE, b);
+      tma_load_3d(sm + FwdSmem::QA + BOX_BYTES, &tmQ, q_full, h * HD + 64, qtA * TILE, b);
+      if (hasB) {
+        tma_load_3d(sm + FwdSmem::QB, &tmQ, q_full, h * HD, qtB * TILE, b);
+        tma_load_3d(sm + FwdSmem::QB + BOX_BYTES, &tmQ, q_full, h * HD + 64, qtB * TILE, b);
+      }
       int issued = 0;
       for (int t = 0; t < n_kv; ++t) {
         const int st = t & 1;
@@ -159,159 +185,202 @@ __global__ void __launch_bounds__(192, 1)
         const int k0 = (j_lo + t) * TILE;
         uint8_t* ks = sm + FwdSmem::K0 + st * TILE_BYTES;
         uint8_t* vs = sm + FwdSmem::V0 + st * TILE_BYTES;
-        mbar_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(ks, &tmK, &k_full[st], hk * HD, k0, b);
-        tma_load_3d(ks + BOX_BYTES, &tmK, &k_full[st], hk * HD + 64, k0, b);
-        mbar_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(vs, &tmV, &v_full[st], hk * HD, k0, b);
-        tma_load_3d(vs + BOX_BYTES, &tmV, &v_full[st], hk * HD + 64, k0, b);
+        mbar_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_3d(ks, &tmK, &kv_full[st], hk * HD, k0, b);
+        tma_load_3d(ks + BOX_BYTES, &tmK, &kv_full[st], hk * HD + 64, k0, b);
+        tma_load_3d(vs, &tmV, &kv_full[st], hk * HD, k0, b);
+        tma_load_3d(vs + BOX_BYTES, &tmV, &kv_full[st], hk * HD + 64, k0, b);
         ++issued;
       }
-      // drain copies still in flight
       mbar_wait(q_full, 0, 0x1Fu, nullptr);
-      for (int t = max(0, issued - 2); t < issued; ++t) {
-        mbar_wait(&k_full[t & 1], (t >> 1) & 1, 0x1Du, nullptr);
-        mbar_wait(&v_full[t & 1], (t >> 1) & 1, 0x1Eu, nullptr);
-      }
+      for (int t = max(0, issued - 2); t < issued; ++t) mbar_wait(&kv_full[t & 1], (t >> 1) & 1, 0x1Du, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(TILE, TILE, 0, 0);      // S = Q K^T
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(TILE, HD, 0, 1);     // O += P V (V MN-major)
-      const uint32_t q_addr = smem_u32(sm + FwdSmem::Q);
-      const uint32_t p_addr = smem_u32(sm + FwdSmem::P);
+      constexpr uint32_t idesc_s = idesc_bf16_f32(TILE, TILE, 0, 0);   // S = Q K^T
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(TILE, HD, 0, 1);    // O += P V  (P from tensor memory)
+      const uint32_t qa_addr = smem_u32(sm + FwdSmem::QA), qb_addr = smem_u32(sm + FwdSmem::QB);
+      const uint32_t t_oA = tbase, t_oB = tbase + 128, t_sA = tbase + 256, t_sB = tbase + 384;
+      int iA = 0, iB = 0;  // S tiles issued per query tile
+      int uA = 0, uB = 0;  // PV products issued per query tile
       bool ok = mbar_wait(q_full, 0, 0x20u, abort_flag);
-      for (int t = 0; ok && t <= n_kv; ++t) {
-        if (t < n_kv) {
-          const int st = t & 1;
-          if (!mbar_wait(&k_full[st], (t >> 1) & 1, 0x21u, abort_flag)) break;
-          if (!mbar_wait(&s_free[st], ((t >> 1) & 1) ^ 1u, 0x22u, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sm + FwdSmem::K0 + st * TILE_BYTES);
-#pragma unroll
-          for (int j = 0; j < HD / 16; ++j)
-            umma_bf16(t_s + st * 128, kmajor_desc(q_addr, j), kmajor_desc(k_addr, j), idesc, j > 0);
-          umma_commit(&s_full[st]);
-        }
-        if (t > 0) {
-          const int u = t - 1, su = u & 1;
-          if (!mbar_wait(p_full, u & 1, 0x23u, abort_flag)) break;
-          if (!mbar_wait(&v_full[su], (u >> 1) & 1, 0x24u, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sm + FwdSmem::V0 + su * TILE_BYTES);
-#pragma unroll
-          for (int j = 0; j < TILE / 16; ++j)
-            umma_bf16(t_o, kmajor_desc(p_addr, j), mnmajor_desc(v_addr, j), idesc_pv, (u > 0 || j > 0) ? 1u : 0u);
-          umma_commit(o_done);
-          umma_commit(&kv_empty[su]);
-        }
+      // S_X of key tile t for query tile X (0: A, 1: B) when X sees that tile
+      auto sees = [&](int X, int t) -> bool {
+        const int j = j_lo + t;
+        return X == 0 ? (j >= loA && j <= hiA) : (hasB && j >= loB && j <= hiB);
+      };
+      auto issue_s = [&](int X, int t) -> bool {
+        const int st = t & 1;
+        if (!mbar_wait(&kv_full[st], (t >> 1) & 1, 0x21u, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm + FwdSmem::K0 + st * TILE_BYTES);
+        const uint32_t qx = X ? qb_addr : qa_addr, tsx = X ? t_sB : t_sA;
+#pragma unroll 1
+        for (int q = 0; q < HD / 16; ++q) umma_bf16(tsx, kmajor_desc(qx, q), kmajor_desc(k_addr, q), idesc_s, q > 0);
+        umma_commit(&s_full[X]);
+        if (X) ++iB; else ++iA;
+        return true;
+      };
+      auto issue_pv = [&](int X, int t) -> bool {
+        int& u = X ? uB : uA;
+        if (!mbar_wait(&p_full[X], u & 1, 0x23u + X, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sm + FwdSmem::V0 + (t & 1) * TILE_BYTES);
+        const uint32_t tox = X ? t_oB : t_oA, tsx = X ? t_sB : t_sA;
+#pragma unroll 1
+        for (int q = 0; q < TILE / 16; ++q)
+          umma_bf16_tmem_a(tox, tsx + q * 8, mnmajor_desc(v_addr, q), idesc_pv, (u > 0 || q > 0) ? 1u : 0u);
+        umma_commit(&o_done[X]);
+        ++u;
+        return true;
+      };
+      // Order: S_A(0) S_B(0) | PV_A(t) S_A(t+1) PV_B(t) S_B(t+1) | ...  Each tile's next S follows its own
+      // PV at once, so one warpgroup's softmax overlaps the other tile's PV and S.  S_X(t+1) overwrites
+      // the columns P_X(t) occupies; it is issued after PV_X(t), and MMAs from one thread run in order.
+      if (ok && n_kv > 0) {
+        if (sees(0, 0)) ok = issue_s(0, 0);
+        if (ok && sees(1, 0)) ok = issue_s(1, 0);
       }
+      for (int t = 0; ok && t < n_kv; ++t) {
+        for (int X = 0; ok && X < 2; ++X) {
+          if (sees(X, t)) ok = issue_pv(X, t);
+          if (ok && t + 1 < n_kv && sees(X, t + 1)) ok = issue_s(X, t + 1);
+        }
+        if (ok) umma_commit(&kv_empty[t & 1]);
+      }
+      (void)iA;
+      (void)iB;
     }
   } else {
-    // ------------------------------------------------------------ softmax warps
+    // ------------------------------------------------------------ softmax warpgroups
+    const int grp = warp < 6 ? 0 : 1;  // 0: tile A, 1: tile B
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
+    const int qt = grp ? qtB : qtA;
+    const int lo = grp ? loB : loA;
+    const int n = grp ? nB : nA;
+    const int q0 = qt * TILE;
     const int qi = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* pbuf = sm + FwdSmem::P;
+    const uint32_t t_o = tbase + grp * 128, t_s = tbase + 256 + grp * 128;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int t = 0; t < n_kv; ++t) {
-      const int st = t & 1;
-      const int k0 = (j_lo + t) * TILE;
-      if (!mbar_wait(&s_full[st], (t >> 1) & 1, 0x30u, abort_flag)) { ok = false; break; }
+    for (int i = 0; i < n; ++i) {
+      const int k0 = (lo + i) * TILE;
+      if (!mbar_wait(&s_full[grp], i & 1, 0x30u, abort_flag)) { ok = false; break; }
       __syncwarp();
       tc_fence_after();
-      float s[TILE];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_s + st * 128 + lane_off + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * p.scale_log2;
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);
       const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
-      if (boundary) {
-#pragma unroll
-        for (int i = 0; i < TILE; ++i) {
-          const int kj = k0 + i;
-          const bool valid = kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window);
-          if (!valid) s[i] = -INFINITY;
-        }
-      }
+      // pass 1: row max of the scaled, masked scores
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_s + lane_off + c * 32, v);
+        tmem_wait_ld();
+        float xs[32];
 #pragma unroll
-      for (int i = 0; i < TILE; ++i) mx = fmaxf(mx, s[i]);
+        for (int e = 0; e < 32; ++e) xs[e] = __uint_as_float(v[e]) * p.scale_log2;
+        if (boundary) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int kj = k0 + c * 32 + e;
+            xs[e] = (kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window)) ? xs[e] : -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, xs[e]);
+      }
       // lazy rescale: keep the old reference max unless the row grew by more than 2^8
       float m_new = m;
-      if (t == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
-      const float alpha = (t == 0 || m_new == m) ? 1.f : fast_exp2(m - m_new);
+      if (i == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
+      const float alpha = (i == 0 || m_new == m) ? 1.f : fast_exp2(m - m_new);
       const float mref = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < TILE; ++i) {
-        s[i] = fast_exp2(s[i] - mref);
-        sum += s[i];
-      }
-      l = l * alpha + sum;
-      if (t > 0) {
-        // PV of the previous tile must be complete before O is touched or P is overwritten
-        if (!mbar_wait(o_done, (t - 1) & 1, 0x31u, abort_flag)) { ok = false; break; }
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O holds every earlier product: wait for the last one, then scale O in place
+        if (!mbar_wait(&o_done[grp], (i - 1) & 1, 0x31u, abort_flag)) { ok = false; break; }
         __syncwarp();
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t v[32];
-            tmem_ld32(t_o + lane_off + c * 32, v);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(t_o + lane_off + c * 32, v);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st16(t_o + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-            tmem_st16(t_o + lane_off + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-          }
-          tmem_wait_st();
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st16(t_o + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+          tmem_st16(t_o + lane_off + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
         }
+        tmem_wait_st();
       }
       m = m_new;
+      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_s + lane_off + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+        float xs[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 w = make_uint4(pack_bf16x2(s[8 * c + 0], s[8 * c + 1]), pack_bf16x2(s[8 * c + 2], s[8 * c + 3]),
-                             pack_bf16x2(s[8 * c + 4], s[8 * c + 5]), pack_bf16x2(s[8 * c + 6], s[8 * c + 7]));
-        *reinterpret_cast<uint4*>(pbuf + swz_off(r, c)) = w;
+        for (int e = 0; e < 32; ++e) xs[e] = __uint_as_float(v[e]) * p.scale_log2 - mref;
+        if (boundary) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int kj = k0 + c * 32 + e;
+            xs[e] = (kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window)) ? xs[e] : -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float e0 = fast_exp2(xs[e]), e1 = fast_exp2(xs[e + 1]);
+          sum += e0 + e1;
+          pk[e / 2] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + lane_off + c * 16, pk);
       }
-      fence_proxy_async_smem();
+      l = l * alpha + sum;
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[grp]);
     }
-    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, 0x32u, abort_flag)) {
+    // epilogue: O / l -> this tile's Q buffer (its last reader, S of the last key tile, is done once
+    // the last PV product is) -> bulk tensor store; lse per row.  Every thread of the group reaches
+    // the group barrier, whether or not its waits succeeded; a shared flag vetoes the store.
+    volatile int* veto = abort_flag + 1 + grp;
+    const bool fin = ok && n > 0 && mbar_wait(&o_done[grp], (n - 1) & 1, 0x32u, abort_flag);
+    uint8_t* ob = sm + (grp ? FwdSmem::QB : FwdSmem::QA);
+    if (!fin) *veto = 1;
+    if (fin) {
       __syncwarp();
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + (static_cast<int64_t>(b) * p.T + qi) * p.ldo + h * HD;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
-        __syncwarp();
         tmem_ld32(t_o + lane_off + c * 32, v);
         tmem_wait_ld();
-        if (qi < p.T) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w = make_uint4(pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
-                                 pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
-                                 pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
-                                 pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) = w;
-          }
+        for (int g = 0; g < 4; ++g) {
+          const int i = 8 * g;
+          uint4 w = make_uint4(pack_bf16x2(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(v[i + 4]) * inv, __uint_as_float(v[i + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(v[i + 6]) * inv, __uint_as_float(v[i + 7]) * inv));
+          *reinterpret_cast<uint4*>(ob + swz_off(r, c * 4 + g)) = w;
         }
       }
-      if (qi < p.T)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + qi] = (m * 0.6931471805599453f) + logf(l);
+      if (qi < p.T) p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + qi] = (m * 0.6931471805599453f) + logf(l);
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(2 + grp, 128);
+    if (r == 0 && n > 0 && !*veto) {
+      tma_store_3d(&tmO, ob, h * HD, q0, b);
+      tma_store_3d(&tmO, ob + BOX_BYTES, h * HD + 64, q0, b);
+      tma_store_commit();
+      tma_store_wait0();
     }
   }
   tc_fence_before();
@@ -546,25 +615,29 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         uint32_t sv[32];
         tmem_ld32(t_s + lane_off + c * 32, sv);
         tmem_wait_ld();
+        if (r == 0 && c == 0) stamp(p, 2, it, 6);
         uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
+        // the mask is applied in a separate loop so the unrolled exp loop carries no branches
+        float xs[32];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
-          float pp[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qi = q0 + c * 32 + i + e;
-            float v = fast_exp2(__uint_as_float(sv[i + e]) * p.scale_log2 - (e ? l2.y : l2.x));
-            if (boundary) {
-              const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
-              if (!valid) v = 0.f;
-            }
-            pp[e] = v;
-          }
-          pk[i / 2] = pack_bf16x2(pp[0], pp[1]);
+          xs[i] = __uint_as_float(sv[i]) * p.scale_log2 - l2.x;
+          xs[i + 1] = __uint_as_float(sv[i + 1]) * p.scale_log2 - l2.y;
         }
+        if (boundary) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int qi = q0 + c * 32 + i;
+            const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+            xs[i] = valid ? xs[i] : -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) pk[i / 2] = pack_bf16x2(fast_exp2(xs[i]), fast_exp2(xs[i + 1]));
         // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier chunk
         tmem_st16(t_s + lane_off + c * 16, pk);
+        if (r == 0 && c == 0) stamp(p, 2, it, 7);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -823,14 +896,16 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tq = tile_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B);
   CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
+  CUtensorMap to = tile_map(a.o, static_cast<int64_t>(a.H) * HD, a.ldo, a.T, a.B);
   Params p = make_params(a);
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::TOTAL);
     configured = true;
   }
-  dim3 grid((a.T + TILE - 1) / TILE, a.H, a.B);
-  attn_fwd_kernel<<<grid, 192, FwdSmem::TOTAL, s>>>(tq, tk, tv, p);
+  const int n_qt = (a.T + TILE - 1) / TILE;
+  dim3 grid((n_qt + 1) / 2, a.H, a.B);
+  attn_fwd_kernel<<<grid, FWD_THREADS, FwdSmem::TOTAL, s>>>(tq, tk, tv, to, p);
   return 0;
 }
 

@@ -6,6 +6,7 @@
 
 #include "attention_sm100.h"
 #include "comm.h"
+#include "linear_attn.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
 #include "optim.h"
@@ -369,6 +370,48 @@ void p2p_reduce_scatter(const Tensor& peers, const Tensor& pads, const Tensor& s
      "p2p_reduce_scatter");
 }
 
+// ------------------------------------------------------------------ linear-attention elementwise
+void conv_silu_fwd(const Tensor& x, const Tensor& w, const Tensor& y, const OptT& pre) {
+  check_rows(x, "x");
+  check_rows(y, "y");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "conv weight must be contiguous fp32 [C, K]");
+  const int B = static_cast<int>(x.size(0)), T = static_cast<int>(x.size(1)), C = static_cast<int>(x.size(2));
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_causal_conv_silu_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), mptr_or_null(pre), B, T, C,
+                             static_cast<int>(w.size(-1)), stream()),
+     "conv_silu_fwd");
+}
+
+void conv_silu_bwd(const Tensor& x, const Tensor& pre, const Tensor& dy, const Tensor& w, const Tensor& dx,
+                   const Tensor& dw) {
+  for (auto* t : {&x, &pre, &dy, &dx}) check_rows(*t, "conv operand");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && dw.scalar_type() == at::kFloat, "conv weights are fp32");
+  const int B = static_cast<int>(x.size(0)), T = static_cast<int>(x.size(1)), C = static_cast<int>(x.size(2));
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_causal_conv_silu_bwd(x.data_ptr(), pre.data_ptr(), dy.data_ptr(), w.data_ptr<float>(), dx.data_ptr(),
+                             dw.data_ptr<float>(), B, T, C, static_cast<int>(w.size(-1)), stream()),
+     "conv_silu_bwd");
+}
+
+void gated_rmsnorm_fwd(const Tensor& x, const Tensor& g, const Tensor& gain, const Tensor& y, const Tensor& rstd) {
+  for (auto* t : {&x, &g, &y}) check_rows(*t, "gated norm operand");
+  const int D = static_cast<int>(gain.numel());
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_gated_rmsnorm_fwd(x.data_ptr(), g.data_ptr(), gain.data_ptr<float>(), y.data_ptr(), rstd.data_ptr<float>(),
+                          x.numel() / D, D, stream()),
+     "gated_rmsnorm_fwd");
+}
+
+void gated_rmsnorm_bwd(const Tensor& x, const Tensor& g, const Tensor& gain, const Tensor& rstd, const Tensor& dy,
+                       const Tensor& dx, const Tensor& dg, const Tensor& dgain) {
+  for (auto* t : {&x, &g, &dy, &dx, &dg}) check_rows(*t, "gated norm operand");
+  const int D = static_cast<int>(gain.numel());
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_gated_rmsnorm_bwd(x.data_ptr(), g.data_ptr(), gain.data_ptr<float>(), rstd.data_ptr<float>(), dy.data_ptr(),
+                          dx.data_ptr(), dg.data_ptr(), dgain.data_ptr<float>(), x.numel() / D, D, stream()),
+     "gated_rmsnorm_bwd");
+}
+
 std::vector<int64_t> read_comm_errors() {
   unsigned w = 0;
   const int c = nt_comm_read_error(&w);
@@ -410,6 +453,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_errors", &read_errors);
   m.def("gemm_ce_fwd", &gemm_ce_fwd);
   m.def("p2p_reduce_scatter", &p2p_reduce_scatter);
+  m.def("conv_silu_fwd", &conv_silu_fwd);
+  m.def("conv_silu_bwd", &conv_silu_bwd);
+  m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);
+  m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);
   m.def("read_comm_errors", &read_comm_errors);
   m.def("gemm_ce_dgrad", &gemm_ce_dgrad);
   m.attr("EPI_BF16") = static_cast<int>(EPI_BF16);
