@@ -2,8 +2,15 @@
 """Headline benchmark: train tokens/s (all GPUs, max-over-ranks device time) of the dense GQA
 decoder of the benchmark configuration, at a global batch of 524,288 tokens per update.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--method M]
     torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1)
+
+Without ``--method`` (or with ``dense``) the headline configuration below runs.  ``--method``
+selects another benchmark configuration of the survey on the generic model path
+(``models.build_model``): ``gdn_hybrid_swa`` / ``kda_hybrid`` (depth 24, width 1536, 12 heads of
+128, chunk 64, sequence 4096, 524,288 tokens per update), ``nsa`` / ``moba`` (depth 24, width
+1536, 16 query heads / 1 KV group, sequence 8192) and ``moe`` (depth 16, width 2048, 16 / 4 heads,
+64 experts of FFN 1024, top-8 + 1 shared, sequence 4096, 1,048,576 tokens per update).
 
 Model: depth 20, width 1280, 10 query heads / 5 KV heads of dim 128, RoPE, RMSNorm, ReLU^2 MLP
 4x, vocab 65536, sequence 2048, on the shared shell (value embeddings, smear, backout, soft-cap
@@ -34,6 +41,20 @@ BASELINE_TOKS = None  # BASELINE.md publishes no number for this configuration
 MODEL = dict(sequence_len=2048, vocab_size=65536, n_layer=20, n_head=10, n_kv_head=5, n_embd=1280,
              window_pattern="L")
 GLOBAL_BATCH = 524288
+METHOD_CONFIGS = {
+    "gdn_hybrid_swa": (dict(method="gdn_hybrid_swa", layers=24, width=1536, heads=12, mlp_width=6144,
+                            sequence_len=4096, backend="fla_chunk64", sliding_window=2048, window_pattern="L",
+                            scale="custom"), 524288),
+    "kda_hybrid": (dict(method="kda_hybrid", layers=24, width=1536, heads=12, mlp_width=6144, sequence_len=4096,
+                        backend="fla_chunk64", window_pattern="L", scale="custom"), 524288),
+    "nsa": (dict(method="nsa", layers=24, width=1536, heads=16, kv_heads=1, mlp_width=6144, sequence_len=8192,
+                 compression_size=32, compression_stride=16, block_size=64, sparse_topk=1024, local_window=512,
+                 window_pattern="L", scale="custom"), 524288),
+    "moba": (dict(method="moba", layers=24, width=1536, heads=16, kv_heads=1, mlp_width=6144, sequence_len=8192,
+                  block_size=512, sparse_topk=1536, window_pattern="L", scale="custom"), 524288),
+    "moe": (dict(method="moe", layers=16, width=2048, heads=16, kv_heads=4, mlp_width=8192, sequence_len=4096,
+                 moe_experts=64, moe_topk=8, moe_ffn=1024, moe_shared=1, window_pattern="L", scale="custom"), 1048576),
+}
 METRIC = "train tokens/sec on 8\u00d7B200 (max over ranks) per method at matched FLOPs/token"
 
 
@@ -46,6 +67,8 @@ def parse():
     p.add_argument("--micro-batch", type=int, default=0, help="rows per micro-batch (default 32 ours / 16 reference)")
     p.add_argument("--comm", choices=("nccl", "p2p"), default="p2p",
                    help="gradient averaging of our arm on N > 1: NCCL collectives or the peer-memory kernel")
+    p.add_argument("--method", default="dense", choices=("dense", *METHOD_CONFIGS),
+                   help="benchmark configuration (default: the dense headline configuration)")
     p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
     p.add_argument("--no-e2e", action="store_true", help=argparse.SUPPRESS)
     return p.parse_args()
@@ -147,6 +170,125 @@ def count_own_kernels(step_fn):
     return n
 
 
+def timed_steps(step_fn, xs, ys, steps, world, device):
+    import torch
+    import torch.distributed as dist
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize()
+    start.record()
+    out = None
+    for _ in range(steps):
+        out = step_fn(xs, ys)
+    end.record()
+    if world > 1:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end) / steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), out
+
+
+def bench_method(args, rank, world, local, device):
+    """One survey benchmark configuration on the generic model path (ours or the reference's)."""
+    import torch
+    from nexttransformer_b200.runtime.process import shutdown
+    raw, global_batch = METHOD_CONFIGS[args.method]
+    T = raw["sequence_len"]
+    per_rank = global_batch // world
+    micro = args.micro_batch or max(1, min(8, per_rank // T))
+    accum = per_rank // (micro * T)
+    try:
+        if args.impl == "ours":
+            from nexttransformer_b200.models.lm import build_model
+            from nexttransformer_b200.optim.groups import protocol_groups
+            from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+            from nexttransformer_b200.training.engine import Trainer
+            from dataclasses import replace
+            from nexttransformer_b200.models.config import candidate_config
+            config = replace(candidate_config(raw["method"]), **{k: v for k, v in raw.items() if k != "method"})
+            model = build_model(config, device, seed=42)
+            if raw["method"] == "moe" and world > 1:
+                from nexttransformer_b200.parallel.expert import enable_expert_parallel
+                enable_expert_parallel(model)
+            shadows = {}
+            if model.fused_supported():
+                shadows = {p: s for p, s in model.fused_state().casts}
+            opt = MuonAdamW(protocol_groups(model), shadows=shadows)
+            trainer = Trainer(model, opt, accumulation=accum)
+            step_device, step_e2e = trainer.step_device, trainer.step
+        else:
+            from nexttransformer.models import build_model as ref_build
+            from nexttransformer.models.config import ModelConfig as RefConfig
+            config = RefConfig(**{k: v for k, v in raw.items() if k in RefConfig.__dataclass_fields__})
+            model = ref_build(config, device)
+            opt = model.setup_optimizer() if hasattr(model, "setup_optimizer") else None
+            if opt is None:
+                raise RuntimeError("the reference model exposes no optimizer setup")
+
+            def step_device(xs, ys):
+                tot = torch.zeros((), device=device)
+                for x, y in zip(xs, ys):
+                    loss = model(x, y)
+                    (loss / accum).backward()
+                    tot += loss.detach()
+                opt.step()
+                model.zero_grad(set_to_none=True)
+                return tot / accum
+
+            def step_e2e(xs, ys):
+                return float(step_device([x.to(device, non_blocking=True) for x in xs],
+                                         [y.to(device, non_blocking=True) for y in ys]))
+        vocab = raw.get("vocab_size", 32768)
+        dev_x, dev_y = synthetic_batches(accum, micro, T, vocab, seed=1000 + rank, device=device)
+        host_x, host_y = synthetic_batches(accum, micro, T, vocab, seed=2000 + rank, pinned=True)
+        for _ in range(args.warmup):
+            step_device(dev_x, dev_y)
+        sampler = ClockSampler(local == 0)
+        with sampler:
+            ms, loss = timed_steps(step_device, dev_x, dev_y, args.steps, world, device)
+        e2e = None
+        if not args.no_e2e:
+            ms2, _ = timed_steps(step_e2e, host_x, host_y, args.steps, world, device)
+            h2d = sum(x.numel() * x.element_size() + y.numel() * y.element_size() for x, y in zip(host_x, host_y))
+            e2e = {"value": global_batch / (ms2 / 1000.0), "unit": "tokens/s", "ms_per_step": ms2,
+                   "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4}
+        launches = None
+        if args.impl == "ours":
+            try:
+                launches = count_own_kernels(lambda: step_device(dev_x, dev_y)) * args.steps
+            except Exception:
+                launches = None
+    except (ImportError, RuntimeError, NotImplementedError, TypeError) as exc:
+        if args.impl == "reference" and rank == 0:
+            print(json.dumps({"impl": "reference", "method": args.method,
+                              "unavailable": f"{type(exc).__name__}: {exc}"[:300]}), flush=True)
+            shutdown()
+            return
+        raise
+    value = global_batch / (ms / 1000.0)
+    gpus = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(world))).split(",")
+            if x.strip().isdigit()] or list(range(world))
+    clocks = sampler.summary(set(gpus[:world]) if local == 0 else set())
+    if rank == 0:
+        par = f"dp{world}" + (f"+ep{world}" if raw["method"] == "moe" and world > 1 else "")
+        out = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+               "vs_baseline": None, "dtype": "bf16", "data": "synthetic uniform tokens, random-init weights",
+               "config": {"model": args.method, "method_config": raw, "global_batch": global_batch, "seq_len": T,
+                          "parallelism": par, "micro_batch": micro, "grad_accum": accum,
+                          "l2": "working set >> L2 (no flush needed)"},
+               "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": float(loss)}
+        if args.impl == "reference":
+            out["impl"] = "reference"
+            out.pop("gpu_launches")
+        print(json.dumps(out), flush=True)
+    del model
+    shutdown()
+
+
 def main():
     args = parse()
     import torch
@@ -170,6 +312,8 @@ def main():
     rank, world, device = initialize(seed=42, timeout_s=900)
     if device.type != "cuda":
         raise SystemExit("bench.py needs a CUDA device")
+    if args.method != "dense":
+        return bench_method(args, rank, world, local, device)
     micro = args.micro_batch or (32 if args.impl == "ours" else 16)
     T = MODEL["sequence_len"]
     per_rank = GLOBAL_BATCH // world

@@ -7,6 +7,8 @@
 #include "attention_sm100.h"
 #include "comm.h"
 #include "linear_attn.h"
+#include "delta_scan.h"
+#include "moe.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
 #include "optim.h"
@@ -370,6 +372,168 @@ void p2p_reduce_scatter(const Tensor& peers, const Tensor& pads, const Tensor& s
      "p2p_reduce_scatter");
 }
 
+// ------------------------------------------------------------------ grouped (expert) GEMM
+// k_mode false: A [M, K] (or [K, M] with a_mn), B a stack [E, N, K] (or [E, K, N] with b_mn),
+//   C [M, N]; grp int32 [ceil(M / 128)] names the expert of every 128-row tile (-1: empty).
+// k_mode true: A [K, M] / [M, K], B [K, N] / [N, K] (single matrices), C fp32 [E, M, N] accumulated
+//   (EPI_F32_ACC); grp int32 [E + 1] row offsets of each expert along K (multiples of 64).
+void gemm_grouped(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const Tensor& C, int64_t epi,
+                  const Tensor& grp, bool k_mode, const OptT& R, const OptT& P, double s_acc) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_cuda(C, "C");
+  TORCH_CHECK(grp.is_cuda() && grp.scalar_type() == at::kInt && grp.is_contiguous(), "grp must be int32 CUDA");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1 && C.stride(-1) == 1, "gemm needs unit inner stride");
+  GemmArgs g;
+  if (!k_mode) {
+    TORCH_CHECK(A.dim() == 2 && B.dim() == 3 && C.dim() == 2, "grouped-M: A 2-D, B 3-D, C 2-D");
+    g.groups = static_cast<int>(B.size(0));
+    g.M = static_cast<int>(C.size(0));
+    g.N = static_cast<int>(C.size(1));
+    TORCH_CHECK(grp.numel() >= (g.M + 127) / 128, "grp too short");
+    g.grp_m = grp.data_ptr<int>();
+    g.strideB = B.stride(0);
+  } else {
+    TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 3, "grouped-K: A 2-D, B 2-D, C 3-D");
+    TORCH_CHECK(epi == EPI_F32_ACC, "grouped-K accumulates (EPI_F32_ACC)");
+    g.groups = static_cast<int>(C.size(0));
+    g.M = static_cast<int>(C.size(1));
+    g.N = static_cast<int>(C.size(2));
+    TORCH_CHECK(grp.numel() == g.groups + 1, "grp must hold E + 1 offsets");
+    g.grp_k = grp.data_ptr<int>();
+    g.strideC = C.stride(0);
+  }
+  g.K = static_cast<int>(a_mn ? A.size(-2) : A.size(-1));
+  TORCH_CHECK((a_mn ? A.size(-1) : A.size(-2)) == g.M, "A rows != C rows");
+  TORCH_CHECK((b_mn ? B.size(-1) : B.size(-2)) == g.N, "B rows != C cols");
+  TORCH_CHECK((b_mn ? B.size(-2) : B.size(-1)) == g.K, "A/B reduction mismatch");
+  g.A = A.data_ptr();
+  g.lda = A.stride(-2);
+  g.a_mn = a_mn;
+  g.B = B.data_ptr();
+  g.ldb = B.stride(-2);
+  g.b_mn = b_mn;
+  g.C = C.data_ptr();
+  g.ldc = C.stride(-2);
+  const bool f32_out = epi == EPI_F32 || epi == EPI_F32_ACC;
+  TORCH_CHECK(C.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm output dtype does not match epilogue");
+  if (epi == EPI_RELU2_BWD) {
+    TORCH_CHECK(R.has_value() && R->defined() && R->scalar_type() == at::kBFloat16 && R->stride(-1) == 1 &&
+                    R->dim() == 2 && R->size(0) == g.M && R->size(1) == g.N,
+                "R must be bf16 [M, N]");
+    g.R = R->data_ptr();
+    g.ldr = R->stride(0);
+  }
+  if (epi == EPI_RELU2) {
+    TORCH_CHECK(P.has_value() && P->defined() && P->scalar_type() == at::kBFloat16 && P->stride(-1) == 1 &&
+                    P->dim() == 2 && P->size(0) == g.M && P->size(1) == g.N,
+                "P must be bf16 [M, N]");
+    g.P = P->data_ptr();
+    g.ldp = P->stride(0);
+  }
+  TORCH_CHECK(epi == EPI_BF16 || epi == EPI_RELU2 || epi == EPI_RELU2_BWD || epi == EPI_F32 || epi == EPI_F32_ACC,
+              "grouped GEMM epilogue");
+  g.s_acc = static_cast<float>(s_acc);
+  g.epi = static_cast<int>(epi);
+  g.num_sms = num_sms(C);
+  const c10::cuda::CUDAGuard guard(C.device());
+  nt_gemm_launch(g, stream());
+}
+
+// ------------------------------------------------------------------ peer barrier / put
+void p2p_barrier(const Tensor& pads, int64_t rank, int64_t world, int64_t epoch, double timeout_s) {
+  TORCH_CHECK(pads.is_cuda() && pads.scalar_type() == at::kLong, "pads: int64 CUDA pointer table");
+  const c10::cuda::CUDAGuard guard(pads.device());
+  ok(nt_p2p_barrier(reinterpret_cast<const uint64_t*>(pads.data_ptr<int64_t>()), static_cast<int>(rank),
+                    static_cast<int>(world), static_cast<uint32_t>(epoch), static_cast<uint64_t>(timeout_s * 1e9),
+                    stream()),
+     "p2p_barrier");
+}
+
+void p2p_put(const Tensor& peers, int64_t world, int64_t dst_off, const Tensor& src) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "src must be contiguous CUDA");
+  const c10::cuda::CUDAGuard guard(src.device());
+  ok(nt_p2p_put(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), static_cast<int>(world), dst_off,
+                src.data_ptr(), src.numel() * src.element_size(), stream()),
+     "p2p_put");
+}
+
+// ------------------------------------------------------------------ MoE row movement
+void check_i32(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), name, " must be contiguous int32 CUDA");
+}
+
+void moe_gather_rows(const Tensor& src, const Tensor& src_of, const Tensor& out) {
+  check_rows(src, "src");
+  check_rows(out, "out");
+  check_i32(src_of, "src_of");
+  TORCH_CHECK(src_of.numel() == out.size(0) && src.size(-1) == out.size(-1), "gather shapes");
+  const c10::cuda::CUDAGuard guard(out.device());
+  ok(nt_moe_gather_rows(src.data_ptr(), src_of.data_ptr<int>(), out.data_ptr(), out.size(0), out.size(-1), stream()),
+     "moe_gather_rows");
+}
+
+void moe_combine(const Tensor& rows, const Tensor& row_of, const OptT& w, const OptT& add, const Tensor& out) {
+  check_rows(rows, "rows");
+  check_rows(out, "out");
+  check_i32(row_of, "row_of");
+  const int T = static_cast<int>(out.size(0)), k = static_cast<int>(row_of.numel() / std::max<int64_t>(1, out.size(0)));
+  const float* wp = nullptr;
+  if (w.has_value() && w->defined()) {
+    TORCH_CHECK(w->scalar_type() == at::kFloat && w->is_contiguous() && w->numel() == row_of.numel(), "w: fp32 [T, k]");
+    wp = w->data_ptr<float>();
+  }
+  const void* ap = nullptr;
+  if (add.has_value() && add->defined()) {
+    check_rows(*add, "add");
+    ap = add->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(out.device());
+  ok(nt_moe_combine(rows.data_ptr(), row_of.data_ptr<int>(), wp, ap, out.data_ptr(), T, k,
+                    static_cast<int>(out.size(-1)), stream()),
+     "moe_combine");
+}
+
+void moe_combine_bwd(const Tensor& dy, const Tensor& rows, const Tensor& row_of, const Tensor& w, const Tensor& d_rows,
+                     const Tensor& dw) {
+  check_rows(dy, "dy");
+  check_rows(rows, "rows");
+  check_rows(d_rows, "d_rows");
+  check_i32(row_of, "row_of");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && dw.scalar_type() == at::kFloat && w.is_contiguous() && dw.is_contiguous(),
+              "w / dw fp32");
+  const int T = static_cast<int>(dy.size(0)), k = static_cast<int>(row_of.numel() / std::max<int64_t>(1, dy.size(0)));
+  const c10::cuda::CUDAGuard guard(dy.device());
+  ok(nt_moe_combine_bwd(dy.data_ptr(), rows.data_ptr(), row_of.data_ptr<int>(), w.data_ptr<float>(), d_rows.data_ptr(),
+                        dw.data_ptr<float>(), T, k, static_cast<int>(dy.size(-1)), stream()),
+     "moe_combine_bwd");
+}
+
+void moe_pull_rows(const Tensor& peers, const Tensor& src_rank, const Tensor& src_row, const Tensor& out) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
+  check_i32(src_rank, "src_rank");
+  check_i32(src_row, "src_row");
+  check_rows(out, "out");
+  const c10::cuda::CUDAGuard guard(out.device());
+  ok(nt_moe_pull_rows(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), src_rank.data_ptr<int>(),
+                      src_row.data_ptr<int>(), out.data_ptr(), out.size(0), static_cast<int>(out.size(-1)), stream()),
+     "moe_pull_rows");
+}
+
+void moe_push_rows(const Tensor& rows, const Tensor& peers, const Tensor& dst_rank, const Tensor& dst_row) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
+  check_i32(dst_rank, "dst_rank");
+  check_i32(dst_row, "dst_row");
+  check_rows(rows, "rows");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  ok(nt_moe_push_rows(rows.data_ptr(), reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                      dst_rank.data_ptr<int>(), dst_row.data_ptr<int>(), rows.size(0), static_cast<int>(rows.size(-1)),
+                      stream()),
+     "moe_push_rows");
+}
+
 // ------------------------------------------------------------------ linear-attention elementwise
 void conv_silu_fwd(const Tensor& x, const Tensor& w, const Tensor& y, const OptT& pre) {
   check_rows(x, "x");
@@ -412,6 +576,56 @@ void gated_rmsnorm_bwd(const Tensor& x, const Tensor& g, const Tensor& gain, con
      "gated_rmsnorm_bwd");
 }
 
+// ------------------------------------------------------------------ delta-rule chunk scan
+void check_chunks(const Tensor& t, int64_t cols, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous() && t.dim() == 4 &&
+                  t.size(-1) == cols,
+              name, " must be a contiguous bf16 CUDA tensor [BH, N, rows, ", cols, "]");
+}
+
+void delta_scan_fwd(const Tensor& w, const Tensor& qt, const Tensor& kc, const Tensor& aqk, const Tensor& u0,
+                    const Tensor& carry, const Tensor& o, const Tensor& states, const Tensor& u) {
+  for (auto* t : {&w, &qt, &kc, &u0, &o, &u}) check_chunks(*t, 128, "delta scan operand");
+  check_chunks(aqk, 64, "aqk");
+  check_chunks(states, 128, "states");
+  TORCH_CHECK(w.size(2) == 64 && states.size(2) == 128, "chunk length 64, state 128 x 128");
+  TORCH_CHECK(carry.scalar_type() == at::kFloat && carry.is_contiguous() && carry.numel() == w.size(0) * w.size(1) * 128,
+              "carry must be contiguous fp32 [BH, N, 128]");
+  DeltaScanFwdArgs a;
+  a.BH = static_cast<int>(w.size(0));
+  a.N = static_cast<int>(w.size(1));
+  a.w = w.data_ptr(); a.qt = qt.data_ptr(); a.kc = kc.data_ptr(); a.aqk = aqk.data_ptr(); a.u0 = u0.data_ptr();
+  a.carry = carry.data_ptr<float>();
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.states = reinterpret_cast<__nv_bfloat16*>(states.data_ptr());
+  a.u = reinterpret_cast<__nv_bfloat16*>(u.data_ptr());
+  const c10::cuda::CUDAGuard guard(w.device());
+  ok(nt_delta_scan_fwd(a, stream()), "delta_scan_fwd");
+}
+
+void delta_scan_bwd(const Tensor& dout, const Tensor& w, const Tensor& qt, const Tensor& kc, const Tensor& aqk,
+                    const Tensor& carry, const Tensor& states, const Tensor& ds, const Tensor& dut,
+                    const Tensor& dcarry) {
+  for (auto* t : {&dout, &w, &qt, &kc}) check_chunks(*t, 128, "delta scan operand");
+  check_chunks(aqk, 64, "aqk");
+  check_chunks(dut, 64, "du^T");
+  check_chunks(states, 128, "states");
+  check_chunks(ds, 128, "dS");
+  TORCH_CHECK(carry.scalar_type() == at::kFloat && dcarry.scalar_type() == at::kFloat && dcarry.is_contiguous(),
+              "carry / dcarry are fp32");
+  DeltaScanBwdArgs a;
+  a.BH = static_cast<int>(w.size(0));
+  a.N = static_cast<int>(w.size(1));
+  a.dout = dout.data_ptr(); a.w = w.data_ptr(); a.qt = qt.data_ptr(); a.kc = kc.data_ptr(); a.aqk = aqk.data_ptr();
+  a.carry = carry.data_ptr<float>();
+  a.states = reinterpret_cast<const __nv_bfloat16*>(states.data_ptr());
+  a.ds = reinterpret_cast<__nv_bfloat16*>(ds.data_ptr());
+  a.dut = reinterpret_cast<__nv_bfloat16*>(dut.data_ptr());
+  a.dcarry = dcarry.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(w.device());
+  ok(nt_delta_scan_bwd(a, stream()), "delta_scan_bwd");
+}
+
 std::vector<int64_t> read_comm_errors() {
   unsigned w = 0;
   const int c = nt_comm_read_error(&w);
@@ -423,7 +637,9 @@ std::vector<int64_t> read_errors() {
   const int g = nt_gemm_read_error(&w);
   unsigned wa = 0;
   const int a = nt_attention_read_error(&wa);
-  return {g, static_cast<int64_t>(w), a, static_cast<int64_t>(wa)};
+  unsigned wd = 0;
+  const int d = nt_delta_scan_read_error(&wd);
+  return {g, static_cast<int64_t>(w), a, static_cast<int64_t>(wa), d, static_cast<int64_t>(wd)};
 }
 
 }  // namespace
@@ -454,6 +670,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ce_fwd", &gemm_ce_fwd);
   m.def("p2p_reduce_scatter", &p2p_reduce_scatter);
   m.def("conv_silu_fwd", &conv_silu_fwd);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_gather_rows", &moe_gather_rows);
+  m.def("p2p_barrier", &p2p_barrier);
+  m.def("p2p_put", &p2p_put);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine_bwd", &moe_combine_bwd);
+  m.def("moe_pull_rows", &moe_pull_rows);
+  m.def("moe_push_rows", &moe_push_rows);
+  m.def("delta_scan_fwd", &delta_scan_fwd);
+  m.def("delta_scan_bwd", &delta_scan_bwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);
   m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);

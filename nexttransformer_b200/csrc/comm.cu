@@ -84,8 +84,43 @@ __global__ void __launch_bounds__(256) p2p_reduce_scatter_kernel(const uint64_t*
   peer_barrier(pads, rank, world, 1, epoch, timeout_ns, 0x900u);
 }
 
+// A standalone barrier with every peer (one block; region 0 of the pads, `world` slots).
+__global__ void p2p_barrier_kernel(const uint64_t* __restrict__ pads, int rank, int world, uint32_t epoch,
+                                   uint64_t timeout_ns) {
+  peer_barrier(pads, rank, world, 0, epoch, timeout_ns, 0xA00u);
+}
+
+// Copy n16 16-byte words from src to byte offset dst_off of every peer's buffer (plain peer stores).
+__global__ void p2p_put_kernel(const uint64_t* __restrict__ peers, int world, int64_t dst_off,
+                               const uint4* __restrict__ src, int64_t n16) {
+  for (int p = 0; p < world; ++p) {
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers[p]) + dst_off);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      dst[i] = src[i];
+  }
+}
+
 }  // namespace comm
 }  // namespace nt
+
+int nt_p2p_barrier(const uint64_t* pads_dev, int rank, int world, uint32_t epoch, uint64_t timeout_ns,
+                   cudaStream_t stream) {
+  if (world < 1 || world > 64 || rank < 0 || rank >= world) return -1;
+  nt::comm::p2p_barrier_kernel<<<1, 64, 0, stream>>>(pads_dev, rank, world, epoch, timeout_ns);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int nt_p2p_put(const uint64_t* peers_dev, int world, int64_t dst_off, const void* src, int64_t nbytes,
+               cudaStream_t stream) {
+  if (world < 1 || nbytes % 16 || dst_off % 16 || reinterpret_cast<uintptr_t>(src) % 16) return -1;
+  const int64_t n16 = nbytes / 16;
+  if (!n16) return 0;
+  const int blocks = static_cast<int>(n16 / 256 + 1 < 64 ? n16 / 256 + 1 : 64);
+  nt::comm::p2p_put_kernel<<<blocks, 256, 0, stream>>>(peers_dev, world, dst_off, reinterpret_cast<const uint4*>(src),
+                                                       n16);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
 
 int nt_p2p_reduce_scatter(const uint64_t* peers_dev, const uint64_t* pads_dev, const int64_t* seg_off,
                           const int64_t* seg_len, int nseg, int rank, int world, float scale, uint32_t epoch,

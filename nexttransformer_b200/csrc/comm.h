@@ -10,4 +10,10 @@
 int nt_p2p_reduce_scatter(const uint64_t* peers_dev, const uint64_t* pads_dev, const int64_t* seg_off,
                           const int64_t* seg_len, int nseg, int rank, int world, float scale, uint32_t epoch,
                           int blocks, uint64_t timeout_ns, cudaStream_t stream);
+// Barrier with every peer (bounded wait; needs `world` 32-bit signal-pad slots; epoch as above).
+int nt_p2p_barrier(const uint64_t* pads_dev, int rank, int world, uint32_t epoch, uint64_t timeout_ns,
+                   cudaStream_t stream);
+// Copy nbytes (multiple of 16) from local src to byte offset dst_off of every peer's buffer.
+int nt_p2p_put(const uint64_t* peers_dev, int world, int64_t dst_off, const void* src, int64_t nbytes,
+               cudaStream_t stream);
 int nt_comm_read_error(unsigned* where);

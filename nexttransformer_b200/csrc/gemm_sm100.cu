@@ -70,7 +70,34 @@ struct Params {
   int64_t strideSplit; // elements between the partial-output slices of the workspace
   CeArgs ce;           // cross-entropy epilogues only
   int tma_out;         // 1: bf16 outputs leave through shared memory and bulk tensor stores
+  // Grouped (expert) modes.  grp_m: per 128-row tile of A/C, the batch index of B (-1: no work);
+  // A and C unbatched.  grp_k: per batch of C, the row range [grp_k[b], grp_k[b+1]) of the
+  // reduction dimension (multiples of 64); A and B unbatched.
+  const int* grp_m;
+  const int* grp_k;
 };
+
+struct TileWork {
+  int zA, zB, zC, kb_lo, kb_hi;
+};
+// Batch coordinates of the three operands and the k-block range of one tile; false = no work.
+NT_DEVICE bool tile_work(const Params& p, int b, int mb, int ks, int num_kb, TileWork& w) {
+  w.zA = w.zB = w.zC = b;
+  w.kb_lo = ks * p.kb_per_split;
+  w.kb_hi = min(num_kb, w.kb_lo + p.kb_per_split);
+  if (p.grp_m) {
+    w.zA = w.zC = 0;
+    w.zB = p.grp_m[mb];
+    return w.zB >= 0;
+  }
+  if (p.grp_k) {
+    w.zA = w.zB = 0;
+    w.kb_lo = p.grp_k[b] / BK;
+    w.kb_hi = p.grp_k[b + 1] / BK;
+    return w.kb_hi > w.kb_lo;
+  }
+  return true;
+}
 
 NT_DEVICE void tile_coords(int t, const Params& p, int& b, int& mb, int& nb, int& ks) {
   const int per_slice = p.tiles_m * p.tiles_n;
@@ -435,8 +462,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         int b, mb, nb, ks;
         tile_coords(t, p, b, mb, nb, ks);
+        TileWork tw;
+        if (!tile_work(p, b, mb, ks, num_kb, tw)) continue;
         const int m0 = mb * BM, n0 = nb * BN;
-        const int kb_lo = ks * p.kb_per_split, kb_hi = min(num_kb, kb_lo + p.kb_per_split);
+        const int kb_lo = tw.kb_lo, kb_hi = tw.kb_hi;
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, 0x100u + stage, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
@@ -444,16 +473,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           mbar_expect_tx(&full[stage], S::STAGE_BYTES);
           const int k0 = kb * BK;
           if constexpr (A_MN == 0) {
-            tma_load_3d(sA, &tmA, &full[stage], k0, m0, b);
+            tma_load_3d(sA, &tmA, &full[stage], k0, m0, tw.zA);
           } else {
-            tma_load_3d(sA, &tmA, &full[stage], m0, k0, b);
-            tma_load_3d(sA + 8192, &tmA, &full[stage], m0 + 64, k0, b);
+            tma_load_3d(sA, &tmA, &full[stage], m0, k0, tw.zA);
+            tma_load_3d(sA + 8192, &tmA, &full[stage], m0 + 64, k0, tw.zA);
           }
           if constexpr (B_MN == 0) {
-            tma_load_3d(sB, &tmB, &full[stage], k0, n0, b);
+            tma_load_3d(sB, &tmB, &full[stage], k0, n0, tw.zB);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, b);
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, tw.zB);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -477,14 +506,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int local = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        int tb, tmb, tnb, tks;
+        tile_coords(t, p, tb, tmb, tnb, tks);
+        TileWork tw;
+        if (!tile_work(p, tb, tmb, tks, num_kb, tw)) { --local; continue; }
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, 0x200u + acc, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int tb, tmb, tnb, tks;
-        tile_coords(t, p, tb, tmb, tnb, tks);
-        const int kb_lo = tks * p.kb_per_split, kb_hi = min(num_kb, kb_lo + p.kb_per_split);
+        const int kb_lo = tw.kb_lo, kb_hi = tw.kb_hi;
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, 0x300u + stage, abort_flag)) { ok = false; break; }
           tc_fence_after();
@@ -519,13 +550,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int g = 0;
         int local = 0;
         for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+          int b, mb, nb, ks;
+          tile_coords(t, p, b, mb, nb, ks);
+          TileWork tw;
+          if (!tile_work(p, b, mb, ks, num_kb, tw)) { --local; continue; }
+          b = tw.zC;
           const int acc = local & 1;
           const uint32_t acc_phase = (local >> 1) & 1;
           if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
           __syncwarp();
           tc_fence_after();
-          int b, mb, nb, ks;
-          tile_coords(t, p, b, mb, nb, ks);
           const int row0 = mb * BM + quad * 32;
           const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -572,13 +606,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int g = 0;
         int local = 0;
         for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+          int b, mb, nb, ks;
+          tile_coords(t, p, b, mb, nb, ks);
+          TileWork tw;
+          if (!tile_work(p, b, mb, ks, num_kb, tw)) { --local; continue; }
+          b = tw.zC;
           const int acc = local & 1;
           const uint32_t acc_phase = (local >> 1) & 1;
           if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
           __syncwarp();
           tc_fence_after();
-          int b, mb, nb, ks;
-          tile_coords(t, p, b, mb, nb, ks);
           const int row = mb * BM + row_in_tile;
           const int row0 = mb * BM + quad * 32;
           const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
@@ -632,13 +669,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (!(bf16_out<EPI>() || EPI == EPI_F32 || EPI == EPI_F32_ACC) || !p.tma_out) {
       int local = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        int b, mb, nb, ks;
+        tile_coords(t, p, b, mb, nb, ks);
+        TileWork tw;
+        if (!tile_work(p, b, mb, ks, num_kb, tw)) { --local; continue; }
+        b = tw.zC;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
         __syncwarp();
         tc_fence_after();
-        int b, mb, nb, ks;
-        tile_coords(t, p, b, mb, nb, ks);
         const int row = mb * BM + row_in_tile;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
         if constexpr (EPI == EPI_CE_FWD) {
@@ -794,12 +834,18 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   using S = Smem<BN, STAGES>;
   // A: logical [M, K].  K-major storage [M rows, K cols] (inner = K); M-major [K rows, M cols].
-  CUtensorMap ta = A_MN == 0 ? make_map(g.A, g.K, g.M, g.lda, g.batch, g.strideA, BM)
-                             : make_map(g.A, g.M, g.K, g.lda, g.batch, g.strideA, BK);
-  CUtensorMap tb = B_MN == 0 ? make_map(g.B, g.K, g.N, g.ldb, g.batch, g.strideB, BN)
-                             : make_map(g.B, g.N, g.K, g.ldb, g.batch, g.strideB, BK);
+  const bool grouped = g.grp_m || g.grp_k;
+  const int bA = grouped ? 1 : g.batch;
+  const int bB = g.grp_m ? g.groups : (g.grp_k ? 1 : g.batch);
+  const int bC = g.grp_m ? 1 : (g.grp_k ? g.groups : g.batch);
+  CUtensorMap ta = A_MN == 0 ? make_map(g.A, g.K, g.M, g.lda, bA, g.strideA, BM)
+                             : make_map(g.A, g.M, g.K, g.lda, bA, g.strideA, BK);
+  CUtensorMap tb = B_MN == 0 ? make_map(g.B, g.K, g.N, g.ldb, bB, g.strideB, BN)
+                             : make_map(g.B, g.N, g.K, g.ldb, bB, g.strideB, BK);
   Params p;
-  p.M = g.M; p.N = g.N; p.K = g.K; p.batch = g.batch;
+  p.M = g.M; p.N = g.N; p.K = g.K; p.batch = bC;
+  p.grp_m = g.grp_m;
+  p.grp_k = g.grp_k;
   p.tiles_m = (g.M + BM - 1) / BM;
   p.tiles_n = (g.N + BN - 1) / BN;
   p.epi = EPI;
@@ -820,13 +866,13 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   CUtensorMap tc = ta, tp = ta;  // placeholders when the direct epilogue runs
   p.tma_out = 0;
   if (bf16_out<EPI>() && p.split == 1 && g.tma_out_ok) {
-    bool ok = out_map(tc, g.C, g.N, g.M, g.ldc, g.batch, g.strideC);
-    if (EPI == EPI_RELU2) ok = ok && out_map(tp, g.P, g.N, g.M, g.ldp, g.batch, g.strideP);
+    bool ok = out_map(tc, g.C, g.N, g.M, g.ldc, bC, g.strideC);
+    if (EPI == EPI_RELU2) ok = ok && out_map(tp, g.P, g.N, g.M, g.ldp, bC, g.strideP);
     p.tma_out = ok ? 1 : 0;
   }
   if ((EPI == EPI_F32 || EPI == EPI_F32_ACC) && g.tma_out_ok) {
     const bool ok = p.split > 1 ? out_map_f32(tc, p.C, g.N, g.M, p.ldc, p.split, p.strideSplit)
-                                : out_map_f32(tc, g.C, g.N, g.M, g.ldc, g.batch, g.strideC);
+                                : out_map_f32(tc, g.C, g.N, g.M, g.ldc, bC, g.strideC);
     p.tma_out = ok ? 1 : 0;
   }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
@@ -902,8 +948,13 @@ void nt_gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
   using namespace nt::gemm;
   GemmArgs g = g_in;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return;
+  if (g.grp_m || g.grp_k) {
+    if (g.groups <= 0 || (g.grp_m && g.grp_k) || (g.grp_k && g.epi != EPI_F32_ACC))
+      throw std::runtime_error("grouped GEMM: one table, groups > 0, and EPI_F32_ACC for grp_k");
+    g.batch = g.grp_k ? g.groups : 1;
+  }
   g.split_k = 1;
-  const int split = choose_split(g);
+  const int split = (g.grp_m || g.grp_k) ? 1 : choose_split(g);
   if (split > 1 && g.workspace && g.workspace_bytes >= static_cast<size_t>(split) * g.M * g.N * sizeof(float))
     g.split_k = split;
   // BN = 256 halves B-operand shared-memory traffic per MMA (128-wide tiles are bound by

@@ -62,6 +62,15 @@ struct GemmArgs {
   // bf16 outputs leave through shared memory and bulk tensor stores when the layout allows it
   // (16-byte aligned base and row stride); 0 forces per-thread global stores.
   int tma_out_ok = 1;
+  // Grouped (expert) modes, at most one set; device tables, so the host never reads the counts.
+  //  grp_m [ceil(M/128)]: batch index of B for each 128-row tile of A and C (-1: tile has no
+  //        rows); A and C are single matrices, B is a stack of `groups` matrices (strideB).
+  //  grp_k [groups + 1]: row offsets (multiples of 64) of each group along the reduction
+  //        dimension; A and B are single matrices, C a stack of `groups` (strideC).  Groups with
+  //        no rows leave C untouched, so only EPI_F32_ACC is allowed.
+  const int* grp_m = nullptr;
+  const int* grp_k = nullptr;
+  int groups = 0;
 };
 
 // Bytes of workspace nt_gemm_launch would use for split-K on this problem (0 = no split).

@@ -67,13 +67,18 @@ def recurrent_scan(q, k, v, *, kind, decay=None, beta=None, initial_state=None, 
         else:
             S = initial_state
     outs = []
+    # per-token views through unbind: its backward stacks the token gradients once (indexing
+    # q[:, t] would add T full-size gradient buffers, a cost quadratic in T)
+    qs, ks, vs = q.unbind(1), k.unbind(1), v.unbind(1)
+    ds = decay.unbind(1) if decay is not None else None
+    bs = beta.unbind(1) if beta is not None else None
     for t in range(T):
-        qt, kt, vt = q[:, t], k[:, t], v[:, t]
+        qt, kt, vt = qs[t], ks[t], vs[t]
         if decay is not None:
-            S = S * decay[:, t].to(q).unsqueeze(-1)
+            S = S * ds[t].to(q).unsqueeze(-1)
         if kind in ("deltanet", "kda"):
             pred = torch.einsum("bhd,bhde->bhe", kt, S)
-            S = S + kt.unsqueeze(-1) * ((vt - pred) * beta[:, t].to(q).unsqueeze(-1)).unsqueeze(-2)
+            S = S + kt.unsqueeze(-1) * ((vt - pred) * bs[t].to(q).unsqueeze(-1)).unsqueeze(-2)
         else:
             S = S + kt.unsqueeze(-1) * vt.unsqueeze(-2)
         o = torch.einsum("bhd,bhde->bhe", qt, S)
@@ -98,13 +103,16 @@ def _tril(C, device, strict=False):
     return torch.ones(C, C, dtype=torch.bool, device=device).tril(-1 if strict else 0)
 
 
-def _delta_chunks(q, k, v, g, beta, C, per_feature):
-    """Gated delta rule over chunks.  g: log decay per token (per head [..,C] or per feature [..,C,D]).
+def _delta_terms(q, k, v, g, beta, C, per_feature):
+    """Per-chunk terms of the gated delta rule.  g: log decay per token (per head [..,C] or per
+    feature [..,C,D]).
 
     Inside chunk n with cumulative log decay b_i (<= 0 increments):
       (I + strict_tril(beta_i k~_i . k^_j)) [w | u0] = beta [k~ | v],   k~ = k e^{b}, k^ = k e^{-b}
+    and the scan below runs
       u = u0 - w S,   o = (q e^{b}) S + tril((q e^{b}) . k^) u,   S <- e^{b_C} S + (k e^{b_C - b})^T u
     (per-head gates use pairwise e^{b_i - b_j} <= 1 directly, so no factor can overflow).
+    Returns (w, u0, qt, kc, aqk, carry) with carry None (no decay), [..,N,1,1] or [..,N,D,1].
     """
     causal = _tril(C, q.device)
     wgt = beta[..., None]
@@ -133,7 +141,12 @@ def _delta_chunks(q, k, v, g, beta, C, per_feature):
     rhs = torch.cat((wgt * kt, wgt * v), -1)
     sol = torch.linalg.solve_triangular(wgt * akk, rhs, upper=False, unitriangular=True)
     w, u0 = sol.split((k.shape[-1], v.shape[-1]), -1)
-    N = q.shape[2]
+    return w, u0, qt, kc, aqk, carry
+
+
+def _delta_scan(w, u0, qt, kc, aqk, carry):
+    """The sequential part over chunks (state S [Dk, Dv] carried in the input dtype)."""
+    N = qt.shape[2]
     S = None
     outs = []
     for n in range(N):
@@ -151,6 +164,11 @@ def _delta_chunks(q, k, v, g, beta, C, per_feature):
         else:
             S = (S if carry is None else S * carry[:, :, n]) + upd
     return torch.stack(outs, 2)
+
+
+def _delta_chunks(q, k, v, g, beta, C, per_feature):
+    """Gated delta rule over chunks: the per-chunk terms, then the scan."""
+    return _delta_scan(*_delta_terms(q, k, v, g, beta, C, per_feature))
 
 
 def _scalar_decay_chunks(q, k, v, g, C):

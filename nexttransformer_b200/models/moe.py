@@ -8,8 +8,9 @@ exactly the reference's normalised top-k softmax, ``nexttransformer/scaling/refe
 towards balance (sign of mean load minus expert load), as in aux-loss-free load balancing.
 
 Execution: tokens are sorted by expert and each expert runs on its contiguous slice (grouped
-execution); with an expert-parallel group set (``parallel.expert``) tokens are exchanged with
-all-to-all before and after the experts.
+execution).  On CUDA all experts run in one grouped GEMM per projection (``ops.moe``); on the CPU
+each expert runs on its slice in turn.  With an expert-parallel group set (``parallel.expert``)
+tokens are exchanged between the ranks before and after the experts.
 """
 import torch
 from torch import nn
@@ -41,6 +42,7 @@ class MoEFFN(nn.Module):
         self.register_buffer("load", torch.zeros(num_experts), persistent=False)
         self.ep_group = None       # set by parallel.expert.enable_expert_parallel (None = world group)
         self.ep_size = 1
+        self.ep_exchange = "peer"  # "peer": NVLink peer-memory exchange on CUDA; "nccl": all-to-all
         self.last_stats = {}
 
     def route(self, rows):
@@ -58,8 +60,16 @@ class MoEFFN(nn.Module):
             self.load += torch.bincount(choice.flatten(), minlength=self.num_experts).float()
         out = self.shared(rows) if self.shared is not None else torch.zeros_like(rows)
         if self.ep_size > 1:
-            from nexttransformer_b200.parallel.expert import expert_parallel_combine
-            routed = expert_parallel_combine(self, rows, choice, w)
+            from nexttransformer_b200.parallel import expert as ep
+            if ep.peer_exchange_supported(self, rows) and self.ep_exchange == "peer":
+                routed = ep.peer_expert_combine(self, rows, choice, w)
+            else:
+                routed = ep.expert_parallel_combine(self, rows, choice, w)
+        elif rows.is_cuda and rows.shape[-1] % 64 == 0 and self.experts[0].c_fc.weight.shape[0] % 64 == 0:
+            from nexttransformer_b200.ops.moe import grouped_experts
+            w_fc = torch.stack([e.c_fc.weight for e in self.experts])
+            w_proj = torch.stack([e.c_proj.weight for e in self.experts])
+            routed = grouped_experts(rows, choice, w, w_fc, w_proj)
         else:
             routed = self.local_experts(rows, choice, w)
         out = out + routed

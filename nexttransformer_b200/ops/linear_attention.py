@@ -74,11 +74,78 @@ def gated_rms_norm(y, gate, gain):
     return _GatedRMSNorm.apply(y, gate, gain)
 
 
+class _DeltaScan(Function):
+    """The inter-chunk scan on the sm_100a kernels; inputs [B, H, N, 64, 128|64] (fp32 or bf16),
+    carry [B, H, N, 128].  The per-chunk gradient products run as batched GEMMs on the engine."""
+
+    @staticmethod
+    def forward(ctx, w, u0, qt, kc, aqk, carry):
+        B, H, N = w.shape[:3]
+        BH = B * H
+
+        def bf(t):
+            return t.reshape(BH, N, *t.shape[3:]).to(torch.bfloat16).contiguous()
+        wb, u0b, qtb, kcb, aqkb = bf(w), bf(u0), bf(qt), bf(kc), bf(aqk)
+        cb = carry.reshape(BH, N, 128).float().contiguous()
+        o = torch.empty_like(u0b)
+        u = torch.empty_like(u0b)
+        states = torch.empty(BH, N, 128, 128, device=w.device, dtype=torch.bfloat16)
+        ext().delta_scan_fwd(wb, qtb, kcb, aqkb, u0b, cb, o, states, u)
+        ctx.save_for_backward(wb, qtb, kcb, aqkb, cb, states, u)
+        ctx.shape = (B, H, N)
+        return o.reshape(B, H, N, 64, 128)
+
+    @staticmethod
+    def backward(ctx, do):
+        from nexttransformer_b200.ops.gemm import EPI_F32, gemm
+        wb, qtb, kcb, aqkb, cb, states, u = ctx.saved_tensors
+        B, H, N = ctx.shape
+        BH = B * H
+        dob = do.reshape(BH, N, 64, 128).to(torch.bfloat16).contiguous()
+        ds = torch.empty_like(states)
+        dut = torch.empty(BH, N, 128, 64, device=do.device, dtype=torch.bfloat16)
+        dcarry = torch.empty_like(cb)
+        ext().delta_scan_bwd(dob, wb, qtb, kcb, aqkb, cb, states, ds, dut, dcarry)
+        M = BH * N
+
+        def f32(rows, cols):
+            return torch.empty(M, rows, cols, device=do.device, dtype=torch.float32)
+        flat = lambda t: t.reshape(M, *t.shape[2:])
+        dqt = gemm(flat(dob), flat(states), f32(64, 128), epi=EPI_F32)                # do S^T
+        dw = gemm(flat(dut), flat(states), f32(64, 128), a_mn=True, epi=EPI_F32, s_acc=-1.0)   # -du S^T
+        daqk = gemm(flat(dob), flat(u), f32(64, 64), epi=EPI_F32)                     # do u^T
+        dkc = gemm(flat(u), flat(ds), f32(64, 128), epi=EPI_F32)                      # u dS^T
+        du0 = dut.transpose(-1, -2).float()
+        shp = (B, H, N, 64)
+        return (dw.reshape(*shp, 128), du0.reshape(*shp, 128), dqt.reshape(*shp, 128), dkc.reshape(*shp, 128),
+                daqk.reshape(*shp, 64), dcarry.reshape(B, H, N, 128))
+
+
+def scan_supported(q, v, chunk):
+    return q.is_cuda and chunk == 64 and q.shape[-1] == 128 and v.shape[-1] == 128
+
+
 def delta_chunk_cuda(q, k, v, *, kind, g=None, beta=None, chunk, qk_l2norm_scale=None):
-    from nexttransformer_b200.models.linear import chunk_scan
+    """Chunked (gated) delta rule on CUDA: q, k, v [B, T, H, 128]; g log decay (GDN [B, T, H],
+    KDA [B, T, H, 128]); beta [B, T, H].  The per-chunk WY terms are formed in fp32 with torch
+    (triangular solve included), the scan runs on the sm_100a kernels."""
+    from nexttransformer_b200.models.linear import _chunked, _delta_scan, _delta_terms
     dt = q.dtype
+    T = q.shape[1]
+    q, k, v = q.float(), k.float(), v.float()
     if qk_l2norm_scale is not None:
-        q, k = F.normalize(q.float(), dim=-1) * qk_l2norm_scale, F.normalize(k.float(), dim=-1)
-    out = chunk_scan(q.float(), k.float(), v.float(), kind=kind, g=None if g is None else g.float(),
-                     beta=None if beta is None else beta.float(), chunk=chunk)
-    return out.to(dt)
+        q, k = F.normalize(q, dim=-1) * qk_l2norm_scale, F.normalize(k, dim=-1)
+    qc, kc_, vc = (_chunked(x, chunk) for x in (q, k, v))
+    gc = None if g is None else _chunked(g.float(), chunk)
+    w, u0, qt, kc, aqk, carry = _delta_terms(qc, kc_, vc, gc, _chunked(beta.float(), chunk), chunk,
+                                             per_feature=(kind == "kda"))
+    if scan_supported(q, v, chunk):
+        B, H, N = w.shape[:3]
+        if carry is None:
+            carry = w.new_ones(B, H, N, 128)
+        else:
+            carry = carry.squeeze(-1).expand(B, H, N, 128)
+        out = _DeltaScan.apply(w, u0, qt, kc, aqk, carry)
+    else:
+        out = _delta_scan(w, u0, qt, kc, aqk, carry)
+    return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)

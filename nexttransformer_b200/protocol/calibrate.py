@@ -22,6 +22,7 @@ import torch
 from nexttransformer_b200.models.config import CHUNK_BACKENDS, LINEAR, LOOPED, candidate_config
 from nexttransformer_b200.models.looped import huginn_depth
 from nexttransformer_b200.models.registry import PLUGIN_METHODS
+from nexttransformer_b200.protocol import fingerprint
 from nexttransformer_b200.protocol.compute import FORMULA_VERSION, audit_graph
 from nexttransformer_b200.protocol.spec import Protocol, config_file, write_config
 
@@ -79,8 +80,11 @@ def method_cost(c):
     """(flops per input token, proof record) of one configuration."""
     p = Protocol()
     records, weighted = [], 0
+    executed = set()
     for stage, depth, steps in stages(c):
-        r = full_cost(c, stage, depth)
+        with fingerprint.traced() as ran:
+            r = full_cost(c, stage, depth)
+        executed |= ran
         if r["unknown"]:
             raise RuntimeError(f"uncovered floating operators: {r['unknown']}")
         records.append(dict(stage=stage, depth=depth, optimizer_steps=steps,
@@ -89,36 +93,115 @@ def method_cost(c):
         weighted += steps * r["total"]
     proof = dict(method=c.method, model_hash=c.fingerprint, protocol_hash=p.fingerprint,
                  formula_version=FORMULA_VERSION, torch=torch.__version__, total_training_flops=weighted,
-                 flops_per_token=weighted / p.total_tokens, stages=records, unknown={})
+                 flops_per_token=weighted / p.total_tokens, stages=records, unknown={},
+                 method_source=fingerprint.record(executed))
     return weighted / p.total_tokens, proof
 
 
-def search(c, anchor, tolerance=.01):
-    """Closest registered configuration to the anchor: FFN width on the 3d..5d grid (step 128)."""
-    best = (abs(method_cost(c)[0] / anchor - 1), c)
-    if best[0] <= tolerance:
-        return best[1]
-    lo, hi = 3 * c.width, 5 * c.width
-    for width in range(lo - lo % 128 + (128 if lo % 128 else 0), hi + 1, 128):
-        cand = replace(c, mlp_width=width)
-        err = abs(method_cost(cand)[0] / anchor - 1)
-        if err < best[0]:
-            best = (err, cand)
-    return best[1]
+def ffn_slope(c):
+    """d(FLOPs per token)/d(FFN width) from the exact difference of two short-length audits per stage."""
+    other = replace(c, mlp_width=c.mlp_width + 128)
+    chunk = CHUNK_BACKENDS.get(c.backend)
+    first, second = (16, 32) if chunk is None else (3 * chunk, 4 * chunk)
+    weighted = 0
+    for stage, depth, steps in stages(c):
+        delta = [audit_graph(other, sequence_len=t, batch=BATCH, stage=stage, depth=depth)["total"]
+                 - audit_graph(c, sequence_len=t, batch=BATCH, stage=stage, depth=depth)["total"] for t in (first, second)]
+        weighted += steps * (delta[0] + (delta[1] - delta[0]) * (c.sequence_len - first) // (second - first))
+    return weighted / Protocol().total_tokens / 128
 
 
-def calibrate(method, out_dir, anchor=None):
+def structure(c, initial, target, tol):
+    """Adjacent integer depths first (layers 16..32, or core layers 1..16 for looped stacks), stopping
+    at the first bracket around the target."""
+    if abs(initial / target - 1) <= tol:
+        return c, initial, []
+    field = "core_layers" if c.method in LOOPED else "layers"
+    lo, hi = (1, 16) if field == "core_layers" else (16, 32)
+    step = 1 if initial < target else -1
+    best_c, best, trials, prev = c, initial, [], initial - target
+    for value in range(getattr(c, field) + step, (hi + 1) if step > 0 else (lo - 1), step):
+        cand = replace(c, **{field: value})
+        cost = method_cost(cand)[0]
+        trials.append(dict(field=field, value=value, flops_per_token=cost))
+        if abs(cost - target) < abs(best - target):
+            best_c, best = cand, cost
+        if (cost - target) * prev <= 0 or abs(cost / target - 1) <= tol:
+            break
+        prev = cost - target
+    return best_c, best, trials
+
+
+def v2_grid(c, target, tol):
+    """Hybrids, no-VE controls and plugins: audit every allowed depth 16..32 at the starting FFN with its
+    FFN slope, estimate every width on the [3d, 5d] 128-grid, then fully audit the estimated-within-tolerance
+    candidates in tie-break order (width closest to the start, smallest |error|, depth closest to the
+    start, shallower) and keep the first whose audit is within tolerance."""
+    from nexttransformer_b200.models.config import LAYER_MULTIPLE
+    depths, cands = [], []
+    for n in range(16, 33):
+        if n % LAYER_MULTIPLE.get(c.method, 1):
+            continue
+        trial = replace(c, layers=n)
+        cost, slope = method_cost(trial)[0], ffn_slope(trial)
+        depths.append(dict(layers=n, flops_per_token=cost, ffn_slope=slope))
+        for width in range(3 * c.width, 5 * c.width + 1, 128):
+            est = (cost + (width - c.mlp_width) * slope) / target - 1
+            if abs(est) <= tol:
+                cands.append(dict(layers=n, mlp_width=width, estimated_error=est))
+    cands.sort(key=lambda t: (abs(t["mlp_width"] - c.mlp_width), abs(t["estimated_error"]), abs(t["layers"] - c.layers),
+                              t["layers"]))
+    table = dict(rule="v2 tie-break", start=dict(layers=c.layers, mlp_width=c.mlp_width), depths=depths,
+                 candidates=cands)
+    for cand in cands:
+        chosen = replace(c, layers=cand["layers"], mlp_width=cand["mlp_width"])
+        cost = method_cost(chosen)[0]
+        cand["audited_error"] = cost / target - 1
+        if abs(cand["audited_error"]) <= tol:
+            return chosen, cost, table
+    raise RuntimeError(f"{c.method}: no registered-grid candidate within tolerance")
+
+
+def search(c, anchor, tol=None):
+    """Registered selection: v2 grid for hybrids/no-VE/plugins; otherwise depth structure search, then
+    the FFN width from the exact slope, rounded to the 128-grid inside [3d, 5d]."""
+    from nexttransformer_b200.models.config import V2_CALIBRATION
+    tol = Protocol().preflight_tolerance if tol is None else tol
+    if c.method in V2_CALIBRATION:
+        return v2_grid(c, anchor, tol)[0]
+    chosen, cost, _ = structure(c, method_cost(c)[0], anchor, tol)
+    if abs(cost / anchor - 1) > tol:
+        wanted = chosen.mlp_width + (anchor - cost) / ffn_slope(chosen)
+        width = 128 * round(wanted / 128)
+        if not 3 * c.width <= width <= 5 * c.width:
+            raise RuntimeError(f"{c.method}: the FFN grid cannot meet the budget")
+        chosen = replace(chosen, mlp_width=width)
+    return chosen
+
+
+def calibrate(method, out_dir, anchor=None, reuse=None):
+    """Audit a method and write its configuration and cost proof.  With ``reuse`` (a configuration
+    directory) the stored structure is re-audited unchanged instead of searched."""
+    from nexttransformer_b200.protocol.spec import load_config
     anchor = anchor or method_cost(candidate_config("dense"))[0]
-    c = search(candidate_config(method), anchor)
+    previous = config_file(reuse, method) if reuse else None
+    if previous is not None and previous.exists():
+        c = load_config(previous)
+    elif method == "dense":
+        c = candidate_config("dense")
+    else:
+        c = search(candidate_config(method), anchor)
     per_token, proof = method_cost(c)
     path = config_file(out_dir, method)
     proof_path = path.with_name(f"{method}.cost.json")
     path.parent.mkdir(parents=True, exist_ok=True)
     proof_path.write_text(json.dumps(proof, indent=1) + "\n")
-    write_config(path, c, dict(status="theoretical_preflight_passed", formula_version=FORMULA_VERSION,
+    deviation = per_token / anchor - 1
+    status = "theoretical_preflight_passed" if abs(deviation) <= Protocol().preflight_tolerance else "budget_mismatch"
+    write_config(path, c, dict(status=status, formula_version=FORMULA_VERSION,
                                flops_per_token=per_token, dense_flops_per_token=anchor,
-                               relative_error=per_token / anchor - 1, cost_record=proof_path.name,
-                               torch=torch.__version__))
+                               relative_error=deviation, cost_record=proof_path.name,
+                               torch=torch.__version__, method_source_hash=proof["method_source"]["hash"]))
     return path
 
 
@@ -126,10 +209,11 @@ def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--methods", nargs="+", required=True)
     ap.add_argument("--out", type=Path, default=Path("configs"))
+    ap.add_argument("--reuse-configs", type=Path, help="re-audit the structures stored here instead of searching")
     a = ap.parse_args(argv)
     anchor = method_cost(candidate_config("dense"))[0]
     for m in a.methods:
-        print(calibrate(m, a.out, anchor))
+        print(calibrate(m, a.out, anchor, a.reuse_configs), flush=True)
 
 
 if __name__ == "__main__":
