@@ -9,6 +9,8 @@
 #include "linear_attn.h"
 #include "delta_scan.h"
 #include "moe.h"
+#include "sparse_attn.h"
+#include "residual.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
 #include "optim.h"
@@ -297,6 +299,62 @@ void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o
   ok(nt_attention_bwd(a, stream()), "attention_bwd");
 }
 
+// Block-sparse attention (lists of 64-key blocks per query tile, see sparse_attn.h).
+SparseAttnArgs sparse_args(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lists, const Tensor& masks,
+                           int64_t B, int64_t T, int64_t H, int64_t Hk, double scale) {
+  for (auto* t : {&q, &k, &v}) {
+    check_cuda(*t, "sparse attention operand");
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->stride(-1) == 1, "q / k / v: bf16 rows with unit inner stride");
+  }
+  TORCH_CHECK(lists.is_cuda() && lists.scalar_type() == at::kInt && lists.is_contiguous() && lists.dim() == 4,
+              "lists: int32 [B, G, n_qt, Lmax]");
+  TORCH_CHECK(masks.is_cuda() && masks.scalar_type() == at::kInt && masks.is_contiguous() && masks.dim() == 5 &&
+                  masks.size(-1) == 4,
+              "masks: int32 [B, G, n_qt, Lmax, 4]");
+  TORCH_CHECK(lists.size(0) == B && lists.size(2) == (T + 127) / 128 && masks.size(3) == lists.size(3),
+              "list shapes");
+  SparseAttnArgs a;
+  a.B = static_cast<int>(B); a.T = static_cast<int>(T); a.H = static_cast<int>(H); a.Hk = static_cast<int>(Hk);
+  a.G = static_cast<int>(lists.size(1)); a.Lmax = static_cast<int>(lists.size(3));
+  a.scale = static_cast<float>(scale);
+  a.q = q.data_ptr(); a.ldq = q.stride(-2);
+  a.k = k.data_ptr(); a.ldk = k.stride(-2);
+  a.v = v.data_ptr(); a.ldv = v.stride(-2);
+  a.lists = lists.data_ptr<int>();
+  a.masks = reinterpret_cast<const uint32_t*>(masks.data_ptr<int>());
+  return a;
+}
+
+void sparse_attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lists, const Tensor& masks,
+                     const Tensor& o, const Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale) {
+  SparseAttnArgs a = sparse_args(q, k, v, lists, masks, B, T, H, Hk, scale);
+  TORCH_CHECK(o.scalar_type() == at::kBFloat16 && o.stride(-1) == 1 && lse.scalar_type() == at::kFloat, "o / lse");
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr()); a.ldo = o.stride(-2);
+  a.lse = lse.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_sparse_attn_fwd(a, stream()), "sparse_attn_fwd");
+}
+
+void sparse_attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lists, const Tensor& masks,
+                     const Tensor& lse, const Tensor& dout, const Tensor& delta, const Tensor& dq, const Tensor& dk_acc,
+                     const Tensor& dv_acc, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale) {
+  SparseAttnArgs a = sparse_args(q, k, v, lists, masks, B, T, H, Hk, scale);
+  TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.stride(-1) == 1 && dq.scalar_type() == at::kBFloat16 &&
+                  dq.stride(-1) == 1,
+              "dout / dq: bf16 rows");
+  TORCH_CHECK(dk_acc.scalar_type() == at::kFloat && dv_acc.scalar_type() == at::kFloat && dk_acc.is_contiguous() &&
+                  dv_acc.is_contiguous(),
+              "dk / dv accumulators: contiguous fp32");
+  a.lse = lse.data_ptr<float>();
+  a.dout = dout.data_ptr(); a.lddo = dout.stride(-2);
+  a.delta = delta.data_ptr<float>();
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()); a.lddq = dq.stride(-2);
+  a.dk_acc = dk_acc.data_ptr<float>();
+  a.dv_acc = dv_acc.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_sparse_attn_bwd(a, stream()), "sparse_attn_bwd");
+}
+
 // LM head + soft-capped cross-entropy, forward: G = e (1 - t^2) for x = hf W^T (see EPI_CE_FWD),
 // per-row partial sums and target logits, then the row statistics.
 void gemm_ce_fwd(const Tensor& hf, const Tensor& w, const Tensor& G, const Tensor& tgt, const Tensor& part,
@@ -451,6 +509,22 @@ void p2p_barrier(const Tensor& pads, int64_t rank, int64_t world, int64_t epoch,
      "p2p_barrier");
 }
 
+void p2p_gather(const Tensor& peers, const Tensor& pads, const Tensor& seg_off, const Tensor& seg_len,
+                const Tensor& seg_owner, const Tensor& seg_shadow, int64_t rank, int64_t world, int64_t epoch,
+                int64_t blocks, double timeout_s) {
+  for (auto* t : {&peers, &pads, &seg_off, &seg_len, &seg_shadow})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kLong && t->is_contiguous(), "p2p_gather tables: int64 CUDA");
+  TORCH_CHECK(seg_owner.is_cuda() && seg_owner.scalar_type() == at::kInt, "seg_owner: int32 CUDA");
+  const c10::cuda::CUDAGuard guard(peers.device());
+  ok(nt_p2p_gather(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                   reinterpret_cast<const uint64_t*>(pads.data_ptr<int64_t>()), seg_off.data_ptr<int64_t>(),
+                   seg_len.data_ptr<int64_t>(), seg_owner.data_ptr<int>(),
+                   reinterpret_cast<const uint64_t*>(seg_shadow.data_ptr<int64_t>()), static_cast<int>(seg_off.numel()),
+                   static_cast<int>(rank), static_cast<int>(world), static_cast<uint32_t>(epoch), static_cast<int>(blocks),
+                   static_cast<uint64_t>(timeout_s * 1e9), stream()),
+     "p2p_gather");
+}
+
 void p2p_put(const Tensor& peers, int64_t world, int64_t dst_off, const Tensor& src) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
   TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "src must be contiguous CUDA");
@@ -458,6 +532,28 @@ void p2p_put(const Tensor& peers, int64_t world, int64_t dst_off, const Tensor& 
   ok(nt_p2p_put(reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), static_cast<int>(world), dst_off,
                 src.data_ptr(), src.numel() * src.element_size(), stream()),
      "p2p_put");
+}
+
+// ------------------------------------------------------------------ mHC Sinkhorn-Knopp
+void sinkhorn_fwd(const Tensor& logits, const Tensor& out, int64_t iterations) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kFloat && logits.is_contiguous() && out.is_contiguous(),
+              "sinkhorn: contiguous fp32 [.., n, n]");
+  const int n = static_cast<int>(logits.size(-1));
+  const c10::cuda::CUDAGuard guard(logits.device());
+  ok(nt_sinkhorn_fwd(logits.data_ptr<float>(), out.data_ptr<float>(), logits.numel() / (n * n), n,
+                     static_cast<int>(iterations), stream()),
+     "sinkhorn_fwd");
+}
+
+void sinkhorn_bwd(const Tensor& logits, const Tensor& dout, const Tensor& dlogits, int64_t iterations) {
+  TORCH_CHECK(logits.is_contiguous() && dout.is_contiguous() && dlogits.is_contiguous() &&
+                  dout.scalar_type() == at::kFloat,
+              "sinkhorn: contiguous fp32");
+  const int n = static_cast<int>(logits.size(-1));
+  const c10::cuda::CUDAGuard guard(logits.device());
+  ok(nt_sinkhorn_bwd(logits.data_ptr<float>(), dout.data_ptr<float>(), dlogits.data_ptr<float>(),
+                     logits.numel() / (n * n), n, static_cast<int>(iterations), stream()),
+     "sinkhorn_bwd");
 }
 
 // ------------------------------------------------------------------ MoE row movement
@@ -639,7 +735,10 @@ std::vector<int64_t> read_errors() {
   const int a = nt_attention_read_error(&wa);
   unsigned wd = 0;
   const int d = nt_delta_scan_read_error(&wd);
-  return {g, static_cast<int64_t>(w), a, static_cast<int64_t>(wa), d, static_cast<int64_t>(wd)};
+  unsigned ws = 0;
+  const int sp = nt_sparse_attn_read_error(&ws);
+  return {g, static_cast<int64_t>(w), a, static_cast<int64_t>(wa), d, static_cast<int64_t>(wd), sp,
+          static_cast<int64_t>(ws)};
 }
 
 }  // namespace
@@ -671,9 +770,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_reduce_scatter", &p2p_reduce_scatter);
   m.def("conv_silu_fwd", &conv_silu_fwd);
   m.def("gemm_grouped", &gemm_grouped);
+  m.def("sinkhorn_fwd", &sinkhorn_fwd);
+  m.def("sinkhorn_bwd", &sinkhorn_bwd);
+  m.def("sparse_attn_fwd", &sparse_attn_fwd);
+  m.def("sparse_attn_bwd", &sparse_attn_bwd);
   m.def("moe_gather_rows", &moe_gather_rows);
   m.def("p2p_barrier", &p2p_barrier);
   m.def("p2p_put", &p2p_put);
+  m.def("p2p_gather", &p2p_gather);
   m.def("moe_combine", &moe_combine);
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("moe_pull_rows", &moe_pull_rows);

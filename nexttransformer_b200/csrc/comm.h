@@ -10,6 +10,12 @@
 int nt_p2p_reduce_scatter(const uint64_t* peers_dev, const uint64_t* pads_dev, const int64_t* seg_off,
                           const int64_t* seg_len, int nseg, int rank, int world, float scale, uint32_t epoch,
                           int blocks, uint64_t timeout_ns, cudaStream_t stream);
+// Parameter all-gather over symmetric memory: segment s (element offset, length, both multiples of 4)
+// is read from rank seg_owner[s]'s buffer into this rank's (skipped when owned here) and, when
+// seg_shadow[s] != 0, written as bf16 to that address.  One entry barrier; `blocks * world` slots.
+int nt_p2p_gather(const uint64_t* peers_dev, const uint64_t* pads_dev, const int64_t* seg_off, const int64_t* seg_len,
+                  const int* seg_owner, const uint64_t* seg_shadow, int nseg, int rank, int world, uint32_t epoch,
+                  int blocks, uint64_t timeout_ns, cudaStream_t stream);
 // Barrier with every peer (bounded wait; needs `world` 32-bit signal-pad slots; epoch as above).
 int nt_p2p_barrier(const uint64_t* pads_dev, int rank, int world, uint32_t epoch, uint64_t timeout_ns,
                    cudaStream_t stream);

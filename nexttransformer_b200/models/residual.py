@@ -16,8 +16,34 @@ def coef(x):
     return x.to(torch.promote_types(x.dtype, torch.float32))
 
 
+class _SinkhornKernel(torch.autograd.Function):
+    """The whole Sinkhorn-Knopp projection in one sm_100a kernel per direction (csrc/residual.cu)."""
+
+    @staticmethod
+    def forward(ctx, logits, iterations):
+        from nexttransformer_b200.ops._ext import ext
+        z = logits.float().contiguous()
+        out = torch.empty_like(z)
+        ext().sinkhorn_fwd(z, out, iterations)
+        ctx.save_for_backward(z)
+        ctx.iterations, ctx.dtype = iterations, logits.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from nexttransformer_b200.ops._ext import ext
+        (z,) = ctx.saved_tensors
+        dz = torch.empty_like(z)
+        ext().sinkhorn_bwd(z, dout.float().contiguous(), dz, ctx.iterations)
+        return dz.to(ctx.dtype), None
+
+
 def sinkhorn_knopp(logits, iterations):
     """Alternate column / row normalisation of exp(logits) kept in the log domain."""
+    if logits.is_cuda and logits.shape[-1] == logits.shape[-2] == 4 and iterations <= 32 \
+            and logits.dtype in (torch.float32, torch.bfloat16) and type(logits) is torch.Tensor:
+        return _SinkhornKernel.apply(logits, iterations)
+
     def lognorm(z, dim):
         z = z - z.amax(dim, keepdim=True).detach()
         return z - z.exp().sum(dim, keepdim=True).log()

@@ -235,6 +235,8 @@ class SparseMixer(nn.Module):
         if self.backend not in BACKENDS:
             raise ValueError(f"unknown sparse backend {self.backend!r}")
         kernel = self.backend == "kernel" and x.is_cuda
+        if kernel and self._blocks_supported(x):
+            return self._forward_blocks(x, q, k, v)
         aux, outputs = [], []
         edges = teacher_edges = 0
         chunk = c.reference_chunk
@@ -328,6 +330,75 @@ class SparseMixer(nn.Module):
         y = torch.cat(outputs, 2).transpose(1, 2).reshape(B, T, d)
         self.last_aux = sum(aux, x.new_zeros(())) * c.index_loss_weight
         self.last_stats = {"selected_edges": edges, "teacher_dense_score_edges": teacher_edges, "burnin": burnin,
+                           "backend": self.backend}
+        return self.c_proj(y)
+
+    # ------------------------------------------------------------ block-sparse kernel path
+    def _blocks_supported(self, x):
+        """MoBA and NSA whose selection unit is a multiple of 64 keys run the block-sparse kernels."""
+        c = self.config
+        if self.kind not in ("moba", "nsa") or self.head_dim != 128 or x.dtype != torch.bfloat16:
+            return False
+        sel = c.block_size if (self.kind == "moba" or c.compression_stride) else c.compression_size
+        return sel % 64 == 0
+
+    def _forward_blocks(self, x, q, k, v, rows_per_pass=1024):
+        """Same selection as the chunked reference path, computed for every row, then one pass of
+        the block-sparse kernels (``ops.sparse_attention``) over the selected 64-key blocks."""
+        from nexttransformer_b200.ops.attention import attention_bthd
+        from nexttransformer_b200.ops.sparse_attention import block_lists, block_sparse_attention
+        c = self.config
+        B, T, d = x.shape
+        H, Hk, D = self.n_head, self.n_kv_head, self.head_dim
+        rep = H // Hk
+        k_raw, v_raw = k[:, ::rep].transpose(1, 2), v[:, ::rep].transpose(1, 2)   # [B, T, Hk, D]
+        dev = x.device
+        mems, compressed, edges = [], [], 0
+        if self.kind == "moba":
+            size = c.block_size
+            pooled = pool_blocks(k, size)
+            topk = max(0, c.sparse_topk // size - 1)
+        else:
+            ck, cv, ends = self._nsa_compress(k, v)
+            gates = self.branch_gate(x).sigmoid().view(B, T, H, 3)
+            size = c.block_size if c.compression_stride else c.compression_size
+            topk = max(1, c.sparse_topk // size)
+        nsel = (T + size - 1) // size
+        for start in range(0, T, rows_per_pass):
+            stop = min(start + rows_per_pass, T)
+            pos = torch.arange(start, stop, device=dev)
+            qq = q[:, :, start:stop]
+            if self.kind == "moba":
+                sc = torch.matmul(qq, pooled.transpose(-2, -1))
+            else:
+                complete = ends[None, :] <= pos[:, None]
+                sc = torch.matmul(qq, ck.transpose(-2, -1)) * c.head_dim ** -.5
+                prob = safe_softmax(sc, complete[None, None])
+                compressed.append(torch.matmul(prob, cv))
+                sc = self._selection_importance(prob, ends, size, T) if c.compression_stride else prob
+            full = (torch.arange(nsel, device=dev) + 1) * size - 1 <= pos[:, None]
+            cur = pos // size
+            eligible = full & (torch.arange(nsel, device=dev)[None, :] != cur[:, None])
+            chosen, ok = select_tokens(sc, eligible[None, None], topk)
+            mem = torch.zeros(*sc.shape[:3], nsel, dtype=torch.bool, device=dev).scatter_(-1, chosen, ok)
+            mem.scatter_(-1, cur[None, None, :, None].expand(B, H, -1, 1), True)
+            mems.append(mem)
+            edges += int(ok.sum()) * size + B * H * int(((pos % size) + 1).sum())
+        mem = torch.cat(mems, 2)                                             # [B, H, T, nsel]
+        blocks = mem.repeat_interleave(size // 64, -1)[..., :(T + 63) // 64]
+        lists, masks = block_lists(blocks)
+        selected = block_sparse_attention(q.transpose(1, 2), k_raw, v_raw, lists, masks, D ** -.5)   # [B, T, H, D]
+        if self.kind == "moba":
+            y = selected
+        else:
+            local = attention_bthd(q.transpose(1, 2), k_raw, v_raw, c.local_window - 1)
+            comp = torch.cat(compressed, 2).transpose(1, 2).to(selected.dtype)
+            y = comp * gates[..., 0:1] + selected * gates[..., 1:2] + local * gates[..., 2:3]
+            lw = torch.arange(T, device=dev).clamp_max(c.local_window - 1) + 1
+            edges += B * H * int(lw.sum()) + B * H * T * ck.shape[2]
+        y = y.reshape(B, T, d)
+        self.last_aux = x.new_zeros(())
+        self.last_stats = {"selected_edges": edges, "teacher_dense_score_edges": 0, "burnin": False,
                            "backend": self.backend}
         return self.c_proj(y)
 

@@ -34,7 +34,7 @@ def available():
 
 def check_errors():
     """Raise if a bounded device-side wait in a kernel gave up (see csrc/common.cuh)."""
-    g, gw, a, aw, d, dw = ext().read_errors()
-    if g or a or d:
+    g, gw, a, aw, d, dw, sp, sw = ext().read_errors()
+    if g or a or d or sp:
         raise RuntimeError(f"device pipeline wait expired: gemm code {g} at {gw:#x}, attention code {a} at {aw:#x}, "
-                           f"delta scan code {d} at {dw:#x}")
+                           f"delta scan code {d} at {dw:#x}, sparse attention code {sp} at {sw:#x}")

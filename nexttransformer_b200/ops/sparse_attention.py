@@ -1,16 +1,83 @@
-"""Attention under an explicit key mask for the sparse mixers' "kernel" backend.
+"""Attention over selected key blocks for the sparse mixers (NSA selected blocks, MoBA).
 
-``masked_attention(q, k, v, mask)``: q [B, H, Q, D], k / v [B, H, T, D], mask [B, H, Q, T]
-(nonzero = key visible).  Rows with no visible key return zeros, as the reference's safe softmax
-does.  This runs PyTorch's memory-efficient attention with a boolean mask (a library kernel);
-the "reference" backend (gathered keys, ``models.sparse.indexed_attention``) is the default of
-every admitted sparse configuration.
+``block_lists(blocks)`` turns a per-row selection of 64-key blocks (``blocks`` bool [B, G, T, NB]:
+row t of list group g selects keys [64 j, 64 j + 64)) into what the sm_100a kernels walk: per
+128-row query tile the sorted union of the selected blocks (int32 lists [B, G, n_qt, Lmax], -1
+padded) and per listed block a 128-bit row mask (int32 [B, G, n_qt, Lmax, 4]).
+
+``block_sparse_attention(q, k, v, lists, masks, scale)`` (q [B, T, H, 128], k / v [B, T, Hk, 128],
+bf16) runs ``csrc/sparse_attn.cu``: row t of head h attends to the keys j <= t of the blocks its
+list group h / (H / G) selected; rows that see no key give 0, as the reference's safe softmax.
+
+``masked_attention(q, k, v, mask)`` keeps the explicit-mask interface of the "kernel" backend for
+selections that are not made of 64-key blocks (PyTorch's memory-efficient attention, a library
+kernel).
 """
 import torch
+from torch.autograd import Function
 import torch.nn.functional as F
+
+from nexttransformer_b200.ops._ext import ext
+
+QT, KB = 128, 64
+
+
+def block_lists(blocks):
+    B, G, T, NB = blocks.shape
+    n_qt = (T + QT - 1) // QT
+    pad = n_qt * QT - T
+    mem = F.pad(blocks, (0, 0, 0, pad)) if pad else blocks
+    mem = mem.view(B, G, n_qt, QT, NB)
+    union = mem.any(3)
+    Lmax = max(1, int(union.sum(-1).max()))
+    key = (~union).to(torch.int64) * NB + torch.arange(NB, device=blocks.device)
+    order = key.argsort(-1)[..., :Lmax]
+    valid = union.gather(-1, order)
+    lists = torch.where(valid, order, torch.full_like(order, -1)).to(torch.int32).contiguous()
+    rows = mem.permute(0, 1, 2, 4, 3).gather(3, order[..., None].expand(-1, -1, -1, -1, QT))
+    rows = rows & valid[..., None]
+    bits = rows.view(B, G, n_qt, Lmax, 4, 32).to(torch.int64) << torch.arange(32, device=blocks.device)
+    words = bits.sum(-1)
+    words = torch.where(words >= 2 ** 31, words - 2 ** 32, words)
+    return lists, words.to(torch.int32).contiguous()
+
+
+class _BlockSparseAttention(Function):
+    @staticmethod
+    def forward(ctx, q, k, v, lists, masks, scale):
+        B, T, H, D = q.shape
+        Hk = k.shape[2]
+        qf = q.reshape(B * T, H * D).contiguous()
+        kf = k.reshape(B * T, Hk * D).contiguous()
+        vf = v.reshape(B * T, Hk * D).contiguous()
+        o = torch.empty_like(qf)
+        lse = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
+        ext().sparse_attn_fwd(qf, kf, vf, lists, masks, o, lse, B, T, H, Hk, float(scale))
+        ctx.save_for_backward(qf, kf, vf, lists, masks, o, lse)
+        ctx.dims = (B, T, H, Hk, D, float(scale))
+        return o.view(B, T, H, D)
+
+    @staticmethod
+    def backward(ctx, do):
+        qf, kf, vf, lists, masks, o, lse = ctx.saved_tensors
+        B, T, H, Hk, D, scale = ctx.dims
+        dof = do.reshape(B * T, H * D).to(torch.bfloat16).contiguous()
+        delta = (dof.float() * o.float()).view(B, T, H, D).sum(-1).permute(0, 2, 1).contiguous()
+        dq = torch.empty_like(qf)
+        dk = torch.zeros(B * T, Hk * D, device=qf.device, dtype=torch.float32)
+        dv = torch.zeros_like(dk)
+        ext().sparse_attn_bwd(qf, kf, vf, lists, masks, lse, dof, delta, dq, dk, dv, B, T, H, Hk, scale)
+        return (dq.view(B, T, H, D), dk.to(torch.bfloat16).view(B, T, Hk, D), dv.to(torch.bfloat16).view(B, T, Hk, D),
+                None, None, None)
+
+
+def block_sparse_attention(q, k, v, lists, masks, scale=None):
+    scale = q.shape[-1] ** -.5 if scale is None else scale
+    return _BlockSparseAttention.apply(q, k, v, lists, masks, scale)
 
 
 def masked_attention(q, k, v, mask):
+    """q [B, H, Q, D], k / v [B, H, T, D], mask [B, H, Q, T] (nonzero = visible)."""
     keep = mask > 0
     out = F.scaled_dot_product_attention(q, k, v, attn_mask=keep)
     return torch.where(keep.any(-1, keepdim=True), out, torch.zeros_like(out))

@@ -92,9 +92,15 @@ class MuonAdamW(torch.optim.Optimizer):
         # Optional peer-memory reduce-scatter (parallel.symmetric.PeerReduceScatter) and the set of
         # parameters whose gradients it averages in place; the others use NCCL collectives.
         self.p2p, self.p2p_params = None, frozenset()
+        self.gather, self.gather_params = None, frozenset()
 
     def use_peer_reduce_scatter(self, reducer, covered):
         self.p2p, self.p2p_params = reducer, frozenset(covered)
+
+    def use_peer_gather(self, gather, covered):
+        """Parameters in ``covered`` (fp32 masters in a symmetric arena) are all-gathered, shadows
+        included, by ``gather()`` at the end of every step instead of NCCL broadcasts / gathers."""
+        self.gather, self.gather_params = gather, frozenset(covered)
 
     # -------------------------------------------------------------- helpers
     @staticmethod
@@ -154,12 +160,12 @@ class MuonAdamW(torch.optim.Optimizer):
                     sh = shadow
                 ext().adamw(pv, gv.contiguous(), st["exp_avg"], st["exp_avg_sq"], sh, group["lr"], b1, b2,
                             group["eps"], group["weight_decay"], st["step"])
-                if shadow is not None and sh is None:
+                if shadow is not None and sh is None and p not in self.gather_params:
                     gathers.append(("shadow", p, shadow))
             else:
                 adamw_reference(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], b1, b2,
                                 group["eps"], group["weight_decay"])
-            if rows is not None:
+            if rows is not None and p not in self.gather_params:
                 gathers.append(("adamw", p, dist.all_gather_into_tensor(p.data, p.data[rows].contiguous(),
                                                                           async_op=True)))
 
@@ -218,6 +224,8 @@ class MuonAdamW(torch.optim.Optimizer):
                         self.shadows[p].copy_(p.data)
         if world > 1:
             for i, p in enumerate(params):
+                if p in self.gather_params:
+                    continue
                 src = min(i // chunk, world - 1)
                 gathers.append(("muon", p, dist.broadcast(p.data, src=src, async_op=True)))
                 if p in self.shadows:
@@ -309,3 +317,5 @@ class MuonAdamW(torch.optim.Optimizer):
         for kind, p, item in gathers:
             if kind == "shadow":
                 item.copy_(p.data)
+        if self.gather is not None and world > 1:
+            self.gather()

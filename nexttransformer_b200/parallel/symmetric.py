@@ -5,6 +5,12 @@ aligned).  With a process group the allocation is symmetric memory (``torch.dist
 _symmetric_memory``): the same buffer is mapped into every rank's address space over NVLink, so a
 kernel can read every peer's gradients directly.
 
+``ParamArena`` / ``PeerParamGather`` do the reverse for the parameters: the fp32 masters of the
+covered parameters move into a symmetric allocation laid out like the gradient arena, every
+owner updates its segments in place, and one kernel per update (after an entry barrier) reads
+every other owner's segments with plain peer loads and writes the bf16 shadows the forward reads
+- the parameter all-gather and the shadow cast in one pass.
+
 ``PeerReduceScatter`` turns the optimizer's ownership (whole Muon matrices per owner rank, row
 shards of the large AdamW tables) into per-rank segment tables and runs ``csrc/comm.cu``: one
 kernel per update reads the owned segments from every peer, averages them in a fixed order and
@@ -129,3 +135,85 @@ def ownership_segments(optimizer, arena, world):
                 segs.extend((off + r * per, per, r) for r in range(world))
                 covered.add(p)
     return segs, covered
+
+
+def param_segments(optimizer, arena, world):
+    """[(element offset, length, owner, param, param offset)] in the gradient arena's layout for
+    every parameter the peer reduce-scatter covers (same ownership as ``ownership_segments``)."""
+    import math
+    from nexttransformer_b200.optim.muon_adamw import grad_of
+    out = []
+    for group in optimizer.param_groups:
+        params = group["params"]
+        if group["kind"] == "muon":
+            chunk = math.ceil(len(params) / world)
+            for i, p in enumerate(params):
+                g = grad_of(p)
+                if g is None or not g.is_contiguous():
+                    continue
+                off = arena.offset_of(g)
+                if off % 4 or g.numel() % 4:
+                    continue
+                out.append((off, g.numel(), min(i // chunk, world - 1), p, off))
+        else:
+            for p in params:
+                g = grad_of(p)
+                if g is None or not g.is_contiguous() or p.numel() < 1024 or p.shape[0] % world:
+                    continue
+                per = p.shape[0] // world * (p.numel() // p.shape[0])
+                off = arena.offset_of(g)
+                if off % 4 or per % 4:
+                    continue
+                out.extend((off + r * per, per, r, p, off) for r in range(world))
+    return out
+
+
+class ParamArena:
+    """fp32 masters of the covered parameters in symmetric memory, at their gradients' offsets."""
+
+    def __init__(self, grad_arena, segments, group):
+        import torch.distributed._symmetric_memory as symm
+        self.buf = symm.empty(grad_arena.total, dtype=torch.float32, device=grad_arena.buf.device)
+        self.buf.zero_()
+        self.handle = symm.rendezvous(self.buf, group)
+        self.params = {}
+        for _, _, _, p, base in segments:
+            if p in self.params:
+                continue
+            view = self.buf[base:base + p.numel()].view(p.shape)
+            view.copy_(p.data)
+            p.data = view
+            self.params[p] = base
+
+
+class PeerParamGather:
+    """All-gather of the updated parameters (and their bf16 shadows) through peer memory."""
+
+    def __init__(self, arena, segments, shadows, rank, world, blocks=None, timeout_s=60.0):
+        h = arena.handle
+        dev = arena.buf.device
+        self.rank, self.world, self.timeout_s = rank, world, timeout_s
+        self.peers = torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=dev)
+        self.pads = torch.tensor(list(h.signal_pad_ptrs), dtype=torch.int64, device=dev)
+        self.blocks = max(1, min(blocks or 2 * torch.cuda.get_device_properties(dev).multi_processor_count,
+                                 h.signal_pad_size // 4 // world))
+        offs, lens, owners, shadow = [], [], [], []
+        for off, n, owner, p, base in segments:
+            sh = shadows.get(p)
+            ok = sh is not None and sh.is_contiguous() and sh.dtype == torch.bfloat16
+            offs.append(off)
+            lens.append(n)
+            owners.append(owner)
+            shadow.append(sh.data_ptr() + (off - base) * 2 if ok else 0)
+        self.covered = frozenset(p for *_, p, _ in segments)
+        self.seg_off = torch.tensor(offs or [0], dtype=torch.int64, device=dev)
+        self.seg_len = torch.tensor(lens or [0], dtype=torch.int64, device=dev)
+        self.seg_owner = torch.tensor(owners or [0], dtype=torch.int32, device=dev)
+        self.seg_shadow = torch.tensor(shadow or [0], dtype=torch.int64, device=dev)
+        self.epoch = 0
+
+    def __call__(self):
+        from nexttransformer_b200.ops._ext import ext
+        self.epoch += 1
+        ext().p2p_gather(self.peers, self.pads, self.seg_off, self.seg_len, self.seg_owner, self.seg_shadow,
+                         self.rank, self.world, self.epoch, self.blocks, self.timeout_s)

@@ -58,6 +58,7 @@ def test_linear_mixer_cuda_matches_cpu(kind):
     x, y = tok[:, :-1], tok[:, 1:]
     cpu = build_model(c, "cpu", seed=3)
     gpu = build_model(c, "cuda", seed=3)
+    gpu.load_state_dict(cpu.state_dict())
     lc = cpu(x, y)
     lg = gpu(x.cuda(), y.cuda())
     lc.backward()
