@@ -220,9 +220,17 @@ def bench_method(args, rank, world, local, device):
             trainer = Trainer(model, opt, accumulation=accum)
             step_device, step_e2e = trainer.step_device, trainer.step
         else:
+            from dataclasses import replace
             from nexttransformer.models import build_model as ref_build
-            from nexttransformer.models.config import ModelConfig as RefConfig
-            config = RefConfig(**{k: v for k, v in raw.items() if k in RefConfig.__dataclass_fields__})
+            import nexttransformer.models.config as rc
+            fields = rc.ModelConfig.__dataclass_fields__
+            missing = sorted(k for k in raw if k not in fields and k != "scale")
+            if missing:
+                raise NotImplementedError(f"the reference's ModelConfig has no {', '.join(missing)} "
+                                          f"(this configuration needs them)")
+            # the reference admits only formal (d24 shell) and debug scales; debug takes any dimensions
+            config = replace(rc.candidate_config(raw["method"]),
+                             **{k: v for k, v in raw.items() if k not in ("method", "scale")}, scale="debug")
             model = ref_build(config, device)
             opt = model.setup_optimizer() if hasattr(model, "setup_optimizer") else None
             if opt is None:

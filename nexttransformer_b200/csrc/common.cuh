@@ -1,7 +1,7 @@
 // Shared device helpers for the sm_100a kernels of nexttransformer_b200.
 //
 // Everything here is hand-written for Blackwell (compute_100a): mbarrier waits with
-// iteration limits, TMA tile loads (no cluster multicast anywhere in this library),
+// iteration limits, TMA tile loads (no TMA load in this library uses cluster multicast),
 // tcgen05 MMA / TMEM allocation / TMEM loads, and the warp reductions the elementwise
 // kernels use.  Descriptor bit layouts follow the public PTX ISA description of the
 // tcgen05 shared-memory and instruction descriptors.
@@ -289,6 +289,61 @@ NT_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
+}
+
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+// Two CTAs of a cluster share one MMA: the leader (rank 0) issues it over both CTAs' shared
+// memory (A split by rows, B by columns) and each CTA's tensor memory holds its 128 rows.
+NT_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+NT_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the leader CTA's copy of a local barrier (rank bit cleared).
+NT_DEVICE uint32_t leader_bar(uint64_t* bar) { return smem_u32(bar) & 0xFEFFFFFFu; }
+// Tile load into this CTA's shared memory whose completion counts on the leader's barrier.
+NT_DEVICE void tma_load_3d_pair(void* smem_dst, const void* desc, uint32_t bar_cluster, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+NT_DEVICE void umma_bf16_pair(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` in every CTA of `mask` once the pair's MMAs issued so far have completed.
+NT_DEVICE void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+NT_DEVICE void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols));
+}
+NT_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+NT_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+// Arrive on the copy of a local barrier in CTA `rank` of the cluster.
+NT_DEVICE void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 
 NT_DEVICE bool elect_one() {

@@ -23,6 +23,7 @@
 
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -76,6 +77,13 @@ struct Params {
   const int* grp_m;
   const int* grp_k;
 };
+
+// Epilogue threads release an accumulator buffer on the MMA issuer's barrier (the leader's for a pair).
+template <bool PAIR>
+NT_DEVICE void arrive_tempty(uint64_t* bar, uint32_t crank) {
+  if (PAIR && crank != 0) mbar_arrive_cluster(bar, 0);
+  else mbar_arrive(bar);
+}
 
 struct TileWork {
   int zA, zB, zC, kb_lo, kb_hi;
@@ -408,11 +416,16 @@ NT_DEVICE void epilogue32(const Params& p, float sacc, int b, int ks, int row, i
   }
 }
 
-template <int BN, int A_MN, int B_MN, int EPI, int STAGES>
+// PAIR: a cluster of two CTAs computes 256 x BN tiles with cta_group::2 MMAs issued by the leader
+// (rank 0): each CTA stages its 128 rows of A and its BN / 2 rows of B, so each SM reads half of
+// the B operand per MMA; each CTA's tensor memory receives its own 128 rows of the accumulator.
+template <int BN, int A_MN, int B_MN, int EPI, int STAGES, bool PAIR = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmP, Params p) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<PAIR ? BN / 2 : BN, STAGES>;
+  constexpr int BNC = PAIR ? BN / 2 : BN;  // B rows staged by this CTA
+  constexpr int TM = PAIR ? 2 * BM : BM;    // rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFFSET);
@@ -426,6 +439,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int num_kb = (p.K + BK - 1) / BK;
   const int total_tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const int tile0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tstride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const bool leader = crank == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -434,7 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], PAIR ? 256 : 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -444,11 +461,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 2 * BN);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, 2 * BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, 2 * BN);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before either signals the other
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -459,37 +482,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles && ok; t += tstride) {
         int b, mb, nb, ks;
         tile_coords(t, p, b, mb, nb, ks);
         TileWork tw;
         if (!tile_work(p, b, mb, ks, num_kb, tw)) continue;
-        const int m0 = mb * BM, n0 = nb * BN;
+        const int m0 = mb * TM + static_cast<int>(crank) * BM, n0 = nb * BN + static_cast<int>(crank) * BNC;
         const int kb_lo = tw.kb_lo, kb_hi = tw.kb_hi;
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, 0x100u + stage, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
           uint8_t* sB = sA + S::A_BYTES;
-          mbar_expect_tx(&full[stage], S::STAGE_BYTES);
           const int k0 = kb * BK;
-          if constexpr (A_MN == 0) {
-            tma_load_3d(sA, &tmA, &full[stage], k0, m0, tw.zA);
-          } else {
-            tma_load_3d(sA, &tmA, &full[stage], m0, k0, tw.zA);
-            tma_load_3d(sA + 8192, &tmA, &full[stage], m0 + 64, k0, tw.zA);
-          }
-          if constexpr (B_MN == 0) {
-            tma_load_3d(sB, &tmB, &full[stage], k0, n0, tw.zB);
-          } else {
+          if constexpr (PAIR) {
+            // both CTAs' copies count on the leader's barrier; only the leader arms it
+            if (leader) mbar_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+            const uint32_t fb = leader_bar(&full[stage]);
+            if constexpr (A_MN == 0) {
+              tma_load_3d_pair(sA, &tmA, fb, k0, m0, tw.zA);
+            } else {
+              tma_load_3d_pair(sA, &tmA, fb, m0, k0, tw.zA);
+              tma_load_3d_pair(sA + 8192, &tmA, fb, m0 + 64, k0, tw.zA);
+            }
+            if constexpr (B_MN == 0) {
+              tma_load_3d_pair(sB, &tmB, fb, k0, n0, tw.zB);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, tw.zB);
+              for (int j = 0; j < BNC / 64; ++j) tma_load_3d_pair(sB + j * 8192, &tmB, fb, n0 + 64 * j, k0, tw.zB);
+            }
+          } else {
+            mbar_expect_tx(&full[stage], S::STAGE_BYTES);
+            if constexpr (A_MN == 0) {
+              tma_load_3d(sA, &tmA, &full[stage], k0, m0, tw.zA);
+            } else {
+              tma_load_3d(sA, &tmA, &full[stage], m0, k0, tw.zA);
+              tma_load_3d(sA + 8192, &tmA, &full[stage], m0 + 64, k0, tw.zA);
+            }
+            if constexpr (B_MN == 0) {
+              tma_load_3d(sB, &tmB, &full[stage], k0, n0, tw.zB);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, tw.zB);
+            }
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: wait (bounded) until the copies of the last issued stages have landed.
-      const int outstanding = issued < STAGES ? issued : STAGES;
+      // Drain: wait (bounded) until the copies of the last issued stages have landed (a pair's
+      // copies all count on the leader's barriers).
+      const int outstanding = (!PAIR || leader) ? (issued < STAGES ? issued : STAGES) : 0;
       int s = stage;
       uint32_t ph = phase;
       for (int i = 0; i < outstanding; ++i) {
@@ -499,13 +541,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_bf16_f32(TM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = tile0; t < total_tiles && ok; t += tstride, ++local) {
         int tb, tmb, tnb, tks;
         tile_coords(t, p, tb, tmb, tnb, tks);
         TileWork tw;
@@ -527,12 +569,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // MN-major: step 16 rows of 128 bytes (two 8-row swizzle atoms).
             const uint64_t ad = A_MN ? smem_desc(a_addr + j * 2048, 8192, 1024) : smem_desc(a_addr + j * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc(b_addr + j * 2048, 8192, 1024) : smem_desc(b_addr + j * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb_lo || j != 0) ? 1u : 0u);
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_lo || j != 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, ad, bd, idesc, (kb > kb_lo || j != 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) umma_commit_pair(&empty[stage], 0x3);
+          else umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) {
+          if constexpr (PAIR) umma_commit_pair(&tfull[acc], 0x3);
+          else umma_commit(&tfull[acc]);
+        }
       }
     }
   } else {
@@ -549,7 +596,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const bool reduce = EPI == EPI_F32_ACC && p.split == 1;
         int g = 0;
         int local = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        for (int t = tile0; t < total_tiles; t += tstride, ++local) {
           int b, mb, nb, ks;
           tile_coords(t, p, b, mb, nb, ks);
           TileWork tw;
@@ -560,7 +607,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
           __syncwarp();
           tc_fence_after();
-          const int row0 = mb * BM + quad * 32;
+          const int row0 = (mb * TM + static_cast<int>(crank) * BM) + quad * 32;
           const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c, ++g) {
@@ -570,7 +617,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_ld();
             if (c == BN / 32 - 1) {
               tc_fence_before();
-              mbar_arrive(&tempty[acc]);
+              arrive_tempty<PAIR>(&tempty[acc], crank);
             }
             const int col0 = nb * BN + c * 32;
             uint8_t* sc = stg + (g & 1) * (2 * STG_BOX);  // 4 KB box
@@ -605,7 +652,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int nparts = (p.N + 127) / 128;
         int g = 0;
         int local = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        for (int t = tile0; t < total_tiles; t += tstride, ++local) {
           int b, mb, nb, ks;
           tile_coords(t, p, b, mb, nb, ks);
           TileWork tw;
@@ -616,8 +663,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
           __syncwarp();
           tc_fence_after();
-          const int row = mb * BM + row_in_tile;
-          const int row0 = mb * BM + quad * 32;
+          const int row = (mb * TM + static_cast<int>(crank) * BM) + row_in_tile;
+          const int row0 = (mb * TM + static_cast<int>(crank) * BM) + quad * 32;
           const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
           float se = 0.f;
 #pragma unroll 1
@@ -628,7 +675,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_ld();
             if (c == BN / 32 - 1) {
               tc_fence_before();
-              mbar_arrive(&tempty[acc]);  // the accumulator is in registers: MMA may reuse it
+              arrive_tempty<PAIR>(&tempty[acc], crank);  // the accumulator is in registers: MMA may reuse it
             }
             const int col0 = nb * BN + c * 32;
             uint32_t out[16], pre[16];
@@ -668,7 +715,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (!(bf16_out<EPI>() || EPI == EPI_F32 || EPI == EPI_F32_ACC) || !p.tma_out) {
       int local = 0;
-      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      for (int t = tile0; t < total_tiles; t += tstride, ++local) {
         int b, mb, nb, ks;
         tile_coords(t, p, b, mb, nb, ks);
         TileWork tw;
@@ -679,7 +726,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&tfull[acc], acc_phase, 0x400u + acc, abort_flag)) break;
         __syncwarp();
         tc_fence_after();
-        const int row = mb * BM + row_in_tile;
+        const int row = (mb * TM + static_cast<int>(crank) * BM) + row_in_tile;
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
         if constexpr (EPI == EPI_CE_FWD) {
           const int nparts = (p.N + 127) / 128;
@@ -710,16 +757,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        arrive_tempty<PAIR>(&tempty[acc], crank);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's epilogue has read its tensor memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, 2 * BN);
+    else tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
@@ -829,10 +878,12 @@ static bool out_map_f32(CUtensorMap& map, const void* base, int64_t N, int64_t M
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int A_MN, int B_MN, int EPI>
+template <int BN, int A_MN, int B_MN, int EPI, bool PAIR = false>
 static void launch_t(const GemmArgs& g, cudaStream_t stream) {
-  constexpr int STAGES = BN == 256 ? 4 : 6;
-  using S = Smem<BN, STAGES>;
+  constexpr int BNC = PAIR ? BN / 2 : BN;   // B rows per CTA
+  constexpr int TM = PAIR ? 2 * BM : BM;    // rows per tile
+  constexpr int STAGES = BNC == 256 ? 4 : 6;
+  using S = Smem<BNC, STAGES>;
   // A: logical [M, K].  K-major storage [M rows, K cols] (inner = K); M-major [K rows, M cols].
   const bool grouped = g.grp_m || g.grp_k;
   const int bA = grouped ? 1 : g.batch;
@@ -840,13 +891,13 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   const int bC = g.grp_m ? 1 : (g.grp_k ? g.groups : g.batch);
   CUtensorMap ta = A_MN == 0 ? make_map(g.A, g.K, g.M, g.lda, bA, g.strideA, BM)
                              : make_map(g.A, g.M, g.K, g.lda, bA, g.strideA, BK);
-  CUtensorMap tb = B_MN == 0 ? make_map(g.B, g.K, g.N, g.ldb, bB, g.strideB, BN)
+  CUtensorMap tb = B_MN == 0 ? make_map(g.B, g.K, g.N, g.ldb, bB, g.strideB, BNC)
                              : make_map(g.B, g.N, g.K, g.ldb, bB, g.strideB, BK);
   Params p;
   p.M = g.M; p.N = g.N; p.K = g.K; p.batch = bC;
   p.grp_m = g.grp_m;
   p.grp_k = g.grp_k;
-  p.tiles_m = (g.M + BM - 1) / BM;
+  p.tiles_m = (g.M + TM - 1) / TM;
   p.tiles_n = (g.N + BN - 1) / BN;
   p.epi = EPI;
   p.C = g.C; p.ldc = g.ldc; p.strideC = g.strideC;
@@ -875,15 +926,32 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
                                 : out_map_f32(tc, g.C, g.N, g.M, g.ldc, bC, g.strideC);
     p.tma_out = ok ? 1 : 0;
   }
-  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES, PAIR>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     configured = true;
   }
   const int tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
-  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, tc, tp, p);
+  if constexpr (PAIR) {
+    const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = S::TOTAL;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tp, p);
+  } else {
+    const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+    kern<<<grid, NUM_THREADS, S::TOTAL, stream>>>(ta, tb, tc, tp, p);
+  }
   if (p.split > 1) {
     const int64_t n = static_cast<int64_t>(g.M) * g.N;
     splitk_reduce_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, stream>>>(
@@ -892,31 +960,31 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
   }
 }
 
-template <int BN, int A_MN, int B_MN>
+template <int BN, int A_MN, int B_MN, bool PAIR>
 static void dispatch_epi(const GemmArgs& g, cudaStream_t s) {
   switch (g.epi) {
-    case EPI_BF16: return launch_t<BN, A_MN, B_MN, EPI_BF16>(g, s);
-    case EPI_F32: return launch_t<BN, A_MN, B_MN, EPI_F32>(g, s);
-    case EPI_F32_ACC: return launch_t<BN, A_MN, B_MN, EPI_F32_ACC>(g, s);
-    case EPI_BF16_AXPBY: return launch_t<BN, A_MN, B_MN, EPI_BF16_AXPBY>(g, s);
-    case EPI_RELU2: return launch_t<BN, A_MN, B_MN, EPI_RELU2>(g, s);
-    case EPI_RELU2_BWD: return launch_t<BN, A_MN, B_MN, EPI_RELU2_BWD>(g, s);
+    case EPI_BF16: return launch_t<BN, A_MN, B_MN, EPI_BF16, PAIR>(g, s);
+    case EPI_F32: return launch_t<BN, A_MN, B_MN, EPI_F32, PAIR>(g, s);
+    case EPI_F32_ACC: return launch_t<BN, A_MN, B_MN, EPI_F32_ACC, PAIR>(g, s);
+    case EPI_BF16_AXPBY: return launch_t<BN, A_MN, B_MN, EPI_BF16_AXPBY, PAIR>(g, s);
+    case EPI_RELU2: return launch_t<BN, A_MN, B_MN, EPI_RELU2, PAIR>(g, s);
+    case EPI_RELU2_BWD: return launch_t<BN, A_MN, B_MN, EPI_RELU2_BWD, PAIR>(g, s);
     case EPI_CE_FWD:
-      if constexpr (A_MN == 0 && B_MN == 0) return launch_t<BN, 0, 0, EPI_CE_FWD>(g, s);
+      if constexpr (A_MN == 0 && B_MN == 0) return launch_t<BN, 0, 0, EPI_CE_FWD, PAIR>(g, s);
       throw std::runtime_error("cross-entropy forward epilogue needs K-major operands");
     case EPI_CE_DGRAD:
-      if constexpr (A_MN == 0 && B_MN == 1) return launch_t<BN, 0, 1, EPI_CE_DGRAD>(g, s);
+      if constexpr (A_MN == 0 && B_MN == 1) return launch_t<BN, 0, 1, EPI_CE_DGRAD, PAIR>(g, s);
       throw std::runtime_error("cross-entropy input-gradient epilogue needs A K-major, B N-major");
     default: throw std::runtime_error("unknown gemm epilogue");
   }
 }
 
-template <int BN>
+template <int BN, bool PAIR = false>
 static void dispatch_major(const GemmArgs& g, cudaStream_t s) {
-  if (!g.a_mn && !g.b_mn) return dispatch_epi<BN, 0, 0>(g, s);
-  if (!g.a_mn && g.b_mn) return dispatch_epi<BN, 0, 1>(g, s);
-  if (g.a_mn && !g.b_mn) return dispatch_epi<BN, 1, 0>(g, s);
-  return dispatch_epi<BN, 1, 1>(g, s);
+  if (!g.a_mn && !g.b_mn) return dispatch_epi<BN, 0, 0, PAIR>(g, s);
+  if (!g.a_mn && g.b_mn) return dispatch_epi<BN, 0, 1, PAIR>(g, s);
+  if (g.a_mn && !g.b_mn) return dispatch_epi<BN, 1, 0, PAIR>(g, s);
+  return dispatch_epi<BN, 1, 1, PAIR>(g, s);
 }
 
 }  // namespace gemm
@@ -938,6 +1006,15 @@ int choose_split(const GemmArgs& g) {
   return split;
 }
 }  // namespace
+
+// CTA-pair tiles are the default; NT_GEMM_PAIRS=0 in the environment keeps single-CTA tiles.
+bool gemm_pairs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("NT_GEMM_PAIRS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 size_t nt_gemm_splitk_bytes(const GemmArgs& g) {
   const int split = choose_split(g);
@@ -961,7 +1038,12 @@ void nt_gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
   // shared-memory bandwidth); 128-wide tiles are kept only when 256-wide ones cannot fill the GPU.
   const long tiles256 = static_cast<long>(g.batch) * g.split_k * ((g.M + 127) / 128) * ((g.N + 255) / 256);
   const bool wide = g.N >= 256 && tiles256 >= g.num_sms;
-  if (wide) dispatch_major<256>(g, stream);
+  // CTA pairs (256 x 256 tiles over two SMs) when the problem still fills every SM pair
+  const long pair_tiles = static_cast<long>(g.batch) * ((g.M + 255) / 256) * ((g.N + 255) / 256);
+  const bool pair = wide && g.split_k == 1 && !g.grp_m && !g.grp_k && pair_tiles >= g.num_sms / 2 &&
+                    gemm_pairs_enabled();
+  if (pair) dispatch_major<256, true>(g, stream);
+  else if (wide) dispatch_major<256>(g, stream);
   else dispatch_major<128>(g, stream);
 }
 

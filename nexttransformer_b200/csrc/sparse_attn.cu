@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(192, 1)
     const int qpos = q0 + r;
     const uint32_t lrow = static_cast<uint32_t>(quad * 32) << 16;
     float m_used = -INFINITY, lsum = 0.f;
-    int consumed = 0;  // completions of o_done observed
+    int consumed = 0;  // completions of o_done observed (consumed == l or l - 1 at step l)
     bool ok = true;
     for (int l = 0; l < L && ok; ++l) {
       const int st = l & 1;
@@ -225,13 +225,15 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = 0; i < 64; ++i) mx = fmaxf(mx, x[i]);
       const float m_new = fmaxf(m_used, mx);
       const bool grow = m_new > m_used + 8.f;
+      // o_done completes once per block.  Completion l - 1 is waited for here, at step l and before
+      // this step's p_full arrival: completion l needs that arrival, so the barrier is in phase
+      // l - 1 or l and the parity wait is unambiguous (a lazier wait could fall two phases behind).
+      if (consumed < l) {
+        if (!warp_wait(o_done, (l - 1) & 1, 0xC31u, abort_flag)) { ok = false; break; }
+        consumed = l;
+      }
       if (__any_sync(0xffffffffu, grow && m_used != -INFINITY)) {
-        // rescale O: every product issued so far must have landed
-        while (consumed < l) {
-          if (!warp_wait(o_done, consumed & 1, 0xC31u, abort_flag)) { ok = false; break; }
-          ++consumed;
-        }
-        if (!ok) break;
+        // rescale O: every product issued so far has landed (waited above)
         tc_fence_after();
         const float f = (grow && m_used != -INFINITY) ? fast_exp2(m_used - m_new) : 1.f;
 #pragma unroll 1
@@ -249,12 +251,7 @@ __global__ void __launch_bounds__(192, 1)
         if (m_used != -INFINITY) lsum *= fast_exp2(m_used - m_new);
         m_used = m_new;
       }
-      // the P buffer of this parity was last read by the product of block l - 2
-      while (consumed < l - 1) {
-        if (!warp_wait(o_done, consumed & 1, 0xC32u, abort_flag)) { ok = false; break; }
-        ++consumed;
-      }
-      if (!ok) break;
+      // the P buffer of this parity was last read by the product of block l - 2 (waited above)
       uint8_t* pb = sm + FwdSmem::P0 + st * QBOX;
       const float mu = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
@@ -273,11 +270,10 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&p_full[st]);
     }
-    if (ok) {
-      while (consumed < L) {
-        if (!warp_wait(o_done, consumed & 1, 0xC33u, abort_flag)) { ok = false; break; }
-        ++consumed;
-      }
+    if (ok && L > 0 && consumed < L) {
+      // completion L - 1 (the last product); consumed == L - 1 here
+      if (!warp_wait(o_done, (L - 1) & 1, 0xC33u, abort_flag)) ok = false;
+      else consumed = L;
     }
     tc_fence_after();
     const bool live = qpos < p.T;

@@ -17,6 +17,11 @@ Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, v
   muon                                                 - the Muon chain on 20 matrices [5120, 1280]
   step                                                 - one fused training micro-step (all kernels)
   attn_bwd_trace                                       - clock stamps of the first backward CTA per pair
+  delta_scan_fwd, delta_scan_bwd                       - chunked delta-rule scan, B*H = rows/4096*12, T 4096
+  sparse_fwd, sparse_bwd                               - block-sparse attention (NSA shape: 16 / 1 heads,
+                                                         16 selected 64-key blocks per row), T 8192
+  moe_fwd, moe_fwd_bwd                                 - grouped experts: 64 x (2048 -> 1024 -> 2048), top-8
+  sinkhorn                                             - mHC Sinkhorn-Knopp (20 iterations) fwd + bwd
 """
 import argparse
 import json
@@ -145,6 +150,82 @@ def attn_bwd_trace(rows):
     return out
 
 
+def case_delta(kind, rows):
+    from nexttransformer_b200.ops.linear_attention import _DeltaScan
+    T, H = 4096, 12
+    B = max(1, rows // T)
+    N = T // 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def r(*s):
+        return (torch.randn(*s, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    w, u0, qt, kc, aqk = r(B, H, N, 64, 128), r(B, H, N, 64, 128), r(B, H, N, 64, 128), r(B, H, N, 64, 128), \
+        r(B, H, N, 64, 64)
+    carry = torch.full((B, H, N, 128), 0.97, device="cuda")
+    flops_fwd = B * H * N * 2 * (128 * 128 * 128 + 2 * 64 * 64 * 128 + 128 * 64 * 128)
+    if kind == "delta_scan_fwd":
+        return (lambda: _DeltaScan.apply(w, u0, qt, kc, aqk, carry)), flops_fwd
+    ins = [t.clone().requires_grad_() for t in (w, u0, qt, kc, aqk)] + [carry.clone().requires_grad_()]
+    o = _DeltaScan.apply(*ins)
+    do = torch.randn_like(o)
+    return (lambda: torch.autograd.grad(o, ins, do, retain_graph=True)), 2 * flops_fwd
+
+
+def case_sparse(kind, rows):
+    from nexttransformer_b200.ops.sparse_attention import block_lists, block_sparse_attention
+    T, H, Hk, D, nsel = 8192, 16, 1, 128, 16
+    B = max(1, rows // T)
+    NB = T // 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+    score = torch.rand(B, 1, T, NB, device="cuda", generator=g)
+    pos_blk = torch.arange(T, device="cuda") // 64
+    allowed = torch.arange(NB, device="cuda")[None, :] <= pos_blk[:, None]
+    top = score.masked_fill(~allowed, -1.0).topk(nsel, -1).indices
+    blocks = torch.zeros(B, 1, T, NB, dtype=torch.bool, device="cuda").scatter_(-1, top, True) & allowed
+    lists, masks = block_lists(blocks)
+    q = _bf16(B, T, H, D).mul_(0.3).requires_grad_(kind == "sparse_bwd")
+    k = _bf16(B, T, Hk, D).mul_(0.3).requires_grad_(kind == "sparse_bwd")
+    v = _bf16(B, T, Hk, D).requires_grad_(kind == "sparse_bwd")
+    pairs = int((blocks.repeat_interleave(64, -1)[..., :T] &
+                 (torch.arange(T, device="cuda")[None, :] <= torch.arange(T, device="cuda")[:, None])).sum()) * H
+    flops = 4 * D * pairs
+    if kind == "sparse_fwd":
+        return (lambda: block_sparse_attention(q, k, v, lists, masks)), flops
+    y = block_sparse_attention(q, k, v, lists, masks)
+    dy = torch.randn_like(y)
+    return (lambda: torch.autograd.grad(y, (q, k, v), dy, retain_graph=True)), 2.5 * flops
+
+
+def case_moe(kind, rows):
+    from nexttransformer_b200.ops.moe import grouped_experts
+    E, k, d, F = 64, 8, 2048, 1024
+    T = rows // 4
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = _bf16(T, d).requires_grad_(kind == "moe_fwd_bwd")
+    choice = torch.rand(T, E, device="cuda", generator=g).topk(k, -1).indices
+    w = torch.full((T, k), 1.0 / k, device="cuda")
+    wf = (torch.randn(E, F, d, device="cuda") * 0.02).requires_grad_(kind == "moe_fwd_bwd")
+    wp = (torch.randn(E, d, F, device="cuda") * 0.02).requires_grad_(kind == "moe_fwd_bwd")
+    flops = 2 * T * k * 2 * d * F
+    if kind == "moe_fwd":
+        return (lambda: grouped_experts(x, choice, w, wf, wp)), flops
+
+    def run():
+        y = grouped_experts(x, choice, w, wf, wp)
+        torch.autograd.grad(y, (x, wf, wp), torch.ones_like(y))
+    return run, 3 * flops
+
+
+def case_sinkhorn(rows):
+    from nexttransformer_b200.models.residual import sinkhorn_knopp
+    z = torch.randn(rows, 4, 4, device="cuda").requires_grad_()
+    g = torch.randn(rows, 4, 4, device="cuda")
+
+    def run():
+        torch.autograd.grad(sinkhorn_knopp(z, 20), z, g)
+    return run, None, rows * 16 * 4 * 5
+
+
 def case_ce(rows):
     from nexttransformer_b200.ops._ext import ext
     logits = _bf16(rows, VOCAB)
@@ -219,6 +300,14 @@ def main(argv=None):
         fn, flops = case_gemm(a.case, a.rows)
     elif a.case.startswith("attn_"):
         fn, flops = case_attn(a.case, a.rows)
+    elif a.case.startswith("delta_scan"):
+        fn, flops = case_delta(a.case, a.rows)
+    elif a.case.startswith("sparse_"):
+        fn, flops = case_sparse(a.case, a.rows)
+    elif a.case.startswith("moe_"):
+        fn, flops = case_moe(a.case, a.rows)
+    elif a.case == "sinkhorn":
+        fn, flops, byts = case_sinkhorn(a.rows)
     elif a.case == "ce":
         fn, flops, byts = case_ce(a.rows)
     elif a.case == "adamw":

@@ -4,8 +4,9 @@ Column-parallel: each rank holds an output slice W_r [N / P, K]; y_r = x W_r^T, 
 all-gathered.  Row-parallel: each rank holds an input slice W_r [N, K / P] and its activation
 slice x_r; y = sum_r x_r W_r^T via a reduce-scatter over tokens (sequence-parallel output) or an
 all-reduce.  ``MLPTP`` pairs them (column fc -> ReLU^2 -> row proj), the standard Megatron split
-with one collective per direction.  On CUDA the GEMM -> reduce-scatter and all-gather -> GEMM
-pairs run as fused peer-memory kernels (``parallel.fused``); elsewhere NCCL/gloo collectives.
+with one collective per direction.  The collectives are NCCL (gloo on CPU) calls around the GEMMs:
+this is the baseline form; the all-gather -> GEMM and GEMM -> reduce-scatter pairs are not yet fused
+into peer-memory kernels.
 """
 import torch
 import torch.distributed as dist

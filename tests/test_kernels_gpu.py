@@ -37,10 +37,11 @@ def test_gemm_storage_orders(M, N, K, a_mn, b_mn):
     check_errors()
 
 
-def test_gemm_epilogues():
+@pytest.mark.parametrize("M,N,K", [(512, 384, 256), (4096, 4608, 384), (3000, 4864, 320)])
+def test_gemm_epilogues(M, N, K):
+    """Every epilogue; the larger shapes run on CTA pairs (256 x 256 tiles over two SMs)."""
     from nexttransformer_b200.ops import gemm as G
     torch.manual_seed(1)
-    M, N, K = 512, 384, 256
     A = torch.randn(M, K, device="cuda").bfloat16()
     B = (torch.randn(N, K, device="cuda") / 16).bfloat16()
     ref = A.float() @ B.float().t()
