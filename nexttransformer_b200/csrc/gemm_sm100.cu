@@ -1007,11 +1007,11 @@ int choose_split(const GemmArgs& g) {
 }
 }  // namespace
 
-// CTA-pair tiles are the default; NT_GEMM_PAIRS=0 in the environment keeps single-CTA tiles.
+// CTA-pair tiles run when NT_GEMM_PAIRS=1 is set in the environment (single-CTA tiles otherwise).
 bool gemm_pairs_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("NT_GEMM_PAIRS");
-    return !(v && v[0] == '0');
+    return v && v[0] == '1';
   }();
   return on;
 }
