@@ -496,17 +496,19 @@ __global__ void __launch_bounds__(320, 1)
     }
     if (ok && L > 0 && !warp_wait(mma2_done, (L - 1) & 1, 0xD32u, abort_flag)) ok = false;
     tc_fence_after();
-    if (live) {
-      __nv_bfloat16* drow = p.dq + (static_cast<int64_t>(b) * p.T + qpos) * p.lddq + h * HD;
+    // the aligned TMEM loads run on every lane (warp-uniform condition); only live rows store
+    __nv_bfloat16* drow = p.dq + (static_cast<int64_t>(b) * p.T + (live ? qpos : 0)) * p.lddq + h * HD;
+    const bool have = L > 0 && ok;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t a[32];
+    for (int c = 0; c < 4; ++c) {
+      uint32_t a[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] = 0u;
-        if (L > 0 && ok) {
-          tmem_ld32(t_dq + lrow + c * 32, a);
-          tmem_wait_ld();
-        }
+      for (int i = 0; i < 32; ++i) a[i] = 0u;
+      if (have) {
+        tmem_ld32(t_dq + lrow + c * 32, a);
+        tmem_wait_ld();
+      }
+      if (live) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           *reinterpret_cast<uint4*>(drow + c * 32 + j * 8) =
@@ -514,14 +516,6 @@ __global__ void __launch_bounds__(320, 1)
                          pack_bf16x2(__uint_as_float(a[j * 8 + 2]), __uint_as_float(a[j * 8 + 3])),
                          pack_bf16x2(__uint_as_float(a[j * 8 + 4]), __uint_as_float(a[j * 8 + 5])),
                          pack_bf16x2(__uint_as_float(a[j * 8 + 6]), __uint_as_float(a[j * 8 + 7])));
-      }
-    } else if (L > 0 && ok) {
-      // keep the warp converged for the aligned TMEM loads of its live lanes
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t a[32];
-        tmem_ld32(t_dq + lrow + c * 32, a);
-        tmem_wait_ld();
       }
     }
   } else {

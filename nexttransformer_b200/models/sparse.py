@@ -235,7 +235,7 @@ class SparseMixer(nn.Module):
         if self.backend not in BACKENDS:
             raise ValueError(f"unknown sparse backend {self.backend!r}")
         kernel = self.backend == "kernel" and x.is_cuda
-        if kernel and self._blocks_supported(x):
+        if self.backend == "kernel" and self._blocks_supported(x):
             return self._forward_blocks(x, q, k, v)
         aux, outputs = [], []
         edges = teacher_edges = 0
@@ -337,7 +337,9 @@ class SparseMixer(nn.Module):
     def _blocks_supported(self, x):
         """MoBA and NSA whose selection unit is a multiple of 64 keys run the block-sparse kernels."""
         c = self.config
-        if self.kind not in ("moba", "nsa") or self.head_dim != 128 or x.dtype != torch.bfloat16:
+        if self.kind not in ("moba", "nsa") or self.head_dim != 128:
+            return False
+        if x.is_cuda and x.dtype != torch.bfloat16:
             return False
         sel = c.block_size if (self.kind == "moba" or c.compression_stride) else c.compression_size
         return sel % 64 == 0
@@ -391,7 +393,12 @@ class SparseMixer(nn.Module):
         if self.kind == "moba":
             y = selected
         else:
-            local = attention_bthd(q.transpose(1, 2), k_raw, v_raw, c.local_window - 1)
+            if x.is_cuda:
+                local = attention_bthd(q.transpose(1, 2), k_raw, v_raw, c.local_window - 1)
+            else:
+                pos = torch.arange(T, device=dev)
+                win = (pos[None, :] <= pos[:, None]) & (pos[:, None] - pos[None, :] < c.local_window)
+                local = F.scaled_dot_product_attention(q, k, v, attn_mask=win).transpose(1, 2)
             comp = torch.cat(compressed, 2).transpose(1, 2).to(selected.dtype)
             y = comp * gates[..., 0:1] + selected * gates[..., 1:2] + local * gates[..., 2:3]
             lw = torch.arange(T, device=dev).clamp_max(c.local_window - 1) + 1

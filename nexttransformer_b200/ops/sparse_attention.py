@@ -71,8 +71,38 @@ class _BlockSparseAttention(Function):
                 None, None, None)
 
 
+def visibility(lists, masks, T):
+    """Dense [B, G, T, T] key visibility of block lists (row t sees key j of its selected blocks, j <= t)."""
+    B, G, n_qt, Lmax = lists.shape
+    bits = ((masks.to(torch.int64) & 0xFFFFFFFF)[..., None] >> torch.arange(32, device=masks.device)) & 1
+    rows = bits.reshape(B, G, n_qt, Lmax, QT).bool()                     # [B, G, n_qt, L, 128]
+    nb = (T + KB - 1) // KB
+    # padding entries (-1) scatter into an extra column that is dropped
+    sel = torch.zeros(B, G, n_qt, QT, nb + 1, dtype=torch.bool, device=lists.device)
+    idx = torch.where(lists >= 0, lists, torch.full_like(lists, nb)).long()[..., None, :].expand(-1, -1, -1, QT, -1)
+    sel.scatter_(-1, idx, rows.transpose(-1, -2))
+    sel = sel[..., :nb].reshape(B, G, n_qt * QT, nb)[:, :, :T].repeat_interleave(KB, -1)[..., :T]
+    pos = torch.arange(T, device=lists.device)
+    return sel & (pos[None, :] <= pos[:, None])
+
+
+def block_sparse_reference(q, k, v, lists, masks, scale):
+    """The same attention in fp32 PyTorch (dense masked softmax), the oracle of the kernels."""
+    B, T, H, D = q.shape
+    Hk, G = k.shape[2], lists.shape[1]
+    vis = visibility(lists, masks, T).repeat_interleave(H // G, 1)
+    kk = k.float().repeat_interleave(H // Hk, 2).transpose(1, 2)
+    vv = v.float().repeat_interleave(H // Hk, 2).transpose(1, 2)
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float().transpose(1, 2), kk) * scale
+    s = s.masked_fill(~vis, -torch.inf)
+    p = torch.where(vis.any(-1, keepdim=True), s.softmax(-1).nan_to_num(0.0), torch.zeros_like(s))
+    return torch.einsum("bhqk,bhkd->bhqd", p, vv).transpose(1, 2).to(q.dtype)
+
+
 def block_sparse_attention(q, k, v, lists, masks, scale=None):
     scale = q.shape[-1] ** -.5 if scale is None else scale
+    if not q.is_cuda:
+        return block_sparse_reference(q, k, v, lists, masks, scale)
     return _BlockSparseAttention.apply(q, k, v, lists, masks, scale)
 
 

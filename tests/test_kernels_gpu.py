@@ -303,3 +303,40 @@ def test_fused_head_cross_entropy(M, V, d):
     e1 = (dh.float() - ref_dh).abs().max().item() / ref_dh.abs().max().item()
     e2 = (dW - ref_dw).abs().max().item() / ref_dw.abs().max().item()
     assert e1 < 2e-2 and e2 < 2e-2, (e1, e2)
+
+
+PAIR_CHECK = r"""
+import torch, torch.nn.functional as F
+from nexttransformer_b200.ops import gemm as G
+from nexttransformer_b200.ops._ext import check_errors
+torch.manual_seed(0)
+def close(a, b, rtol, atol):
+    err = (a.float() - b.float()).abs().max().item(); ref = b.float().abs().max().item()
+    assert err <= atol + rtol * ref, (err, ref)
+for M, N, K in ((4096, 2560, 1280), (3000, 4864, 320)):
+    for a_mn, b_mn in ((False, False), (False, True), (True, False), (True, True)):
+        A = torch.randn(M, K, device="cuda").bfloat16(); B = (torch.randn(N, K, device="cuda") / 16).bfloat16()
+        a = A.t().contiguous() if a_mn else A; b = B.t().contiguous() if b_mn else B
+        ref = A.float() @ B.float().t()
+        C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        G.gemm(a, b, C, a_mn=a_mn, b_mn=b_mn); torch.cuda.synchronize(); close(C, ref, 1e-2, 1e-1)
+        Cf = torch.ones(M, N, device="cuda")
+        G.gemm(a, b, Cf, a_mn=a_mn, b_mn=b_mn, epi=G.EPI_F32_ACC, s_acc=0.5); close(Cf, 1 + 0.5 * ref, 1e-3, 1e-2)
+        P = torch.empty_like(C)
+        G.gemm(a, b, C, a_mn=a_mn, b_mn=b_mn, epi=G.EPI_RELU2, p=P)
+        close(P, ref, 1e-2, 5e-2); close(C, F.relu(P.float()).square(), 1e-2, 5e-2)
+        R = torch.randn(M, N, device="cuda").bfloat16()
+        G.gemm(a, b, C, a_mn=a_mn, b_mn=b_mn, epi=G.EPI_BF16_AXPBY, r=R, s_acc=2.0, s_res=-0.5)
+        close(C, 2 * ref - 0.5 * R.float(), 2e-2, 5e-2)
+torch.cuda.synchronize(); check_errors(); print("pairs ok")
+"""
+
+
+def test_gemm_cta_pairs():
+    """CTA-pair tiles (NT_GEMM_PAIRS=1, read once per process) on shapes that select them."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, NT_GEMM_PAIRS="1")
+    r = subprocess.run([sys.executable, "-c", PAIR_CHECK], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "pairs ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
