@@ -892,6 +892,7 @@ static bool supported(const AttnArgs& a) {
 }
 
 int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
+  nt::current_context();
   if (!supported(a)) return -1;
   CUtensorMap tq = tile_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B);
   CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
@@ -910,6 +911,7 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
 }
 
 int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
+  nt::current_context();
   if (!supported(a)) return -1;
   if (reinterpret_cast<uintptr_t>(a.dq) % 8 || a.lddq % 4) return -1;
   const int64_t rows = static_cast<int64_t>(a.B) * a.T;

@@ -15,6 +15,14 @@
 
 namespace nt {
 
+// Host side: make the device's primary context current in the calling thread.  Tensor maps are
+// encoded with a driver call, which needs a current context; an autograd worker thread whose
+// first CUDA work is one of our backward functions may not have one yet.
+inline void current_context() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+}
+
 // ---------------------------------------------------------------- error flag
 // Every bounded wait in this library gives up after a time limit, records where it gave
 // up in a device-global error word and lets the kernel fall through, so a broken pipeline

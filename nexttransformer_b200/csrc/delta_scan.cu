@@ -547,6 +547,7 @@ CUtensorMap map2d(const void* base, int64_t cols, int64_t rows) {
 using namespace nt;
 
 int nt_delta_scan_fwd(const DeltaScanFwdArgs& a, cudaStream_t stream) {
+  nt::current_context();
   if (a.BH <= 0 || a.N <= 0) return -1;
   const int64_t rows = static_cast<int64_t>(a.BH) * a.N * CH;
   const CUtensorMap tw = map2d(a.w, DK, rows), tq = map2d(a.qt, DK, rows), tk = map2d(a.kc, DK, rows),
@@ -561,6 +562,7 @@ int nt_delta_scan_fwd(const DeltaScanFwdArgs& a, cudaStream_t stream) {
 }
 
 int nt_delta_scan_bwd(const DeltaScanBwdArgs& a, cudaStream_t stream) {
+  nt::current_context();
   if (a.BH <= 0 || a.N <= 0) return -1;
   const int64_t rows = static_cast<int64_t>(a.BH) * a.N * CH;
   const CUtensorMap td = map2d(a.dout, DV, rows), ta = map2d(a.aqk, CH, rows), tk = map2d(a.kc, DK, rows),

@@ -1007,11 +1007,11 @@ int choose_split(const GemmArgs& g) {
 }
 }  // namespace
 
-// CTA-pair tiles run when NT_GEMM_PAIRS=1 is set in the environment (single-CTA tiles otherwise).
+// CTA-pair tiles are the default; NT_GEMM_PAIRS=0 in the environment keeps single-CTA tiles.
 bool gemm_pairs_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("NT_GEMM_PAIRS");
-    return v && v[0] == '1';
+    return !(v && v[0] == '0');
   }();
   return on;
 }
@@ -1022,6 +1022,7 @@ size_t nt_gemm_splitk_bytes(const GemmArgs& g) {
 }
 
 void nt_gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
+  nt::current_context();
   using namespace nt::gemm;
   GemmArgs g = g_in;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return;

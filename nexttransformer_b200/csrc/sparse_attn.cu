@@ -647,6 +647,7 @@ Params make_params(const SparseAttnArgs& a) {
 using namespace nt::bsa;
 
 int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s) {
+  nt::current_context();
   if (a.D != HD || a.H % a.Hk || a.H % a.G || a.Lmax <= 0 || a.T <= 0) return -1;
   const Params p = make_params(a);
   const CUtensorMap tq = row_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B, QT);
@@ -661,6 +662,7 @@ int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s) {
 }
 
 int nt_sparse_attn_bwd(const SparseAttnArgs& a, cudaStream_t s) {
+  nt::current_context();
   if (a.D != HD || a.H % a.Hk || a.H % a.G || a.Lmax <= 0 || a.T <= 0) return -1;
   const Params p = make_params(a);
   const CUtensorMap tq = row_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B, QT);
