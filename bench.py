@@ -210,6 +210,8 @@ def bench_method(args, rank, world, local, device):
             from nexttransformer_b200.models.config import candidate_config
             config = replace(candidate_config(raw["method"]), **{k: v for k, v in raw.items() if k != "method"})
             model = build_model(config, device, seed=42)
+            if raw["method"] in ("nsa", "moba"):
+                model.set_sparse_backend("kernel")      # block-sparse sm_100a kernels
             if raw["method"] == "moe" and world > 1:
                 from nexttransformer_b200.parallel.expert import enable_expert_parallel
                 enable_expert_parallel(model)

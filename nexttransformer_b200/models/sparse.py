@@ -240,6 +240,11 @@ class SparseMixer(nn.Module):
         aux, outputs = [], []
         edges = teacher_edges = 0
         chunk = c.reference_chunk
+        # Seer on the kernel backend: selection and distillation as below, attention in one
+        # block-sparse pass over the collected block membership
+        collect = self.backend == "kernel" and self.kind == "seer" and self.head_dim == 128 \
+            and c.block_size % 64 == 0 and (x.dtype == torch.bfloat16 or not x.is_cuda)
+        mems = []
         if learned:
             iq, ik, iw, size = self._index(x)
         else:
@@ -297,7 +302,14 @@ class SparseMixer(nn.Module):
                 if burnin:
                     idx = torch.arange(T, device=x.device)[None, None, None].expand(B, H, stop - start, -1)
                     valid = causal[None, None].expand_as(idx)
-                out = self._attend(qq, k, v, idx, valid, T, kernel)
+                if collect:
+                    nsel = ik.shape[2]
+                    cnt = torch.zeros(B, 1, stop - start, nsel, dtype=torch.int32, device=x.device)
+                    cnt.scatter_add_(-1, (idx[:, :1] // size).clamp_max(nsel - 1), valid[:, :1].to(torch.int32))
+                    mems.append(cnt > 0)
+                    out = None
+                else:
+                    out = self._attend(qq, k, v, idx, valid, T, kernel)
             elif self.kind == "moba":
                 sc = torch.matmul(qq, pooled.transpose(-2, -1))
                 complete = (torch.arange(pooled.shape[2], device=x.device) + 1) * size - 1 <= pos[:, None]
@@ -327,13 +339,32 @@ class SparseMixer(nn.Module):
                 edges += int(lv.sum()) + B * H * (stop - start) * ck.shape[2]
             edges += int(valid.sum())
             outputs.append(out)
-        y = torch.cat(outputs, 2).transpose(1, 2).reshape(B, T, d)
+        if collect:
+            y = self._collected_attention(x, q, k, v, mems, size, burnin).reshape(B, T, d)
+        else:
+            y = torch.cat(outputs, 2).transpose(1, 2).reshape(B, T, d)
         self.last_aux = sum(aux, x.new_zeros(())) * c.index_loss_weight
         self.last_stats = {"selected_edges": edges, "teacher_dense_score_edges": teacher_edges, "burnin": burnin,
                            "backend": self.backend}
         return self.c_proj(y)
 
     # ------------------------------------------------------------ block-sparse kernel path
+    def _collected_attention(self, x, q, k, v, mems, size, dense):
+        """Attention of every row over its collected blocks (all causal keys when `dense`): one pass of
+        the block-sparse kernels (the causal kernel during burn-in), [B, T, H, D]."""
+        from nexttransformer_b200.ops.sparse_attention import block_lists, block_sparse_attention
+        B, H, T, D = q.shape
+        rep = H // self.n_kv_head
+        k_raw, v_raw = k[:, ::rep].transpose(1, 2), v[:, ::rep].transpose(1, 2)
+        if dense:
+            if x.is_cuda:
+                from nexttransformer_b200.ops.attention import attention_bthd
+                return attention_bthd(q.transpose(1, 2), k_raw, v_raw, -1)
+            return F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2)
+        blocks = torch.cat(mems, 2).repeat_interleave(size // 64, -1)[..., :(T + 63) // 64]
+        lists, masks = block_lists(blocks)
+        return block_sparse_attention(q.transpose(1, 2), k_raw, v_raw, lists, masks, D ** -.5)
+
     def _blocks_supported(self, x):
         """MoBA and NSA whose selection unit is a multiple of 64 keys run the block-sparse kernels."""
         c = self.config

@@ -44,3 +44,26 @@ def test_block_lists_visibility_roundtrip():
     pos = torch.arange(T)
     want = blocks.repeat_interleave(64, -1)[..., :T] & (pos[None, :] <= pos[:, None])
     assert torch.equal(vis, want)
+
+
+@pytest.mark.parametrize("burnin", [False, True])
+def test_seer_block_path_matches_reference(burnin):
+    """Seer (learned 64-key block selection): the collected block pass against the gathered-key path,
+    aux (distillation) loss included."""
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.models.sparse import SparseMixer
+    T = 256
+    c = replace(debug_config("seer", width=256, sequence_len=T), heads=2, block_size=64, sparse_topk=128)
+    torch.manual_seed(2)
+    mix = SparseMixer(c, 1)
+    mix.train()
+    mix.in_burnin = burnin
+    x = torch.randn(2, T, 256)
+    cs = _cos_sin(T, 128)
+    outs, auxs = [], []
+    for backend in ("reference", "kernel"):
+        mix.backend = backend
+        outs.append(mix(x, None, cs, None))
+        auxs.append(mix.last_aux)
+    torch.testing.assert_close(outs[1], outs[0], atol=2e-5, rtol=1e-4)
+    torch.testing.assert_close(auxs[1], auxs[0])
