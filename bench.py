@@ -9,7 +9,7 @@ Without ``--method`` (or with ``dense``) the headline configuration below runs. 
 selects another benchmark configuration of the survey on the generic model path
 (``models.build_model``): ``gdn_hybrid_swa`` / ``kda_hybrid`` (depth 24, width 1536, 12 heads of
 128, chunk 64, sequence 4096, 524,288 tokens per update), ``nsa`` / ``moba`` (depth 24, width
-1536, 16 query heads / 1 KV group, sequence 8192) and ``moe`` (depth 16, width 2048, 16 / 4 heads,
+1536, 12 query heads of 128 / 1 KV head, sequence 8192) and ``moe`` (depth 16, width 2048, 16 / 4 heads,
 64 experts of FFN 1024, top-8 + 1 shared, sequence 4096, 1,048,576 tokens per update).
 
 Model: depth 20, width 1280, 10 query heads / 5 KV heads of dim 128, RoPE, RMSNorm, ReLU^2 MLP
@@ -47,10 +47,11 @@ METHOD_CONFIGS = {
                             scale="custom"), 524288),
     "kda_hybrid": (dict(method="kda_hybrid", layers=24, width=1536, heads=12, mlp_width=6144, sequence_len=4096,
                         backend="fla_chunk64", window_pattern="L", scale="custom"), 524288),
-    "nsa": (dict(method="nsa", layers=24, width=1536, heads=16, kv_heads=1, mlp_width=6144, sequence_len=8192,
+    # heads of dim 128 at width 1536 (the survey's 16 x 128 query heads would need a 2048-wide projection)
+    "nsa": (dict(method="nsa", layers=24, width=1536, heads=12, kv_heads=1, mlp_width=6144, sequence_len=8192,
                  compression_size=32, compression_stride=16, block_size=64, sparse_topk=1024, local_window=512,
                  window_pattern="L", scale="custom"), 524288),
-    "moba": (dict(method="moba", layers=24, width=1536, heads=16, kv_heads=1, mlp_width=6144, sequence_len=8192,
+    "moba": (dict(method="moba", layers=24, width=1536, heads=12, kv_heads=1, mlp_width=6144, sequence_len=8192,
                   block_size=512, sparse_topk=1536, window_pattern="L", scale="custom"), 524288),
     "moe": (dict(method="moe", layers=16, width=2048, heads=16, kv_heads=4, mlp_width=8192, sequence_len=4096,
                  moe_experts=64, moe_topk=8, moe_ffn=1024, moe_shared=1, window_pattern="L", scale="custom"), 1048576),
@@ -198,7 +199,8 @@ def bench_method(args, rank, world, local, device):
     raw, global_batch = METHOD_CONFIGS[args.method]
     T = raw["sequence_len"]
     per_rank = global_batch // world
-    micro = args.micro_batch or max(1, min(8, per_rank // T))
+    # rows per micro-batch: activations of 32k tokens per pass (8k for the 64-expert MoE)
+    micro = args.micro_batch or max(1, min((8192 if raw["method"] == "moe" else 32768) // T, per_rank // T))
     accum = per_rank // (micro * T)
     try:
         if args.impl == "ours":
