@@ -444,6 +444,15 @@ def main():
         e2e = {"value": GLOBAL_BATCH / (ms2 / 1000.0), "unit": "tokens/s", "ms_per_step": ms2,
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4}
 
+    # every rank must hold the same parameters after the updates (checks the parameter all-gather)
+    params_agree = None
+    if world > 1:
+        digest = torch.stack([sum(p.detach().double().sum() for p in model.parameters()),
+                              sum(p.detach().double().abs().sum() for p in model.parameters())])
+        all_d = [torch.empty_like(digest) for _ in range(world)]
+        dist.all_gather(all_d, digest)
+        params_agree = all(bool(torch.equal(d, all_d[0])) for d in all_d)
+
     launches = None
     if args.impl == "ours":
         try:
@@ -469,7 +478,7 @@ def main():
                           "grad_comm": (args.comm if world > 1 else "none") if args.impl == "ours" else "nccl",
                           "param_gather": ("p2p" if args.comm == "p2p" else "nccl") if world > 1 and args.impl == "ours"
                           else ("none" if world == 1 else "nccl"),
-                          "flops_per_token": flops_per_token},
+                          "flops_per_token": flops_per_token, "params_equal_across_ranks": params_agree},
                "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": final_loss}
         if args.impl == "reference":
             out["impl"] = "reference"
