@@ -715,16 +715,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_after();
       const bool leader = threadIdx.x == 192;  // warp 6, lane 0: issues the bulk reductions
       uint8_t* stg = sm + BwdSmem::DST;
-#pragma unroll 1
+      // the whole dQ row comes into registers first, so tDP is released for the next dP^T at once
+      uint32_t vq[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_dp + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&vq[c * 32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dq_free);  // tDP may take the next dP^T
+#pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t v[64];
-        tmem_ld32(t_dp + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(t_dp + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_wait_ld();
-        if (half == 1) {
-          tc_fence_before();
-          mbar_arrive(dq_free);  // tDP may take the next dP^T
-        }
+        const uint32_t* v = vq + half * 64;
         // staging must be free: read by the previous reduction (none before the first half of pair 0)
         const int k = 2 * it + half - 1;
         if (k >= 0 && !mbar_wait(stg_free, k & 1, 0x7Au, abort_flag)) { it = n_it; break; }

@@ -100,3 +100,34 @@ def test_sparse_mixer_kernel_matches_reference(kind):
         mix.zero_grad()
     assert _rel(outs[1], outs[0]) < 3e-2
     assert _rel(grads[1], grads[0]) < 5e-2
+
+
+@pytest.mark.parametrize("kind", ["moba", "nsa"])
+def test_sparse_mixer_kernel_matches_reference_bench_shape(kind):
+    """The benchmark's selection shapes (MoBA 512-key blocks top-3, NSA stride-16 compression with
+    64-key selection, 12 query heads / 1 KV head) at T 2048: kernel path against the reference path."""
+    from dataclasses import replace
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.models.sparse import SparseMixer
+    T = 2048
+    c = debug_config(kind, width=1536, sequence_len=T)
+    extra = dict(block_size=512, sparse_topk=1536) if kind == "moba" else \
+        dict(compression_size=32, compression_stride=16, block_size=64, sparse_topk=1024, local_window=512)
+    c = replace(c, heads=12, kv_heads=1, **extra)
+    torch.manual_seed(5)
+    mix = SparseMixer(c, 1).cuda().to(torch.bfloat16)
+    x = torch.randn(1, T, 1536, device="cuda").to(torch.bfloat16)
+    t = torch.arange(T, dtype=torch.float32, device="cuda")
+    f = torch.outer(t, 1.0 / (100000 ** (torch.arange(0, 128, 2, device="cuda").float() / 128)))
+    cos_sin = (f.cos().to(torch.bfloat16)[None, :, None, :], f.sin().to(torch.bfloat16)[None, :, None, :])
+    outs, grads = [], []
+    for backend in ("reference", "kernel"):
+        mix.backend = backend
+        xi = x.clone().requires_grad_()
+        y = mix(xi, None, cos_sin, None)
+        y.float().square().mean().backward()
+        outs.append(y.detach())
+        grads.append(xi.grad.detach())
+        mix.zero_grad()
+    assert _rel(outs[1], outs[0]) < 3e-2
+    assert _rel(grads[1], grads[0]) < 5e-2
