@@ -325,9 +325,25 @@ SparseAttnArgs sparse_args(const Tensor& q, const Tensor& k, const Tensor& v, co
   return a;
 }
 
+void set_rel(SparseAttnArgs& a, const OptT& rel, const OptT& drel) {
+  if (!(rel.has_value() && rel->defined())) return;
+  TORCH_CHECK(rel->is_cuda() && rel->scalar_type() == at::kFloat && rel->is_contiguous() && rel->dim() == 4 &&
+                  rel->size(0) == a.B && rel->size(1) == a.H && rel->size(2) == a.T && rel->size(3) >= a.T,
+              "rel: contiguous fp32 [B, H, T, extent >= T]");
+  a.rel = rel->data_ptr<float>();
+  a.rel_extent = static_cast<int>(rel->size(3));
+  if (drel.has_value() && drel->defined()) {
+    TORCH_CHECK(drel->sizes() == rel->sizes() && drel->is_contiguous() && drel->scalar_type() == at::kFloat,
+                "drel: like rel");
+    a.drel = drel->data_ptr<float>();
+  }
+}
+
 void sparse_attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lists, const Tensor& masks,
-                     const Tensor& o, const Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale) {
+                     const Tensor& o, const Tensor& lse, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale,
+                     const OptT& rel) {
   SparseAttnArgs a = sparse_args(q, k, v, lists, masks, B, T, H, Hk, scale);
+  set_rel(a, rel, c10::nullopt);
   TORCH_CHECK(o.scalar_type() == at::kBFloat16 && o.stride(-1) == 1 && lse.scalar_type() == at::kFloat, "o / lse");
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr()); a.ldo = o.stride(-2);
   a.lse = lse.data_ptr<float>();
@@ -337,8 +353,11 @@ void sparse_attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Te
 
 void sparse_attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& lists, const Tensor& masks,
                      const Tensor& lse, const Tensor& dout, const Tensor& delta, const Tensor& dq, const Tensor& dk_acc,
-                     const Tensor& dv_acc, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale) {
+                     const Tensor& dv_acc, int64_t B, int64_t T, int64_t H, int64_t Hk, double scale,
+                     const OptT& rel, const OptT& drel) {
   SparseAttnArgs a = sparse_args(q, k, v, lists, masks, B, T, H, Hk, scale);
+  set_rel(a, rel, drel);
+  TORCH_CHECK(!a.rel || a.drel, "the backward with a relative bias needs drel");
   TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.stride(-1) == 1 && dq.scalar_type() == at::kBFloat16 &&
                   dq.stride(-1) == 1,
               "dout / dq: bf16 rows");

@@ -19,6 +19,9 @@
 //   head dimension) go to the drain warps, which transpose them through shared memory and add
 //   them into fp32 dK / dV buffers with bulk tensor add-reductions (heads of a KV group and
 //   query tiles that share a block add into the same rows).  dQ is complete per tile.
+// Optional additive relative bias (Inkling REL, nexttransformer/methods/inkling_rel of the
+// reference): logit(i, j) += rel[b, h, i, i - j]; the backward writes d rel at (i, i - j) once per
+// selected pair (no atomics: a distance has one key per row).
 // Every wait is bounded (common.cuh).  No TMA load uses cluster multicast.
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -50,6 +53,9 @@ struct Params {
   const float* delta;
   __nv_bfloat16* dq;
   int64_t lddq;
+  const float* rel;
+  float* drel;
+  int rel_extent;
 };
 
 NT_DEVICE uint8_t* align1024(uint8_t* p) {
@@ -216,6 +222,13 @@ __global__ void __launch_bounds__(192, 1)
       }
       // keys past this row's position (or past T) and unselected blocks are masked
       const int lim = bit ? min(qpos, p.T - 1) - k0 : -1;
+      if (p.rel && qpos < p.T) {
+        // relative bias of row qpos at distances qpos - (k0 + i), i <= lim (contiguous, descending)
+        const float* rrow = p.rel + ((static_cast<int64_t>(b) * p.H + h) * p.T + qpos) * p.rel_extent + (qpos - k0);
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i <= lim) x[i] += rrow[-i] * LOG2E;
+      }
       float mx = -INFINITY;
       if (lim < KB - 1) {
 #pragma unroll
@@ -465,6 +478,13 @@ __global__ void __launch_bounds__(320, 1)
       if (l > 0 && !warp_wait(mma2_done, (l - 1) & 1, 0xD31u, abort_flag)) { ok = false; break; }
       uint8_t* pbuf = sm + BwdSmem::P;
       uint8_t* sbuf = sm + BwdSmem::DS;
+      const float* rrow = nullptr;
+      float* drow = nullptr;
+      if (p.rel && live) {
+        const int64_t off = ((static_cast<int64_t>(b) * p.H + h) * p.T + qpos) * p.rel_extent + (qpos - k0);
+        rrow = p.rel + off;
+        drow = p.drel + off;
+      }
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         uint32_t a[32];
@@ -473,6 +493,11 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) pr[i] = __uint_as_float(a[i]) * p.scale_log2 - lse2;
+        if (rrow) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i <= lim) pr[i] += rrow[-(c * 32 + i)] * LOG2E;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) pr[i] = c * 32 + i <= lim ? fast_exp2(pr[i]) : 0.f;
 #pragma unroll
@@ -483,7 +508,14 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(t_dp + lrow + c * 32, a);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pr[i] *= (__uint_as_float(a[i]) - dlt) * p.scale;
+        for (int i = 0; i < 32; ++i) pr[i] *= __uint_as_float(a[i]) - dlt;   // dL / d(logit)
+        if (drow) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i <= lim) drow[-(c * 32 + i)] = pr[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pr[i] *= p.scale;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           *reinterpret_cast<uint4*>(sbuf + swz(r, c * 4 + j)) =
@@ -638,6 +670,9 @@ Params make_params(const SparseAttnArgs& a) {
   p.lse = a.lse;
   p.delta = a.delta;
   p.dq = a.dq; p.lddq = a.lddq;
+  p.rel = a.rel;
+  p.drel = a.drel;
+  p.rel_extent = a.rel_extent;
   return p;
 }
 
@@ -649,6 +684,7 @@ using namespace nt::bsa;
 int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s) {
   nt::current_context();
   if (a.D != HD || a.H % a.Hk || a.H % a.G || a.Lmax <= 0 || a.T <= 0) return -1;
+  if (a.rel && a.rel_extent < a.T) return -1;
   const Params p = make_params(a);
   const CUtensorMap tq = row_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B, QT);
   const CUtensorMap tk = row_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B, KB);
@@ -664,6 +700,7 @@ int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s) {
 int nt_sparse_attn_bwd(const SparseAttnArgs& a, cudaStream_t s) {
   nt::current_context();
   if (a.D != HD || a.H % a.Hk || a.H % a.G || a.Lmax <= 0 || a.T <= 0) return -1;
+  if (a.rel && (a.rel_extent < a.T || !a.drel)) return -1;
   const Params p = make_params(a);
   const CUtensorMap tq = row_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B, QT);
   const CUtensorMap tk = row_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B, KB);

@@ -29,6 +29,10 @@ struct SparseAttnArgs {
   int64_t lddq = 0;
   float* dk_acc = nullptr;      // fp32 [B, T, Hk*128], added into
   float* dv_acc = nullptr;
+  // optional additive relative bias (Inkling REL): logit(i, j) += rel[b, h, i, i - j] for j <= i
+  const float* rel = nullptr;   // fp32 [B, H, T, rel_extent], rel_extent >= T
+  float* drel = nullptr;        // backward: fp32 [B, H, T, rel_extent], entry (i, i - j) written once
+  int rel_extent = 0;
 };
 
 int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s);

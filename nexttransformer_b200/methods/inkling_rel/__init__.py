@@ -51,7 +51,13 @@ class RelativeSelfAttention(CausalSelfAttention):
         q, k = norm(q) * 1.2, norm(k) * 1.2
         r = self.c_r(x).view(B, T, self.n_head, self.d_rel)
         table = self.rel_logits_proj.proj.to(r.dtype)
-        if q.is_cuda:
+        if q.is_cuda and q.dtype == torch.bfloat16 and self.head_dim == 128:
+            # the block-sparse sm_100a kernels over dense causal lists, the bias read from r @ E
+            from nexttransformer_b200.ops.sparse_attention import block_sparse_attention, causal_lists
+            lists, masks = causal_lists(B, T, q.device)
+            rel = (r.float() @ table.float()).transpose(1, 2).contiguous()       # [B, H, T, extent]
+            y = block_sparse_attention(q, k, v, lists, masks, self.head_dim ** -0.5, rel)
+        elif q.is_cuda:
             from nexttransformer_b200.methods.inkling_rel.dense import relative_attention_dense
             y = relative_attention_dense(q, k, v, r, table)
         else:

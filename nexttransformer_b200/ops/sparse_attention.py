@@ -44,7 +44,7 @@ def block_lists(blocks):
 
 class _BlockSparseAttention(Function):
     @staticmethod
-    def forward(ctx, q, k, v, lists, masks, scale):
+    def forward(ctx, q, k, v, lists, masks, scale, rel):
         B, T, H, D = q.shape
         Hk = k.shape[2]
         qf = q.reshape(B * T, H * D).contiguous()
@@ -52,23 +52,26 @@ class _BlockSparseAttention(Function):
         vf = v.reshape(B * T, Hk * D).contiguous()
         o = torch.empty_like(qf)
         lse = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
-        ext().sparse_attn_fwd(qf, kf, vf, lists, masks, o, lse, B, T, H, Hk, float(scale))
-        ctx.save_for_backward(qf, kf, vf, lists, masks, o, lse)
+        relf = None if rel is None else rel.float().contiguous()
+        ext().sparse_attn_fwd(qf, kf, vf, lists, masks, o, lse, B, T, H, Hk, float(scale), relf)
+        ctx.save_for_backward(qf, kf, vf, lists, masks, o, lse, relf)
         ctx.dims = (B, T, H, Hk, D, float(scale))
+        ctx.rel_dtype = None if rel is None else rel.dtype
         return o.view(B, T, H, D)
 
     @staticmethod
     def backward(ctx, do):
-        qf, kf, vf, lists, masks, o, lse = ctx.saved_tensors
+        qf, kf, vf, lists, masks, o, lse, relf = ctx.saved_tensors
         B, T, H, Hk, D, scale = ctx.dims
         dof = do.reshape(B * T, H * D).to(torch.bfloat16).contiguous()
         delta = (dof.float() * o.float()).view(B, T, H, D).sum(-1).permute(0, 2, 1).contiguous()
         dq = torch.empty_like(qf)
         dk = torch.zeros(B * T, Hk * D, device=qf.device, dtype=torch.float32)
         dv = torch.zeros_like(dk)
-        ext().sparse_attn_bwd(qf, kf, vf, lists, masks, lse, dof, delta, dq, dk, dv, B, T, H, Hk, scale)
+        drel = None if relf is None else torch.zeros_like(relf)
+        ext().sparse_attn_bwd(qf, kf, vf, lists, masks, lse, dof, delta, dq, dk, dv, B, T, H, Hk, scale, relf, drel)
         return (dq.view(B, T, H, D), dk.to(torch.bfloat16).view(B, T, Hk, D), dv.to(torch.bfloat16).view(B, T, Hk, D),
-                None, None, None)
+                None, None, None, None if drel is None else drel.to(ctx.rel_dtype))
 
 
 def visibility(lists, masks, T):
@@ -86,7 +89,7 @@ def visibility(lists, masks, T):
     return sel & (pos[None, :] <= pos[:, None])
 
 
-def block_sparse_reference(q, k, v, lists, masks, scale):
+def block_sparse_reference(q, k, v, lists, masks, scale, rel=None):
     """The same attention in fp32 PyTorch (dense masked softmax), the oracle of the kernels."""
     B, T, H, D = q.shape
     Hk, G = k.shape[2], lists.shape[1]
@@ -94,16 +97,29 @@ def block_sparse_reference(q, k, v, lists, masks, scale):
     kk = k.float().repeat_interleave(H // Hk, 2).transpose(1, 2)
     vv = v.float().repeat_interleave(H // Hk, 2).transpose(1, 2)
     s = torch.einsum("bhqd,bhkd->bhqk", q.float().transpose(1, 2), kk) * scale
+    if rel is not None:
+        pos = torch.arange(T, device=q.device)
+        dist = (pos[:, None] - pos[None, :]).clamp_min(0)
+        s = s + rel.float().gather(-1, dist[None, None].expand(B, H, T, T))
     s = s.masked_fill(~vis, -torch.inf)
     p = torch.where(vis.any(-1, keepdim=True), s.softmax(-1).nan_to_num(0.0), torch.zeros_like(s))
     return torch.einsum("bhqk,bhkd->bhqd", p, vv).transpose(1, 2).to(q.dtype)
 
 
-def block_sparse_attention(q, k, v, lists, masks, scale=None):
+def block_sparse_attention(q, k, v, lists, masks, scale=None, rel=None):
+    """``rel`` (optional, [B, H, T, extent >= T]): additive bias, logit(i, j) += rel[b, h, i, i - j]."""
     scale = q.shape[-1] ** -.5 if scale is None else scale
     if not q.is_cuda:
-        return block_sparse_reference(q, k, v, lists, masks, scale)
-    return _BlockSparseAttention.apply(q, k, v, lists, masks, scale)
+        return block_sparse_reference(q, k, v, lists, masks, scale, rel)
+    return _BlockSparseAttention.apply(q, k, v, lists, masks, scale, rel)
+
+
+def causal_lists(B, T, device):
+    """Lists of every 64-key block at or before each query tile (dense causal attention), one group."""
+    nb = (T + KB - 1) // KB
+    pos_blk = torch.arange(T, device=device) // KB
+    blocks = (torch.arange(nb, device=device)[None, :] <= pos_blk[:, None])[None, None].expand(B, 1, T, nb)
+    return block_lists(blocks.contiguous())
 
 
 def masked_attention(q, k, v, mask):

@@ -106,6 +106,7 @@ class PeerExpertExchange:
 
     def __init__(self, group, rows, d, num_experts, device, timeout_s=60.0):
         import torch.distributed._symmetric_memory as symm
+        group = group if group is not None else dist.group.WORLD
         self.group = group
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         self.rows, self.d, self.E, self.timeout_s = rows, d, num_experts, timeout_s

@@ -73,6 +73,7 @@ class PeerReduceScatter:
     def __init__(self, arena, ownership, rank, world, blocks=None, timeout_s=60.0):
         if arena.handle is None:
             raise ValueError("the gradient arena is not in symmetric memory")
+        self.arena = arena   # keeps the symmetric-memory handle (peer mappings) alive
         h = arena.handle
         dev = arena.buf.device
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
@@ -190,6 +191,9 @@ class PeerParamGather:
     """All-gather of the updated parameters (and their bf16 shadows) through peer memory."""
 
     def __init__(self, arena, segments, shadows, rank, world, blocks=None, timeout_s=60.0):
+        # the arena (its buffer and symmetric-memory handle, i.e. the peer mappings) lives as long
+        # as this object: the kernel reads the peers' buffers through those mappings
+        self.arena = arena
         h = arena.handle
         dev = arena.buf.device
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
