@@ -118,7 +118,8 @@ class PeerExpertExchange:
         self.buf.zero_()
         h = symm.rendezvous(self.buf, group)
         self.handle = h
-        base = torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=device)
+        from nexttransformer_b200.parallel.symmetric import peer_pointers
+        base = torch.tensor(peer_pointers(self.buf, h, self.rank), dtype=torch.int64, device=device)
         self.send_peers = base.clone()
         self.ret_peers = base + self.ret_off
         self.cnt_peers = base + self.cnt_off

@@ -23,6 +23,14 @@ import torch.distributed as dist
 ALIGN = 64  # elements (256 bytes)
 
 
+def peer_pointers(tensor, handle, rank):
+    """Device addresses of `tensor` on every rank: the handle's buffer pointers are the bases of the
+    symmetric allocations, and a tensor can start at an offset inside its allocation (the allocator
+    pools symmetric memory), the same offset on every rank."""
+    offset = tensor.data_ptr() - int(handle.buffer_ptrs[rank])
+    return [int(p) + offset for p in handle.buffer_ptrs]
+
+
 class GradArena:
     def __init__(self, shapes, device, group=None):
         self.offsets, total = [], 0
@@ -77,7 +85,7 @@ class PeerReduceScatter:
         h = arena.handle
         dev = arena.buf.device
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
-        self.peers = torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=dev)
+        self.peers = torch.tensor(peer_pointers(arena.buf, h, rank), dtype=torch.int64, device=dev)
         self.pads = torch.tensor(list(h.signal_pad_ptrs), dtype=torch.int64, device=dev)
         pad_slots = h.signal_pad_size // 4
         self.blocks = max(1, min(blocks or 2 * torch.cuda.get_device_properties(dev).multi_processor_count,
@@ -197,7 +205,7 @@ class PeerParamGather:
         h = arena.handle
         dev = arena.buf.device
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
-        self.peers = torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=dev)
+        self.peers = torch.tensor(peer_pointers(arena.buf, h, rank), dtype=torch.int64, device=dev)
         self.pads = torch.tensor(list(h.signal_pad_ptrs), dtype=torch.int64, device=dev)
         self.blocks = max(1, min(blocks or 2 * torch.cuda.get_device_properties(dev).multi_processor_count,
                                  h.signal_pad_size // 4 // world))
