@@ -358,10 +358,11 @@ def main():
             from nexttransformer_b200.parallel.symmetric import ParamArena, PeerParamGather, param_segments
             segs, covered = ownership_segments(opt, st.arena, world)
             opt.use_peer_reduce_scatter(PeerReduceScatter(st.arena, segs, rank, world), covered)
-            psegs = param_segments(opt, st.arena, world)
-            gather = PeerParamGather(ParamArena(st.arena, psegs, dist.group.WORLD), psegs,
-                                     {p: s for p, s in st.casts}, rank, world)
-            opt.use_peer_gather(gather, gather.covered)
+            if os.environ.get("NT_P2P_GATHER", "1") != "0":
+                psegs = param_segments(opt, st.arena, world)
+                gather = PeerParamGather(ParamArena(st.arena, psegs, dist.group.WORLD), psegs,
+                                         {p: s for p, s in st.casts}, rank, world)
+                opt.use_peer_gather(gather, gather.covered)
         trainer = Trainer(model, opt, accumulation=accum)
 
         def step_device(xs, ys):
@@ -476,7 +477,8 @@ def main():
                           "global_batch": GLOBAL_BATCH, "seq_len": T, "parallelism": f"dp{world}",
                           "micro_batch": micro, "grad_accum": accum, "l2": "working set >> L2 (no flush needed)",
                           "grad_comm": (args.comm if world > 1 else "none") if args.impl == "ours" else "nccl",
-                          "param_gather": ("p2p" if args.comm == "p2p" else "nccl") if world > 1 and args.impl == "ours"
+                          "param_gather": ("p2p" if args.comm == "p2p" and os.environ.get("NT_P2P_GATHER", "1") != "0"
+                                           else "nccl") if world > 1 and args.impl == "ours"
                           else ("none" if world == 1 else "nccl"),
                           "flops_per_token": flops_per_token, "params_equal_across_ranks": params_agree},
                "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": final_loss}

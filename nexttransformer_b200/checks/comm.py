@@ -18,6 +18,50 @@ import torch.distributed as dist
 PEER_GBS = 770.0
 
 
+def check_gather(rank, world, device):
+    """Parameter all-gather through peer memory: every rank owns row shards and whole matrices of a
+    synthetic layout, writes its own values, and after the gather every rank must hold every owner's
+    values exactly (fp32 masters) and their bf16 casts (shadows)."""
+    import types
+    from nexttransformer_b200.parallel.symmetric import GradArena, ParamArena, PeerParamGather
+    shapes = [(1024, 256), (640, 128), (2048, 64)]
+    arena = GradArena(shapes, device, group=dist.group.WORLD)
+    grads = [arena.alloc(s) for s in shapes]
+    params = [torch.nn.Parameter(torch.zeros(s, device=device)) for s in shapes]
+    segs = []
+    for i, (p, g) in enumerate(zip(params, grads)):
+        base = arena.offset_of(g)
+        if i == 1:                                      # a whole matrix owned by one rank
+            segs.append((base, p.numel(), i % world, p, base))
+        else:                                           # equal row shards
+            per = p.numel() // world
+            segs.extend((base + r * per, per, r, p, base) for r in range(world))
+    pa = ParamArena(arena, segs, dist.group.WORLD)
+    shadows = {p: torch.zeros(p.shape, device=device, dtype=torch.bfloat16) for p in params}
+    gather = PeerParamGather(pa, segs, shadows, rank, world)
+    flat = {id(p): p.data.view(-1) for p in params}
+    for off, n, owner, p, base in segs:
+        if owner == rank:
+            idx = torch.arange(n, device=device, dtype=torch.float32)
+            flat[id(p)][off - base:off - base + n] = (owner + 1) * 1000.0 + idx % 977
+    torch.cuda.synchronize()
+    dist.barrier()
+    gather()
+    torch.cuda.synchronize()
+    err = 0.0
+    for off, n, owner, p, base in segs:
+        idx = torch.arange(n, device=device, dtype=torch.float32)
+        want = (owner + 1) * 1000.0 + idx % 977
+        got = flat[id(p)][off - base:off - base + n]
+        err = max(err, (got - want).abs().max().item())
+        sh = shadows[p].view(-1)[off - base:off - base + n].float()
+        err = max(err, (sh - want.to(torch.bfloat16).float()).abs().max().item())
+    t = torch.tensor([err], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del gather, pa, arena
+    return float(t)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--mib", type=int, default=256, help="arena size in MiB of fp32")
@@ -71,8 +115,14 @@ def main(argv=None):
                frac_of_peer_peak_p2p=bytes_ / ms_p2p / 1e6 / PEER_GBS)
     if rank == 0:
         print(json.dumps(res), flush=True)
+    gather_err = check_gather(rank, world, device)
+    res["gather_max_abs_err"] = gather_err
+    if rank == 0:
+        print(json.dumps({"param_gather_max_abs_err": gather_err}), flush=True)
     del red, arena, buf
     shutdown()
+    if gather_err > 0:
+        raise SystemExit(f"peer parameter gather differs from the owners' values by {gather_err}")
     if err > 1e-5:
         raise SystemExit(f"peer reduce-scatter differs from NCCL by {err}")
     return res
