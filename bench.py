@@ -66,8 +66,10 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--micro-batch", type=int, default=0, help="rows per micro-batch (default 32 ours / 16 reference)")
-    p.add_argument("--comm", choices=("nccl", "p2p"), default="p2p",
-                   help="gradient averaging of our arm on N > 1: NCCL collectives or the peer-memory kernel")
+    p.add_argument("--comm", choices=("nccl", "p2p"), default="nccl",
+                   help="gradient averaging / parameter gather of our arm on N > 1: NCCL collectives (default) "
+                        "or the peer-memory kernels (their standalone checks are exact; the training step "
+                        "with them is still being validated)")
     p.add_argument("--method", default="dense", choices=("dense", *METHOD_CONFIGS),
                    help="benchmark configuration (default: the dense headline configuration)")
     p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
