@@ -266,6 +266,9 @@ def chunk_attention(q, k, v, *, kind, g=None, beta=None, chunk, qk_l2norm_scale=
         return delta_chunk_cuda(q, k, v, kind=kind, g=g, beta=beta, chunk=chunk, qk_l2norm_scale=qk_l2norm_scale)
     if kind == "retnet":
         g = g.expand(*q.shape[:2], -1)
+        if q.is_cuda:
+            from nexttransformer_b200.ops.linear_attention import scalar_chunk_cuda
+            return scalar_chunk_cuda(q, k, v, g, chunk)
     if qk_l2norm_scale is not None:
         q, k = F.normalize(q, dim=-1) * qk_l2norm_scale, F.normalize(k, dim=-1)
     return chunk_scan(q, k, v, kind=kind, g=g, beta=beta, chunk=chunk)

@@ -149,3 +149,32 @@ def delta_chunk_cuda(q, k, v, *, kind, g=None, beta=None, chunk, qk_l2norm_scale
     else:
         out = _delta_scan(w, u0, qt, kc, aqk, carry)
     return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)
+
+
+def scalar_chunk_cuda(q, k, v, g, chunk):
+    """Linear attention with a per-head scalar log decay g [B, T, H] (RetNet) on the scan kernels:
+    the delta-rule scan with w = 0 and u0 = v is S <- c S + k_c^T v, o = q~ S + aqk v, the chunk
+    form of ``models/linear.py`` ``_scalar_decay_chunks``."""
+    import math
+    from nexttransformer_b200.models.linear import _chunked, _scalar_decay_chunks, _tril
+    dt = q.dtype
+    T = q.shape[1]
+    qc, kc_, vc = (_chunked(x.float(), chunk) for x in (q, k, v))
+    if not scan_supported(q, v, chunk):
+        out = _scalar_decay_chunks(qc, kc_, vc, None if g is None else _chunked(g.float(), chunk), chunk)
+        return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)
+    causal = _tril(chunk, q.device)
+    B, H, N = qc.shape[:3]
+    if g is None:
+        aqk = (qc @ kc_.transpose(-1, -2)).masked_fill(~causal, 0)
+        qt, kc, carry = qc, kc_, qc.new_ones(B, H, N, 128)
+    else:
+        b = _chunked(g.float(), chunk).cumsum(-1)
+        pair = (b[..., :, None] - b[..., None, :]).masked_fill(~causal, -math.inf).exp()
+        aqk = (qc @ kc_.transpose(-1, -2)) * pair
+        qt = qc * b.exp()[..., None]
+        kc = kc_ * (b[..., -1:] - b).exp()[..., None]
+        carry = b[..., -1].exp()[..., None].expand(B, H, N, 128)
+    w = torch.zeros_like(qt)
+    out = _DeltaScan.apply(w, vc, qt, kc, aqk, carry)
+    return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)

@@ -110,3 +110,28 @@ def test_delta_chunk_scan_matches_fp32(kind, T):
     assert _rel(y, yr) < 2e-2
     for a, b in zip(leaves, ref):
         assert _rel(a.grad, b.grad) < 5e-2
+
+
+@pytest.mark.parametrize("T", [64, 200])
+def test_retnet_chunk_scan_matches_fp32(T):
+    """RetNet's scalar-decay chunk form on the scan kernels (w = 0) against the fp32 torch chunk form."""
+    from nexttransformer_b200.models.linear import chunk_scan
+    from nexttransformer_b200.ops.linear_attention import scalar_chunk_cuda
+    torch.manual_seed(6)
+    B, H, D = 2, 3, 128
+    q = torch.randn(B, T, H, D, device="cuda") * D ** -.5
+    k = torch.randn(B, T, H, D, device="cuda")
+    v = torch.randn(B, T, H, D, device="cuda")
+    gamma = 1 - 2. ** (-5 - torch.arange(H, device="cuda", dtype=torch.float32))
+    g = gamma.log()[None, None].expand(B, T, H)
+    leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+    y = scalar_chunk_cuda(*leaves, g, 64)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    ref = [t.clone().requires_grad_() for t in (q, k, v)]
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yr = chunk_scan(*ref, kind="retnet", g=g, chunk=64)
+    yr.backward(dy)
+    assert _rel(y, yr) < 2e-2
+    for a, b in zip(leaves, ref):
+        assert _rel(a.grad, b.grad) < 5e-2
