@@ -1,0 +1,182 @@
+"""Scaling-stage configuration, MoE recipe, per-node checkpoints and trainer on CPU (tiny shapes;
+two gloo ranks stand for two nodes without a shared filesystem)."""
+from dataclasses import replace
+import json
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from nexttransformer_b200.scaling.config import (ScalingModelConfig, ScalingTrainConfig, config_hash, load_config,
+                                                 write_config)
+
+TINY = dict(width=48, heads=2, mlp_width=192, vocab_size=96, sequence_len=16, dense_layers=3, window_pattern="SL")
+
+
+def _config(tmp_path, **train):
+    kw = dict(total_tokens=128, global_batch_tokens=32, val_tokens=32, final_bpb_tokens=32, val_every=2,
+              checkpoint_every=1, milestone_every=2, core_every=0)
+    kw.update(train)
+    path = tmp_path / "tiny.json"
+    write_config(path, ScalingModelConfig(**TINY), ScalingTrainConfig(**kw))
+    return path
+
+
+def test_config_defaults_hash_and_rules(tmp_path):
+    mc, tc = ScalingModelConfig(), ScalingTrainConfig()
+    # the serialized form leaves the value-embedding switch out at its default
+    assert "value_embeddings" not in mc.serialized()
+    assert config_hash(mc, tc).startswith("f8f69c5183c9")
+    assert tc.batch_scale == 2.0 and tc.is_milestone(10_000) and not tc.is_milestone(9_000)
+    assert tc.core_steps()[-1] == tc.steps
+    with pytest.raises(ValueError):
+        ScalingTrainConfig(milestone_every=1500)
+    with pytest.raises(ValueError):
+        ScalingTrainConfig(total_tokens=3 * 2_097_152 + 1)
+    path = _config(tmp_path)
+    mc2, tc2 = load_config(path)
+    assert mc2.width == 48 and tc2.steps == 4
+    raw = json.loads(path.read_text())
+    raw["train"]["global_batch_tokens"] = 40
+    raw["train"]["total_tokens"] = 160
+    (tmp_path / "bad.json").write_text(json.dumps(raw))
+    with pytest.raises(ValueError):
+        load_config(tmp_path / "bad.json")
+
+
+def test_shipped_scaling_configs_load():
+    root = os.path.join(os.path.dirname(__file__), "..", "configs", "scaling")
+    for name in ("dense_200b.json", "t3_dense_l20.json", "t3_dense_l28.json"):
+        mc, tc = load_config(os.path.join(root, name))
+        assert mc.architecture == "dense" and tc.steps > 0
+
+
+def test_moe_recipe_matches_manifest(tmp_path):
+    from nexttransformer_b200.scaling.moe_recipe import MANIFEST, MoERecipe, load_t3_recipe
+    data = json.loads(MANIFEST.read_text())
+    for cell in data["cells"]:
+        if cell["family"] in ("moe", "looped"):
+            r = load_t3_recipe(cell["id"])
+            assert r.estimate()["estimated_updates"] == cell["estimatedUpdates"], cell["id"]
+    r = load_t3_recipe("moe-T3-L20")
+    c = r.counts()
+    assert r.expert_width == r.width // 4 and c["model_total"] == c["block_total"] + c["embedding_and_head"] + \
+        c["native_small_parameters"]
+    assert r.block_active() < c["block_total"]
+    assert load_t3_recipe("kda-dsa-T3-L20").estimate()["estimated_updates"] is None
+    dbg = r.debug()
+    assert dbg.width == 32 and dbg.layers == 3
+    with pytest.raises(ValueError):
+        MoERecipe(layers=4, width=64, heads=4, expert_width=8)
+    data["families"][1]["recipe"]["routedExperts"] = 128
+    changed = tmp_path / "t3.json"
+    changed.write_text(json.dumps(data))
+    with pytest.raises(ValueError):
+        load_t3_recipe("moe-T3-L20", changed)
+
+
+def _final_weights(output, step, node=0):
+    return torch.load(output / f"checkpoint_{step:08d}" / f"node_{node:03d}" / "model.pt", weights_only=False)["model"]
+
+
+def test_scaling_smoke_resume_stop_and_benchmark(tmp_path, monkeypatch, capsys):
+    from nexttransformer_b200.scaling import train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    cfg = _config(tmp_path)
+    base = ["--config", str(cfg), "--micro-batch", "1", "--log-every", "1"]
+    full = train.main(base + ["--output", str(tmp_path / "full"), "--smoke-steps", "3"])
+    assert full["step"] == 3 and full["input_tokens"] == 96
+    status = json.loads((tmp_path / "full" / "run_status.json").read_text())
+    assert status["phase"] == "smoke_complete"
+    assert (tmp_path / "full" / "checkpoint_00000003" / "node_000" / "complete.json").exists()
+    # a second launch into the same output without --resume is refused
+    with pytest.raises(ValueError):
+        train.main(base + ["--output", str(tmp_path / "full"), "--smoke-steps", "3"])
+    # stop after one update, resume for the rest: the same weights as the continuous run
+    seg = tmp_path / "seg"
+    got = train.main(base + ["--output", str(seg), "--smoke-steps", "3", "--stop-after", "1"])
+    assert got["step"] == 1
+    assert json.loads((seg / "run_status.json").read_text())["phase"] == "stopped"
+    # an incomplete newer checkpoint is set aside, never deleted
+    (seg / "checkpoint_00000002" / "node_000").mkdir(parents=True)
+    train.main(base + ["--output", str(seg), "--smoke-steps", "3", "--resume", "auto"])
+    assert list((seg / "abandoned").rglob("checkpoint_00000002"))
+    a, b = _final_weights(tmp_path / "full", 3), _final_weights(seg, 3)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    # a STOP file stops after the current update and is consumed
+    stop = tmp_path / "stop"
+    stop.mkdir()
+    (stop / "STOP").write_text("")
+    got = train.main(base + ["--output", str(stop), "--smoke-steps", "3"])
+    assert got["step"] == 1 and (stop / "STOP.consumed-00000001").exists()
+    # benchmark mode writes no checkpoint and prints one summary line
+    capsys.readouterr()
+    train.main(["--config", str(cfg), "--micro-batch", "1", "--benchmark", "2", "--output", str(tmp_path / "bench")])
+    summary = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert summary["event"] == "benchmark" and summary["measured_steps"] == 1
+    assert not list((tmp_path / "bench").glob("checkpoint_*"))
+
+
+def test_scaling_nonfinite_exits_3(tmp_path, monkeypatch):
+    from nexttransformer_b200.scaling import train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    cfg = _config(tmp_path)
+    from nexttransformer_b200.models.native import model as native_model
+    real = native_model.NativeExperiment.forward
+
+    def poisoned(self, *a, **k):
+        out = real(self, *a, **k)
+        if isinstance(out, dict):
+            out["loss"] = out["loss"] * float("nan")
+        return out
+    monkeypatch.setattr(native_model.NativeExperiment, "forward", poisoned)
+    with pytest.raises(SystemExit) as e:
+        train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "nan"), "--smoke-steps", "2"])
+    assert e.value.code == train.NONFINITE_EXIT
+
+
+def test_dry_run(tmp_path, capsys):
+    from nexttransformer_b200.scaling import train
+    train.main(["--config", str(_config(tmp_path)), "--dry-run", "--world-size", "2", "--micro-batch", "1"])
+    out = json.loads(capsys.readouterr().out)
+    assert out["accumulation"] == 1 and out["scaling_parameters"] > 0 and out["muon_weight_decay"] > 0
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_nodes(rank, port, cfg, output, argv_extra, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE="2", RANK=str(rank),
+                      LOCAL_RANK="0", LOCAL_WORLD_SIZE="1")
+    from nexttransformer_b200.scaling import train
+    try:
+        state = train.main(["--config", cfg, "--micro-batch", "1", "--output", output] + argv_extra)
+        results[rank] = state["step"]
+    except Exception as e:  # reported to the parent
+        results[rank] = repr(e)
+
+
+@pytest.mark.timeout(300)
+def test_two_nodes_checkpoint_and_resume(tmp_path):
+    cfg = str(_config(tmp_path, global_batch_tokens=32, total_tokens=128))
+    out = tmp_path / "run"
+    with mp.Manager() as manager:
+        for extra in (["--smoke-steps", "2", "--stop-after", "1"], ["--smoke-steps", "2", "--resume", "auto", "--bf16-grad-reduce"]):
+            results = manager.dict()
+            port = _port()
+            mp.start_processes(_two_nodes, args=(port, cfg, str(out), extra, results), nprocs=2, start_method="spawn")
+            assert dict(results) == {0: results[0], 1: results[1]}
+            assert all(isinstance(v, int) for v in results.values()), dict(results)
+    # each node wrote its own complete checkpoint of the same model
+    for node in (0, 1):
+        assert (out / "checkpoint_00000002" / f"node_{node:03d}" / "complete.json").exists()
+    a, b = _final_weights(out, 2, 0), _final_weights(out, 2, 1)
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    assert (out / "status.node000.json").exists() and (out / "status.node001.json").exists()
