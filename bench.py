@@ -360,11 +360,15 @@ def main():
             from nexttransformer_b200.parallel.symmetric import ParamArena, PeerParamGather, param_segments
             segs, covered = ownership_segments(opt, st.arena, world)
             opt.use_peer_reduce_scatter(PeerReduceScatter(st.arena, segs, rank, world), covered)
-            if os.environ.get("NT_P2P_GATHER", "1") != "0":
+            if os.environ.get("NT_P2P_GATHER", "0") == "1":
                 psegs = param_segments(opt, st.arena, world)
                 gather = PeerParamGather(ParamArena(st.arena, psegs, dist.group.WORLD), psegs,
                                          {p: s for p, s in st.casts}, rank, world)
                 opt.use_peer_gather(gather, gather.covered)
+                if rank == 0:
+                    print(f"peer-memory step: reduce-scatter pad {int(opt.p2p.pads[rank]):#x}, gather pad "
+                          f"{int(gather.pads[rank]):#x}, {len(segs)} segments, {opt.p2p.blocks} / {gather.blocks} "
+                          f"blocks", file=sys.stderr)
         trainer = Trainer(model, opt, accumulation=accum)
 
         def step_device(xs, ys):
@@ -420,6 +424,8 @@ def main():
         end.record()
         barrier()
     ms = start.elapsed_time(end) / args.steps
+    if rank == 0:
+        print(f"timed region done: {ms:.1f} ms per step", file=sys.stderr, flush=True)
     t = torch.tensor([ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -447,6 +453,8 @@ def main():
         e2e = {"value": GLOBAL_BATCH / (ms2 / 1000.0), "unit": "tokens/s", "ms_per_step": ms2,
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4}
 
+    if rank == 0:
+        print("end-to-end region done", file=sys.stderr, flush=True)
     # every rank must hold the same parameters after the updates (checks the parameter all-gather)
     params_agree = None
     if world > 1:
@@ -479,7 +487,7 @@ def main():
                           "global_batch": GLOBAL_BATCH, "seq_len": T, "parallelism": f"dp{world}",
                           "micro_batch": micro, "grad_accum": accum, "l2": "working set >> L2 (no flush needed)",
                           "grad_comm": (args.comm if world > 1 else "none") if args.impl == "ours" else "nccl",
-                          "param_gather": ("p2p" if args.comm == "p2p" and os.environ.get("NT_P2P_GATHER", "1") != "0"
+                          "param_gather": ("p2p" if args.comm == "p2p" and os.environ.get("NT_P2P_GATHER", "0") == "1"
                                            else "nccl") if world > 1 and args.impl == "ours"
                           else ("none" if world == 1 else "nccl"),
                           "flops_per_token": flops_per_token, "params_equal_across_ranks": params_agree},

@@ -84,10 +84,12 @@ __global__ void __launch_bounds__(256) p2p_reduce_scatter_kernel(const uint64_t*
   peer_barrier(pads, rank, world, 1, epoch, timeout_ns, 0x900u);
 }
 
-// Parameter all-gather over peer memory: after one entry barrier (every owner has written its
+// Parameter all-gather over peer memory: after an entry barrier (every owner has written its
 // updated fp32 parameters), every segment owned by another rank is read from the owner's
 // buffer with plain peer loads and written here; every segment with a shadow pointer also gets
-// its bf16 copy written (the forward reads the shadows).
+// its bf16 copy written (the forward reads the shadows).  Its barriers use slot regions 2 and 3,
+// the reduce-scatter's 0 and 1, so the two kernels never see each other's flags even when their
+// buffers share one allocation (and with it one signal pad).
 __global__ void __launch_bounds__(256) p2p_gather_kernel(const uint64_t* __restrict__ peers,
                                                          const uint64_t* __restrict__ pads,
                                                          const int64_t* __restrict__ seg_off,
@@ -95,22 +97,25 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const uint64_t* __restr
                                                          const int* __restrict__ seg_owner,
                                                          const uint64_t* __restrict__ seg_shadow, int nseg, int rank,
                                                          int world, uint32_t epoch, uint64_t timeout_ns) {
-  const bool ok = peer_barrier(pads, rank, world, 0, epoch, timeout_ns, 0xB00u);
-  if (!ok) return;
-  float* mine = reinterpret_cast<float*>(peers[rank]);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int s = 0; s < nseg; ++s) {
-    const int owner = seg_owner[s];
-    const int64_t off = seg_off[s], n4 = seg_len[s] >> 2;
-    const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(peers[owner]) + off);
-    float4* dst = reinterpret_cast<float4*>(mine + off);
-    uint2* sh = reinterpret_cast<uint2*>(seg_shadow[s]);
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
-      const float4 v = src[i];
-      if (owner != rank) dst[i] = v;
-      if (sh) sh[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  const bool ok = peer_barrier(pads, rank, world, 2, epoch, timeout_ns, 0xB00u);
+  if (ok) {
+    float* mine = reinterpret_cast<float*>(peers[rank]);
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int s = 0; s < nseg; ++s) {
+      const int owner = seg_owner[s];
+      const int64_t off = seg_off[s], n4 = seg_len[s] >> 2;
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(peers[owner]) + off);
+      float4* dst = reinterpret_cast<float4*>(mine + off);
+      uint2* sh = reinterpret_cast<uint2*>(seg_shadow[s]);
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = src[i];
+        if (owner != rank) dst[i] = v;
+        if (sh) sh[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+      }
     }
   }
+  // no owner updates its segments again before every peer has finished copying them
+  peer_barrier(pads, rank, world, 3, epoch, timeout_ns, 0xC00u);
 }
 
 // A standalone barrier with every peer (one block; region 0 of the pads, `world` slots).

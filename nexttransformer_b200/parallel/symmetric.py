@@ -31,6 +31,14 @@ def peer_pointers(tensor, handle, rank):
     return [int(p) + offset for p in handle.buffer_ptrs]
 
 
+def _blocks(blocks, handle, world, device):
+    """Grid size of the reduce-scatter / gather kernels: the signal pad holds four slot regions
+    (entry and exit of each kernel) of one 32-bit slot per (block, peer)."""
+    pad_slots = handle.signal_pad_size // 4
+    return max(1, min(blocks or 2 * torch.cuda.get_device_properties(device).multi_processor_count,
+                      pad_slots // (4 * world)))
+
+
 class GradArena:
     def __init__(self, shapes, device, group=None):
         self.offsets, total = [], 0
@@ -87,9 +95,7 @@ class PeerReduceScatter:
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
         self.peers = torch.tensor(peer_pointers(arena.buf, h, rank), dtype=torch.int64, device=dev)
         self.pads = torch.tensor(list(h.signal_pad_ptrs), dtype=torch.int64, device=dev)
-        pad_slots = h.signal_pad_size // 4
-        self.blocks = max(1, min(blocks or 2 * torch.cuda.get_device_properties(dev).multi_processor_count,
-                                 pad_slots // (2 * world)))
+        self.blocks = _blocks(blocks, h, world, dev)
         mine = [(o, n) for (o, n, owner) in ownership if owner == rank]
         if any(o % 4 or n % 4 for o, n in mine):
             raise ValueError("segments must start and end on 16-byte boundaries")
@@ -207,8 +213,7 @@ class PeerParamGather:
         self.rank, self.world, self.timeout_s = rank, world, timeout_s
         self.peers = torch.tensor(peer_pointers(arena.buf, h, rank), dtype=torch.int64, device=dev)
         self.pads = torch.tensor(list(h.signal_pad_ptrs), dtype=torch.int64, device=dev)
-        self.blocks = max(1, min(blocks or 2 * torch.cuda.get_device_properties(dev).multi_processor_count,
-                                 h.signal_pad_size // 4 // world))
+        self.blocks = _blocks(blocks, h, world, dev)
         offs, lens, owners, shadow = [], [], [], []
         for off, n, owner, p, base in segments:
             sh = shadows.get(p)
