@@ -21,6 +21,8 @@ def main(argv=None):
     p.add_argument("--tokenizer", type=Path)
     p.add_argument("--core", type=Path, help="directory with tasks.json and <label>.jsonl files")
     p.add_argument("--core-max-per-task", type=int, default=-1)
+    from nexttransformer_b200.evaluation.context import add_core_max_tokens
+    add_core_max_tokens(p)
     p.add_argument("--expected-attention", help="refuse to run unless this attention path is active")
     a = p.parse_args(argv)
     from nexttransformer_b200.evaluation.bpb import evaluate_bpb, evaluate_stream_loss
@@ -51,7 +53,16 @@ def main(argv=None):
         tasks = json.loads((a.core / "tasks.json").read_text())
         for t in tasks:
             t["data"] = [json.loads(l) for l in (a.core / f"{t['label']}.jsonl").read_text().splitlines() if l]
-        result["core"] = evaluate_core(model, tok, tasks, dev, rank, world, a.core_max_per_task, cfg.sequence_len)
+        from nexttransformer_b200.evaluation.context import (LengthProbe, check_full_context, core_context,
+                                                             inference_view)
+        if a.core_max_per_task <= 0:
+            check_full_context(cfg, a.core_max_tokens)
+        probe = LengthProbe(inference_view(model, a.core_max_tokens))
+        result["core"] = evaluate_core(probe, tok, tasks, dev, rank, world, a.core_max_per_task, a.core_max_tokens)
+        longest = torch.tensor(probe.longest, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(longest, op=torch.distributed.ReduceOp.MAX)
+        result["core"]["coreContext"] = core_context(cfg.sequence_len, a.core_max_tokens, int(longest.item()))
     if rank == 0:
         print(json.dumps(result))
         if a.output:

@@ -181,6 +181,9 @@ def main(argv=None):
     output = args.output or Path(args.runtime_dir) / "runs" / (args.run_name or "scaling_" + args.config.stem)
     for number in (signal.SIGTERM, signal.SIGINT):
         signal.signal(number, _request_stop)
+    if int(os.environ.get("RANK", "0")) == 0 and not benchmark:
+        from nexttransformer_b200.runtime.tracking_auth import preflight
+        preflight(args.wandb_mode)
     rank, world, device = initialize(tc.seed)
     node, local_rank, _ = ck.topology()
     accumulation = tc.accumulation(mc, world, args.micro_batch)

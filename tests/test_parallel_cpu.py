@@ -81,3 +81,49 @@ def test_parallel_matches_reference(worker):
     for _ in range(2):
         vals = q.get()
         assert max(vals[1:]) < 1e-4, vals
+
+
+def _sharded_worker(rank, port, results):
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+    from nexttransformer_b200.training.sharded import ExperimentOptimizer
+
+    def make():
+        torch.manual_seed(0)
+        ps = [torch.nn.Parameter(torch.randn(64, 32)), torch.nn.Parameter(torch.randn(3)),
+              torch.nn.Parameter(torch.randn(32, 32)), torch.nn.Parameter(torch.randn(32, 32))]
+        groups = [dict(kind="adamw", params=ps[:2], lr=1e-2, betas=(0.9, 0.95), eps=1e-10, weight_decay=0.01),
+                  dict(kind="muon", params=ps[2:], lr=2e-2, momentum=0.95, ns_steps=5, beta2=0.9, weight_decay=0.1)]
+        return ps, groups
+    ref_p, ref_g = make()
+    sh_p, sh_g = make()
+    ref, sharded = MuonAdamW(ref_g), ExperimentOptimizer(sh_g)
+    for step in range(2):
+        g = torch.Generator().manual_seed(100 * step + rank)
+        local = [torch.randn(p.shape, generator=g) for p in ref_p]
+        for p, x in zip(ref_p, local):
+            p.grad = x.clone()
+        for p, x in zip(sh_p, local):          # what DDP would hand over: the average
+            avg = x.clone()
+            dist.all_reduce(avg)
+            p.grad = avg / 2
+        ref.step()
+        sharded.step()
+    results[rank] = max(float((a - b).abs().max()) for a, b in zip(ref_p, sh_p))
+    dist.destroy_process_group()
+
+
+def test_experiment_optimizer_matches_owner_reduction():
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.start_processes(_sharded_worker, args=(port, results), nprocs=2, start_method="spawn")
+        assert results[0] < 1e-5 and results[1] < 1e-5, dict(results)

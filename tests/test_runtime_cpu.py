@@ -98,3 +98,19 @@ def test_kv_cache_decode_matches_full_forward():
         decode(m, ids[:, t:t + 1], cache)
     last = decode(m, ids[:, 9:10], cache)
     assert torch.allclose(last, full, atol=1e-4), (last - full).abs().max()
+
+
+def test_tracking_auth_preflight():
+    import subprocess
+    from types import SimpleNamespace
+    from nexttransformer_b200.runtime.tracking_auth import preflight
+    preflight("disabled", runner=None)          # offline modes never start the check
+    preflight("online", runner=lambda *a, **k: SimpleNamespace(returncode=0))
+    for code in (2, 3, 4, 9):
+        with pytest.raises(RuntimeError):
+            preflight("online", runner=lambda *a, code=code, **k: SimpleNamespace(returncode=code))
+
+    def slow(*a, **k):
+        raise subprocess.TimeoutExpired(a[0], k["timeout"])
+    with pytest.raises(RuntimeError, match="timed out"):
+        preflight("online", timeout=1, runner=slow)
