@@ -180,3 +180,33 @@ def test_two_nodes_checkpoint_and_resume(tmp_path):
     for k in a:
         assert torch.equal(a[k], b[k]), k
     assert (out / "status.node000.json").exists() and (out / "status.node001.json").exists()
+
+
+def test_routed_ffn_oracle_matches_moe_layer():
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.models.moe import MoEFFN
+    from nexttransformer_b200.scaling.reference_blocks import RoutedFFN
+    cfg = debug_config("dsa")
+    torch.manual_seed(0)
+    oracle = RoutedFFN(cfg, 8, 2, cfg.width // 4)
+    layer = MoEFFN(cfg.width, 8, 2, cfg.width // 4, shared=1)
+    layer.load_state_dict({**oracle.state_dict(), "expert_bias": torch.zeros(8)}, strict=False)
+    x = torch.randn(2, 8, cfg.width)
+    got = layer(x)
+    got = got[0] if isinstance(got, tuple) else got
+    torch.testing.assert_close(got, oracle(x), rtol=1e-5, atol=1e-5)
+
+
+def test_kda_dsa_group_and_rule():
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.scaling.reference_blocks import KdaDsaGroup, RoutedFFN, rotary, shared_expert_rule
+    cfg = debug_config("dsa")
+    rule = shared_expert_rule(cfg, 8, 2, cfg.width // 4)
+    assert not isinstance(rule(0), RoutedFFN) and isinstance(rule(1), RoutedFFN)
+    group = KdaDsaGroup(cfg, rule)
+    x = torch.randn(2, cfg.sequence_len, cfg.width)
+    for step in (0, cfg.burnin_steps):
+        group.zero_grad(set_to_none=True)
+        out, aux = group(x, rotary(cfg), step)
+        (out.square().mean() + aux).backward()
+        assert torch.isfinite(out).all()
