@@ -90,6 +90,13 @@ def load_model_config(args):
     return config, proof, findings
 
 
+def _dense_anchor(args):
+    """The dense FLOPs-per-token anchor of the configuration's cost evidence (None without one)."""
+    if not getattr(args, "config", None):
+        return None
+    return json.loads(Path(args.config).read_text()).get("calibration", {}).get("dense_flops_per_token")
+
+
 def stage_cost(proof, step):
     """Audited cost charged to update `step` (the stage that trains it)."""
     if proof is None:
@@ -169,6 +176,7 @@ def main(argv=None):
         atomic_json(out / ("provenance.json" if state["step"] == 0 else f"resume_{state['step']:08d}.json"), dict(
             model=config.serialized(), train=asdict(train), world_size=world, micro_batch=micro,
             gradient_accumulation=accum, findings=findings, mode=state["mode"], torch=torch.__version__,
+            dense_flops_per_token=_dense_anchor(args),
             device=torch.cuda.get_device_name(device) if device.type == "cuda" else "cpu", argv=sys.argv))
     stop = min(args.steps or train.steps, train.steps)
     val_every = args.val_every or proto.val_every
