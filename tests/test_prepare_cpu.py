@@ -66,3 +66,24 @@ def test_core_digest_mismatch_is_refused(tmp_path):
     (core / "eval_bundle" / "core.yaml").write_text("tampered\n")
     with pytest.raises(ValueError, match="checksum"):
         res.verify_core(core)
+
+
+def test_integration_check_on_prepared_resources(tmp_path):
+    from nexttransformer_b200 import prepare
+    from nexttransformer_b200.checks import integration
+    data, manifest = _dataset(tmp_path)
+    core = _core(tmp_path)
+    out = tmp_path / "resources"
+    prepare.main(["--data-dir", str(data), "--resources", str(out), "--source-manifest", str(manifest),
+                  "--existing-core-resources", str(core), "--vocab-size", "300", "--max-chars", "5000"])
+    bundle = tmp_path / "bundle"
+    bundle.mkdir()
+    (bundle / "tasks.json").write_text(json.dumps([{"label": "lm", "random_baseline": 0.0,
+                                                    "meta": {"task_type": "language_modeling", "num_fewshot": 0}}]))
+    items = [{"context": "the quick brown", "continuation": " fox"} for _ in range(12)]
+    (bundle / "lm.jsonl").write_text("".join(json.dumps(i) + "\n" for i in items))
+    res = integration.main(["--data-dir", str(data), "--resources", str(out), "--output", str(tmp_path / "o.json"),
+                            "--device", "cpu", "--sequence-len", "32", "--core", str(bundle),
+                            "--core-methods", "dense", "--core-max-per-task", "11"])
+    assert res["status"] == "passed" and res["bpb_exact"] and len(res["core_smoke"]) == 1
+    assert json.loads((tmp_path / "o.json").read_text())["status"] == "passed"
