@@ -154,7 +154,9 @@ def ownership_segments(optimizer, arena, world):
 
 def param_segments(optimizer, arena, world):
     """[(element offset, length, owner, param, param offset)] in the gradient arena's layout for
-    every parameter the peer reduce-scatter covers (same ownership as ``ownership_segments``)."""
+    every fp32 parameter the peer reduce-scatter covers (same ownership as ``ownership_segments``).
+    Parameters kept in another dtype (the bf16 embedding tables on CUDA) stay out: the arena holds
+    fp32 masters, and moving a bf16 table into it would change the dtype its kernels read."""
     import math
     from nexttransformer_b200.optim.muon_adamw import grad_of
     out = []
@@ -164,7 +166,7 @@ def param_segments(optimizer, arena, world):
             chunk = math.ceil(len(params) / world)
             for i, p in enumerate(params):
                 g = grad_of(p)
-                if g is None or not g.is_contiguous():
+                if g is None or not g.is_contiguous() or p.dtype != torch.float32:
                     continue
                 off = arena.offset_of(g)
                 if off % 4 or g.numel() % 4:
@@ -173,7 +175,8 @@ def param_segments(optimizer, arena, world):
         else:
             for p in params:
                 g = grad_of(p)
-                if g is None or not g.is_contiguous() or p.numel() < 1024 or p.shape[0] % world:
+                if (g is None or not g.is_contiguous() or p.numel() < 1024 or p.shape[0] % world
+                        or p.dtype != torch.float32):
                     continue
                 per = p.shape[0] // world * (p.numel() // p.shape[0])
                 off = arena.offset_of(g)
@@ -195,6 +198,8 @@ class ParamArena:
         for _, _, _, p, base in segments:
             if p in self.params:
                 continue
+            if p.dtype != torch.float32:
+                raise ValueError("the parameter arena holds fp32 masters only")
             view = self.buf[base:base + p.numel()].view(p.shape)
             view.copy_(p.data)
             p.data = view
