@@ -127,3 +127,27 @@ def test_experiment_optimizer_matches_owner_reduction():
         results = m.dict()
         mp.start_processes(_sharded_worker, args=(port, results), nprocs=2, start_method="spawn")
         assert results[0] < 1e-5 and results[1] < 1e-5, dict(results)
+
+
+def test_param_segments_keep_bf16_tables_out():
+    """The fp32 parameter arena of the peer gather never takes a bf16 table (its kernels read bf16)."""
+    import torch
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+    from nexttransformer_b200.parallel.symmetric import GradArena, ownership_segments, param_segments
+    table = torch.nn.Parameter(torch.zeros(64, 32, dtype=torch.bfloat16))
+    head = torch.nn.Parameter(torch.zeros(64, 32))
+    mats = [torch.nn.Parameter(torch.zeros(32, 32)) for _ in range(2)]
+    params = [table, head, *mats]
+    arena = GradArena([tuple(p.shape) for p in params], "cpu")
+    for p in params:
+        p.main_grad = arena.alloc(p.shape)
+    opt = MuonAdamW([dict(kind="adamw", params=[table, head], lr=1e-3, betas=(0.9, 0.95), eps=1e-10,
+                          weight_decay=0.0),
+                     dict(kind="muon", params=mats, lr=1e-2, momentum=0.95, ns_steps=5, beta2=0.9,
+                          weight_decay=0.0)])
+    segs, covered = ownership_segments(opt, arena, 2)
+    assert table in covered and head in covered            # gradients are fp32 either way
+    psegs = param_segments(opt, arena, 2)
+    got = {id(p) for *_, p, _ in psegs}
+    assert id(table) not in got and {id(head), id(mats[0]), id(mats[1])} <= got
+    assert len([s for s in psegs if s[3] is head]) == 2    # one row shard per owner
