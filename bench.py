@@ -466,6 +466,7 @@ def main():
 
     launches = None
     if args.impl == "ours":
+        barrier()       # every rank enters the profiled step together (its peer-memory kernels wait on peers)
         try:
             launches = count_own_kernels(lambda: step_device(dev_x, dev_y)) * args.steps
         except Exception as exc:  # profiler unavailable: report as unknown
@@ -496,8 +497,11 @@ def main():
             out["impl"] = "reference"
             out.pop("gpu_launches")
         print(json.dumps(out), flush=True)
-    del opt, model
+    # symmetric-memory buffers (the peer path) are released after the process group, never while a
+    # peer may still be tearing down its mappings
+    barrier()
     shutdown()
+    del opt, model
 
 
 if __name__ == "__main__":
