@@ -210,3 +210,15 @@ def test_kda_dsa_group_and_rule():
         out, aux = group(x, rotary(cfg), step)
         (out.square().mean() + aux).backward()
         assert torch.isfinite(out).all()
+
+
+def test_recompute_layers_give_the_same_update(tmp_path, monkeypatch):
+    from nexttransformer_b200.scaling import train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    cfg = _config(tmp_path)
+    base = ["--config", str(cfg), "--micro-batch", "1", "--smoke-steps", "1"]
+    train.main(base + ["--output", str(tmp_path / "plain")])
+    train.main(base + ["--output", str(tmp_path / "recompute"), "--recompute-layers", "-1"])
+    a, b = _final_weights(tmp_path / "plain", 1), _final_weights(tmp_path / "recompute", 1)
+    for k in a:
+        torch.testing.assert_close(a[k], b[k], rtol=0, atol=1e-6)
