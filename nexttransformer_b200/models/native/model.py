@@ -92,6 +92,9 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
         self.config = config
         self.max_seq_len = config.sequence_len
         self.last_stats = {}
+        # Dense training steps on CUDA may run the shell's fused sm_100a path; the trainer that sets
+        # this also owns the bf16 shadows (optimizer) and zeroes the fused gradients per update.
+        self.use_fused = False
         if not uses_value_embeddings(config):
             self.value_embeds = nn.ModuleDict()
             for blk in self.transformer.h:
@@ -262,10 +265,16 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
         self.last_stats = self._fresh_stats(idx)
         c = self.config
         if c.architecture == "dense":
-            logits = self.forward_eager(idx)
             d = c.width
             per_tok = 2 * self.num_matmul_params() + sum(4 * d * min(w[0], idx.shape[1]) for w in self.window_sizes)
             self.last_stats.update(forward_flops=idx.numel() * per_tok, active_depth_sum=idx.numel() * c.dense_layers)
+            if (self.use_fused and idx.is_cuda and targets is not None and loss_reduction is None and self.training
+                    and self.fused_supported()):
+                from nexttransformer_b200.models.fused_dense import fused_forward
+                lm = fused_forward(self, idx, targets, "mean")
+                zero = lm.new_zeros(())
+                return dict(loss=lm, lm_loss=lm, router_loss=zero, objective=lm.detach(), compute_loss=zero)
+            logits = self.forward_eager(idx)
             penalty = logits.new_zeros(())
         else:
             hidden, penalty = self._variant_hidden(idx)

@@ -229,11 +229,20 @@ def main(argv=None):
                                                                                  len(model.transformer.h))
     for block in model.transformer.h[:recompute]:
         block.forward = partial(checkpoint, block.forward, use_reentrant=False)
-    optimizer = build_optimizer(model, tc, bf16_reduce=args.bf16_grad_reduce)
+    # On CUDA the dense model trains through the fused sm_100a path (it keeps every activation, so
+    # not with recompute): the optimizer writes the bf16 shadows the fused forward reads.
+    fused = device.type == "cuda" and not recompute and mc.architecture == "dense" and model.fused_supported()
+    shadows = None
+    if fused:
+        shadows = {p: s for p, s in model.fused_state().casts}
+        model.use_fused = True
+    optimizer = build_optimizer(model, tc, shadows=shadows, bf16_reduce=args.bf16_grad_reduce)
     state = dict(step=0, input_tokens=0, next_global_sequence=0, training_flops_estimate=0.,
                  training_seconds=0., validation_seconds=0., completed_val_steps=[], data=identity["data"])
     if resumed is not None:
         saved = ck.load_checkpoint(output, resumed, model, optimizer, stream, device)
+        if fused:
+            model.refresh_shadows()
         if not mc.matches(saved["model_config"]) or saved["train_config"] != asdict(tc):
             raise ValueError("resume configuration differs from checkpoint")
         state = saved["state"]
@@ -259,6 +268,7 @@ def main(argv=None):
             "previous_source_sha256": previous_source, "command": sys.argv, "world_size": world, "nodes": hosts,
             "device": torch.cuda.get_device_name(device) if device.type == "cuda" else str(device),
             "micro_batch": args.micro_batch, "gradient_accumulation": accumulation, "recompute_layers": recompute,
+            "fused_path": fused,
             "bf16_grad_reduce": args.bf16_grad_reduce, "smoke": smoke,
             "parameters": sum(p.numel() for p in model.parameters()), "scaling_parameters": scaling_params(model),
             "muon_weight_decay": muon_weight_decay(model, tc)})
@@ -290,6 +300,8 @@ def main(argv=None):
         if device.type == "cuda":
             torch.cuda.reset_peak_memory_stats(device)
         optimizer.zero_grad(set_to_none=True)
+        if fused:
+            model.zero_main_grads()
         scale = set_schedule(optimizer, step, tc)
         stats = training_stats(mc, device)
         for _ in range(accumulation):
@@ -363,7 +375,7 @@ def main(argv=None):
         seconds = statistics.median(t[0] for t in measured)
         summary = {"event": "benchmark", "world_size": world, "micro_batch": args.micro_batch,
                    "gradient_accumulation": accumulation, "global_batch_tokens": tc.global_batch_tokens,
-                   "recompute_layers": recompute, "bf16_grad_reduce": args.bf16_grad_reduce,
+                   "recompute_layers": recompute, "bf16_grad_reduce": args.bf16_grad_reduce, "fused_path": fused,
                    "measured_steps": len(measured), "step_seconds": seconds,
                    "data_seconds": statistics.median(t[1] for t in measured),
                    "optimizer_seconds": statistics.median(t[2] for t in measured),

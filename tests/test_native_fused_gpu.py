@@ -1,0 +1,52 @@
+"""The native-track dense model on its fused sm_100a path (as the scaling trainer runs it) against
+its own eager path: same weights, same fixed batch, four updates with the scaling optimizer."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _curve(fused, steps=4):
+    from nexttransformer_b200.models.native.model import build_model
+    from nexttransformer_b200.optim.muon_adamw import grad_of
+    from nexttransformer_b200.scaling.config import ScalingModelConfig, ScalingTrainConfig
+    from nexttransformer_b200.scaling.optimizer import build_optimizer
+    mc = ScalingModelConfig(width=256, heads=2, mlp_width=1024, vocab_size=4096, sequence_len=256, dense_layers=2,
+                            window_pattern="SL")
+    tc = ScalingTrainConfig(total_tokens=8 * 4096, global_batch_tokens=4096, val_tokens=4096, final_bpb_tokens=4096,
+                            val_every=1, checkpoint_every=1, milestone_every=1)
+    model = build_model(mc, torch.device("cuda"), seed=3).train()
+    shadows = None
+    if fused:
+        assert model.fused_supported()
+        shadows = {p: s for p, s in model.fused_state().casts}
+        model.use_fused = True
+    opt = build_optimizer(model, tc, shadows=shadows)
+    g = torch.Generator().manual_seed(0)
+    tok = torch.randint(0, 4096, (8, 257), generator=g).cuda()
+    x, y = tok[:, :-1].contiguous(), tok[:, 1:].contiguous()
+    curve = []
+    for _ in range(steps):
+        opt.zero_grad(set_to_none=True)
+        if fused:
+            model.zero_main_grads()
+        tot = 0.0
+        for xs, ys in ((x[:4], y[:4]), (x[4:], y[4:])):
+            out = model(xs, ys)
+            (out["loss"] / 2).backward()
+            tot += out["lm_loss"].item() / 2
+        assert all(grad_of(p) is not None for p in model.parameters())
+        opt.step()
+        curve.append(tot)
+    return curve, model.last_stats["forward_flops"]
+
+
+def test_native_dense_fused_tracks_eager():
+    ours, f1 = _curve(True)
+    eager, f2 = _curve(False)
+    print("fused", ours, "eager", eager)
+    assert f1 == f2
+    assert abs(ours[0] - eager[0]) < 0.02 * eager[0]
+    for a, b in zip(ours[1:], eager[1:]):
+        assert abs(a - b) < 0.08 * b + 0.05, (ours, eager)
+    assert ours[-1] < ours[0]
