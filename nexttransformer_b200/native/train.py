@@ -82,6 +82,8 @@ def update(model, optimizer, stream, mc, tc, accum, micro, world, device, step):
     from nexttransformer_b200.runtime.statistics import accumulate_stats, training_stats
     from nexttransformer_b200.optim.muon_adamw import grad_of
     optimizer.zero_grad(set_to_none=True)
+    if getattr(model, "use_fused", False):
+        model.zero_main_grads()
     stats = training_stats(mc, device)
     for _ in range(accum):
         x, y = stream.batch(micro, device)
@@ -136,7 +138,13 @@ def main(argv=None):
     accum = tc.accumulation(mc, world, micro)
     stream = make_stream(args, mc, rank, world, seed)
     model = build_model(mc, device, seed=seed)
-    optimizer = build_optimizer(model, tc)
+    # The dense model trains through the fused sm_100a path on CUDA; the optimizer then writes the
+    # bf16 shadows that path reads.
+    shadows = None
+    if device.type == "cuda" and mc.architecture == "dense" and model.fused_supported():
+        shadows = {p: s for p, s in model.fused_state().casts}
+        model.use_fused = True
+    optimizer = build_optimizer(model, tc, shadows=shadows)
     state = dict(step=0, input_tokens=0, training_seconds=0.0, smoke=bool(args.smoke_steps))
     if args.resume == "auto":
         if rank == 0:
@@ -145,6 +153,8 @@ def main(argv=None):
         if done:
             state = ckpt.load_checkpoint(out / f"checkpoint_{done[-1]:08d}", model, optimizer, stream, rank,
                                          world)["state"]
+            if shadows is not None:
+                model.refresh_shadows()
     stop = min(args.smoke_steps or tc.steps, tc.steps)
     every = args.checkpoint_every or tc.checkpoint_every
     phase = None

@@ -69,6 +69,19 @@ def verify_checkpoint(path, names):
     return manifest
 
 
+def load_optimizer_state(optimizer, state_dict):
+    """``optimizer.load_state_dict`` that keeps the saved dtype of every floating state tensor.
+    torch casts each parameter's state to the parameter's dtype on load; the update kernels keep fp32
+    moments for the bf16 embedding tables, so those are restored from the saved fp32 tensors."""
+    optimizer.load_state_dict(state_dict)
+    params = [p for group in optimizer.param_groups for p in group["params"]]
+    for index, saved in state_dict["state"].items():
+        live = optimizer.state[params[index]]
+        for key, value in saved.items():
+            if torch.is_tensor(value) and value.is_floating_point() and live[key].dtype != value.dtype:
+                live[key] = value.to(device=params[index].device)
+
+
 def load_checkpoint(path, model, optimizer=None, stream=None, rank=0, world=1):
     path = Path(path)
     manifest = json.loads((path / "complete.json").read_text())
@@ -81,7 +94,7 @@ def load_checkpoint(path, model, optimizer=None, stream=None, rank=0, world=1):
         model.refresh_shadows()
     if optimizer is not None:
         local = torch.load(path / f"rank_{rank:04d}.pt", map_location="cpu", weights_only=False)
-        optimizer.load_state_dict(local["optimizer"])
+        load_optimizer_state(optimizer, local["optimizer"])
         if stream is not None and local["data"] is not None:
             stream.load_state_dict(local["data"])
         restore_rng(local["rng"])

@@ -20,6 +20,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from nexttransformer_b200.runtime.checkpoint import load_optimizer_state
 from nexttransformer_b200.runtime.files import atomic_json, sha256
 from nexttransformer_b200.runtime.process import restore_rng, rng_state
 
@@ -172,7 +173,7 @@ def load_checkpoint(output, step, model, optimizer, stream, device):
     saved = torch.load(directory / "model.pt", map_location="cpu", weights_only=False)
     model.load_state_dict(saved["model"], strict=True)
     local = torch.load(directory / f"rank_{rank:04d}.pt", map_location="cpu", weights_only=False)
-    optimizer.load_state_dict(local["optimizer"])
+    load_optimizer_state(optimizer, local["optimizer"])
     stream.load_state_dict(local["data"])
     restore_rng(local["rng"])
     if local["routing_rng"] is not None and hasattr(model, "restore_routing_rng"):

@@ -114,3 +114,24 @@ def test_tracking_auth_preflight():
         raise subprocess.TimeoutExpired(a[0], k["timeout"])
     with pytest.raises(RuntimeError, match="timed out"):
         preflight("online", timeout=1, runner=slow)
+
+
+def test_optimizer_state_keeps_fp32_moments_of_bf16_tables():
+    """torch's load_state_dict casts state to the parameter dtype; bf16 tables keep fp32 moments."""
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+    from nexttransformer_b200.runtime.checkpoint import load_optimizer_state
+
+    def make():
+        torch.manual_seed(0)
+        table = torch.nn.Parameter(torch.randn(16, 8).to(torch.bfloat16))
+        return table, MuonAdamW([dict(kind="adamw", params=[table], lr=1e-2, betas=(0.9, 0.95), eps=1e-10,
+                                      weight_decay=0.0)])
+    table, opt = make()
+    table.grad = torch.randn(16, 8).to(torch.bfloat16)
+    opt.step()
+    saved = opt.state_dict()
+    fresh_table, fresh = make()
+    load_optimizer_state(fresh, saved)
+    for key in ("exp_avg", "exp_avg_sq"):
+        assert fresh.state[fresh_table][key].dtype == torch.float32
+        assert torch.equal(fresh.state[fresh_table][key], opt.state[table][key])
