@@ -366,6 +366,13 @@ def main(argv=None):
             phase = "stopped"
             break
     complete = phase is None and not smoke and state["step"] == tc.steps
+    if complete:
+        # the final checkpoint precedes this evaluation; a restart repeats only the evaluation
+        final = evaluate_stream_loss(_LossView(model), mc, tc.final_bpb_tokens, args.micro_batch, rank, world,
+                                     device, tc.seed + 1)
+        if rank == 0:
+            atomic_json(output / "bpb_final.json", {"step": state["step"], "val": final})
+        record({"event": "final_bpb", "step": state["step"], **{"final_" + k: v for k, v in final.items()}})
     phase = phase or ("smoke_complete" if smoke else "training_complete" if complete else "stopped")
     if benchmark and timings:
         measured = timings[min(3, len(timings) - 1):]

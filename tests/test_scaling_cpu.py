@@ -222,3 +222,25 @@ def test_recompute_layers_give_the_same_update(tmp_path, monkeypatch):
     a, b = _final_weights(tmp_path / "plain", 1), _final_weights(tmp_path / "recompute", 1)
     for k in a:
         torch.testing.assert_close(a[k], b[k], rtol=0, atol=1e-6)
+
+
+def test_complete_run_exports_a_record(tmp_path, monkeypatch):
+    from nexttransformer_b200.scaling import export, train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    cfg = _config(tmp_path)
+    state = train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "run")])
+    assert state["step"] == 4
+    assert json.loads((tmp_path / "run" / "run_status.json").read_text())["phase"] == "training_complete"
+    rec = export.record(tmp_path / "run", cfg, "tiny", "Tiny", "dense")
+    assert [v["step"] for v in rec["val"]] == [0, 2, 4] and rec["finalVal"] == rec["finalVal"]
+    results = tmp_path / "results"
+    export.write(results, rec)
+    export.write(results, rec)                     # identical export: no-op
+    assert export.check(results) == []
+    changed = dict(rec, name="Other")
+    with pytest.raises(ValueError):
+        export.write(results, changed)
+    # a smoke run is never exported
+    train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "smoke"), "--smoke-steps", "4"])
+    with pytest.raises(ValueError):
+        export.record(tmp_path / "smoke", cfg, "tiny", "Tiny", "dense")
