@@ -122,6 +122,10 @@ def parse(argv=None):
                    help="recompute the first N blocks in the backward (-1: every block)")
     p.add_argument("--bf16-grad-reduce", action="store_true", help="reduce gradients in bf16")
     p.add_argument("--keep-local", type=int, default=3, help="rolling checkpoints kept per node besides milestones")
+    p.add_argument("--core", type=Path, help="CORE bundle (tasks.json + <label>.jsonl): evaluated at the core steps")
+    p.add_argument("--tokenizer", type=Path, help="tokenizer directory for CORE (default: RESOURCES/tokenizer)")
+    from nexttransformer_b200.evaluation.context import add_core_max_tokens
+    add_core_max_tokens(p)
     a = p.parse_args(argv)
     from nexttransformer_b200.runtime.site import resolve
     resolve(a)
@@ -258,6 +262,21 @@ def main(argv=None):
         if state["source_sha256"] != source["sha256"] and not args.allow_source_change:
             raise ValueError("resume source files differ from checkpoint; pass --allow-source-change")
         del saved
+        from nexttransformer_b200.evaluation.context import resume_core_limit
+        args.core_max_tokens = resume_core_limit(state, args.core_max_tokens, mc.sequence_len)
+    state["core_max_tokens"] = args.core_max_tokens
+    tasks, tokenizer = None, None
+    if args.core and not benchmark:
+        from nexttransformer_b200.evaluation.context import check_full_context
+        from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+        tasks = json.loads((args.core / "tasks.json").read_text())
+        for t in tasks:
+            t["data"] = [json.loads(l) for l in (args.core / f"{t['label']}.jsonl").read_text().splitlines() if l]
+        tokenizer = BPETokenizer.from_directory(args.tokenizer or Path(args.resources) / "tokenizer")
+        if tokenizer.get_vocab_size() > mc.vocab_size:
+            raise ValueError("the tokenizer's vocabulary does not fit the model")
+        if not smoke:
+            check_full_context(mc, args.core_max_tokens)
     previous_source = state.get("source_sha256")
     state["source_sha256"], state["smoke"] = source["sha256"], smoke
     if not benchmark and rank == 0:
@@ -278,6 +297,24 @@ def main(argv=None):
         if rank == 0 and not benchmark:
             append_event(output, event)
             print(json.dumps(event), flush=True)
+
+    def core(step, final=False):
+        from nexttransformer_b200.evaluation.context import LengthProbe, core_context, inference_view
+        from nexttransformer_b200.evaluation.core import evaluate_core
+        probe = LengthProbe(inference_view(model, args.core_max_tokens))
+        model.eval()
+        with torch.no_grad():
+            result = evaluate_core(probe, tokenizer, tasks, device, rank, world,
+                                   -1 if final else tc.core_max_per_task, args.core_max_tokens)
+        model.train()
+        longest = torch.tensor(probe.longest, device=device)
+        if world > 1:
+            dist.all_reduce(longest, op=dist.ReduceOp.MAX)
+        result["coreContext"] = core_context(mc.sequence_len, args.core_max_tokens, int(longest.item()))
+        record({"event": "core", "step": step, **result})
+        if rank == 0:
+            atomic_json(output / ("core_final.json" if final else f"core_{step:08d}.json"),
+                        {"event": "core", "step": step, **result})
 
     def validation(step):
         if benchmark or step in state["completed_val_steps"]:
@@ -353,6 +390,8 @@ def main(argv=None):
                     "gpu_hours": world * state["training_seconds"] / 3600, "peak_memory_bytes": memory})
         if state["step"] % tc.val_every == 0 or state["step"] == stop_step:
             validation(state["step"])
+        if tasks is not None and not smoke and state["step"] < tc.steps and state["step"] in tc.core_steps():
+            core(state["step"])
         requested = bool(_stop_signal) or (rank == 0 and not benchmark and (output / "STOP").exists())
         stop = not ck.agree(not requested, device) or bool(args.stop_after and state["step"] - launched >= args.stop_after)
         if not benchmark and (state["step"] % tc.checkpoint_every == 0 or state["step"] == stop_step or stop):
@@ -373,6 +412,8 @@ def main(argv=None):
         if rank == 0:
             atomic_json(output / "bpb_final.json", {"step": state["step"], "val": final})
         record({"event": "final_bpb", "step": state["step"], **{"final_" + k: v for k, v in final.items()}})
+        if tasks is not None:
+            core(state["step"], final=True)
     phase = phase or ("smoke_complete" if smoke else "training_complete" if complete else "stopped")
     if benchmark and timings:
         measured = timings[min(3, len(timings) - 1):]

@@ -244,3 +244,29 @@ def test_complete_run_exports_a_record(tmp_path, monkeypatch):
     train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "smoke"), "--smoke-steps", "4"])
     with pytest.raises(ValueError):
         export.record(tmp_path / "smoke", cfg, "tiny", "Tiny", "dense")
+
+
+def test_core_evaluation_at_core_steps(tmp_path, monkeypatch):
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    from nexttransformer_b200.scaling import train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    docs = ["the quick brown fox jumps over the lazy dog %d" % i for i in range(50)]
+    tok = BPETokenizer.train_from_iterator(docs, vocab_size=300)
+    tok.save(tmp_path / "tok")
+    cfg = tmp_path / "core.json"
+    write_config(cfg, ScalingModelConfig(**dict(TINY, vocab_size=320)),
+                 ScalingTrainConfig(total_tokens=64, global_batch_tokens=32, val_tokens=32, final_bpb_tokens=32,
+                                    val_every=2, checkpoint_every=1, milestone_every=2, core_every=1))
+    bundle = tmp_path / "bundle"
+    bundle.mkdir()
+    (bundle / "tasks.json").write_text(json.dumps([{"label": "lm", "random_baseline": 0.0,
+                                                    "meta": {"task_type": "language_modeling", "num_fewshot": 0}}]))
+    (bundle / "lm.jsonl").write_text("".join(json.dumps({"context": "the quick brown", "continuation": " fox"}) + "\n"
+                                             for _ in range(3)))
+    train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "run"), "--core", str(bundle),
+                "--tokenizer", str(tmp_path / "tok")])
+    events = [json.loads(l) for l in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    core = [e for e in events if e["event"] == "core"]
+    assert [e["step"] for e in core] == [1, 2]
+    assert core[0]["coreContext"]["truncation"] == "none" and 0 <= core[-1]["core_metric"] <= 1
+    assert (tmp_path / "run" / "core_00000001.json").exists() and (tmp_path / "run" / "core_final.json").exists()
