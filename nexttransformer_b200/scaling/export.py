@@ -22,6 +22,14 @@ FIELDS = ("id", "name", "family", "protocol", "configSha256", "model", "paramete
           "finalVal")
 
 
+def _metric(event, prefix=""):
+    """Validation value of an event: bits per byte with real data, the synthetic-stream loss otherwise."""
+    for key in ("val_bpb", "val_loss"):
+        if prefix + key in event:
+            return event[prefix + key]
+    raise ValueError("an evaluation record without a validation value")
+
+
 def record(run, config, run_id, name, family):
     run = Path(run)
     mc, tc = load_config(config)
@@ -37,11 +45,11 @@ def record(run, config, run_id, name, family):
         raise ValueError(f"validation events at {sorted(val)}, scheduled {tc.validation_steps()}")
     for step, e in val.items():
         saved = json.loads((run / f"val_{step:08d}.json").read_text())
-        if saved.get("val_loss") != e["val_loss"]:
+        if _metric(saved) != _metric(e):
             raise ValueError(f"val_{step:08d}.json differs from the event history")
     finals = [e for e in events if e["event"] == "final_bpb"]
     final = json.loads((run / "bpb_final.json").read_text())
-    if len(finals) != 1 or finals[0]["final_val_loss"] != final["val"]["val_loss"]:
+    if len(finals) != 1 or _metric(finals[0], "final_") != _metric(final["val"]):
         raise ValueError("the final evaluation is missing or differs from the event history")
     train = [e for e in events if e["event"] == "train"]
     if not train or not all(math.isfinite(e["lm_loss"]) for e in train):
@@ -52,8 +60,9 @@ def record(run, config, run_id, name, family):
                          "global_batch_tokens": tc.global_batch_tokens, "world_size": provenance["world_size"],
                          "last_lm_loss": train[-1]["lm_loss"]},
             "source": provenance["source_sha256"],
-            "val": [{"step": s, "val_loss": val[s]["val_loss"]} for s in sorted(val)],
-            "finalVal": final["val"]["val_loss"]}
+            "metric": "val_bpb" if "val_bpb" in final["val"] else "val_loss",
+            "val": [{"step": s, "value": _metric(val[s])} for s in sorted(val)],
+            "finalVal": _metric(final["val"])}
 
 
 def write(results, rec):

@@ -316,11 +316,27 @@ def main(argv=None):
             atomic_json(output / ("core_final.json" if final else f"core_{step:08d}.json"),
                         {"event": "core", "step": step, **result})
 
+    def evaluate(tokens, seed_offset=0):
+        """Bits per byte on the validation split with real data; the held-out synthetic stream's loss
+        otherwise."""
+        if args.data == "synthetic":
+            return evaluate_stream_loss(_LossView(model), mc, tokens, args.micro_batch, rank, world, device,
+                                        tc.seed + seed_offset)
+        from nexttransformer_b200.evaluation.bpb import evaluate_bpb
+        from nexttransformer_b200.runtime.data import BestFitStream
+        t0 = time.time()
+        val = BestFitStream(args.data_dir or Path(args.resources) / "base_data_climbmix", stream.tokenizer, "val",
+                            rank, world, mc.sequence_len)
+        steps = max(1, tokens // (world * args.micro_batch * mc.sequence_len))
+        bpb = evaluate_bpb(_LossView(model), val.batches(args.micro_batch, device), steps,
+                           stream.tokenizer.token_bytes().to(device))
+        return {"val_bpb": bpb, "val_tokens": steps * world * args.micro_batch * mc.sequence_len,
+                "seconds": time.time() - t0}
+
     def validation(step):
         if benchmark or step in state["completed_val_steps"]:
             return
-        result = evaluate_stream_loss(_LossView(model), mc, val_tokens, args.micro_batch, rank, world, device,
-                                      tc.seed)
+        result = evaluate(val_tokens)
         state["completed_val_steps"].append(step)
         state["validation_seconds"] += result["seconds"]
         record({"event": "validation", "step": step, **result})
@@ -407,8 +423,7 @@ def main(argv=None):
     complete = phase is None and not smoke and state["step"] == tc.steps
     if complete:
         # the final checkpoint precedes this evaluation; a restart repeats only the evaluation
-        final = evaluate_stream_loss(_LossView(model), mc, tc.final_bpb_tokens, args.micro_batch, rank, world,
-                                     device, tc.seed + 1)
+        final = evaluate(tc.final_bpb_tokens, 1)
         if rank == 0:
             atomic_json(output / "bpb_final.json", {"step": state["step"], "val": final})
         record({"event": "final_bpb", "step": state["step"], **{"final_" + k: v for k, v in final.items()}})

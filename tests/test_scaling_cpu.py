@@ -270,3 +270,29 @@ def test_core_evaluation_at_core_steps(tmp_path, monkeypatch):
     assert [e["step"] for e in core] == [1, 2]
     assert core[0]["coreContext"]["truncation"] == "none" and 0 <= core[-1]["core_metric"] <= 1
     assert (tmp_path / "run" / "core_00000001.json").exists() and (tmp_path / "run" / "core_final.json").exists()
+
+
+def test_real_data_validation_is_bpb(tmp_path, monkeypatch):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+    from nexttransformer_b200.runtime.files import VALIDATION_SHARD
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    from nexttransformer_b200.scaling import export, train
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    docs = ["the quick brown fox jumps over the lazy dog %d" % i for i in range(300)]
+    data = tmp_path / "data"
+    data.mkdir()
+    pq.write_table(pa.table({"text": docs}), data / "shard_00000.parquet")
+    pq.write_table(pa.table({"text": docs[:60]}), data / VALIDATION_SHARD)
+    BPETokenizer.train_from_iterator(docs, vocab_size=300).save(tmp_path / "res" / "tokenizer")
+    cfg = tmp_path / "bpb.json"
+    write_config(cfg, ScalingModelConfig(**dict(TINY, vocab_size=320)),
+                 ScalingTrainConfig(total_tokens=64, global_batch_tokens=32, val_tokens=32, final_bpb_tokens=32,
+                                    val_every=1, checkpoint_every=1, milestone_every=2, core_every=0))
+    train.main(["--config", str(cfg), "--micro-batch", "1", "--output", str(tmp_path / "run"), "--data", "bestfit",
+                "--resources", str(tmp_path / "res"), "--data-dir", str(data)])
+    events = [json.loads(l) for l in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    val = [e for e in events if e["event"] == "validation"]
+    assert [e["step"] for e in val] == [0, 1, 2] and all(0 < e["val_bpb"] < 100 for e in val)
+    rec = export.record(tmp_path / "run", cfg, "bpb", "BPB", "dense")
+    assert rec["metric"] == "val_bpb" and len(rec["val"]) == 3
