@@ -200,8 +200,14 @@ def main(argv=None):
     if world > 1:
         dist.barrier()
     stream = make_stream(args, mc, rank, world, tc.seed)
-    data_identity = hashlib.sha256(json.dumps({"kind": args.data, "vocab": mc.vocab_size, "seq": mc.sequence_len,
-                                               "seed": tc.seed, "world": world}).encode()).hexdigest()
+    described = {"kind": args.data, "vocab": mc.vocab_size, "seq": mc.sequence_len, "seed": tc.seed, "world": world}
+    if args.data == "bestfit":
+        # every node must hold the same shards and the same tokenizer
+        from nexttransformer_b200.runtime.resources import data_inventory, inventory_fingerprint, tokenizer_fingerprint
+        described.update(inventory=inventory_fingerprint(data_inventory(args.data_dir or Path(args.resources)
+                                                                        / "base_data_climbmix")),
+                         tokenizer=tokenizer_fingerprint(args.resources))
+    data_identity = hashlib.sha256(json.dumps(described, sort_keys=True).encode()).hexdigest()
     source = source_manifest()
     identity = dict(source_sha256=source["sha256"], data=data_identity, config_sha256=config_hash(mc, tc),
                     torch=torch.__version__, cuda=torch.version.cuda)
