@@ -57,6 +57,7 @@ def main(argv=None):
                                                              inference_view)
         if a.core_max_per_task <= 0:
             check_full_context(cfg, a.core_max_tokens)
+        model.eval()
         probe = LengthProbe(inference_view(model, a.core_max_tokens))
         result["core"] = evaluate_core(probe, tok, tasks, dev, rank, world, a.core_max_per_task, a.core_max_tokens)
         longest = torch.tensor(probe.longest, device=dev)

@@ -307,8 +307,8 @@ def main(argv=None):
     def core(step, final=False):
         from nexttransformer_b200.evaluation.context import LengthProbe, core_context, inference_view
         from nexttransformer_b200.evaluation.core import evaluate_core
+        model.eval()          # before the view is taken: the shallow copy keeps the mode it was made in
         probe = LengthProbe(inference_view(model, args.core_max_tokens))
-        model.eval()
         with torch.no_grad():
             result = evaluate_core(probe, tokenizer, tasks, device, rank, world,
                                    -1 if final else tc.core_max_per_task, args.core_max_tokens)
