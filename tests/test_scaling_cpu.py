@@ -296,3 +296,25 @@ def test_real_data_validation_is_bpb(tmp_path, monkeypatch):
     assert [e["step"] for e in val] == [0, 1, 2] and all(0 < e["val_bpb"] < 100 for e in val)
     rec = export.record(tmp_path / "run", cfg, "bpb", "BPB", "dense")
     assert rec["metric"] == "val_bpb" and len(rec["val"]) == 3
+
+
+@pytest.mark.parametrize("burnin", [True, False])
+def test_kda_dsa_group_is_causal_and_trains_its_indexer(burnin):
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.scaling.reference_blocks import KdaDsaGroup, rotary
+    torch.manual_seed(42)
+    cfg = debug_config("dsa")
+    group = KdaDsaGroup(cfg)
+    assert [m.kind for m in group.mixers] == ["kda", "kda", "kda", "dsa"]
+    x = torch.randn(1, cfg.sequence_len, cfg.width)
+    step = cfg.burnin_steps - int(burnin)
+    out, aux = group(x, rotary(cfg), step)
+    assert group.mixers[-1].in_burnin is burnin
+    (out.square().mean() + aux).backward()
+    grad = group.mixers[-1].index_q.weight.grad
+    assert torch.isfinite(grad).all() and grad.abs().sum() > 0
+    changed = x.clone()
+    changed[:, -2:] += torch.randn_like(changed[:, -2:])
+    with torch.no_grad():
+        changed_out, _ = group(changed, rotary(cfg), step)
+    torch.testing.assert_close(out[:, :-2], changed_out[:, :-2])
