@@ -899,11 +899,8 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
   CUtensorMap to = tile_map(a.o, static_cast<int64_t>(a.H) * HD, a.ldo, a.T, a.B);
   Params p = make_params(a);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::TOTAL);
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, attn_fwd_kernel, FwdSmem::TOTAL);
   const int n_qt = (a.T + TILE - 1) / TILE;
   dim3 grid((n_qt + 1) / 2, a.H, a.B);
   attn_fwd_kernel<<<grid, FWD_THREADS, FwdSmem::TOTAL, s>>>(tq, tk, tv, to, p);
@@ -934,11 +931,8 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   p.dq_acc = a.dq_acc;
   p.delta = a.delta;
   p.trace = a.trace;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, attn_bwd_kernel, BwdSmem::TOTAL);
   dim3 grid((a.T + TILE - 1) / TILE, a.Hk, a.B);
   attn_bwd_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p);
   const int cols = a.H * HD;

@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define NT_DEVICE __device__ __forceinline__
 
 namespace nt {
@@ -21,6 +23,21 @@ namespace nt {
 inline void current_context() {
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+}
+
+// Host side: raise a kernel's dynamic shared-memory limit on the current device.  The attribute
+// belongs to the device, so a process that drives several GPUs must set it on each of them;
+// `done` is the caller's bitmask of devices (ids 0-63) already set for this kernel.  Concurrent
+// callers may both set it, which is harmless.  Devices beyond 63 set it on every launch.
+template <class Kernel>
+inline cudaError_t smem_limit(std::atomic<uint64_t>& done, Kernel kern, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 // ---------------------------------------------------------------- error flag

@@ -553,10 +553,8 @@ int nt_delta_scan_fwd(const DeltaScanFwdArgs& a, cudaStream_t stream) {
   const CUtensorMap tw = map2d(a.w, DK, rows), tq = map2d(a.qt, DK, rows), tk = map2d(a.kc, DK, rows),
                     ta = map2d(a.aqk, CH, rows), tu = map2d(a.u0, DV, rows);
   FwdParams p{a.N, a.carry, a.o, a.states, a.u};
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(delta_scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::TOTAL);
-  });
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, delta_scan_fwd_kernel, FwdSmem::TOTAL);
   delta_scan_fwd_kernel<<<dim3(DV / VB, a.BH), 192, FwdSmem::TOTAL, stream>>>(tw, tq, tk, ta, tu, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -568,10 +566,8 @@ int nt_delta_scan_bwd(const DeltaScanBwdArgs& a, cudaStream_t stream) {
   const CUtensorMap td = map2d(a.dout, DV, rows), ta = map2d(a.aqk, CH, rows), tk = map2d(a.kc, DK, rows),
                     tq = map2d(a.qt, DK, rows), tw = map2d(a.w, DK, rows);
   BwdParams p{a.N, a.carry, a.states, a.ds, a.dut, a.dcarry};
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(delta_scan_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
-  });
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, delta_scan_bwd_kernel, BwdSmem::TOTAL);
   delta_scan_bwd_kernel<<<a.BH, 192, BwdSmem::TOTAL, stream>>>(td, ta, tk, tq, tw, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -26,14 +26,19 @@
 //    Nothing needs to start at zero: every partial-product element a call reads was written by
 //    that same call first.  Two calls whose kernels overlap on the GPU (different streams without
 //    ordering) race on the array; order them on one stream, or with events.
+//  * Errors: the C declarations and return codes are in gemm_noalloc.h.  A bounded wait that
+//    times out inside the kernel is reported by nt_wgrad_noalloc_read_error once the stream
+//    has finished (the launch itself has already returned NT_NOALLOC_OK by then).
 //  * Set-up: the first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress while that device is current (host code cannot use the array's name as
 //    a device pointer).  That first call should therefore come before any stream capture.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <exception>
 #include <mutex>
 
+#include "gemm_noalloc.h"
 #include "gemm_sm100.h"
 
 namespace {
@@ -53,14 +58,15 @@ std::mutex g_setup_lock;
 
 // Once per device, with that device current: the scratch array's device address and SM count.
 int setup_device(int dev, DeviceSlot** out) {
-  if (dev < 0 || dev >= NT_NOALLOC_MAX_DEVICES) return 4;
+  if (dev < 0 || dev >= NT_NOALLOC_MAX_DEVICES) return NT_NOALLOC_BAD_DEVICE;
   std::lock_guard<std::mutex> guard(g_setup_lock);
   DeviceSlot& slot = g_slots[dev];
   if (!slot.ready) {
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return 2;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return NT_NOALLOC_SETUP_FAILED;
     int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 2;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      return NT_NOALLOC_SETUP_FAILED;
     slot.ptr = ptr;
     slot.sms = sms;
     slot.ready = true;
@@ -70,15 +76,6 @@ int setup_device(int dev, DeviceSlot** out) {
 }
 
 }  // namespace
-
-// Return codes of nt_wgrad_splitk_noalloc.
-enum : int {
-  NT_NOALLOC_OK = 0,
-  NT_NOALLOC_TOO_LARGE = 1,     // split-K partial products exceed the scratch array
-  NT_NOALLOC_SETUP_FAILED = 2,  // the scratch array's device address could not be obtained
-  NT_NOALLOC_BAD_ARGUMENT = 3,  // null pointer, non-positive size or misaligned operand
-  NT_NOALLOC_BAD_DEVICE = 4,    // current device id outside the supported range
-};
 
 extern "C" int nt_wgrad_splitk_noalloc(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc,
                                        int M, int N, int K, float alpha, int accumulate, void* stream) {
@@ -115,9 +112,25 @@ extern "C" int nt_wgrad_splitk_noalloc(const void* A, int64_t lda, const void* B
     g.workspace = slot->ptr;
     g.workspace_bytes = NT_NOALLOC_SCRATCH_BYTES;
   }
-  nt_gemm_launch(g, static_cast<cudaStream_t>(stream));
-  return cudaPeekAtLastError() == cudaSuccess ? NT_NOALLOC_OK : NT_NOALLOC_SETUP_FAILED;
+  // An error left pending by unrelated earlier work is cleared first, so that the error read
+  // after the launch is this launch's own.  No C++ exception may cross the C interface.
+  (void)cudaGetLastError();
+  try {
+    nt_gemm_launch(g, static_cast<cudaStream_t>(stream));
+  } catch (const std::exception&) {
+    return NT_NOALLOC_INTERNAL;
+  } catch (...) {
+    return NT_NOALLOC_INTERNAL;
+  }
+  return cudaGetLastError() == cudaSuccess ? NT_NOALLOC_OK : NT_NOALLOC_LAUNCH_FAILED;
 }
 
-// Capacity of the scratch array in bytes (the size limit of nt_wgrad_splitk_noalloc).
-extern "C" size_t nt_wgrad_splitk_noalloc_scratch_bytes() { return NT_NOALLOC_SCRATCH_BYTES; }
+extern "C" size_t nt_wgrad_splitk_noalloc_scratch_bytes(void) { return NT_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int nt_wgrad_noalloc_read_error(unsigned* where) {
+  try {
+    return nt_gemm_read_error(where);
+  } catch (...) {
+    return -1;
+  }
+}

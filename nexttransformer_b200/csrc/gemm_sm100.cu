@@ -927,11 +927,8 @@ static void launch_t(const GemmArgs& g, cudaStream_t stream) {
     p.tma_out = ok ? 1 : 0;
   }
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, STAGES, PAIR>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, kern, S::TOTAL);
   const int tiles = p.batch * p.split * p.tiles_m * p.tiles_n;
   if constexpr (PAIR) {
     const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;

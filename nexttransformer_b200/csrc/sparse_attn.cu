@@ -689,10 +689,8 @@ int nt_sparse_attn_fwd(const SparseAttnArgs& a, cudaStream_t s) {
   const CUtensorMap tq = row_map(a.q, static_cast<int64_t>(a.H) * HD, a.ldq, a.T, a.B, QT);
   const CUtensorMap tk = row_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B, KB);
   const CUtensorMap tv = row_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B, KB);
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(bsa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdSmem::TOTAL);
-  });
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, bsa_fwd_kernel, FwdSmem::TOTAL);
   bsa_fwd_kernel<<<dim3(p.n_qt, a.H, a.B), 192, FwdSmem::TOTAL, s>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -708,10 +706,8 @@ int nt_sparse_attn_bwd(const SparseAttnArgs& a, cudaStream_t s) {
   const CUtensorMap td = row_map(a.dout, static_cast<int64_t>(a.H) * HD, a.lddo, a.T, a.B, QT);
   const CUtensorMap tdk = acc_map(a.dk_acc, static_cast<int64_t>(a.Hk) * HD, a.T, a.B);
   const CUtensorMap tdv = acc_map(a.dv_acc, static_cast<int64_t>(a.Hk) * HD, a.T, a.B);
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(bsa_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
-  });
+  static std::atomic<uint64_t> smem_set{0};
+  nt::smem_limit(smem_set, bsa_bwd_kernel, BwdSmem::TOTAL);
   bsa_bwd_kernel<<<dim3(p.n_qt, a.H, a.B), 320, BwdSmem::TOTAL, s>>>(tq, tk, tv, td, tdk, tdv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

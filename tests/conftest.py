@@ -2,7 +2,9 @@
 
 Markers: ``gpu`` (needs a CUDA device; the CPU run uses ``-m "not gpu"``) and ``slow``.
 The ``reference`` fixture makes the reference implementation importable from its offline
-install under ``baseline/_ref`` (used as a CPU oracle); tests that need it skip without it.
+install under ``baseline/_ref`` (used as a CPU oracle).  When the install is missing it is made
+from the reference's source tree; when neither exists, tests that need it FAIL rather than skip, so
+a parity regression cannot hide behind a missing oracle.
 """
 import os
 import socket
@@ -35,8 +37,13 @@ def pytest_collection_modifyitems(config, items):
 @pytest.fixture(scope="session")
 def reference():
     """Import path of the reference package (CPU oracle)."""
-    if not (REF / "nanochat").is_dir():
-        pytest.skip("reference install (baseline/_ref) not present")
+    from nexttransformer_b200.utils.reference_install import ensure
+    try:
+        path = ensure(REF)
+    except RuntimeError as exc:
+        pytest.fail(f"reference install under baseline/_ref failed: {exc}")
+    if path is None:
+        pytest.fail("reference not installed under baseline/_ref and no source tree to install it from")
     if str(REF) not in sys.path:
         sys.path.append(str(REF))
     import torch

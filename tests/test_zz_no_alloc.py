@@ -69,17 +69,70 @@ def test_matches_allocating_entry_point(lib, T, N, K, accumulate):
         assert err < 1e-3, err
 
 
+def _split(M, N, K, sms):
+    """The split-K factor the GEMM launcher picks for an fp32 weight-gradient problem."""
+    tiles = -(-M // 128) * -(-N // 256)
+    want = 2 * sms
+    if N < 256 or tiles >= want:
+        return 1
+    split = min(16, -(-want // tiles))
+    while split > 1 and (-(-K // 64)) // split < 16:
+        split -= 1
+    return split
+
+
+def _oversize_shape(sms, cap, K=16384):
+    """(M, N) of a problem whose split-K partial products exceed the scratch on this GPU, or None."""
+    for nt in range(1, 33):
+        N = 256 * nt
+        for mt in range(1, 2 * sms + 1):
+            M = 128 * mt
+            split = _split(M, N, K, sms)
+            if split > 1 and split * M * N * 4 > cap:
+                return M, N
+    return None
+
+
 def test_rejects_oversize_problem(lib):
     mod, fn, cap = lib
-    # 59 x 5 output tiles split in two: 2 * 7552 * 1280 * 4 bytes of partial products > 64 MiB.
-    T, N, K = 4096, 7552, 1280
-    assert 2 * N * K * 4 > cap
-    dy = torch.zeros(T, N, device="cuda", dtype=torch.bfloat16)
-    x = torch.zeros(T, K, device="cuda", dtype=torch.bfloat16)
-    out = torch.full((N, K), 7.0, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    shape = _oversize_shape(sms, cap)
+    if shape is None:
+        pytest.skip(f"with {sms} SMs no split-K problem needs more than {cap} bytes of scratch")
+    M, N = shape
+    T = 16384
+    dy = torch.zeros(T, M, device="cuda", dtype=torch.bfloat16)
+    x = torch.zeros(T, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.full((M, N), 7.0, device="cuda")
     assert call(fn, dy, x, out, accumulate=False) == 1
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)  # nothing was launched
+
+
+def test_allocates_nothing(lib):
+    """A call, including the split-K scratch it uses, leaves the caching allocator untouched."""
+    mod, fn, _ = lib
+    T, N, K = 65536, 1280, 1280
+    dy = torch.randn(T, N, device="cuda").to(torch.bfloat16)
+    x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+    out = torch.zeros(N, K, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _split(N, K, T, sms) > 1  # the scratch array is in use
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_stats()["allocation.all.allocated"]
+    assert call(fn, dy, x, out, accumulate=False) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == before
+    assert lib_error() == 0
+
+
+def lib_error():
+    from nexttransformer_b200.ops._ext import ext
+    handle = ctypes.CDLL(ext().__file__)
+    reader = handle.nt_wgrad_noalloc_read_error
+    reader.restype = ctypes.c_int
+    reader.argtypes = [ctypes.c_void_p]
+    return reader(None)
 
 
 def test_rejects_bad_arguments(lib):
