@@ -9,7 +9,7 @@ Without ``--method`` (or with ``dense``) the headline configuration below runs. 
 selects another benchmark configuration of the survey on the generic model path
 (``models.build_model``): ``gdn_hybrid_swa`` / ``kda_hybrid`` (depth 24, width 1536, 12 heads of
 128, chunk 64, sequence 4096, 524,288 tokens per update), ``nsa`` / ``moba`` (depth 24, width
-1536, 12 query heads of 128 / 1 KV head, sequence 8192) and ``moe`` (depth 16, width 2048, 16 / 4 heads,
+1536, 16 query heads of 128 / 1 KV head, sequence 8192) and ``moe`` (depth 16, width 2048, 16 / 4 heads,
 64 experts of FFN 1024, top-8 + 1 shared, sequence 4096, 1,048,576 tokens per update).
 
 Model: depth 20, width 1280, 10 query heads / 5 KV heads of dim 128, RoPE, RMSNorm, ReLU^2 MLP
@@ -47,12 +47,12 @@ METHOD_CONFIGS = {
                             scale="custom"), 524288),
     "kda_hybrid": (dict(method="kda_hybrid", layers=24, width=1536, heads=12, mlp_width=6144, sequence_len=4096,
                         backend="fla_chunk64", window_pattern="L", scale="custom"), 524288),
-    # heads of dim 128 at width 1536 (the survey's 16 x 128 query heads would need a 2048-wide projection)
-    "nsa": (dict(method="nsa", layers=24, width=1536, heads=12, kv_heads=1, mlp_width=6144, sequence_len=8192,
-                 compression_size=32, compression_stride=16, block_size=64, sparse_topk=1024, local_window=512,
-                 window_pattern="L", scale="custom"), 524288),
-    "moba": (dict(method="moba", layers=24, width=1536, heads=12, kv_heads=1, mlp_width=6144, sequence_len=8192,
-                  block_size=512, sparse_topk=1536, window_pattern="L", scale="custom"), 524288),
+    # 16 query heads / 1 KV group of dim 128 at width 1536: q 1536 -> 2048, output 2048 -> 1536
+    "nsa": (dict(method="nsa", layers=24, width=1536, heads=16, kv_heads=1, attn_head_dim=128, mlp_width=6144,
+                 sequence_len=8192, compression_size=32, compression_stride=16, block_size=64, sparse_topk=1024,
+                 local_window=512, window_pattern="L", scale="custom"), 524288),
+    "moba": (dict(method="moba", layers=24, width=1536, heads=16, kv_heads=1, attn_head_dim=128, mlp_width=6144,
+                  sequence_len=8192, block_size=512, sparse_topk=1536, window_pattern="L", scale="custom"), 524288),
     "moe": (dict(method="moe", layers=16, width=2048, heads=16, kv_heads=4, mlp_width=8192, sequence_len=4096,
                  moe_experts=64, moe_topk=8, moe_ffn=1024, moe_shared=1, window_pattern="L", scale="custom"), 1048576),
 }
@@ -70,6 +70,10 @@ def parse():
                    help="gradient averaging / parameter gather of our arm on N > 1: NCCL collectives (default) "
                         "or the peer-memory kernels (their standalone checks are exact; the training step "
                         "with them is still being validated)")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="N > 1: reduce gradients after the backward and gather parameters before the next "
+                        "forward (default: per-layer reductions during the backward, per-layer gather waits "
+                        "in the next forward)")
     p.add_argument("--method", default="dense", choices=("dense", *METHOD_CONFIGS),
                    help="benchmark configuration (default: the dense headline configuration)")
     p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
@@ -173,7 +177,7 @@ def count_own_kernels(step_fn):
     return n
 
 
-def timed_steps(step_fn, xs, ys, steps, world, device):
+def timed_steps(step_fn, xs, ys, steps, world, device, flush=None):
     import torch
     import torch.distributed as dist
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -184,6 +188,8 @@ def timed_steps(step_fn, xs, ys, steps, world, device):
     out = None
     for _ in range(steps):
         out = step_fn(xs, ys)
+    if flush is not None:
+        flush()     # the last update's parameter gathers belong to the timed work
     end.record()
     if world > 1:
         dist.barrier(device_ids=[device.index])
@@ -219,12 +225,13 @@ def bench_method(args, rank, world, local, device):
             if raw["method"] == "moe" and world > 1:
                 from nexttransformer_b200.parallel.expert import enable_expert_parallel
                 enable_expert_parallel(model)
-            shadows = {}
-            if model.fused_supported():
-                shadows = {p: s for p, s in model.fused_state().casts}
+            shadows = {p: s for p, s in model.fused_state().casts}
             opt = MuonAdamW(protocol_groups(model), shadows=shadows)
+            if world > 1 and not args.no_overlap and model.fused_supported():
+                opt.overlap_with(model)
             trainer = Trainer(model, opt, accumulation=accum)
             step_device, step_e2e = trainer.step_device, trainer.step
+            flush = trainer.flush
         else:
             from dataclasses import replace
             from nexttransformer.models import build_model as ref_build
@@ -255,24 +262,28 @@ def bench_method(args, rank, world, local, device):
             def step_e2e(xs, ys):
                 return float(step_device([x.to(device, non_blocking=True) for x in xs],
                                          [y.to(device, non_blocking=True) for y in ys]))
+
+            def flush():
+                pass
         vocab = raw.get("vocab_size", 32768)
         dev_x, dev_y = synthetic_batches(accum, micro, T, vocab, seed=1000 + rank, device=device)
         host_x, host_y = synthetic_batches(accum, micro, T, vocab, seed=2000 + rank, pinned=True)
         for _ in range(args.warmup):
             step_device(dev_x, dev_y)
+        flush()
         sampler = ClockSampler(local == 0)
         with sampler:
-            ms, loss = timed_steps(step_device, dev_x, dev_y, args.steps, world, device)
+            ms, loss = timed_steps(step_device, dev_x, dev_y, args.steps, world, device, flush)
         e2e = None
         if not args.no_e2e:
-            ms2, _ = timed_steps(step_e2e, host_x, host_y, args.steps, world, device)
+            ms2, _ = timed_steps(step_e2e, host_x, host_y, args.steps, world, device, flush)
             h2d = sum(x.numel() * x.element_size() + y.numel() * y.element_size() for x, y in zip(host_x, host_y))
             e2e = {"value": global_batch / (ms2 / 1000.0), "unit": "tokens/s", "ms_per_step": ms2,
                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4}
         launches = None
         if args.impl == "ours":
             try:
-                launches = count_own_kernels(lambda: step_device(dev_x, dev_y)) * args.steps
+                launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush())) * args.steps
             except Exception:
                 launches = None
     except (ImportError, RuntimeError, NotImplementedError, TypeError) as exc:
@@ -369,6 +380,9 @@ def main():
                     print(f"peer-memory step: reduce-scatter pad {int(opt.p2p.pads[rank]):#x}, gather pad "
                           f"{int(gather.pads[rank]):#x}, {len(segs)} segments, {opt.p2p.blocks} / {gather.blocks} "
                           f"blocks", file=sys.stderr)
+        overlap = world > 1 and not args.no_overlap
+        if overlap:
+            opt.overlap_with(model)
         trainer = Trainer(model, opt, accumulation=accum)
 
         def step_device(xs, ys):
@@ -376,6 +390,7 @@ def main():
 
         def step_e2e(xs, ys):
             return trainer.step(xs, ys)
+        flush = trainer.flush
         flops_per_token = model.estimate_flops()
     else:
         from nexttransformer.models.backbone import GPT, GPTConfig
@@ -398,6 +413,10 @@ def main():
         def step_e2e(xs, ys):
             return float(step_device([x.to(device, non_blocking=True) for x in xs],
                                      [y.to(device, non_blocking=True) for y in ys]))
+
+        def flush():
+            pass
+        overlap = False
         flops_per_token = model.estimate_flops()
 
     vocab = MODEL["vocab_size"]
@@ -411,6 +430,7 @@ def main():
 
     for _ in range(args.warmup):
         step_device(dev_x, dev_y)
+    flush()
     barrier()
 
     # ---- device-timed region
@@ -421,6 +441,7 @@ def main():
         start.record()
         for _ in range(args.steps):
             loss = step_device(dev_x, dev_y)
+        flush()     # the last update's parameter gathers belong to the timed work
         end.record()
         barrier()
     ms = start.elapsed_time(end) / args.steps
@@ -437,11 +458,13 @@ def main():
     if not args.no_e2e:
         for _ in range(1):
             step_e2e(host_x, host_y)
+        flush()
         barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
         for _ in range(args.steps):
             step_e2e(host_x, host_y)
+        flush()
         e2.record()
         barrier()
         ms2 = s2.elapsed_time(e2) / args.steps
@@ -457,6 +480,7 @@ def main():
         print("end-to-end region done", file=sys.stderr, flush=True)
     # every rank must hold the same parameters after the updates (checks the parameter all-gather)
     params_agree = None
+    flush()
     if world > 1:
         digest = torch.stack([sum(p.detach().double().sum() for p in model.parameters()),
                               sum(p.detach().double().abs().sum() for p in model.parameters())])
@@ -468,7 +492,7 @@ def main():
     if args.impl == "ours":
         barrier()       # every rank enters the profiled step together (its peer-memory kernels wait on peers)
         try:
-            launches = count_own_kernels(lambda: step_device(dev_x, dev_y)) * args.steps
+            launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush())) * args.steps
         except Exception as exc:  # profiler unavailable: report as unknown
             launches = None
             if rank == 0:
@@ -488,6 +512,7 @@ def main():
                           "global_batch": GLOBAL_BATCH, "seq_len": T, "parallelism": f"dp{world}",
                           "micro_batch": micro, "grad_accum": accum, "l2": "working set >> L2 (no flush needed)",
                           "grad_comm": (args.comm if world > 1 else "none") if args.impl == "ours" else "nccl",
+                          "overlap": overlap,
                           "param_gather": ("p2p" if args.comm == "p2p" and os.environ.get("NT_P2P_GATHER", "0") == "1"
                                            else "nccl") if world > 1 and args.impl == "ours"
                           else ("none" if world == 1 else "nccl"),

@@ -57,7 +57,7 @@ def main(argv=None):
         model.set_training_stage(step)
         model.set_step(min(step, proto.steps))
         shadows = {}
-        if device.type == "cuda" and model.fused_supported():
+        if device.type == "cuda":
             shadows = {q: s for q, s in model.fused_state().casts}
         opt = MuonAdamW(protocol_groups(model), shadows=shadows)
         set_schedule(opt, step, proto.train_config())

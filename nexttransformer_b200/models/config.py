@@ -30,8 +30,8 @@ SCOPED_FIELDS = {
     **{f: tuple(sorted(MLA_CONFIG)) for f in ("q_rank", "kv_rank", "qk_nope_dim", "qk_rope_dim", "v_head_dim")},
 }
 # Extension fields (not in the reference): serialised only when they differ from the default.
-EXTENSION_FIELDS = ("kv_heads", "value_embeds", "compression_stride", "moe_experts", "moe_topk", "moe_ffn",
-                    "moe_shared", "moe_dense_layers", "moe_bias_rate")
+EXTENSION_FIELDS = ("kv_heads", "attn_head_dim", "value_embeds", "compression_stride", "moe_experts", "moe_topk", "moe_ffn",
+                    "moe_shared", "moe_dense_layers", "moe_bias_rate", "moe_aux_loss_coeff", "moe_z_loss_coeff")
 CHUNK_BACKENDS = {"fla_chunk64": 64}
 CHUNKED_METHODS = frozenset(("deltanet", "kda", "kda_no_ve", "retnet", "elu_linear", "elu_norm", "elu_qknorm", "gdn",
                              *(HYBRID - {"moba_hybrid"})))
@@ -130,6 +130,8 @@ class ModelConfig:
     options: tuple = ()
     # ---- extension fields (B200 configurations) -------------------------------------------
     kv_heads: int = 0              # 0: multi-head attention (kv heads = heads); else GQA group count
+    attn_head_dim: int = 0         # 0: width / heads; else the softmax-attention head dimension (heads x
+                                   # attn_head_dim may differ from width: q and output projections resize)
     value_embeds: int = -1         # -1: the method's rule; 0 / 1 force value embeddings off / on
     compression_stride: int = 0    # NSA compression stride; 0 = compression_size (no overlap)
     moe_experts: int = 64
@@ -138,6 +140,8 @@ class ModelConfig:
     moe_shared: int = 1
     moe_dense_layers: int = 0      # leading layers with a dense FFN instead of experts
     moe_bias_rate: float = 1e-3    # aux-loss-free balancing: router-bias update speed
+    moe_aux_loss_coeff: float = 0.0  # Switch-style load-balance loss weight (0: aux-loss-free only)
+    moe_z_loss_coeff: float = 0.0    # router z-loss weight
 
     # ------------------------------------------------------------------ validation
     def __post_init__(self):
@@ -161,7 +165,8 @@ class ModelConfig:
         for name, users in SCOPED_FIELDS.items():
             if self.method not in users and getattr(self, name) != defaults[name]:
                 raise ValueError(f"{name} is not a parameter of {self.method}")
-        moe_fields = ("moe_experts", "moe_topk", "moe_ffn", "moe_shared", "moe_dense_layers", "moe_bias_rate")
+        moe_fields = ("moe_experts", "moe_topk", "moe_ffn", "moe_shared", "moe_dense_layers", "moe_bias_rate",
+                      "moe_aux_loss_coeff", "moe_z_loss_coeff")
         if self.method not in MOE and any(getattr(self, f) != defaults[f] for f in moe_fields):
             raise ValueError("MoE fields belong to the moe method")
 
@@ -169,7 +174,8 @@ class ModelConfig:
         if min(self.residual_streams, self.sinkhorn_iterations, self.attnres_groups) <= 0 \
                 or not self.residual_gate_init > 0:
             raise ValueError("residual stream, iteration and group counts and gate scale must be positive")
-        if self.width < 24 or self.width % self.heads or self.head_dim % 2:
+        if self.width < 24 or (self.width % self.heads and not self.attn_head_dim) or self.head_dim % 2 \
+                or self.attn_head_dim < 0:
             raise ValueError("width >= 24 divisible by heads with an even head dimension required")
         if self.kv_heads < 0 or (self.kv_heads and self.heads % self.kv_heads):
             raise ValueError("kv_heads must divide heads")
@@ -219,7 +225,8 @@ class ModelConfig:
             if self.kv_heads not in (0, self.heads) or self.method in MOE:
                 raise ValueError("the formal shell is multi-head attention without experts")
         if self.method in MOE:
-            if not 0 < self.moe_topk <= self.moe_experts or self.moe_ffn <= 0 or self.moe_shared < 0:
+            if not 0 < self.moe_topk <= self.moe_experts or self.moe_ffn <= 0 or self.moe_shared < 0 \
+                    or self.moe_aux_loss_coeff < 0 or self.moe_z_loss_coeff < 0:
                 raise ValueError("invalid MoE shape")
         if self.method in PLUGINS:
             from nexttransformer_b200.models.plugins import load
@@ -233,7 +240,7 @@ class ModelConfig:
 
     @property
     def head_dim(self):
-        return self.width // self.heads
+        return self.attn_head_dim or self.width // self.heads
 
     @property
     def n_embd(self):

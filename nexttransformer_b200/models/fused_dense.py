@@ -25,6 +25,8 @@ from nexttransformer_b200.ops.attention import attention_fn
 CE_VARIANT = 0
 # True: the cross-entropy runs in the head GEMM's epilogue; False: GEMM + separate CE kernel.
 FUSED_HEAD_CE = True
+# Grouped expert GEMMs need the expert width and the model width in multiples of 64.
+MIN_EXPERT_DIM = 64
 
 
 class GradSlot:
@@ -44,10 +46,17 @@ class GradSlot:
 
 
 class FusedState:
-    """bf16 weight shadows and fp32 gradient buffers of a ``GPTShell`` on CUDA.
+    """bf16 weight shadows and fp32 gradient buffers of a shell model on CUDA.
 
-    ``c_q | c_k | c_v`` of a layer share one packed shadow (one QKV GEMM) and one packed
-    gradient buffer; every parameter's ``main_grad`` is a view into these buffers.
+    Two registrations, chosen by ``model.fused_supported()``:
+      * trunk mode (the model's trunk runs ``fused_forward``): ``c_q | c_k | c_v`` of every
+        shell attention share one packed shadow (one QKV GEMM) and one packed gradient buffer,
+        the shell MLPs, the head and the embedding-side parameters get gradient buffers written
+        by the fused Functions below;
+      * in both modes every other eligible ``Linear`` of the model (linear / sparse / MLA mixers,
+        looped-block adapters, plugin projections) gets a shadow and a gradient slot and runs on
+        the GEMM engine through ``ops.dense.KernelLinear`` when it is called.
+    Every registered parameter's ``main_grad`` is a view into these buffers.
     """
 
     def __init__(self, model, grad_alloc=None, plan_only=False):
@@ -55,65 +64,173 @@ class FusedState:
         flat arena, e.g. in symmetric memory); ``plan_only`` only walks that order so the caller
         can size the arena, touching no parameter."""
         self.model = model
+        self.trunk = bool(model.fused_supported())
         dev = model.get_device()
         f32, bf = torch.float32, torch.bfloat16
         self.slots = []        # GEMM-written gradients (fresh / accumulate)
         self.zeroed = []       # gradients accumulated with atomics or torch ops
         self.casts = []        # (fp32 master, bf16 shadow)
+        self.kernel_linears = []
         self.arena = None
+        self._plan = plan_only
+        self._seen = set()
+        # data-parallel overlap (optim.muon_adamw.MuonAdamW.overlap_with): the optimizer that
+        # reduces each layer's gradients as soon as the last micro-batch's backward has produced
+        # them, and whose parameter gathers each layer's forward waits for
+        self.optimizer = None
+        self.final_micro = False
+        self._groups = None
 
         def grad(shape):
             if grad_alloc is not None:
                 return grad_alloc(tuple(shape))
             return torch.zeros(tuple(shape), device=dev, dtype=f32)
 
-        if plan_only:
-            for blk in model.transformer.h:
-                a = blk.attn
-                grad((a.c_q.weight.shape[0] + 2 * a.c_k.weight.shape[0], a.c_q.weight.shape[1]))
-                for lin in (a.c_proj, blk.mlp.c_fc, blk.mlp.c_proj):
-                    grad(lin.weight.shape)
-                if a.ve_gate is not None:
-                    grad(a.ve_gate.weight.shape)
-            grad(model.lm_head.weight.shape)
-            for p in self._loose(model):
-                grad(p.shape)
-            return
-
         def shadow(p, out=None):
             out = out if out is not None else torch.empty(p.shape, device=dev, dtype=bf)
             self.casts.append((p, out))
             return out
 
+        self._grad, self._shadow = grad, shadow
+        self._register(model)
+        if not plan_only:
+            self.refresh_shadows()
+
+    # ------------------------------------------------------------------ registration
+    def _register(self, model):
+        from nexttransformer_b200.models.moe import MoEFFN
+        from nexttransformer_b200.models.shell import MLP, Block, CausalSelfAttention
+        grad, shadow, plan = self._grad, self._shadow, self._plan
+        dev = model.get_device()
         for blk in model.transformer.h:
-            a = blk.attn
-            nq, nk, d = a.c_q.weight.shape[0], a.c_k.weight.shape[0], a.c_q.weight.shape[1]
-            a._w_qkv = torch.empty(nq + 2 * nk, d, device=dev, dtype=bf)
-            g = grad((nq + 2 * nk, d))
-            a._g_qkv = GradSlot(g)
-            self.slots.append(a._g_qkv)
-            for lin, lo, hi in ((a.c_q, 0, nq), (a.c_k, nq, nq + nk), (a.c_v, nq + nk, nq + 2 * nk)):
-                lin.weight.main_grad = g[lo:hi]
-                shadow(lin.weight, a._w_qkv[lo:hi])
-            for lin in (a.c_proj, blk.mlp.c_fc, blk.mlp.c_proj):
-                lin._w = shadow(lin.weight)
-                lin.weight.main_grad = grad(lin.weight.shape)
-                lin._g = GradSlot(lin.weight.main_grad)
-                self.slots.append(lin._g)
-            if a.ve_gate is not None:
-                a.ve_gate._w = shadow(a.ve_gate.weight)
-                a.ve_gate.weight.main_grad = grad(a.ve_gate.weight.shape)
-                self.zeroed.append(a.ve_gate.weight.main_grad)
-        head = model.lm_head
-        head._w = shadow(head.weight)
-        head.weight.main_grad = grad(head.weight.shape)
-        head._g = GradSlot(head.weight.main_grad)
-        self.slots.append(head._g)
-        model.smear_gate._w = shadow(model.smear_gate.weight)
-        for p in self._loose(model):
-            p.main_grad = grad(p.shape)
-            self.zeroed.append(p.main_grad)
-        self.refresh_shadows()
+            a, m = getattr(blk, "attn", None), getattr(blk, "mlp", None)
+            if self.trunk and type(blk) is Block and type(a) is CausalSelfAttention:
+                nq, nk, d = a.c_q.weight.shape[0], a.c_k.weight.shape[0], a.c_q.weight.shape[1]
+                g = grad((nq + 2 * nk, d))
+                if not plan:
+                    a._w_qkv = torch.empty(nq + 2 * nk, d, device=dev, dtype=torch.bfloat16)
+                    a._g_qkv = GradSlot(g)
+                    self.slots.append(a._g_qkv)
+                    for lin, lo, hi in ((a.c_q, 0, nq), (a.c_k, nq, nq + nk), (a.c_v, nq + nk, nq + 2 * nk)):
+                        lin.weight.main_grad = g[lo:hi]
+                        shadow(lin.weight, a._w_qkv[lo:hi])
+                self._fused_linear(a.c_proj)
+                if a.ve_gate is not None:
+                    g = grad(a.ve_gate.weight.shape)
+                    if not plan:
+                        a.ve_gate._w = shadow(a.ve_gate.weight)
+                        a.ve_gate.weight.main_grad = g
+                        self.zeroed.append(g)
+                self._seen.update(id(x) for x in (a.c_q, a.c_k, a.c_v, a.ve_gate))
+            if self.trunk and type(blk) is Block and type(m) is MLP:
+                self._fused_linear(m.c_fc)
+                self._fused_linear(m.c_proj)
+            if isinstance(m, MoEFFN):
+                self._experts(m)
+            self._generic(blk)
+        if self.trunk:
+            self._fused_linear(model.lm_head)
+            if not plan:
+                model.smear_gate._w = shadow(model.smear_gate.weight)
+            for p in self._loose(model):
+                g = grad(p.shape)
+                if not plan:
+                    p.main_grad = g
+                    self.zeroed.append(g)
+        self._generic(model)
+
+    def _experts(self, moe):
+        """Routed experts run as grouped GEMMs (``ops.moe``) on stacked bf16 shadows; each expert
+        weight's ``main_grad`` is one slice of a stacked fp32 buffer the grouped weight-gradient
+        GEMMs accumulate into (zeroed once per update).  The router stays on F.linear (fp32
+        logits) and the shared expert runs through the generic kernel linears."""
+        local = moe.local_experts()
+        self._seen.add(id(moe.router))
+        F_, d_ = local[0].c_fc.weight.shape
+        if F_ % MIN_EXPERT_DIM or d_ % MIN_EXPERT_DIM:
+            return
+        for e in local:
+            self._seen.update((id(e), id(e.c_fc), id(e.c_proj)))
+        E = len(local)
+        gf, gp = self._grad((E, F_, d_)), self._grad((E, d_, F_))
+        if self._plan:
+            return
+        dev = local[0].c_fc.weight.device
+        moe._w_fc = torch.empty(E, F_, d_, device=dev, dtype=torch.bfloat16)
+        moe._w_proj = torch.empty(E, d_, F_, device=dev, dtype=torch.bfloat16)
+        moe._g_fc, moe._g_proj = gf, gp
+        for j, e in enumerate(local):
+            e.c_fc.weight.main_grad = gf[j]
+            e.c_proj.weight.main_grad = gp[j]
+            self._shadow(e.c_fc.weight, moe._w_fc[j])
+            self._shadow(e.c_proj.weight, moe._w_proj[j])
+        self.zeroed += [gf, gp]
+
+    def _fused_linear(self, lin):
+        """A Linear whose GEMMs are issued by the fused trunk Functions."""
+        g = self._grad(lin.weight.shape)
+        self._seen.add(id(lin))
+        if self._plan:
+            return
+        lin._w = self._shadow(lin.weight)
+        lin.weight.main_grad = g
+        lin._g = GradSlot(g)
+        self.slots.append(lin._g)
+
+    def _generic(self, module):
+        """Every not yet registered, eligible ``Linear`` under ``module`` runs on the GEMM engine."""
+        from nexttransformer_b200.models.shell import Linear
+        from nexttransformer_b200.ops.dense import linear_eligible
+        for lin in module.modules():
+            if not isinstance(lin, Linear) or id(lin) in self._seen or not linear_eligible(lin.weight):
+                continue
+            self._seen.add(id(lin))
+            g = self._grad(lin.weight.shape)
+            if self._plan:
+                continue
+            lin._w = self._shadow(lin.weight)
+            lin.weight.main_grad = g
+            lin._g = GradSlot(g)
+            lin.weight._nt_slot = lin._g
+            lin._kernel = True
+            self.slots.append(lin._g)
+            self.kernel_linears.append(lin)
+
+    # ------------------------------------------------------------------ overlap hooks
+    def use_groups(self):
+        """Forward-use groups: -1 the embedding side and every shared scalar, i the parameters of
+        layer i (with its value-embedding table), n_layer the head."""
+        if self._groups is None:
+            model = self.model
+            n = len(model.transformer.h)
+            groups = {}
+            taken = set()
+            for i, blk in enumerate(model.transformer.h):
+                ps = list(blk.parameters())
+                if str(i) in model.value_embeds:
+                    ps.append(model.value_embeds[str(i)].weight)
+                groups[i] = ps
+                taken.update(id(p) for p in ps)
+            groups[n] = [model.lm_head.weight]
+            taken.add(id(model.lm_head.weight))
+            groups[-1] = [p for p in model.parameters() if id(p) not in taken]
+            self._groups = groups
+        return self._groups
+
+    def grads_ready(self, group, tables=True):
+        """Called by the backward once group ``group``'s kernel-written gradients are final
+        (``tables``: the layer's value-embedding table included)."""
+        if self.final_micro and self.optimizer is not None:
+            model = self.model
+            skip = set() if tables or str(group) not in model.value_embeds else \
+                {id(model.value_embeds[str(group)].weight)}
+            self.optimizer.issue_reduce([p for p in self.use_groups()[group] if getattr(p, "main_grad", None)
+                                         is not None and p.requires_grad and id(p) not in skip])
+
+    def params_needed(self, group):
+        """Called by the forward before it reads group ``group``'s parameters."""
+        if self.optimizer is not None:
+            self.optimizer.wait_gathers(group)
 
     @staticmethod
     def _loose(model):
@@ -247,6 +364,7 @@ class PreAttnFn(Function):
         dab = part.sum(0)
         model.resid_lambdas.main_grad[layer:layer + 1] += dab[0:1]
         model.x0_lambdas.main_grad[layer:layer + 1] += dab[1:2]
+        model._fused.grads_ready(layer)
         return dx, None, None, None, None, None, None, None, None, None, None
 
 
@@ -373,32 +491,66 @@ class HeadLossFn(Function):
             lam = model.backout_lambda.detach().to(torch.bfloat16)
             dxb = -(lam * dxo)
             model.backout_lambda.main_grad -= (dxo.float() * xb.float()).sum().view(1)
+        model._fused.grads_ready(len(model.transformer.h))
         return dxo, dxb, None, None, None
 
 
 def fused_forward(model, idx, targets, reduction="mean"):
-    """Training loss of the dense shell on CUDA (fp32 parameter gradients land in ``main_grad``)."""
+    """Training loss of a shell model on CUDA: ``(lm_loss, aux)`` with ``aux`` the sum of the
+    mixers' auxiliary losses (None when no mixer has one).
+
+    Per layer the shell's own attention and MLP run the fused Functions above; any other mixer
+    (linear, sparse, MLA) or FFN (MoE) runs its own forward between the kernel mix+RMSNorm and
+    a residual add, with its projections on the GEMM engine (``ops.dense``).  fp32 parameter
+    gradients land in ``main_grad``."""
+    from nexttransformer_b200.models.shell import MLP
+    from nexttransformer_b200.ops.dense import MixNormFn, rms_norm, table_lookup
     cfg = model.shell
     B, T = idx.shape
-    st = model.fused_state()
+    model.fused_state()
     idx_f = idx.reshape(-1).contiguous()
     tgt_f = targets.reshape(-1).contiguous()
     d = cfg.n_embd
-    scratch = StepScratch(B * T, d, idx.device)
+    M = B * T
+    scratch = StepScratch(M, d, idx.device)
     cos = model.cos[0, :T, 0].contiguous()
     sin = model.sin[0, :T, 0].contiguous()
+    cos_sin = (model.cos[:, :T], model.sin[:, :T])
+    st = model._fused
+    st.params_needed(-1)
     x0 = EmbedFn.apply(idx_f, model.transformer.wte.weight, model, scratch, T)
     x = x0
     n = cfg.n_layer
-    backout = None
+    backout = aux = None
     for i, blk in enumerate(model.transformer.h):
-        a = blk.attn
+        a, mlp = blk.attn, blk.mlp
+        st.params_needed(i)
+        window = model.layer_window(i)
         with torch.no_grad():
             ab = torch.stack((model.resid_lambdas[i], model.x0_lambdas[i])).float().contiguous()
-        xm, qkv = PreAttnFn.apply(x, x0, ab, a, model, scratch, idx_f, i, T, cos, sin)
-        y = attention_fn(qkv, B, T, a.n_head, a.n_kv_head, a.head_dim, model.window_sizes[i][0])
-        x = OutProjFn.apply(y, xm, a.c_proj)
-        x = MLPFn.apply(x, blk.mlp)
+        if getattr(a, "_w_qkv", None) is not None:
+            xm, qkv = PreAttnFn.apply(x, x0, ab, a, model, scratch, idx_f, i, T, cos, sin)
+            y = attention_fn(qkv, B, T, a.n_head, a.n_kv_head, a.head_dim, window)
+            x = OutProjFn.apply(y, xm, a.c_proj)
+        else:
+            xm, h = MixNormFn.apply(x, x0, ab, model, scratch, i)
+            key = str(i)
+            ve = table_lookup(idx_f, model.value_embeds[key].weight).view(B, T, -1) \
+                if key in model.value_embeds else None
+            y = a(h.view(B, T, d), ve, cos_sin, (window, 0), None)
+            x = xm + y.reshape(M, d).to(xm.dtype)
+            part = getattr(a, "last_aux", None)
+            if torch.is_tensor(part):
+                aux = part if aux is None else aux + part
+        if type(mlp) is MLP and getattr(mlp.c_fc, "_g", None) is not None and not mlp.c_fc._kernel:
+            x = MLPFn.apply(x, mlp)
+        else:
+            h2 = rms_norm(x)
+            x = x + mlp(h2.view(B, T, d)).reshape(M, d).to(x.dtype)
+            part = getattr(mlp, "last_aux", None)
+            if torch.is_tensor(part):
+                aux = part if aux is None else aux + part
         if i == n // 2:
             backout = x
-    return HeadLossFn.apply(x, backout, model, tgt_f, reduction)
+    st.params_needed(n)
+    return HeadLossFn.apply(x, backout, model, tgt_f, reduction), aux

@@ -38,7 +38,7 @@ PROTOCOL_STEPS = 46875
 def shell_config(c: ModelConfig):
     return ShellConfig(sequence_len=c.sequence_len, vocab_size=c.vocab_size, n_layer=c.n_layer, n_head=c.heads,
                        n_kv_head=c.n_kv_head, n_embd=c.width, mlp_width=c.mlp_width, window_pattern=c.window_pattern,
-                       value_embeddings=c.value_embeddings)
+                       value_embeddings=c.value_embeddings, attn_head_dim=c.attn_head_dim)
 
 
 class LanguageModel(GPTShell):
@@ -65,7 +65,8 @@ class LanguageModel(GPTShell):
             elif c.method in MLA or (c.method in HYBRID and kind in MLA):
                 blk.attn = MLAAttention(c, i)
             if c.method in MOE and i >= c.moe_dense_layers:
-                blk.mlp = MoEFFN(c.width, c.moe_experts, c.moe_topk, c.moe_ffn, c.moe_shared, c.moe_bias_rate)
+                blk.mlp = MoEFFN(c.width, c.moe_experts, c.moe_topk, c.moe_ffn, c.moe_shared, c.moe_bias_rate,
+                                 c.moe_aux_loss_coeff, c.moe_z_loss_coeff)
             if self.plugin and self.plugin.mixer:
                 blk.attn = self.plugin.mixer(c, i)
             if self.plugin and self.plugin.ffn:
@@ -271,20 +272,31 @@ class LanguageModel(GPTShell):
                 streams = hyper.write(mixed, out, w)
                 self._record("residual_map", sublayer=k, streams=c.residual_streams, tokens=idx.numel())
             return streams.sum(2)
-        starts = set(c.attnres_group_starts)
-        blocks, keys, partial = [], [], x
+        return self._attnres_trunk(idx, x, c.attnres_group_starts)
+
+    def _attnres_trunk(self, idx, x, group_starts, adapt=None):
+        """Block AttnRes: sublayer k reads a softmax mixture over its depth sources (the embedding,
+        the sums of completed groups and the current group's partial sum, keyed by their RMSNorm)
+        through pseudo-query ``depth_queries[k]``; a group closes at each layer in
+        ``group_starts``.  ``adapt(k, h)`` (optional) transforms a sublayer's input after the read."""
+        c = self.config
+        starts = set(group_starts)
+        closed, keys, partial = [], [], x
         for k in range(2 * c.n_layer):
+            layer, is_attention = divmod(k, 2)[0], k % 2 == 0
             key = norm(partial)
-            h = depth_attention(self.depth_queries[k], blocks + [partial], keys + [key])
-            self._record("depth_read", sublayer=k, sources=len(blocks) + 1, tokens=idx.numel())
-            if k % 2 == 0 and k // 2 in starts:
-                blocks.append(partial)
+            h = depth_attention(self.depth_queries[k], closed + [partial], keys + [key])
+            self._record("depth_read", sublayer=k, sources=len(closed) + 1, tokens=idx.numel())
+            if is_attention and layer in starts:
+                closed.append(partial)
                 keys.append(key)
                 partial = None
-            out = self._attention_branch(h, idx, k // 2) if k % 2 == 0 else mlp(h, k // 2)
+            if adapt is not None:
+                h = adapt(k, h)
+            out = self._attention_branch(h, idx, layer) if is_attention else self.transformer.h[layer].mlp(norm(h))
             partial = out if partial is None else partial + out
-        h = depth_attention(self.depth_queries[-1], blocks + [partial], keys + [norm(partial)])
-        self._record("depth_read", sublayer=2 * c.n_layer, sources=len(blocks) + 1, tokens=idx.numel())
+        h = depth_attention(self.depth_queries[-1], closed + [partial], keys + [norm(partial)])
+        self._record("depth_read", sublayer=2 * c.n_layer, sources=len(closed) + 1, tokens=idx.numel())
         return h
 
     def _loop_hidden(self, idx, targets=None):
@@ -383,9 +395,17 @@ class LanguageModel(GPTShell):
         return self._readout_trace(x, prelude), aux, None
 
     def fused_supported(self):
+        """True when the trunk runs ``models.fused_dense.fused_forward``: one ordinary pass over
+        plain blocks (dense, sliding-window, linear, sparse, MLA, hybrid and MoE layers); looped,
+        residual-stream and plugin methods run their own forward, with every eligible projection
+        still on the GEMM engine."""
+        from nexttransformer_b200.models.shell import Block
         c = self.config
-        return (c.method not in LOOPED | RESIDUAL and self.plugin is None and c.method not in MOE
-                and super().fused_supported())
+        return (c.method not in LOOPED | RESIDUAL and self.plugin is None
+                and all(type(b) is Block for b in self.transformer.h))
+
+    def layer_window(self, i):
+        return self._window(i, self.config.n_layer)[0]
 
     def forward(self, idx, targets=None, kv_cache=None, loss_reduction="mean"):
         c = self.config
@@ -397,10 +417,11 @@ class LanguageModel(GPTShell):
         if (idx.is_cuda and targets is not None and loss_reduction == "mean" and self.training
                 and self.fused_supported()):
             from nexttransformer_b200.models.fused_dense import fused_forward
-            loss = fused_forward(self, idx, targets, "mean")
-            self.last_lm_loss, self.last_aux_loss = loss.detach(), loss.new_zeros(())
+            loss, aux = fused_forward(self, idx, targets, "mean")
+            aux = loss.new_zeros(()) if aux is None else aux
+            self.last_lm_loss, self.last_aux_loss = loss.detach(), aux
             self.last_stats = {"fused_dense": True}
-            return loss
+            return loss + aux
         if c.method == "dense":
             # the SSSL anchor is the shell's own forward (same graph the cost anchor audits)
             out = self.forward_eager(idx, targets, loss_reduction)
@@ -416,7 +437,8 @@ class LanguageModel(GPTShell):
             x, cached = self._ordinary_hidden(idx)
             logits = self._readout_trace(x, cached)
             aux_src = (m for m in self.modules() if m is not self) if self.plugin else \
-                (b.attn for b in self.transformer.h if isinstance(b.attn, (LinearMixer, SparseMixer)))
+                [*(b.attn for b in self.transformer.h if isinstance(b.attn, (LinearMixer, SparseMixer))),
+                 *(b.mlp for b in self.transformer.h if isinstance(b.mlp, MoEFFN))]
             aux = sum((m.last_aux for m in aux_src if torch.is_tensor(getattr(m, "last_aux", None))),
                       logits.new_zeros(()))
         self.last_aux_loss = aux

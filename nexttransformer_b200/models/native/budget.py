@@ -1,11 +1,18 @@
-"""Route budgets of the native track, updated once per complete optimizer update.
+"""Compute budgets of the native track: Lagrangian dual ascent on measured route statistics.
 
-``SurvivalBudget`` (MoR): per recursion a dual variable on the survival error
-``hard_mean - target``; penalty ``dual * e + strength/2 * e^2`` (forward measures hard survival,
-backward follows the straight-through route surrogate); the dual moves by ``dual_lr * measured
-error`` and is clamped.  ``CircleBudget``: a signed mean-depth dual (EMA-smoothed error, enabled
-after the random warm-up) plus a weak quadratic pull of the survival curve towards the depth law.
-Behaviour: ``nexttransformer/models/native/budget.py:8-96``.
+Both budgets keep fp64 dual variables as buffers and move them once per complete optimizer update
+from the globally reduced counts of that update (never from one micro-batch):
+
+* MoR (``SurvivalBudget``): one dual per routed recursion on the survival error
+  ``e = survival - target``; the training penalty is ``dual e + strength / 2 e^2`` (the forward
+  measures hard survival, the backward follows the straight-through router surrogate) and the
+  dual steps by ``dual_lr e``, clamped to ``+-dual_limit``.
+* Circle (``CircleBudget``): one dual on the relative mean-depth error
+  ``e = sum(survival) / target - 1``, smoothed by an EMA and enabled after the random warm-up,
+  plus a weak quadratic pull of the survival curve beyond the first ring towards the depth law.
+
+Buffer names are the reference's checkpoint keys; behaviour matches
+``nexttransformer/models/native/budget.py``.
 """
 import math
 
@@ -15,7 +22,39 @@ from torch import nn
 from nexttransformer_b200.models.native.depth import depth_reference
 
 
-class CircleBudget(nn.Module):
+class _UpdateClock(nn.Module):
+    """Refuses a second budget update for the same optimizer step."""
+
+    def __init__(self):
+        super().__init__()
+        self.register_buffer("updates", torch.zeros((), dtype=torch.long))
+        self.register_buffer("last_step", torch.tensor(-1, dtype=torch.long))
+
+    def admit(self, step, tokens, what):
+        if tokens <= 0 or step <= int(self.last_step):
+            raise ValueError(f"the {what} moves once per complete optimizer update")
+
+    def tick(self, step):
+        self.last_step.fill_(step)
+        self.updates.add_(1)
+
+    @torch.no_grad()
+    def restart(self):
+        self.updates.zero_()
+        self.last_step.fill_(-1)
+
+
+def dual_ascent(dual, step_size, error, limit):
+    """dual <- clamp(dual + step_size * error, -limit, limit) in place."""
+    dual.add_(step_size * error).clamp_(-limit, limit)
+
+
+def quadratic_penalty(dual, error, weight):
+    """dual . error + weight / 2 |error|^2 with the dual treated as a constant."""
+    return dual.detach().clone().to(error) * error + 0.5 * weight * error.square()
+
+
+class CircleBudget(_UpdateClock):
     def __init__(self, config):
         super().__init__()
         self.config = config
@@ -25,77 +64,84 @@ class CircleBudget(nn.Module):
         self.register_buffer("survival", torch.tensor(self._surv, dtype=torch.float64))
         self.register_buffer("dual", torch.zeros((), dtype=torch.float64))
         self.register_buffer("ema", torch.zeros((), dtype=torch.float64))
-        self.register_buffer("updates", torch.zeros((), dtype=torch.long))
-        self.register_buffer("last_step", torch.tensor(-1, dtype=torch.long))
 
     @torch.no_grad()
     def reset(self):
-        """Buffers are uninitialised after ``to_empty``; restore every one."""
+        """Every buffer back to its initial value (they are uninitialised after ``to_empty``)."""
         self.probabilities.copy_(torch.tensor(self._probs, dtype=torch.float64))
         self.survival.copy_(torch.tensor(self._surv, dtype=torch.float64))
-        for b in (self.dual, self.ema, self.updates):
-            b.zero_()
-        self.last_step.fill_(-1)
+        self.dual.zero_()
+        self.ema.zero_()
+        self.restart()
 
     def penalty(self, survival):
+        """(total, depth term, shape term) for the survival curve of one forward."""
         c = self.config
-        err = survival.sum() / c.circle_target_steps - 1
-        depth = self.dual.detach().clone().to(err) * err + 0.5 * c.circle_depth_rho * err.square()
-        tail = survival[c.core_layers:] - self.survival[c.core_layers:].to(survival)
-        shape = c.circle_shape_weight * tail.square().mean()
+        ring = c.core_layers
+        depth = quadratic_penalty(self.dual, survival.sum() / c.circle_target_steps - 1, c.circle_depth_rho)
+        gap = survival[ring:] - self.survival[ring:].to(survival)
+        shape = c.circle_shape_weight * gap.square().mean()
         return depth + shape, depth, shape
+
+    @staticmethod
+    def _absorbing(surv, ring):
+        """Counts of an absorbing exit process: in [0, 1], non-increasing, 1 through the first ring."""
+        in_range = all(math.isfinite(v) and 0 <= v <= 1 for v in surv)
+        monotone = all(nxt <= cur + 1e-9 for cur, nxt in zip(surv, surv[1:]))
+        dense_ring = all(abs(v - 1) <= 1e-9 for v in surv[:ring])
+        return in_range and monotone and dense_ring
 
     @torch.no_grad()
     def update(self, counts, tokens, step):
         c = self.config
-        if step <= int(self.last_step) or tokens <= 0:
-            raise ValueError("update Circle budget once per complete optimizer step")
+        self.admit(step, tokens, "Circle budget")
         if len(counts) != c.circle_max_steps:
-            raise ValueError("Circle budget needs counts at every block")
+            raise ValueError("the Circle budget needs the active-token count of every step")
         surv = [float(n) / tokens for n in counts]
-        ok = (all(math.isfinite(v) and 0 <= v <= 1 for v in surv)
-              and all(a + 1e-9 >= b for a, b in zip(surv, surv[1:]))
-              and all(abs(v - 1) <= 1e-9 for v in surv[:c.core_layers]))
-        if not ok:
-            raise ValueError("invalid absorbing Circle survival counts")
-        err = sum(surv) / c.circle_target_steps - 1
-        used = float(self.dual)
-        ema = c.circle_budget_beta * float(self.ema) + (1 - c.circle_budget_beta) * err
+        if not self._absorbing(surv, c.core_layers):
+            raise ValueError("Circle survival counts are not those of an absorbing exit process")
+        error = sum(surv) / c.circle_target_steps - 1
+        before = float(self.dual)
+        smoothed = c.circle_budget_beta * float(self.ema) + (1 - c.circle_budget_beta) * error
+        self.ema.fill_(smoothed)
         if step >= c.circle_random_warmup:
-            self.dual.add_(c.circle_dual_lr * ema).clamp_(-c.circle_dual_limit, c.circle_dual_limit)
-        self.ema.fill_(ema)
-        self.last_step.fill_(step)
-        self.updates.add_(1)
-        gaps = [a - b for a, b in zip(surv, self._surv)]
-        tail = gaps[c.core_layers:]
-        return dict(budget_target_steps=c.circle_target_steps, budget_error=err, budget_error_ema=ema,
-                    budget_weight_used=used, budget_weight_next=float(self.dual), budget_survival=surv,
-                    budget_survival_error=gaps, budget_shape_rmse=math.sqrt(sum(g * g for g in tail) / len(tail)),
+            dual_ascent(self.dual, c.circle_dual_lr, smoothed, c.circle_dual_limit)
+        self.tick(step)
+        gaps = [v - law for v, law in zip(surv, self._surv)]
+        beyond = gaps[c.core_layers:]
+        return dict(budget_target_steps=c.circle_target_steps, budget_error=error, budget_error_ema=smoothed,
+                    budget_weight_used=before, budget_weight_next=float(self.dual), budget_survival=surv,
+                    budget_survival_error=gaps,
+                    budget_shape_rmse=math.sqrt(sum(g * g for g in beyond) / len(beyond)),
                     budget_updates=int(self.updates))
 
 
-class SurvivalBudget(nn.Module):
+class SurvivalBudget(_UpdateClock):
     def __init__(self, config):
         super().__init__()
         self.config = config
         self.register_buffer("dual", torch.zeros(config.recursions - 1, dtype=torch.float64))
-        self.register_buffer("updates", torch.zeros((), dtype=torch.long))
-        self.register_buffer("last_step", torch.tensor(-1, dtype=torch.long))
+
+    @torch.no_grad()
+    def reset(self):
+        self.dual.zero_()
+        self.restart()
+
+    def _target(self, like):
+        return like.new_tensor(self.config.mor_target_survival)
 
     def penalty(self, means):
-        err = means - means.new_tensor(self.config.mor_target_survival)
-        return (self.dual.detach().clone().to(err) * err + 0.5 * self.config.mor_budget_strength * err.square()).sum()
+        return quadratic_penalty(self.dual, means - self._target(means), self.config.mor_budget_strength).sum()
 
     @torch.no_grad()
     def update(self, counts, tokens, step):
-        if step <= int(self.last_step) or tokens <= 0:
-            raise ValueError("update budget once per complete optimizer step")
-        mean = self.dual.new_tensor(counts) / tokens
-        if not torch.isfinite(mean).all() or (mean < 0).any() or (mean > 1).any():
-            raise ValueError("invalid survival counts")
-        err = mean - self.dual.new_tensor(self.config.mor_target_survival)
-        self.dual.add_(self.config.mor_dual_lr * err).clamp_(-self.config.mor_dual_limit, self.config.mor_dual_limit)
-        self.last_step.fill_(step)
-        self.updates.add_(1)
-        return {"budget_survival": mean.tolist(), "budget_error": err.tolist(), "budget_dual": self.dual.tolist(),
+        c = self.config
+        self.admit(step, tokens, "MoR budget")
+        survival = self.dual.new_tensor(counts) / tokens
+        if not bool(torch.isfinite(survival).all()) or bool(((survival < 0) | (survival > 1)).any()):
+            raise ValueError("MoR survival counts outside [0, tokens]")
+        error = survival - self._target(survival)
+        dual_ascent(self.dual, c.mor_dual_lr, error, c.mor_dual_limit)
+        self.tick(step)
+        return {"budget_survival": survival.tolist(), "budget_error": error.tolist(), "budget_dual": self.dual.tolist(),
                 "budget_updates": int(self.updates)}

@@ -1,105 +1,145 @@
-"""Circle: a ring of ``core_layers`` blocks run for up to ``circle_max_steps`` steps with sparse,
-absorbing per-token exits.
+"""Circle: the core ring of ``core_layers`` blocks run for up to ``circle_max_steps`` steps with
+sparse, absorbing per-token exits.
 
-The first full ring is dense.  After each later step every still-active token gets an exit score
-from the halter (from the states before and after the step); a token continues while
-``sigmoid(-score) >= 0.5``, its update ``before + q * (candidate - before)`` is weighted by that gate,
-and once stopped it never resumes.  During the random warm-up and the route transition a growing
-fraction of tokens follows depths drawn from the depth law instead (routing RNG per rank, saved in
-checkpoints).  The budget sees the hard survival counts in forward and local straight-through gate
-derivatives in backward.  Behaviour: ``nexttransformer/models/native/circle.py:6-93``.
+Schedule of one forward:
+
+* steps 1 .. ring: every token runs (the first pass around the ring is dense);
+* after each step s in [ring, max_steps): the halter scores every still-active token from its
+  states before and after the step; the continue-gate is ``q = sigmoid(-score)`` and the token
+  stays active for step s + 1 iff ``q >= 0.5``.  A stopped token never resumes.  The next step's
+  update of a token is ``before + q (candidate - before)``, so the gate is trained through the
+  states it blends;
+* curriculum: during the random warm-up every token (during the route transition a growing
+  fraction of tokens) instead follows a depth drawn from the population depth law, with a
+  per-rank routing generator whose state is checkpointed.
+
+The budget sees the hard survival fractions in the forward and the straight-through derivative
+of the learned gates in the backward.  Behaviour matches ``nexttransformer/models/native/circle.py``.
 """
 import torch
 import torch.distributed as dist
 
 
+class _Route:
+    """Per-forward routing state: which tokens are active, the gate of the last exit decision, the
+    tokens forced onto law-drawn depths, and the survival curve the budget penalises."""
+
+    def __init__(self, model, idx, like):
+        self.active = torch.ones_like(idx, dtype=torch.bool)
+        self.forced, self.law_depth = model._circle_random_routes(idx)
+        self.gate = None
+        self.curve = []
+        self.carry = like.new_tensor(1.0, dtype=torch.float32)
+        # a zero-valued term that keeps every gate in the graph even after the last token has stopped
+        self.anchor = like.new_zeros((), dtype=torch.float32)
+
+    def enter(self, step, stats):
+        """Record the active count and the survival value of step ``step`` (1-based)."""
+        count = int(self.active.sum())
+        stats["active_tokens"][step - 1] = count
+        self.curve.append(self.carry)
+        return count
+
+    def blend(self, before, candidate):
+        if self.gate is None:
+            return candidate
+        return before + self.gate.to(candidate.dtype)[..., None] * (candidate - before)
+
+    def decide(self, model, step, before, after, count):
+        """Score the active tokens after ``step`` and choose who continues."""
+        c = model.config
+        live = self.active
+        score = model.halter(before[live], after[live], step - c.core_layers)
+        q = torch.zeros(live.shape, device=live.device, dtype=torch.float32).masked_scatter(live, torch.sigmoid(-score))
+        model.last_stats["forward_flops"] += 2 * count * c.width
+        model.last_stats["halter_extra_forward_ops"] += count * (5 * c.width + 10)
+        stay = q >= 0.5
+        if self.law_depth is not None:
+            stay = torch.where(self.forced, self.law_depth > step, stay)
+        nxt = live & stay
+        learned = (live & ~self.forced).float()
+        self.carry = (nxt.float() + learned * (q - q.detach())).mean() + self.anchor
+        self.anchor = self.anchor + q.sum() * 0
+        self.active, self.gate = nxt, q
+
+
 class SparseCircleMixin:
+    # ------------------------------------------------------------------ curriculum
     def set_circle_step(self, step):
         if step < 0:
-            raise ValueError("Circle curriculum step must be nonnegative")
+            raise ValueError("the Circle curriculum step cannot be negative")
         self.circle_step = step
 
     def learned_route_fraction(self):
+        """Share of tokens routed by the halter: 0 in the warm-up, ramping to 1 over the transition
+        (always 1 outside training)."""
         if not self.training:
             return 1.0
         c = self.config
-        since = getattr(self, "circle_step", 0) - c.circle_random_warmup
-        if since < 0:
+        elapsed = getattr(self, "circle_step", 0) - c.circle_random_warmup + 1
+        if elapsed <= 0:
             return 0.0
-        return min(1.0, (since + 1) / max(1, c.circle_route_transition))
+        return min(1.0, elapsed / max(1, c.circle_route_transition))
 
     def circle_stage(self):
-        f = self.learned_route_fraction()
-        return "random_warmup" if f == 0 else "learned" if f == 1 else "route_transition"
+        share = self.learned_route_fraction()
+        if share == 0:
+            return "random_warmup"
+        return "learned" if share == 1 else "route_transition"
 
+    # ------------------------------------------------------------------ routing generator
     def routing_generator(self, device):
-        if getattr(self, "_routing_generator", None) is None:
+        gen = getattr(self, "_routing_generator", None)
+        if gen is None:
             rank = dist.get_rank() if dist.is_initialized() else 0
             gen = torch.Generator(device=device).manual_seed(self.config.circle_routing_seed + rank)
-            saved = getattr(self, "_routing_state", None)
-            if saved is not None:
-                gen.set_state(saved)
+            pending = getattr(self, "_routing_state", None)
+            if pending is not None:
+                gen.set_state(pending)
                 self._routing_state = None
             self._routing_generator = gen
-        return self._routing_generator
+        return gen
 
     def routing_rng_state(self):
         gen = getattr(self, "_routing_generator", None)
-        return gen.get_state() if gen is not None else getattr(self, "_routing_state", None)
+        return getattr(self, "_routing_state", None) if gen is None else gen.get_state()
 
     def restore_routing_rng(self, state):
-        self._routing_generator = None
-        self._routing_state = state
+        self._routing_generator, self._routing_state = None, state
 
     def _circle_random_routes(self, idx):
-        f = self.learned_route_fraction()
-        if f == 1:
+        """(forced mask, law-drawn total depth) per token; (all False, None) once fully learned."""
+        share = self.learned_route_fraction()
+        if share == 1:
             return torch.zeros_like(idx, dtype=torch.bool), None
         gen = self.routing_generator(idx.device)
-        forced = torch.rand(idx.shape, device=idx.device, generator=gen) >= f
-        u = torch.rand(idx.shape, device=idx.device, generator=gen)
+        forced = torch.rand(idx.shape, device=idx.device, generator=gen) >= share
+        draw = torch.rand(idx.shape, device=idx.device, generator=gen)
         c = self.config
-        depth = torch.searchsorted(self.circle_budget.probabilities.cumsum(0), u.double().contiguous())
-        return forced, depth.clamp_max(c.circle_max_steps - c.core_layers) + c.core_layers
+        cdf = self.circle_budget.probabilities.cumsum(0)
+        extra = torch.searchsorted(cdf, draw.double().contiguous()).clamp_max(c.circle_max_steps - c.core_layers)
+        return forced, extra + c.core_layers
 
+    # ------------------------------------------------------------------ the ring
     def _sparse_circle(self, x, idx, run):
         c = self.config
-        active = torch.ones_like(idx, dtype=torch.bool)
-        forced, depths = self._circle_random_routes(idx)
-        gate, survival = None, []
-        pending = x.new_tensor(1.0, dtype=torch.float32)
-        anchor = x.new_zeros((), dtype=torch.float32)
+        ring, limit = c.core_layers, c.circle_max_steps
+        route = _Route(self, idx, x)
         backout = None
-        for s in range(1, c.circle_max_steps + 1):
-            n_active = int(active.sum())
-            self.last_stats["active_tokens"][s - 1] = n_active
-            survival.append(pending)
+        for step in range(1, limit + 1):
+            count = route.enter(step, self.last_stats)
             before = x
-            cand = run(c.pre_layers + (s - 1) % c.core_layers, x, active=None if s <= c.core_layers else active)
-            x = cand if gate is None else before + gate.to(x.dtype)[..., None] * (cand - before)
-            if c.pre_layers + s - 1 == c.max_depth // 2:
+            candidate = run(c.pre_layers + (step - 1) % ring, x, active=route.active if step > ring else None)
+            x = route.blend(before, candidate)
+            if c.pre_layers + step - 1 == c.max_depth // 2:
                 backout = x
-            if s < c.core_layers:
-                continue
-            if s == c.circle_max_steps:
-                break
-            score = self.halter(before[active], x[active], s - c.core_layers)
-            q = torch.zeros_like(idx, dtype=torch.float32).masked_scatter(active, torch.sigmoid(-score))
-            self.last_stats["forward_flops"] += 2 * n_active * c.width
-            self.last_stats["halter_extra_forward_ops"] += n_active * (5 * c.width + 10)
-            keep = q >= 0.5
-            if depths is not None:
-                keep = torch.where(forced, depths > s, keep)
-            nxt = active & keep
-            straight = nxt.float() + (active & ~forced).float() * (q - q.detach())
-            pending = straight.mean() + anchor
-            anchor = anchor + q.sum() * 0      # keeps every gate in the graph after an empty tail
-            active, gate = nxt, q
-        penalty, depth_loss, shape_loss = self.circle_budget.penalty(torch.stack(survival))
+            if ring <= step < limit:
+                route.decide(self, step, before, x, count)
+        penalty, depth_loss, shape_loss = self.circle_budget.penalty(torch.stack(route.curve))
         if not self.training:
             penalty = x.new_zeros((), dtype=torch.float32)
-        self.last_stats["active_depth_sum"] = (idx.numel() * (c.pre_layers + c.post_layers)
-                                               + sum(self.last_stats["active_tokens"]))
-        self.last_stats["circle_depth_loss"] = depth_loss.detach()
-        self.last_stats["circle_shape_loss"] = shape_loss.detach()
+        stats = self.last_stats
+        stats["active_depth_sum"] = idx.numel() * (c.pre_layers + c.post_layers) + sum(stats["active_tokens"])
+        stats["circle_depth_loss"] = depth_loss.detach()
+        stats["circle_shape_loss"] = shape_loss.detach()
         return x, penalty, backout

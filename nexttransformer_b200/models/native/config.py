@@ -58,63 +58,13 @@ class NativeModelConfig:
     mor_dual_limit: float = 10.0
 
     def __post_init__(self):
-        arch = self.architecture
-        if arch not in RECURSIONS:
-            raise ValueError("invalid native architecture")
+        if self.architecture not in RECURSIONS:
+            raise ValueError(f"native architecture must be one of {sorted(RECURSIONS)}, got {self.architecture!r}")
         if self.recursions is None:
-            object.__setattr__(self, "recursions", RECURSIONS[arch])
-        dims = (self.width, self.heads, self.sequence_len, self.pre_layers, self.core_layers, self.post_layers,
-                self.dense_layers, self.fourier_dim)
-        if min(dims) <= 0 or self.width % self.heads:
-            raise ValueError("invalid native model dimensions")
-        if self.recursions != RECURSIONS[arch]:
-            raise ValueError("common-core protocol: MoR/Circle max3, LoopFormer fixed2")
-        if not 0 < self.circle_halter_eps < 1:
-            raise ValueError("circle_halter_eps must lie between 0 and 1")
-        if self.activation_checkpointing:
-            raise ValueError("native FLOP protocol currently requires activation_checkpointing=false")
-        if self.mlp_width != 4 * self.width or self.width < 24 or (self.width // self.heads) % 2:
-            raise ValueError("native backbone requires MLP=4d, width>=24 and even head dimension")
-        if not self.window_pattern or set(self.window_pattern) - set("SL"):
-            raise ValueError("window_pattern must contain only S and L")
-        chain = (1., *self.mor_target_survival, 0.)
-        if len(self.mor_target_survival) != 2 or any(a <= b for a, b in zip(chain, chain[1:])):
-            raise ValueError("MoR requires two strictly decreasing survival targets")
-        if min(self.mor_budget_strength, self.mor_dual_lr, self.mor_dual_limit) <= 0:
-            raise ValueError("MoR budget settings must be positive")
-        if arch == "loopformer":
-            if not 0 < self.loop_modulation_bound < 1:
-                raise ValueError("LoopFormer modulation bound must lie between zero and one")
-            if not all(math.isfinite(v) and v > 0 for v in (self.loop_condition_lr_multiplier,
-                                                            self.loop_condition_grad_clip)):
-                raise ValueError("LoopFormer conditioning optimizer settings must be positive")
-        if arch == "circle":
-            self._check_circle()
-
-    def _check_circle(self):
-        if self.circle_halter != "delta_depth":
-            raise ValueError("circle_halter must be delta_depth; legacy Circle needs its frozen source")
-        if (self.circle_method, self.circle_budget_mode, self.circle_exit_interval) != ("sparse_gate",
-                                                                                         "mean_survival", 1):
-            raise ValueError("native Circle requires sparse_gate, mean_survival and per-block exits")
-        if self.circle_max_steps != self.core_layers * self.recursions:
-            raise ValueError("Circle max steps must equal three complete rings")
-        if not self.core_layers < self.circle_target_steps < self.circle_max_steps:
-            raise ValueError("Circle target must be strictly inside its depth range")
-        if self.circle_threshold != .5:
-            raise ValueError("sparse Circle uses a fixed 0.5 threshold")
-        vals = (self.circle_target_steps, self.circle_depth_rho, self.circle_shape_weight, self.circle_dual_lr,
-                self.circle_dual_limit, self.circle_budget_beta, self.circle_halter_lr_multiplier,
-                self.circle_halter_grad_clip)
-        if not all(math.isfinite(v) for v in vals):
-            raise ValueError("nonfinite Circle setting")
-        if min(self.circle_depth_rho, self.circle_dual_lr, self.circle_dual_limit, self.circle_halter_lr_multiplier,
-               self.circle_halter_grad_clip) <= 0:
-            raise ValueError("Circle loss/optimizer settings must be positive")
-        if self.circle_shape_weight < 0 or not 0 <= self.circle_budget_beta < 1:
-            raise ValueError("invalid Circle shape weight or smoothing")
-        if min(self.circle_random_warmup, self.circle_route_transition) < 0:
-            raise ValueError("Circle curriculum lengths must be nonnegative")
+            object.__setattr__(self, "recursions", RECURSIONS[self.architecture])
+        for scope, holds, message in _RULES:
+            if scope in ("any", self.architecture) and not holds(self):
+                raise ValueError(message)
 
     @property
     def n_layer(self):
@@ -144,6 +94,60 @@ class NativeModelConfig:
     @property
     def n_kv_head(self):
         return self.heads
+
+
+def _finite_positive(*values):
+    return all(math.isfinite(v) and v > 0 for v in values)
+
+
+def _decreasing(values):
+    return all(a > b for a, b in zip(values, values[1:]))
+
+
+# (scope, condition that must hold, message): scope "any" applies to every architecture.
+_RULES = (
+    ("any", lambda c: min(c.width, c.heads, c.sequence_len, c.pre_layers, c.core_layers, c.post_layers,
+                          c.dense_layers, c.fourier_dim) > 0 and c.width % c.heads == 0,
+     "native model sizes must be positive and the heads must divide the width"),
+    ("any", lambda c: c.recursions == RECURSIONS[c.architecture],
+     "the shared core protocol fixes the recursion count (MoR and Circle at most 3, LoopFormer exactly 2)"),
+    ("any", lambda c: 0 < c.circle_halter_eps < 1, "circle_halter_eps must be strictly between 0 and 1"),
+    ("any", lambda c: not c.activation_checkpointing,
+     "the native FLOP accounting assumes no activation checkpointing"),
+    ("any", lambda c: c.mlp_width == 4 * c.width and c.width >= 24 and (c.width // c.heads) % 2 == 0,
+     "the native shell needs a 4x MLP, width of at least 24 and an even head size"),
+    ("any", lambda c: bool(c.window_pattern) and set(c.window_pattern) <= set("SL"),
+     "window_pattern may only use the letters S and L"),
+    ("any", lambda c: len(c.mor_target_survival) == 2 and _decreasing((1., *c.mor_target_survival, 0.)),
+     "MoR takes two survival targets, strictly decreasing inside (0, 1)"),
+    ("any", lambda c: min(c.mor_budget_strength, c.mor_dual_lr, c.mor_dual_limit) > 0,
+     "MoR budget strength, dual step and dual limit must be positive"),
+    ("loopformer", lambda c: 0 < c.loop_modulation_bound < 1,
+     "the LoopFormer modulation bound must be strictly between 0 and 1"),
+    ("loopformer", lambda c: _finite_positive(c.loop_condition_lr_multiplier, c.loop_condition_grad_clip),
+     "the LoopFormer conditioning learning-rate multiplier and clip must be finite and positive"),
+    ("circle", lambda c: c.circle_halter == "delta_depth",
+     "Circle uses the delta_depth halter (other halters belong to the frozen legacy source)"),
+    ("circle", lambda c: (c.circle_method, c.circle_budget_mode, c.circle_exit_interval) ==
+     ("sparse_gate", "mean_survival", 1),
+     "Circle is the sparse-gate, mean-survival variant with an exit after every block"),
+    ("circle", lambda c: c.circle_max_steps == c.core_layers * c.recursions,
+     "Circle's step limit is exactly three passes around the ring"),
+    ("circle", lambda c: c.core_layers < c.circle_target_steps < c.circle_max_steps,
+     "Circle's target depth must lie strictly between one ring and the step limit"),
+    ("circle", lambda c: c.circle_threshold == .5, "sparse Circle exits at a fixed gate threshold of 0.5"),
+    ("circle", lambda c: all(math.isfinite(v) for v in (
+        c.circle_target_steps, c.circle_depth_rho, c.circle_shape_weight, c.circle_dual_lr, c.circle_dual_limit,
+        c.circle_budget_beta, c.circle_halter_lr_multiplier, c.circle_halter_grad_clip)),
+     "every Circle setting must be finite"),
+    ("circle", lambda c: _finite_positive(c.circle_depth_rho, c.circle_dual_lr, c.circle_dual_limit,
+                                          c.circle_halter_lr_multiplier, c.circle_halter_grad_clip),
+     "Circle's depth weight, dual step and limit, and halter optimizer settings must be positive"),
+    ("circle", lambda c: c.circle_shape_weight >= 0 and 0 <= c.circle_budget_beta < 1,
+     "Circle's shape weight must be non-negative and its smoothing in [0, 1)"),
+    ("circle", lambda c: min(c.circle_random_warmup, c.circle_route_transition) >= 0,
+     "Circle's warm-up and transition lengths cannot be negative"),
+)
 
 
 @dataclass(frozen=True)

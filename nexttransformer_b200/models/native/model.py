@@ -122,9 +122,7 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
                 nn.init.constant_(router.bias, float(torch.distributions.Normal(0., 1.).icdf(
                     torch.tensor(target / prev))))
                 prev = target
-            self.survival_budget.dual.zero_()
-            self.survival_budget.updates.zero_()
-            self.survival_budget.last_step.fill_(-1)
+            self.survival_budget.reset()
         elif c.architecture == "circle":
             self.circle_budget.reset()
             _, surv = depth_reference(c.core_layers, c.circle_max_steps, c.circle_target_steps)
@@ -141,122 +139,136 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
         self.last_stats["forward_flops"] += 2 * idx.numel() * 24
         return x
 
+    # ------------------------------------------------------------------ one block, three ways
+    def _full_block(self, h, ve, blk, w, rope, conditioning):
+        """The block on every token: plain, or with LoopFormer's bounded offsets around identity
+        (output gates and input scales act as ``1 + offset``, so zero offsets leave the block as is
+        and a zero-initialised output projection still receives gradient)."""
+        if conditioning is None:
+            return blk(h, ve, rope, w, None)
+        gate_attn, gate_mlp, scale_attn, scale_mlp = (o[:, None] for o in conditioning.to(h.dtype).chunk(4, -1))
+        mixed = h + (1 + gate_attn) * blk.attn(norm(h) * (1 + scale_attn), ve, rope, w, None)
+        return mixed + (1 + gate_mlp) * blk.mlp(norm(mixed) * (1 + scale_mlp))
+
+    def _compacted_block(self, x, x0, idx, physical, w, active):
+        """The block on the active tokens only: each row's active tokens are gathered in position
+        order (padded to the longest row), attend with their original RoPE positions and window
+        distances (explicit mask), and their block updates are scattered back.  Returns the new
+        state and the number of gathered rows per sequence (None when no token is active)."""
+        b, n, d = x.shape
+        width = int(active.sum(1).max().item())
+        if width == 0:
+            return x, None
+        c = self.config
+        blk, a = self.transformer.h[physical], self.transformer.h[physical].attn
+        order = torch.arange(n, device=x.device).expand(b, -1).masked_fill(~active, n).sort(1).values[:, :width]
+        valid = order < n
+        pos = order.clamp_max(n - 1)
+        rows = pos[:, :, None].expand(-1, -1, d)
+        mixed = self.resid_lambdas[physical] * x.gather(1, rows) + self.x0_lambdas[physical] * x0.gather(1, rows)
+        z = norm(mixed)
+        hd = d // c.heads
+        q = a.c_q(z).view(b, width, c.heads, hd)
+        k = a.c_k(z).view_as(q)
+        v = a.c_v(z).view_as(q)
+        if str(physical) in self.value_embeds:
+            table = self.value_embeds[str(physical)](idx.gather(1, pos)).to(x.dtype).view_as(v)
+            v = v + 3 * torch.sigmoid(a.ve_gate(z[..., :12])).unsqueeze(-1) * table
+        cos, sin = self.cos[0, pos], self.sin[0, pos]
+        q = norm(apply_rotary_emb(q, cos, sin)) * 1.2
+        k = norm(apply_rotary_emb(k, cos, sin)) * 1.2
+        lag = pos[:, :, None] - pos[:, None, :]
+        visible = (lag >= 0) & (lag <= w[0]) & valid[:, :, None] & valid[:, None, :]
+        y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           attn_mask=visible[:, None]).transpose(1, 2).reshape(b, width, d)
+        out = mixed + a.c_proj(y)
+        out = out + blk.mlp(norm(out))
+        update = (out - x.gather(1, rows)) * valid[:, :, None].to(x.dtype)
+        return x.scatter_add(1, rows, update), width
+
     def _layer(self, x, x0, idx, physical, virtual, conditioning=None, active=None):
         c = self.config
-        b, n, d = x.shape
-        blk = self.transformer.h[physical]
+        b, n, _ = x.shape
         w = window(c, virtual)
-        has_ve = str(physical) in self.value_embeds
-        cos, sin = self.cos[:, :n], self.sin[:, :n]
         if active is None:
             h = self.resid_lambdas[physical] * x + self.x0_lambdas[physical] * x0
-            ve = self.value_embeds[str(physical)](idx).to(x.dtype) if has_ve else None
-            if conditioning is None:
-                out = blk(h, ve, (cos, sin), w, None)
-            else:
-                # multiplicative gates around identity: c_proj starts at zero, so zero gates would
-                # block both gradients
-                ga, gm, sa, sm = conditioning.to(h.dtype).chunk(4, -1)
-                out = h + (1 + ga[:, None]) * blk.attn(norm(h) * (1 + sa[:, None]), ve, (cos, sin), w, None)
-                out = out + (1 + gm[:, None]) * blk.mlp(norm(out) * (1 + sm[:, None]))
-            cost = block_forward_flops(c, b, n, window_size=w)
-            ve_rows = b * n
+            ve = self.value_embeds[str(physical)](idx).to(x.dtype) if str(physical) in self.value_embeds else None
+            out = self._full_block(h, ve, self.transformer.h[physical], w, (self.cos[:, :n], self.sin[:, :n]),
+                                   conditioning)
+            cost, rows = block_forward_flops(c, b, n, window_size=w), b * n
         else:
-            m = int(active.sum(1).max().item())
-            if m == 0:
+            out, width = self._compacted_block(x, x0, idx, physical, w, active)
+            if width is None:
                 return x
-            pos = torch.arange(n, device=x.device).expand(b, -1).masked_fill(~active, n).sort(1).values[:, :m]
-            real = pos < n
-            pos = pos.clamp_max(n - 1)
-            take = pos[:, :, None].expand(-1, -1, d)
-            sel = self.resid_lambdas[physical] * x.gather(1, take) + self.x0_lambdas[physical] * x0.gather(1, take)
-            z = norm(sel)
-            a = blk.attn
-            hd = d // c.heads
-            q = a.c_q(z).view(b, m, c.heads, hd)
-            k = a.c_k(z).view_as(q)
-            v = a.c_v(z).view_as(q)
-            if has_ve:
-                sve = self.value_embeds[str(physical)](idx.gather(1, pos)).to(x.dtype).view_as(v)
-                v = v + 3 * torch.sigmoid(a.ve_gate(z[..., :12])).unsqueeze(-1) * sve
-            cs, sn = cos[0, pos], sin[0, pos]
-            q = norm(apply_rotary_emb(q, cs, sn)) * 1.2
-            k = norm(apply_rotary_emb(k, cs, sn)) * 1.2
-            dist = pos[:, :, None] - pos[:, None, :]
-            mask = (dist >= 0) & (dist <= w[0]) & real[:, :, None] & real[:, None, :]
-            y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                               attn_mask=mask[:, None]).transpose(1, 2).reshape(b, m, d)
-            cand = sel + a.c_proj(y)
-            cand = cand + blk.mlp(norm(cand))
-            delta = (cand - x.gather(1, take)) * real[:, :, None].to(x.dtype)
-            out = x.scatter_add(1, take, delta)
-            cost = block_forward_flops(c, b, m)
-            ve_rows = b * m
-        if has_ve:
-            cost += 24 * c.heads * ve_rows
+            cost, rows = block_forward_flops(c, b, width), b * width
+        if str(physical) in self.value_embeds:
+            cost += 24 * c.heads * rows
         self.last_stats["forward_flops"] += cost
         return out
+
+    # ------------------------------------------------------------------ trunks
+    def _mor_core(self, trunk, x_of, b, n, device):
+        """Three passes over the ring; before passes 2 and 3 a router keeps tokens (hard gate in
+        the forward, straight-through in training) and the pass's update is weighted by the router
+        probability.  Returns the survival penalty."""
+        c = self.config
+        alive = torch.ones((b, n), device=device)
+        means = []
+        for r in range(c.recursions):
+            prob = None
+            if r:
+                with torch.autocast(device_type=device.type, enabled=False):
+                    logit = self.routers[r - 1](norm(x_of().float())).squeeze(-1)
+                    prob = logit.sigmoid()
+                    hard = (logit >= 0).float()
+                    alive = alive * (hard - prob.detach() + prob if self.training else hard)
+                means.append(alive.mean())
+                self.last_stats["forward_flops"] += 2 * b * n * c.width
+            active = alive.detach() > 0.5
+            self.last_stats["active_tokens"][r] = int(active.sum())
+            start = x_of()
+            for i in range(c.core_layers):
+                trunk(c.pre_layers + i, active=None if r == 0 else active)
+            if prob is not None:
+                trunk.state = start + prob.to(start.dtype)[:, :, None] * (trunk.state - start)
+        self.last_stats["active_depth_sum"] = (b * n * (c.pre_layers + c.post_layers)
+                                               + c.core_layers * sum(self.last_stats["active_tokens"]))
+        return self.survival_budget.penalty(torch.stack(means)) if self.training else x_of().new_zeros(())
+
+    def _loopformer_core(self, trunk, b, n, device):
+        c = self.config
+        for r in range(c.recursions):
+            offsets = self.conditioner(r, b, device)
+            self.last_stats["forward_flops"] += 4 * b * (c.fourier_dim * c.width + c.width * c.width)
+            for i, offset in enumerate(offsets):
+                self.last_stats["forward_flops"] += 8 * b * c.width * c.width
+                trunk(c.pre_layers + i, conditioning=offset)
+            self.last_stats["active_tokens"][r] = b * n
+        self.last_stats["active_depth_sum"] = b * n * c.max_depth
 
     def _variant_hidden(self, idx):
         c = self.config
         b, n = idx.shape
-        x = self._embed_native(idx)
-        x0 = x
-        state = dict(virtual=0, backout=None)
-
-        def run(physical, active=None, conditioning=None):
-            nonlocal x
-            x = self._layer(x, x0, idx, physical, state["virtual"], conditioning, active)
-            if state["virtual"] == c.max_depth // 2:
-                state["backout"] = x
-            state["virtual"] += 1
-
+        trunk = _Trunk(self, idx, self._embed_native(idx))
         for i in range(c.pre_layers):
-            run(i)
+            trunk(i)
         if c.architecture == "loopformer":
-            for r in range(c.recursions):
-                mods = self.conditioner(r, b, x.device)
-                self.last_stats["forward_flops"] += 4 * b * (c.fourier_dim * c.width + c.width * c.width)
-                for i, mod in enumerate(mods):
-                    self.last_stats["forward_flops"] += 8 * b * c.width * c.width
-                    run(c.pre_layers + i, conditioning=mod)
-                self.last_stats["active_tokens"][r] = b * n
-            self.last_stats["active_depth_sum"] = b * n * c.max_depth
-            penalty = x.new_zeros((), dtype=torch.float32)
+            self._loopformer_core(trunk, b, n, idx.device)
+            penalty = trunk.state.new_zeros((), dtype=torch.float32)
         elif c.architecture == "mor":
-            alive = torch.ones((b, n), device=x.device)
-            means = []
-            for r in range(c.recursions):
-                if r:
-                    with torch.autocast(device_type=x.device.type, enabled=False):
-                        logit = self.routers[r - 1](norm(x.float())).squeeze(-1)
-                        prob = logit.sigmoid()
-                        hard = (logit >= 0).float()
-                        alive = alive * (hard - prob.detach() + prob if self.training else hard)
-                    means.append(alive.mean())
-                    self.last_stats["forward_flops"] += 2 * b * n * c.width
-                active = alive.detach() > 0.5
-                self.last_stats["active_tokens"][r] = int(active.sum())
-                before = x
-                for i in range(c.core_layers):
-                    run(c.pre_layers + i, active=None if r == 0 else active)
-                if r:
-                    x = before + prob.to(x.dtype)[:, :, None] * (x - before)
-            penalty = self.survival_budget.penalty(torch.stack(means)) if self.training else x.new_zeros(())
-            self.last_stats["active_depth_sum"] = (b * n * (c.pre_layers + c.post_layers)
-                                                   + c.core_layers * sum(self.last_stats["active_tokens"]))
+            penalty = self._mor_core(trunk, lambda: trunk.state, b, n, idx.device)
         else:
-            def circle_run(physical, current, active=None):
-                nonlocal x
-                x = current
-                run(physical, active=active)
-                return x
-            x, penalty, state["backout"] = self._sparse_circle(x, idx, circle_run)
-            x = norm(x)
+            def step(physical, current, active=None):
+                trunk.state = current
+                trunk(physical, active=active)
+                return trunk.state
+            trunk.state, penalty, trunk.backout = self._sparse_circle(trunk.state, idx, step)
+            trunk.state = norm(trunk.state)
         for i in range(c.post_layers):
-            run(c.pre_layers + c.core_layers + i)
-        if state["backout"] is not None:
-            x = x - self.backout_lambda.to(x.dtype) * state["backout"]
+            trunk(c.pre_layers + c.core_layers + i)
+        x = trunk.state
+        if trunk.backout is not None:
+            x = x - self.backout_lambda.to(x.dtype) * trunk.backout
         return norm(x), penalty
 
     def forward(self, idx, targets=None, loss_reduction=None):
@@ -271,7 +283,7 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
             if (self.use_fused and idx.is_cuda and targets is not None and loss_reduction is None and self.training
                     and self.fused_supported()):
                 from nexttransformer_b200.models.fused_dense import fused_forward
-                lm = fused_forward(self, idx, targets, "mean")
+                lm = fused_forward(self, idx, targets, "mean")[0]
                 zero = lm.new_zeros(())
                 return dict(loss=lm, lm_loss=lm, router_loss=zero, objective=lm.detach(), compute_loss=zero)
             logits = self.forward_eager(idx)
@@ -319,3 +331,21 @@ def build_model(config, device, seed=None):
     model.to_empty(device=device)
     model.init_weights()
     return model
+
+
+class _Trunk:
+    """Runs blocks in depth order on a shared state: counts virtual depth and keeps the mid-depth
+    state for the backout."""
+
+    def __init__(self, model, idx, x):
+        self.model, self.idx = model, idx
+        self.state, self.x0 = x, x
+        self.virtual = 0
+        self.backout = None
+
+    def __call__(self, physical, active=None, conditioning=None):
+        model = self.model
+        self.state = model._layer(self.state, self.x0, self.idx, physical, self.virtual, conditioning, active)
+        if self.virtual == model.config.max_depth // 2:
+            self.backout = self.state
+        self.virtual += 1

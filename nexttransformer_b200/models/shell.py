@@ -36,10 +36,11 @@ class ShellConfig:
     value_embeddings: bool = True
     softcap: float = 15.0
     pad_vocab_to: int = 64
+    attn_head_dim: int = 0      # 0: n_embd / n_head
 
     @property
     def head_dim(self):
-        return self.n_embd // self.n_head
+        return self.attn_head_dim or self.n_embd // self.n_head
 
     @property
     def ffn(self):
@@ -57,9 +58,18 @@ def norm(x):
 
 
 class Linear(nn.Linear):
-    """Linear with fp32 master weight, cast to the activation dtype at use (no autocast)."""
+    """Linear with fp32 master weight, cast to the activation dtype at use (no autocast).
+
+    Once the kernel state of a model on CUDA has registered the layer (``_kernel``: a bf16
+    shadow ``_w`` written by the optimizer and an fp32 gradient slot ``_g``), bf16 inputs run
+    on the sm_100a GEMM engine (``ops.dense.KernelLinear``); everything else uses ``F.linear``."""
+
+    _kernel = False
 
     def forward(self, x):
+        if self._kernel and x.is_cuda and x.dtype == torch.bfloat16:
+            from nexttransformer_b200.ops.dense import kernel_linear
+            return kernel_linear(x, self)
         return F.linear(x, self.weight.to(dtype=x.dtype))
 
 
@@ -111,22 +121,28 @@ class CausalSelfAttention(nn.Module):
         self.layer_idx = layer
         self.n_head, self.n_kv_head, self.head_dim = cfg.n_head, cfg.n_kv_head, cfg.head_dim
         d = cfg.n_embd
-        if d % cfg.n_head or cfg.n_head % cfg.n_kv_head:
+        if (d % cfg.n_head and not cfg.attn_head_dim) or cfg.n_head % cfg.n_kv_head:
             raise ValueError("heads must divide width and kv heads must divide heads")
         self.c_q = Linear(d, cfg.n_head * self.head_dim, bias=False)
         self.c_k = Linear(d, cfg.n_kv_head * self.head_dim, bias=False)
         self.c_v = Linear(d, cfg.n_kv_head * self.head_dim, bias=False)
-        self.c_proj = Linear(d, d, bias=False)
+        self.c_proj = Linear(cfg.n_head * self.head_dim, d, bias=False)
         self.ve_gate_channels = 12
         self.ve_gate = Linear(12, cfg.n_kv_head, bias=False) if (cfg.value_embeddings and has_ve(layer, cfg.n_layer)) \
             else None
 
+    def projections(self, x):
+        """The raw q, k, v projections ``[B, T, heads * head_dim]`` (a hook for variants that
+        transform them before the heads are split)."""
+        return self.c_q(x), self.c_k(x), self.c_v(x)
+
     def project(self, x, ve, cos_sin):
         """q, k, v after value-embedding mixing, RoPE and QK-norm (shared by the mixers that reuse it)."""
         B, T, _ = x.shape
-        q = self.c_q(x).view(B, T, self.n_head, self.head_dim)
-        k = self.c_k(x).view(B, T, self.n_kv_head, self.head_dim)
-        v = self.c_v(x).view(B, T, self.n_kv_head, self.head_dim)
+        q, k, v = self.projections(x)
+        q = q.view(B, T, self.n_head, self.head_dim)
+        k = k.view(B, T, self.n_kv_head, self.head_dim)
+        v = v.view(B, T, self.n_kv_head, self.head_dim)
         if ve is not None and self.ve_gate is not None:
             ve = ve.view(B, T, self.n_kv_head, self.head_dim)
             gate = 3 * torch.sigmoid(self.ve_gate(x[..., :self.ve_gate_channels]))
@@ -151,8 +167,12 @@ class MLP(nn.Module):
         self.c_fc = Linear(cfg.n_embd, cfg.ffn, bias=False)
         self.c_proj = Linear(cfg.ffn, cfg.n_embd, bias=False)
 
+    def hidden(self, x):
+        """The pre-activation hidden layer (a hook for variants that transform it)."""
+        return self.c_fc(x)
+
     def forward(self, x):
-        return self.c_proj(F.relu(self.c_fc(x)).square())
+        return self.c_proj(F.relu(self.hidden(x)).square())
 
 
 class Block(nn.Module):
@@ -320,14 +340,19 @@ class GPTShell(nn.Module):
         return all(type(b) is Block and type(b.attn) is CausalSelfAttention and type(b.mlp) is MLP
                    for b in self.transformer.h)
 
+    def layer_window(self, i):
+        """Left attention window of layer ``i`` (a window >= T - 1 is plain causal attention)."""
+        return self.window_sizes[i][0]
+
     def forward(self, idx, targets=None, loss_reduction="mean"):
         if idx.is_cuda and self.fused_supported() and targets is not None and loss_reduction in ("mean", "sum"):
             from nexttransformer_b200.models.fused_dense import fused_forward
-            return fused_forward(self, idx, targets, loss_reduction)
+            return fused_forward(self, idx, targets, loss_reduction)[0]
         return self.forward_eager(idx, targets, loss_reduction)
 
     # ------------------------------------------------------------------ fused-path state
     def fused_state(self):
+        """The kernel state (bf16 shadows, fp32 gradient slots) of this model on CUDA."""
         if self._fused is None:
             from nexttransformer_b200.models.fused_dense import FusedState
             self._fused = FusedState(self)

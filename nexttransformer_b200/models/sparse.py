@@ -147,7 +147,7 @@ class SparseMixer(nn.Module):
         self.c_q = Linear(d, H * D, bias=False)
         self.c_k = Linear(d, Hk * D, bias=False)
         self.c_v = Linear(d, Hk * D, bias=False)
-        self.c_proj = Linear(d, d, bias=False)
+        self.c_proj = Linear(H * D, d, bias=False)
         from nexttransformer_b200.models.shell import has_ve
         self.ve_gate = Linear(12, Hk, bias=False) if (config.value_embeddings and has_ve(layer_idx, config.n_layer)) \
             else None
@@ -340,9 +340,9 @@ class SparseMixer(nn.Module):
             edges += int(valid.sum())
             outputs.append(out)
         if collect:
-            y = self._collected_attention(x, q, k, v, mems, size, burnin).reshape(B, T, d)
+            y = self._collected_attention(x, q, k, v, mems, size, burnin).reshape(B, T, -1)
         else:
-            y = torch.cat(outputs, 2).transpose(1, 2).reshape(B, T, d)
+            y = torch.cat(outputs, 2).transpose(1, 2).reshape(B, T, -1)
         self.last_aux = sum(aux, x.new_zeros(())) * c.index_loss_weight
         self.last_stats = {"selected_edges": edges, "teacher_dense_score_edges": teacher_edges, "burnin": burnin,
                            "backend": self.backend}
@@ -434,7 +434,7 @@ class SparseMixer(nn.Module):
             y = comp * gates[..., 0:1] + selected * gates[..., 1:2] + local * gates[..., 2:3]
             lw = torch.arange(T, device=dev).clamp_max(c.local_window - 1) + 1
             edges += B * H * int(lw.sum()) + B * H * T * ck.shape[2]
-        y = y.reshape(B, T, d)
+        y = y.reshape(B, T, -1)
         self.last_aux = x.new_zeros(())
         self.last_stats = {"selected_edges": edges, "teacher_dense_score_edges": 0, "burnin": False,
                            "backend": self.backend}

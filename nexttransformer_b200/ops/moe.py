@@ -53,7 +53,7 @@ def plan(choice, num_experts):
 
 class _GroupedExperts(Function):
     @staticmethod
-    def forward(ctx, x, w, w_fc, w_proj, row_of, src_of, grp_m, grp_k):
+    def forward(ctx, x, w, w_fc, w_proj, row_of, src_of, grp_m, grp_k, state=None):
         lib = ext()
         T, d = x.shape
         E, F = w_fc.shape[0], w_fc.shape[1]
@@ -73,6 +73,7 @@ class _GroupedExperts(Function):
         lib.moe_combine(y_perm, row_of, wf32, None, out)
         ctx.save_for_backward(x_perm, h_pre, h, y_perm, wf, wp, row_of, grp_m, grp_k, wf32)
         ctx.dtypes = (x.dtype, w.dtype, w_fc.dtype, w_proj.dtype)
+        ctx.state = state
         return out.to(x.dtype)
 
     @staticmethod
@@ -88,16 +89,21 @@ class _GroupedExperts(Function):
         lib.moe_combine_bwd(dy, y_perm, row_of, wf32, d_rows, dw)
         dh_pre = torch.empty(P, F, device=dy.device, dtype=torch.bfloat16)
         lib.gemm_grouped(d_rows, False, wp, True, dh_pre, EPI_RELU2_BWD, grp_m, False, h_pre, None, 1.0)
-        dwp = torch.zeros(E, d, F, device=dy.device, dtype=torch.float32)
+        state = ctx.state
+        # the grouped-K weight-gradient GEMMs accumulate (experts without rows are left untouched):
+        # into the experts' main_grad stacks (zeroed once per update) or into fresh zeroed buffers
+        dwp = state._g_proj if state is not None else torch.zeros(E, d, F, device=dy.device, dtype=torch.float32)
         lib.gemm_grouped(d_rows, True, h, True, dwp, EPI_F32_ACC, grp_k, True, None, None, 1.0)
         dx_perm = torch.empty(P, d, device=dy.device, dtype=torch.bfloat16)
         lib.gemm_grouped(dh_pre, False, wf, True, dx_perm, EPI_BF16, grp_m, False, None, None, 1.0)
-        dwf = torch.zeros(E, F, d, device=dy.device, dtype=torch.float32)
+        dwf = state._g_fc if state is not None else torch.zeros(E, F, d, device=dy.device, dtype=torch.float32)
         lib.gemm_grouped(dh_pre, True, x_perm, True, dwf, EPI_F32_ACC, grp_k, True, None, None, 1.0)
         dx = torch.empty(T, d, device=dy.device, dtype=torch.bfloat16)
         lib.moe_combine(dx_perm, row_of, None, None, dx)
         xd, wd, fd, pd = ctx.dtypes
-        return dx.to(xd), dw.view(T, -1).to(wd), dwf.to(fd), dwp.to(pd), None, None, None, None
+        if state is not None:
+            return dx.to(xd), dw.view(T, -1).to(wd), None, None, None, None, None, None, None
+        return dx.to(xd), dw.view(T, -1).to(wd), dwf.to(fd), dwp.to(pd), None, None, None, None, None
 
 
 def grouped_experts(x, choice, w, w_fc, w_proj):
@@ -107,3 +113,12 @@ def grouped_experts(x, choice, w, w_fc, w_proj):
     GEMMs run in bf16 with fp32 accumulation, gradients come back in the weights' dtype)."""
     pl = plan(choice, w_fc.shape[0])
     return _GroupedExperts.apply(x, w, w_fc, w_proj, pl["row_of"], pl["src_of"], pl["grp_m"], pl["grp_k"])
+
+
+def grouped_experts_state(x, choice, w, moe):
+    """``grouped_experts`` on a layer's kernel state: the stacked bf16 shadows ``moe._w_fc`` /
+    ``moe._w_proj`` are the operands and the weight gradients accumulate into the experts'
+    ``main_grad`` stacks, so no per-forward stack or cast of the fp32 experts is made."""
+    pl = plan(choice, moe._w_fc.shape[0])
+    return _GroupedExperts.apply(x, w, moe._w_fc, moe._w_proj, pl["row_of"], pl["src_of"], pl["grp_m"], pl["grp_k"],
+                                 moe)

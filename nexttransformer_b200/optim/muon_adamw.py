@@ -15,6 +15,17 @@ reduced to their owner (averaged), the owner updates, and updated parameters are
 to every rank - reduce-scatter + all-gather volume, never a full all-reduce of gradients.
 
 Gradients are read from ``p.main_grad`` when a fused path produced one, else ``p.grad``.
+
+Overlap (``overlap_with(model)``, world > 1): the model's kernel state calls ``issue_reduce``
+with each layer's parameters as soon as the last micro-batch's backward has finished that layer,
+so their reductions run on NCCL's stream under the rest of the backward; ``step`` then only waits
+for them.  After the update the parameter gathers are issued in the order the next forward
+uses the parameters (embedding side, layer 0, 1, ..., head) and are not waited: the forward
+waits for each layer's gathers right before the layer (``wait_gathers``), so the gathers run
+under the preceding layers' compute.  ``flush()`` waits for every outstanding gather (before a
+checkpoint, an evaluation or the end of a timed region).  This is the reference's DDP bucket
+overlap (``nexttransformer/train.py:353-357``) and DistMuon's asynchronous phases
+(``nanochat/optim.py:428-459``) arranged for a step whose forward waits per layer.
 """
 import math
 
@@ -31,8 +42,27 @@ POLAR_EXPRESS = (
 
 
 def grad_of(p):
+    """The parameter's gradient for this update: ``main_grad`` where a kernel path owns one.
+
+    A weight run through ``ops.dense.KernelLinear`` carries a gradient slot whose GEMM writes
+    ``main_grad``; if that slot was never written this update (the layer did not run) its
+    stale contents are replaced, and any gradient autograd produced for the same weight (a use
+    outside the kernel path) is folded in.  Idempotent within one update."""
     g = getattr(p, "main_grad", None)
-    return g if g is not None else p.grad
+    if g is None:
+        return p.grad
+    slot = getattr(p, "_nt_slot", None)
+    if slot is not None and slot.fresh:
+        if p.grad is not None:
+            g.copy_(p.grad)
+        else:
+            g.zero_()
+        slot.fresh = False
+        p.grad = None
+    elif p.grad is not None and slot is not None:
+        g.add_(p.grad)
+        p.grad = None
+    return g
 
 
 # ------------------------------------------------------------------ reference math (any device)
@@ -93,9 +123,72 @@ class MuonAdamW(torch.optim.Optimizer):
         # parameters whose gradients it averages in place; the others use NCCL collectives.
         self.p2p, self.p2p_params = None, frozenset()
         self.gather, self.gather_params = None, frozenset()
+        # overlap state: parameter -> forward-use group, early-issued reductions, deferred gathers
+        self.use_group = {}
+        self.defer_gathers = False
+        self._early = {}
+        self._pending = {}
+        self._meta = None
 
     def use_peer_reduce_scatter(self, reducer, covered):
         self.p2p, self.p2p_params = reducer, frozenset(covered)
+
+    # -------------------------------------------------------------- overlap
+    def overlap_with(self, model):
+        """Reduce each layer's gradients during the backward and let the next forward wait for each
+        layer's gathered parameters (no effect on one rank).  Needs the model's fused trunk."""
+        st = model.fused_state()
+        self.use_group = {p: g for g, ps in st.use_groups().items() for p in ps}
+        self.defer_gathers = True
+        st.optimizer = self
+
+    def _param_meta(self):
+        """parameter -> ('adamw', group) or ('muon', group, index in its group)."""
+        if self._meta is None:
+            meta = {}
+            for group in self.param_groups:
+                for i, p in enumerate(group["params"]):
+                    meta[p] = (group["kind"], group, i)
+            self._meta = meta
+        return self._meta
+
+    def issue_reduce(self, params):
+        """Start the reductions of ``params`` now (their gradients are final for this update)."""
+        rank, world = self._dist()
+        if world == 1:
+            return
+        meta = self._param_meta()
+        for p in params:
+            if p in self._early or p in self.p2p_params or p not in meta:
+                continue
+            kind, group, i = meta[p]
+            if kind == "adamw":
+                self._early[p] = self._adamw_issue(p, rank, world)
+            else:
+                chunk = math.ceil(len(group["params"]) / world)
+                self._early[p] = self._muon_issue(p, min(i // chunk, world - 1))
+
+    def wait_gathers(self, group):
+        """Make the current stream wait for the gathers of forward-use group ``group`` and refresh
+        those parameters' bf16 shadows."""
+        items = self._pending.pop(group, None)
+        if not items:
+            return
+        for kind, p, item in items:
+            if kind != "shadow":
+                item.wait()
+        for kind, p, item in items:
+            if kind == "shadow":
+                item.copy_(p.data)
+
+    def flush(self):
+        """Wait for every outstanding parameter gather (all groups, in use order)."""
+        for group in sorted(self._pending):
+            self.wait_gathers(group)
+
+    def state_dict(self):
+        self.flush()
+        return super().state_dict()
 
     def use_peer_gather(self, gather, covered):
         """Parameters in ``covered`` (fp32 masters in a symmetric arena) are all-gathered, shadows
@@ -120,28 +213,25 @@ class MuonAdamW(torch.optim.Optimizer):
         return st
 
     # -------------------------------------------------------------- AdamW
+    def _adamw_issue(self, p, rank, world):
+        """(param, row slice or None, reduce work handle, reduced grad slice) of one parameter."""
+        g = grad_of(p)
+        if g is None:
+            raise RuntimeError("missing gradient in the fixed training graph")
+        if world == 1:
+            return (p, None, None, g)
+        if p in self.p2p_params:
+            n = p.shape[0] // world   # this rank's rows were averaged in place by the peer kernel
+            return (p, slice(rank * n, (rank + 1) * n), None, g[slice(rank * n, (rank + 1) * n)])
+        if p.numel() < 1024 or p.shape[0] % world:
+            return (p, None, dist.all_reduce(g, op=dist.ReduceOp.AVG, async_op=True), g)
+        n = p.shape[0] // world
+        out = torch.empty((n, *g.shape[1:]), device=g.device, dtype=g.dtype)
+        work = dist.reduce_scatter_tensor(out, g.contiguous(), op=dist.ReduceOp.AVG, async_op=True)
+        return (p, slice(rank * n, (rank + 1) * n), work, out)
+
     def _adamw_plan(self, group, rank, world):
-        """(param, row slice or None, reduce work handle, reduced grad slice) per parameter."""
-        plans = []
-        for p in group["params"]:
-            g = grad_of(p)
-            if g is None:
-                raise RuntimeError("missing gradient in the fixed training graph")
-            if world == 1:
-                plans.append((p, None, None, g))
-            elif p in self.p2p_params:
-                n = p.shape[0] // world   # this rank's rows were averaged in place by the peer kernel
-                rows = slice(rank * n, (rank + 1) * n)
-                plans.append((p, rows, None, g[rows]))
-            elif p.numel() < 1024 or p.shape[0] % world:
-                work = dist.all_reduce(g, op=dist.ReduceOp.AVG, async_op=True)
-                plans.append((p, None, work, g))
-            else:
-                n = p.shape[0] // world
-                out = torch.empty((n, *g.shape[1:]), device=g.device, dtype=g.dtype)
-                work = dist.reduce_scatter_tensor(out, g.contiguous(), op=dist.ReduceOp.AVG, async_op=True)
-                plans.append((p, slice(rank * n, (rank + 1) * n), work, out))
-        return plans
+        return [self._early.pop(p, None) or self._adamw_issue(p, rank, world) for p in group["params"]]
 
     def _adamw_apply(self, group, plans, world, gathers):
         b1, b2 = group["betas"]
@@ -166,8 +256,8 @@ class MuonAdamW(torch.optim.Optimizer):
                 adamw_reference(pv, gv, st["exp_avg"], st["exp_avg_sq"], st["step"], group["lr"], b1, b2,
                                 group["eps"], group["weight_decay"])
             if rows is not None and p not in self.gather_params:
-                gathers.append(("adamw", p, dist.all_gather_into_tensor(p.data, p.data[rows].contiguous(),
-                                                                          async_op=True)))
+                gathers.append(("adamw", p, lambda p=p, rows=rows: dist.all_gather_into_tensor(
+                    p.data, p.data[rows].contiguous(), async_op=True)))
 
     # -------------------------------------------------------------- Muon
     def _muon_owned(self, group, rank, world):
@@ -175,6 +265,10 @@ class MuonAdamW(torch.optim.Optimizer):
         chunk = math.ceil(len(params) / world)
         lo = rank * chunk
         return params, chunk, list(range(lo, min(lo + chunk, len(params))))
+
+    @staticmethod
+    def _muon_issue(p, owner):
+        return dist.reduce(grad_of(p), dst=owner, op=dist.ReduceOp.SUM, async_op=True)
 
     def _muon_reduce(self, group, rank, world):
         params, chunk, _ = self._muon_owned(group, rank, world)
@@ -184,8 +278,8 @@ class MuonAdamW(torch.optim.Optimizer):
         for i, p in enumerate(params):
             if p in self.p2p_params:
                 continue
-            works.append(dist.reduce(grad_of(p), dst=min(i // chunk, world - 1), op=dist.ReduceOp.SUM,
-                                     async_op=True))
+            work = self._early.pop(p, None)
+            works.append(work if work is not None else self._muon_issue(p, min(i // chunk, world - 1)))
         return works
 
     def _muon_apply(self, group, rank, world, works, gathers):
@@ -227,7 +321,7 @@ class MuonAdamW(torch.optim.Optimizer):
                 if p in self.gather_params:
                     continue
                 src = min(i // chunk, world - 1)
-                gathers.append(("muon", p, dist.broadcast(p.data, src=src, async_op=True)))
+                gathers.append(("muon", p, lambda p=p, src=src: dist.broadcast(p.data, src=src, async_op=True)))
                 if p in self.shadows:
                     gathers.append(("shadow", p, self.shadows[p]))
 
@@ -293,6 +387,7 @@ class MuonAdamW(torch.optim.Optimizer):
     # -------------------------------------------------------------- step
     @torch.no_grad()
     def step(self):
+        self.flush()
         rank, world = self._dist()
         if self.p2p is not None and world > 1:
             self.p2p()
@@ -310,12 +405,16 @@ class MuonAdamW(torch.optim.Optimizer):
                 self._adamw_apply(group, plan, world, gathers)
             else:
                 self._muon_apply(group, rank, world, plan, gathers)
-        for kind, p, item in gathers:
-            if kind == "shadow":
-                continue
-            item.wait()
-        for kind, p, item in gathers:
-            if kind == "shadow":
-                item.copy_(p.data)
+        if self._early:
+            raise RuntimeError("a reduction was started for a parameter outside the optimizer's groups")
+        # gathers start after every update, in the order the next forward uses the parameters
+        order = sorted(range(len(gathers)), key=lambda j: (self.use_group.get(gathers[j][1], -1), j))
+        pending = {}
+        for j in order:
+            kind, p, item = gathers[j]
+            pending.setdefault(self.use_group.get(p, -1), []).append((kind, p, item if kind == "shadow" else item()))
+        self._pending = pending
+        if not self.defer_gathers:
+            self.flush()
         if self.gather is not None and world > 1:
             self.gather()

@@ -1,10 +1,13 @@
 """Expert parallelism for ``models.moe.MoEFFN``.
 
-With an expert-parallel group of size E_p, rank r holds experts [r E/E_p, (r+1) E/E_p).  Each
-rank routes its own tokens; every (token, expert) assignment is processed by the expert's owner
-and the weighted outputs are summed back per token on the token's rank.  Gradients of expert
-weights are local to their owner; the dense and router parameters are reduced over the
-data-parallel group as usual.
+With an expert-parallel group of size E_p, rank r holds experts [r E/E_p, (r+1) E/E_p) and no
+others: ``enable_expert_parallel`` drops the other experts' modules, so each rank stores only its
+own shard (the kept experts keep their global names in the state dict).  Each rank routes its own
+tokens; every (token, expert) assignment is processed by the expert's owner and the weighted
+outputs are summed back per token on the token's rank.  Gradients of expert weights are local to
+their owner; ``expert_data_parallel_groups`` gives the groups over which copies of one expert
+shard (one per expert-parallel group) average their gradients, and the dense and router
+parameters are reduced over the whole data-parallel group as usual.
 
 Two exchanges implement this:
 
@@ -44,7 +47,8 @@ def all_to_all(x, send_counts, recv_counts, group=None):
 
 
 def enable_expert_parallel(model, group=None):
-    """Shard every MoE layer's experts over `group`; returns the number of local experts."""
+    """Shard every MoE layer's experts over `group` (this rank keeps only its own experts); returns
+    the number of local experts.  Call before the optimizer and the kernel state are built."""
     from nexttransformer_b200.models.moe import MoEFFN
     size = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -53,14 +57,28 @@ def enable_expert_parallel(model, group=None):
         if isinstance(m, MoEFFN):
             if m.num_experts % size:
                 raise ValueError("experts must divide evenly over the expert-parallel group")
+            if m._w_fc is not None:
+                raise RuntimeError("enable expert parallelism before building the kernel state")
             per = m.num_experts // size
             m.ep_group, m.ep_rank, m.ep_size, m.ep_per = group, rank, size, per
-            for i, e in enumerate(m.experts):
+            m.keep_experts(rank * per, per)
+            for e in m.local_experts():
                 for p in e.parameters():
-                    p.requires_grad_(rank * per <= i < (rank + 1) * per)
-                    p.expert_owner = i // per
+                    p.expert_owner = rank
+                    p.expert_parallel = True
             local = per
     return local
+
+
+def expert_data_parallel_groups(world, ep_size):
+    """Rank lists of the expert-data-parallel groups: ranks holding the same expert shard.
+
+    With ``world = ep_size * dp`` ranks laid out as consecutive expert-parallel groups
+    (ranks [g ep_size, (g + 1) ep_size) form group g), shard s is held by ranks s, s + ep_size, ...
+    (the reference's Megatron ``expt_dp`` groups, ``nexttransformer/scaling/megatron_optimizer.py``)."""
+    if ep_size <= 0 or world % ep_size:
+        raise ValueError("the expert-parallel size must divide the world size")
+    return [list(range(s, world, ep_size)) for s in range(ep_size)]
 
 
 def expert_parallel_combine(moe, rows, choice, w):
@@ -87,7 +105,7 @@ def expert_parallel_combine(moe, rows, choice, w):
     outs, start = [], 0
     for e, n in enumerate(counts):
         if n:
-            outs.append(moe.experts[me * per + e](xin[start:start + n]))
+            outs.append(moe.expert(me * per + e)(xin[start:start + n]))
         start += n
     y = torch.cat(outs) if outs else xin[:0]
     back = torch.empty_like(y).index_copy(0, srt, y) if y.shape[0] else y
@@ -187,7 +205,7 @@ def _owner_tables(cnt, me, per):
 
 class _PeerExperts(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, w_fc, w_proj, choice, ex, per):
+    def forward(ctx, x, w, w_fc, w_proj, choice, ex, per, state):
         from nexttransformer_b200.ops._ext import ext
         lib = ext()
         T, k = choice.shape
@@ -221,7 +239,7 @@ class _PeerExperts(torch.autograd.Function):
         lib.moe_combine(ex.ret[:n], send_row_of, w32, None, out)
         y_rows = ex.ret[:n].clone()
         ctx.save_for_backward(x_perm, h_pre, h, wf, wp, src_rank, src_row, grp_m, grp_k, send_row_of, w32, y_rows)
-        ctx.ex, ctx.P = ex, P
+        ctx.ex, ctx.P, ctx.state = ex, P, state
         ctx.dtypes = (x.dtype, w.dtype, w_fc.dtype, w_proj.dtype)
         return out.to(x.dtype)
 
@@ -240,8 +258,12 @@ class _PeerExperts(torch.autograd.Function):
         dw = torch.empty_like(w32)
         lib.moe_combine_bwd(dy, y_rows, send_row_of, w32, ex.send[:n], dw)
         ex.barrier()                                       # weighted output gradients are in the send buffers
-        dwf = torch.zeros(E_loc, F, d, device=dev, dtype=torch.float32)
-        dwp = torch.zeros(E_loc, d, F, device=dev, dtype=torch.float32)
+        state = ctx.state
+        if state is not None:      # accumulate straight into the experts' main_grad stacks
+            dwf, dwp = state._g_fc, state._g_proj
+        else:
+            dwf = torch.zeros(E_loc, F, d, device=dev, dtype=torch.float32)
+            dwp = torch.zeros(E_loc, d, F, device=dev, dtype=torch.float32)
         if P:
             d_rows = torch.empty(P, d, device=dev, dtype=torch.bfloat16)
             lib.moe_pull_rows(ex.send_peers, src_rank, src_row, d_rows)
@@ -256,21 +278,25 @@ class _PeerExperts(torch.autograd.Function):
         dx = torch.empty(T, d, device=dev, dtype=torch.bfloat16)
         lib.moe_combine(ex.ret[:n], send_row_of, None, None, dx)
         xd, wd, fd, pd = ctx.dtypes
-        return dx.to(xd), dw.view(T, -1).to(wd), dwf.to(fd), dwp.to(pd), None, None, None
+        if state is not None:
+            return dx.to(xd), dw.view(T, -1).to(wd), None, None, None, None, None, None
+        return dx.to(xd), dw.view(T, -1).to(wd), dwf.to(fd), dwp.to(pd), None, None, None, None
 
 
 def peer_expert_combine(moe, rows, choice, w):
     """Routed-expert output for `rows` [T, d] (CUDA) through the peer-memory exchange."""
     per, me = moe.ep_per, moe.ep_rank
     ex = peer_exchange(moe, choice.numel(), rows.shape[-1], rows.device)
-    local = moe.experts[me * per:(me + 1) * per]
+    if moe._w_fc is not None:     # kernel state: stacked bf16 shadows, gradients into main_grad
+        return _PeerExperts.apply(rows, w, moe._w_fc, moe._w_proj, choice, ex, per, moe)
+    local = moe.local_experts()
     w_fc = torch.stack([e.c_fc.weight for e in local])
     w_proj = torch.stack([e.c_proj.weight for e in local])
-    return _PeerExperts.apply(rows, w, w_fc, w_proj, choice, ex, per)
+    return _PeerExperts.apply(rows, w, w_fc, w_proj, choice, ex, per, None)
 
 
 def peer_exchange_supported(moe, rows):
-    if not rows.is_cuda or rows.shape[-1] % 64 or moe.experts[0].c_fc.weight.shape[0] % 64:
+    if not rows.is_cuda or rows.shape[-1] % 64 or moe.local_experts()[0].c_fc.weight.shape[0] % 64:
         return False
     try:
         import torch.distributed._symmetric_memory  # noqa: F401

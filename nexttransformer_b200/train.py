@@ -153,7 +153,7 @@ def main(argv=None):
     model.set_sparse_backend(args.sparse_backend)
     stage = model.set_training_stage(0)
     shadows = {}
-    if device.type == "cuda" and model.fused_supported():
+    if device.type == "cuda":    # every eligible projection on the sm_100a GEMM engine
         shadows = {p: s for p, s in model.fused_state().casts}
     optimizer = MuonAdamW(protocol_groups(model, train), shadows=shadows)
     budget = BudgetState()

@@ -33,13 +33,28 @@ class Trainer:
             set_schedule(self.optimizer, self.step_index, self.train_config)
         self.zero_grad()
         total = torch.zeros((), device=self.device, dtype=torch.float32)
-        for x, y in zip(inputs, targets):
+        st = getattr(self.model, "_fused", None)
+        n = len(inputs)
+        for j, (x, y) in enumerate(zip(inputs, targets)):
+            if st is not None:
+                st.final_micro = j == n - 1    # the last backward may start the gradient reductions
             loss = self.model(x, y)
             (loss / self.accumulation).backward()
             total += loss.detach().float()
+        if st is not None:
+            st.final_micro = False
         self.optimizer.step()
+        if hasattr(self.model, "update_router_bias"):
+            self.model.update_router_bias()     # MoE aux-loss-free balancing, once per update
         self.step_index += 1
         return total / self.accumulation
+
+    def flush(self):
+        """Wait (on the current stream) for the parameter gathers the last update left running
+        under the next forward; call before reading parameters outside the training step."""
+        flush = getattr(self.optimizer, "flush", None)
+        if flush is not None:
+            flush()
 
     def step(self, inputs, targets):
         """One update from host (pinned) micro-batches; returns the mean loss as a Python float."""

@@ -41,7 +41,8 @@ def _ep_worker(rank, world, port, q):
     own = [i for i in range(4) if i // 2 == rank]
     g_all = torch.stack([ref.experts[i].c_fc.weight.grad for i in range(4)])
     dist.all_reduce(g_all)
-    g_ep = torch.cat([ep.experts[i].c_fc.weight.grad.flatten() for i in own])
+    assert len(ep.local_experts()) == 2     # only this rank's experts are held
+    g_ep = torch.cat([ep.expert(i).c_fc.weight.grad.flatten() for i in own])
     g_ref = torch.cat([g_all[i].flatten() for i in own])
     q.put((rank, fwd, dx, (g_ep - g_ref).abs().max().item()))
     dist.destroy_process_group()
@@ -151,3 +152,57 @@ def test_param_segments_keep_bf16_tables_out():
     got = {id(p) for *_, p, _ in psegs}
     assert id(table) not in got and {id(head), id(mats[0]), id(mats[1])} <= got
     assert len([s for s in psegs if s[3] is head]) == 2    # one row shard per owner
+
+
+def _overlap_worker(rank, port, results):
+    """Early per-group reductions and deferred, use-ordered gathers give the same update."""
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+
+    def make():
+        torch.manual_seed(0)
+        ps = [torch.nn.Parameter(torch.randn(64, 32)), torch.nn.Parameter(torch.randn(3)),
+              *[torch.nn.Parameter(torch.randn(32, 32)) for _ in range(3)], torch.nn.Parameter(torch.randn(48, 32))]
+        groups = [dict(kind="adamw", params=[ps[0], ps[1], ps[5]], lr=1e-2, betas=(0.9, 0.95), eps=1e-10,
+                       weight_decay=0.01),
+                  dict(kind="muon", params=ps[2:5], lr=2e-2, momentum=0.95, ns_steps=5, beta2=0.9, weight_decay=0.1)]
+        return ps, groups
+    ref_p, ref_g = make()
+    ov_p, ov_g = make()
+    ref, ov = MuonAdamW(ref_g), MuonAdamW(ov_g)
+    # forward-use groups: -1 the small vector, 0 two matrices and the table, 1 the rest
+    ov.use_group = {ov_p[1]: -1, ov_p[0]: 0, ov_p[2]: 0, ov_p[3]: 0, ov_p[4]: 1, ov_p[5]: 1}
+    ov.defer_gathers = True
+    for step in range(3):
+        g = torch.Generator().manual_seed(100 * step + rank)
+        local = [torch.randn(p.shape, generator=g) for p in ref_p]
+        for p, x in zip(ref_p, local):
+            p.grad = x.clone()
+        for p, x in zip(ov_p, local):
+            p.grad = x.clone()
+        ov.issue_reduce([ov_p[4], ov_p[0]])      # as the backward would, layer by layer
+        ov.issue_reduce([ov_p[2], ov_p[3]])
+        ref.step()
+        ov.step()
+        assert set(ov._pending) <= {-1, 0, 1}
+        for group in (-1, 0, 1):                 # as the next forward would
+            ov.wait_gathers(group)
+        assert not ov._pending
+    results[rank] = max(float((a - b).abs().max()) for a, b in zip(ref_p, ov_p))
+    dist.destroy_process_group()
+
+
+def test_overlapped_reduce_and_deferred_gathers_match():
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.start_processes(_overlap_worker, args=(port, results), nprocs=2, start_method="spawn")
+        assert results[0] == 0.0 and results[1] == 0.0, dict(results)
