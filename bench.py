@@ -37,7 +37,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-BASELINE_TOKS = None  # BASELINE.md publishes no number for this configuration
+BASELINE_TOKS = None  # the reference publishes no number for this configuration
 MODEL = dict(sequence_len=2048, vocab_size=65536, n_layer=20, n_head=10, n_kv_head=5, n_embd=1280,
              window_pattern="L")
 GLOBAL_BATCH = 524288

@@ -17,7 +17,7 @@ from pathlib import Path
 
 REPO = Path(__file__).resolve().parents[2]
 PKG = "nexttransformer_b200/"
-NO_TESTS = ("profiles/", "README.md", "DESIGN.md", "docs/")
+NO_TESTS = ("profiles/", "docs/")      # plus every top-level Markdown file (prose only)
 GPU = (PKG + "csrc/", PKG + "ops/", PKG + "models/fused_dense.py", PKG + "optim/muon_adamw.py", PKG + "build.py")
 CONTRACT = (PKG + "protocol/", PKG + "evaluation/", PKG + "training/", PKG + "runtime/", PKG + "train.py",
             PKG + "evaluate.py", PKG + "optim/", PKG + "models/shell.py", PKG + "models/lm.py", PKG + "models/config.py")
@@ -52,7 +52,7 @@ def affected_methods(paths):
 
 def classify(paths):
     paths = list(paths)
-    return dict(tests=any(not p.startswith(NO_TESTS) for p in paths),
+    return dict(tests=any(not (p.startswith(NO_TESTS) or ("/" not in p and p.endswith(".md"))) for p in paths),
                 gpu=any(p.startswith(GPU) for p in paths),
                 contract=sorted(p for p in paths if p.startswith(CONTRACT)),
                 affected=affected_methods(paths))

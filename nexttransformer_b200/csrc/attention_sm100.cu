@@ -50,6 +50,7 @@ struct Params {
   float* dq_acc;
   const float* delta;
   long long* trace;
+  int dq_slices;  // 0: dQ added into one fp32 buffer (bulk reductions); else one slice per key tile
 };
 
 // Clock stamp of (role, pair, event) for the first CTA when a trace buffer is given.
@@ -745,8 +746,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         mbar_arrive(stg_full);
         if (leader) {
           if (mbar_wait(stg_full, (2 * it + half) & 1, 0x7Bu, abort_flag)) {
-            tma_reduce_add_3d(&tmDQ, stg, h * HD + half * 64, q0, b);
-            tma_reduce_add_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, b);
+            if (p.dq_slices) {
+              // deterministic mode: this key tile's contribution goes to its own slice (plain stores);
+              // the convert kernel sums the slices in key-tile order
+              const int z = kt * p.B + b;
+              tma_store_3d(&tmDQ, stg, h * HD + half * 64, q0, z);
+              tma_store_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, z);
+            } else {
+              tma_reduce_add_3d(&tmDQ, stg, h * HD + half * 64, q0, b);
+              tma_reduce_add_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, b);
+            }
             tma_store_commit();
             tma_store_wait_read0();
             stamp(p, 3, it, 2 + 2 * half);
@@ -813,14 +822,20 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t l
   }
 }
 
-// dq (bf16, strided rows) = dq_acc (fp32 [B*T, H*128])
+// dq (bf16, strided rows) = sum over `slices` slices of dq_acc (fp32 [slices][B*T, H*128]), in slice
+// order (one slice: a plain conversion)
 __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t lddq,
-                                       int64_t rows, int cols) {
+                                       int64_t rows, int cols, int slices) {
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-  if (i >= rows * cols) return;
+  const int64_t n = rows * cols;
+  if (i >= n) return;
   const int64_t r = i / cols;
   const int c = static_cast<int>(i - r * cols);
-  const float4 v = *reinterpret_cast<const float4*>(acc + i);
+  float4 v = *reinterpret_cast<const float4*>(acc + i);
+  for (int s = 1; s < slices; ++s) {
+    const float4 u = *reinterpret_cast<const float4*>(acc + s * n + i);
+    v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+  }
   uint2 w = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
   *reinterpret_cast<uint2*>(dq + r * lddq + c) = w;
 }
@@ -920,8 +935,11 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tk = tile_map(a.k, static_cast<int64_t>(a.Hk) * HD, a.ldk, a.T, a.B);
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
   CUtensorMap tdo = tile_map(a.dout, static_cast<int64_t>(a.H) * HD, a.lddo, a.T, a.B);
-  CUtensorMap tdq = dq_map(a.dq_acc, static_cast<int64_t>(a.H) * HD, a.T, a.B);
+  const int n_kt = (a.T + TILE - 1) / TILE;
+  if (a.dq_slices && a.dq_slices != n_kt) return -1;
+  CUtensorMap tdq = dq_map(a.dq_acc, static_cast<int64_t>(a.H) * HD, a.T, a.dq_slices ? a.B * n_kt : a.B);
   Params p = make_params(a);
+  p.dq_slices = a.dq_slices;
   p.dout = reinterpret_cast<const __nv_bfloat16*>(a.dout);
   p.lddo = a.lddo;
   p.dk = reinterpret_cast<__nv_bfloat16*>(a.dk);
@@ -938,7 +956,7 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   const int cols = a.H * HD;
   const int64_t n = rows * cols;
   attn_dq_convert_kernel<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, s>>>(
-      a.dq_acc, reinterpret_cast<__nv_bfloat16*>(a.dq), a.lddq, rows, cols);
+      a.dq_acc, reinterpret_cast<__nv_bfloat16*>(a.dq), a.lddq, rows, cols, a.dq_slices ? a.dq_slices : 1);
   return 0;
 }
 

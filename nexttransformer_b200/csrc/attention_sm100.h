@@ -26,7 +26,11 @@ struct AttnArgs {
   void* dk = nullptr;
   void* dv = nullptr;
   int64_t lddq = 0, lddk = 0, lddv = 0;
-  float* dq_acc = nullptr;  // fp32 [B*T, H*D] workspace
+  float* dq_acc = nullptr;  // fp32 [B*T, H*D] workspace (zeroed), or [dq_slices][B*T, H*D] (zeroed)
+  // 0: dQ contributions of the key tiles are added into dq_acc with bulk reductions (order not
+  // fixed); ceil(T / 128): deterministic mode, one slice per key tile written with plain stores
+  // and summed in key-tile order by the conversion
+  int dq_slices = 0;
   float* delta = nullptr;   // fp32 [B, H, T] workspace
   // Optional pipeline trace of the first CTA (int64 [4 roles][64 pairs][8 events] of SM clock
   // stamps; zero-filled by the caller).  Diagnostics only.

@@ -287,8 +287,10 @@ void attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o
 void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
               const Tensor& dout, const Tensor& dq, const Tensor& dk, const Tensor& dv, const Tensor& dq_acc,
               const Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window,
-              double scale, const OptT& trace) {
+              double scale, const OptT& trace, int64_t dq_slices) {
   AttnArgs a = attn_args(q, k, v, o, lse, B, T, H, Hk, D, window, scale);
+  a.dq_slices = static_cast<int>(dq_slices);
+  TORCH_CHECK(dq_acc.numel() >= (dq_slices ? dq_slices : 1) * B * T * H * D, "dq_acc too small");
   a.dout = dout.data_ptr(); a.lddo = dout.stride(-2);
   a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr();
   a.lddq = dq.stride(-2); a.lddk = dk.stride(-2); a.lddv = dv.stride(-2);
@@ -747,6 +749,8 @@ std::vector<int64_t> read_comm_errors() {
   return {c, static_cast<int64_t>(w)};
 }
 
+void clear_comm_errors() { ok(nt_comm_clear_error(), "clear_comm_errors"); }
+
 std::vector<int64_t> read_errors() {
   unsigned w = 0;
   const int g = nt_gemm_read_error(&w);
@@ -783,7 +787,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"), py::arg("delta"), py::arg("B"),
         py::arg("T"), py::arg("H"), py::arg("Hk"), py::arg("D"), py::arg("window"), py::arg("scale"),
-        py::arg("trace") = py::none());
+        py::arg("trace") = py::none(), py::arg("dq_slices") = 0);
   m.def("read_errors", &read_errors);
   m.def("gemm_ce_fwd", &gemm_ce_fwd);
   m.def("p2p_reduce_scatter", &p2p_reduce_scatter);
@@ -795,6 +799,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_attn_bwd", &sparse_attn_bwd);
   m.def("moe_gather_rows", &moe_gather_rows);
   m.def("p2p_barrier", &p2p_barrier);
+  m.def("clear_comm_errors", &clear_comm_errors, "reset the peer-collective error word");
   m.def("p2p_put", &p2p_put);
   m.def("p2p_gather", &p2p_gather);
   m.def("moe_combine", &moe_combine);

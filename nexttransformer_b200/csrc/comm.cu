@@ -180,3 +180,8 @@ int nt_comm_read_error(unsigned* where) {
   if (where) *where = w.where;
   return static_cast<int>(w.code);
 }
+
+int nt_comm_clear_error() {
+  const nt::ErrorWord zero{0, 0};
+  return cudaMemcpyToSymbol(nt::g_nt_error, &zero, sizeof(zero)) == cudaSuccess ? 0 : -2;
+}

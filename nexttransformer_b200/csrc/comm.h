@@ -23,3 +23,5 @@ int nt_p2p_barrier(const uint64_t* pads_dev, int rank, int world, uint32_t epoch
 int nt_p2p_put(const uint64_t* peers_dev, int world, int64_t dst_off, const void* src, int64_t nbytes,
                cudaStream_t stream);
 int nt_comm_read_error(unsigned* where);
+// Reset the error word after the host has handled a recorded failure (synchronous).
+int nt_comm_clear_error();

@@ -20,6 +20,7 @@ from torch.autograd import Function
 from nexttransformer_b200.ops import gemm as G
 from nexttransformer_b200.ops._ext import ext
 from nexttransformer_b200.ops.attention import attention_fn
+from nexttransformer_b200.utils.trace import nvtx_range
 
 # Cross-entropy kernel variant (0: automatic, 1: two-pass); kept selectable for numerics checks.
 CE_VARIANT = 0
@@ -221,16 +222,21 @@ class FusedState:
         """Called by the backward once group ``group``'s kernel-written gradients are final
         (``tables``: the layer's value-embedding table included)."""
         if self.final_micro and self.optimizer is not None:
-            model = self.model
-            skip = set() if tables or str(group) not in model.value_embeds else \
-                {id(model.value_embeds[str(group)].weight)}
-            self.optimizer.issue_reduce([p for p in self.use_groups()[group] if getattr(p, "main_grad", None)
-                                         is not None and p.requires_grad and id(p) not in skip])
+            with nvtx_range(f"group{group}.reduce_issue"):
+                self._issue(group, tables)
+
+    def _issue(self, group, tables):
+        model = self.model
+        skip = set() if tables or str(group) not in model.value_embeds else \
+            {id(model.value_embeds[str(group)].weight)}
+        self.optimizer.issue_reduce([p for p in self.use_groups()[group] if getattr(p, "main_grad", None)
+                                     is not None and p.requires_grad and id(p) not in skip])
 
     def params_needed(self, group):
         """Called by the forward before it reads group ``group``'s parameters."""
         if self.optimizer is not None:
-            self.optimizer.wait_gathers(group)
+            with nvtx_range(f"group{group}.gather_wait"):
+                self.optimizer.wait_gathers(group)
 
     @staticmethod
     def _loose(model):
@@ -503,16 +509,12 @@ def fused_forward(model, idx, targets, reduction="mean"):
     (linear, sparse, MLA) or FFN (MoE) runs its own forward between the kernel mix+RMSNorm and
     a residual add, with its projections on the GEMM engine (``ops.dense``).  fp32 parameter
     gradients land in ``main_grad``."""
-    from nexttransformer_b200.models.shell import MLP
-    from nexttransformer_b200.ops.dense import MixNormFn, rms_norm, table_lookup
     cfg = model.shell
     B, T = idx.shape
     model.fused_state()
     idx_f = idx.reshape(-1).contiguous()
     tgt_f = targets.reshape(-1).contiguous()
-    d = cfg.n_embd
-    M = B * T
-    scratch = StepScratch(M, d, idx.device)
+    scratch = StepScratch(B * T, cfg.n_embd, idx.device)
     cos = model.cos[0, :T, 0].contiguous()
     sin = model.sin[0, :T, 0].contiguous()
     cos_sin = (model.cos[:, :T], model.sin[:, :T])
@@ -523,34 +525,45 @@ def fused_forward(model, idx, targets, reduction="mean"):
     n = cfg.n_layer
     backout = aux = None
     for i, blk in enumerate(model.transformer.h):
-        a, mlp = blk.attn, blk.mlp
-        st.params_needed(i)
-        window = model.layer_window(i)
-        with torch.no_grad():
-            ab = torch.stack((model.resid_lambdas[i], model.x0_lambdas[i])).float().contiguous()
-        if getattr(a, "_w_qkv", None) is not None:
-            xm, qkv = PreAttnFn.apply(x, x0, ab, a, model, scratch, idx_f, i, T, cos, sin)
-            y = attention_fn(qkv, B, T, a.n_head, a.n_kv_head, a.head_dim, window)
-            x = OutProjFn.apply(y, xm, a.c_proj)
-        else:
-            xm, h = MixNormFn.apply(x, x0, ab, model, scratch, i)
-            key = str(i)
-            ve = table_lookup(idx_f, model.value_embeds[key].weight).view(B, T, -1) \
-                if key in model.value_embeds else None
-            y = a(h.view(B, T, d), ve, cos_sin, (window, 0), None)
-            x = xm + y.reshape(M, d).to(xm.dtype)
-            part = getattr(a, "last_aux", None)
-            if torch.is_tensor(part):
-                aux = part if aux is None else aux + part
-        if type(mlp) is MLP and getattr(mlp.c_fc, "_g", None) is not None and not mlp.c_fc._kernel:
-            x = MLPFn.apply(x, mlp)
-        else:
-            h2 = rms_norm(x)
-            x = x + mlp(h2.view(B, T, d)).reshape(M, d).to(x.dtype)
-            part = getattr(mlp, "last_aux", None)
-            if torch.is_tensor(part):
-                aux = part if aux is None else aux + part
+        with nvtx_range(f"layer{i}.forward"):
+            x, aux = _layer_forward(model, st, i, blk, x, x0, aux, idx_f, B, T, cos, sin, cos_sin, scratch)
         if i == n // 2:
             backout = x
     st.params_needed(n)
-    return HeadLossFn.apply(x, backout, model, tgt_f, reduction), aux
+    with nvtx_range("head.forward"):
+        return HeadLossFn.apply(x, backout, model, tgt_f, reduction), aux
+
+
+def _layer_forward(model, st, i, blk, x, x0, aux, idx_f, B, T, cos, sin, cos_sin, scratch):
+    """One layer of ``fused_forward``: (new state, running auxiliary loss)."""
+    from nexttransformer_b200.models.shell import MLP
+    from nexttransformer_b200.ops.dense import MixNormFn, rms_norm, table_lookup
+    M, d = x.shape
+    a, mlp = blk.attn, blk.mlp
+    st.params_needed(i)
+    window = model.layer_window(i)
+    with torch.no_grad():
+        ab = torch.stack((model.resid_lambdas[i], model.x0_lambdas[i])).float().contiguous()
+    if getattr(a, "_w_qkv", None) is not None:
+        xm, qkv = PreAttnFn.apply(x, x0, ab, a, model, scratch, idx_f, i, T, cos, sin)
+        y = attention_fn(qkv, B, T, a.n_head, a.n_kv_head, a.head_dim, window)
+        x = OutProjFn.apply(y, xm, a.c_proj)
+    else:
+        xm, h = MixNormFn.apply(x, x0, ab, model, scratch, i)
+        key = str(i)
+        ve = table_lookup(idx_f, model.value_embeds[key].weight).view(B, T, -1) \
+            if key in model.value_embeds else None
+        y = a(h.view(B, T, d), ve, cos_sin, (window, 0), None)
+        x = xm + y.reshape(M, d).to(xm.dtype)
+        part = getattr(a, "last_aux", None)
+        if torch.is_tensor(part):
+            aux = part if aux is None else aux + part
+    if type(mlp) is MLP and getattr(mlp.c_fc, "_g", None) is not None and not mlp.c_fc._kernel:
+        x = MLPFn.apply(x, mlp)
+    else:
+        h2 = rms_norm(x)
+        x = x + mlp(h2.view(B, T, d)).reshape(M, d).to(x.dtype)
+        part = getattr(mlp, "last_aux", None)
+        if torch.is_tensor(part):
+            aux = part if aux is None else aux + part
+    return x, aux

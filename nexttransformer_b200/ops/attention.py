@@ -18,6 +18,22 @@ from nexttransformer_b200.models.shell import sdpa
 
 # Set by the kernel module once the tcgen05 path is validated for a (D, dtype) pair.
 KERNEL_HEAD_DIMS = (128,)
+# Deterministic backward: every key tile writes its dQ contribution to its own fp32 slice and the
+# slices are summed in key-tile order (bitwise reproducible; ceil(T / 128) x the dQ workspace).
+# Default: contributions are added into one buffer with bulk reductions whose order is not fixed.
+_deterministic = False
+
+
+def set_deterministic(on=True):
+    """Select the deterministic attention backward (the reference's ``--deterministic-attention``)."""
+    global _deterministic
+    _deterministic = bool(on)
+
+
+def _dq_workspace(M, cols, T, device):
+    """(zeroed fp32 dQ workspace, slice count) for the current backward mode."""
+    slices = (T + 127) // 128 if _deterministic else 0
+    return torch.zeros(max(slices, 1) * M, cols, device=device, dtype=torch.float32), slices
 
 
 def _use_kernel(qkv, D):
@@ -50,11 +66,11 @@ class _KernelAttn(Function):
         lib = ext()
         M = B * T
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.zeros(M, H * D, device=qkv.device, dtype=torch.float32)
+        dq_acc, slices = _dq_workspace(M, H * D, T, qkv.device)
         delta = torch.empty(B, H, T, device=qkv.device, dtype=torch.float32)
         lib.attn_bwd(qkv[:, :H * D], qkv[:, H * D:(H + Hk) * D], qkv[:, (H + Hk) * D:], o, lse, do.contiguous(),
                      dqkv[:, :H * D], dqkv[:, H * D:(H + Hk) * D], dqkv[:, (H + Hk) * D:], dq_acc, delta,
-                     B, T, H, Hk, D, w, 1.0 / math.sqrt(D))
+                     B, T, H, Hk, D, w, 1.0 / math.sqrt(D), None, slices)
         return dqkv, None, None, None, None, None, None
 
 
@@ -101,11 +117,11 @@ class _KernelAttnBTHD(Function):
         B, T, H, D = q.shape
         Hk = k.shape[2]
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        dq_acc = torch.zeros(B * T, H * D, device=q.device, dtype=torch.float32)
+        dq_acc, slices = _dq_workspace(B * T, H * D, T, q.device)
         delta = torch.empty(B, H, T, device=q.device, dtype=torch.float32)
         ext().attn_bwd(q.view(B * T, -1), k.view(B * T, -1), v.view(B * T, -1), o, lse,
                        do.contiguous().view(B * T, -1), dq.view(B * T, -1), dk.view(B * T, -1), dv.view(B * T, -1),
-                       dq_acc, delta, B, T, H, Hk, D, ctx.w, 1.0 / math.sqrt(D))
+                       dq_acc, delta, B, T, H, Hk, D, ctx.w, 1.0 / math.sqrt(D), None, slices)
         return dq, dk, dv, None
 
 

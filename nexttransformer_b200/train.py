@@ -7,8 +7,13 @@ Modes (reference: ``nexttransformer/train.py``):
   * ``--research`` (default): any configuration (file, ``--method`` candidate or debug scale),
     findings recorded in provenance; results are never admitted.
 Per update: schedule -> micro-batches (forward/backward; fused sm_100a path on CUDA) ->
-non-finite check -> Muon/AdamW step (gradients reduced to their owners) -> router-bias update ->
-budget charge -> events (``metrics.jsonl``) -> scheduled evaluation -> checkpoints.
+gradient norm (one multi-tensor norm) and the loss sums reduced over the ranks in ONE collective,
+read by the host once -> non-finite check -> Muon/AdamW step (gradients reduced to their owners)
+-> router-bias update -> budget charge and rolling cost-window check (``budget_anomaly``) ->
+events (``metrics.jsonl``; step time from CUDA events, maximum over ranks) -> scheduled
+evaluation (validation bits per byte on the protocol's schedule, CORE at the protocol's core
+steps) -> checkpoints.  A completed run ends with the final train / validation bits per byte,
+the final CORE score, ``budget.json`` and ``run_status.json`` with the budget's final status.
 Resume: ``--resume auto`` restarts from the newest complete checkpoint (incomplete ones are moved
 aside, later events archived); ``--max-wall-hours`` ends a segment after a checkpoint; a
 non-finite loss or gradient records an event and exits with code 3.
@@ -56,6 +61,11 @@ def parse(argv=None):
     p.add_argument("--val-tokens", type=int, default=0)
     p.add_argument("--sparse-backend", choices=("reference", "kernel"), default="reference")
     p.add_argument("--log-every", type=int, default=1)
+    p.add_argument("--core", type=Path, help="CORE bundle (tasks.json + <label>.jsonl) scored at the core steps")
+    p.add_argument("--tokenizer", type=Path, help="tokenizer directory (default: <resources>/tokenizer)")
+    p.add_argument("--core-max-per-task", type=int, default=-1)
+    p.add_argument("--deterministic-attention", action="store_true",
+                   help="attention backward without atomics (dQ accumulated per query tile in a fixed order)")
     p.add_argument("--seed", type=int, default=42)
     args = p.parse_args(argv)
     from nexttransformer_b200.runtime.site import resolve
@@ -66,7 +76,26 @@ def parse(argv=None):
         p.error("--resume takes never or auto")
     if args.config is None and args.method is None:
         p.error("give --config or --method")
+    if not hasattr(args, "core_max_tokens"):
+        args.core_max_tokens = None
     return args
+
+
+def grad_norm_sq(params):
+    """Squared global gradient norm: one multi-tensor norm over the gradients (no copies)."""
+    from nexttransformer_b200.optim.muon_adamw import grad_of
+    grads = [g for g in (grad_of(p) for p in params) if g is not None]
+    if not grads:
+        return torch.zeros((), dtype=torch.float64)
+    by_dtype = {}
+    for g in grads:
+        by_dtype.setdefault((g.device, g.dtype), []).append(g)
+    total = None
+    for group in by_dtype.values():
+        norms = torch._foreach_norm(group)
+        part = torch.stack([n.double() for n in norms]).square().sum()
+        total = part if total is None else total + part
+    return total
 
 
 def load_model_config(args):
@@ -182,8 +211,49 @@ def main(argv=None):
     val_every = args.val_every or proto.val_every
     started = time.time()
     phase = None
+    dense_anchor = _dense_anchor(args)
+    if args.deterministic_attention:
+        from nexttransformer_b200.ops import attention as attention_ops
+        attention_ops.set_deterministic(True)
+    evaluator = _evaluator(args, model, config, train, rank, world, device, micro, stream_rank, stream_world)
+    window = []
+    start_ev = torch.cuda.Event(enable_timing=True) if device.type == "cuda" else None
+    end_ev = torch.cuda.Event(enable_timing=True) if device.type == "cuda" else None
     with start_tracker(out, rank, args.wandb_mode, dict(model=config.serialized()), device) as tracker:
         model.train()
+
+        def event(payload):
+            if rank == 0:
+                tracker.log(payload)
+
+        def scheduled_evaluations(step):
+            """Validation and CORE due after update ``step`` (formal: the protocol's schedule)."""
+            if args.formal:
+                due = events_at(step)
+                due_val = due["val"] and step not in budget.val_steps
+                due_core = due["core"] and not due["final"] and step not in budget.core_steps
+            else:
+                due_val = bool(args.val_tokens or args.data == "bestfit") and (step % val_every == 0 or step == stop)
+                due_core = evaluator.has_core and step in proto.core_steps and step < proto.steps
+            if due_val:
+                result = evaluator.validation(args.val_tokens or proto.val_tokens)
+                if args.formal:
+                    budget.record_eval("val")
+                payload = {"event": "validation", "step": step, **result}
+                if "bpb" in result:
+                    payload["val_bpb"] = result["bpb"]
+                event(payload)
+                if rank == 0:
+                    atomic_json(out / f"val_{step:08d}.json", payload)
+            if due_core and evaluator.has_core:
+                result = evaluator.core()
+                if args.formal:
+                    budget.record_eval("core")
+                payload = {"event": "core", "step": step, **result}
+                event(payload)
+                if rank == 0:
+                    atomic_json(out / f"core_{step:08d}.json", payload)
+
         for step in range(state["step"], stop):
             if config.method == "ouro":
                 stage = model.set_training_stage(step)
@@ -191,11 +261,13 @@ def main(argv=None):
             mult = set_schedule(optimizer, step, train)
             synchronize(device)
             t0 = time.time()
+            if start_ev is not None:
+                start_ev.record()
             for p in model.parameters():
                 p.grad = None
             if hasattr(model, "zero_main_grads"):
                 model.zero_main_grads()
-            totals = torch.zeros(3, device=device, dtype=torch.float64)  # lm loss sum, aux sum, tokens
+            totals = torch.zeros(5, device=device, dtype=torch.float64)  # lm, aux, tokens, |g|^2, non-finite
             for micro_i in range(accum):
                 x, y = stream.batch(micro, device)
                 if hasattr(model, "set_row_offset"):
@@ -203,27 +275,30 @@ def main(argv=None):
                 loss = model(x, y)
                 (loss / accum).backward()
                 lm = model.last_lm_loss if model.last_lm_loss is not None else loss.detach()
-                totals += torch.stack((lm.detach().double(), (loss.detach() - lm.detach()).double(),
-                                       torch.tensor(float(y.numel()), device=device, dtype=torch.float64)))
-            gsq = torch.zeros((), device=device, dtype=torch.float64)
-            for p in model.parameters():
-                g = grad_of(p)
-                if g is not None:
-                    gsq += g.double().pow(2).sum()
-            finite = torch.tensor([0. if torch.isfinite(gsq) and torch.isfinite(totals).all() else 1.], device=device)
-            reduce_max(finite)
-            reduce_sum(totals)
-            if finite.item():
+                totals[:3] += torch.stack((lm.detach().double(), (loss.detach() - lm.detach()).double(),
+                                           torch.full((), float(y.numel()), device=device, dtype=torch.float64)))
+            gsq = grad_norm_sq(model.parameters()).to(device)
+            totals[3] = gsq
+            totals[4] = (~torch.isfinite(gsq) | ~torch.isfinite(totals[:2]).all()).double()
+            reduce_sum(totals)            # one collective and one host read per update
+            lm_sum, aux_sum, tokens, gsq_all, bad = totals.tolist()
+            if bad:
                 if rank == 0:
-                    tracker.log({"event": "nonfinite", "step": step + 1, "lm_loss": float(totals[0] / (world * accum))})
+                    tracker.log({"event": "nonfinite", "step": step + 1, "lm_loss": lm_sum / (world * accum)})
                 phase = "nonfinite"
                 break
             optimizer.step()
             if hasattr(model, "update_router_bias"):
                 model.update_router_bias()
+            if end_ev is not None:
+                end_ev.record()
             synchronize(device)
             dt = time.time() - t0
-            tokens = int(totals[2].item())
+            if start_ev is not None:
+                dt_dev = torch.tensor([start_ev.elapsed_time(end_ev) / 1e3], device=device, dtype=torch.float64)
+                reduce_max(dt_dev)
+                dt = float(dt_dev.item())
+            tokens = int(tokens)
             if tokens != train.global_batch_tokens:
                 raise RuntimeError("training input-token budget drift")
             cost = stage_cost(proof, step)
@@ -231,23 +306,25 @@ def main(argv=None):
                 budget.advance(tokens, cost)
             state.update(step=step + 1, input_tokens=state["input_tokens"] + tokens,
                          training_seconds=state["training_seconds"] + dt, budget=budget.state_dict())
+            if cost is not None and dense_anchor:
+                window = (window + [cost])[-proto.val_every:]
+                rolling = sum(window) / (len(window) * proto.global_batch_tokens * dense_anchor) - 1
+                if len(window) == proto.val_every and abs(rolling) > proto.routing_warning:
+                    event({"event": "budget_anomaly", "step": step + 1, "rolling_relative_error": rolling})
             if rank == 0 and ((step + 1) % args.log_every == 0 or step + 1 == stop):
                 tracker.log({"event": "train", "step": step + 1, "input_tokens": state["input_tokens"],
-                             "lm_loss": float(totals[0] / (world * accum)), "aux_loss": float(totals[1] / (world * accum)),
-                             "grad_norm": float(gsq.sqrt()) if world == 1 else None, "lr_multiplier": mult,
+                             "lm_loss": lm_sum / (world * accum), "aux_loss": aux_sum / (world * accum),
+                             "grad_norm": math.sqrt(gsq_all) if world == 1 else None,
+                             "grad_norm_rank_sum_sq": gsq_all, "lr_multiplier": mult,
                              "stage": stage, "step_seconds": dt, "tokens_per_second": tokens / dt,
                              "theory_flops": cost})
             done = step + 1 == stop
-            if args.val_tokens and ((step + 1) % val_every == 0 or done):
-                from nexttransformer_b200.evaluation.bpb import evaluate_stream_loss
-                result = evaluate_stream_loss(model, config, args.val_tokens, micro, rank, world, device, args.seed)
-                if rank == 0:
-                    tracker.log({"event": "validation", "step": step + 1, **result})
-                    atomic_json(out / f"val_{step + 1:08d}.json", {"step": step + 1, **result})
+            scheduled_evaluations(step + 1)
             wall_up = args.max_wall_hours and (time.time() - started) / 3600 >= args.max_wall_hours
             protocol_ckpt = args.checkpoint_every and (step + 1) % args.checkpoint_every == 0
-            rolling = args.rolling_every and (step + 1) % args.rolling_every == 0
-            if protocol_ckpt or rolling or done or wall_up:
+            rolling_ckpt = args.rolling_every and (step + 1) % args.rolling_every == 0
+            if protocol_ckpt or rolling_ckpt or done or wall_up:
+                optimizer.flush()
                 ckpt.save_checkpoint(out, model, optimizer, stream, config, train, state, rank, world)
                 if rank == 0 and args.rolling_keep:
                     keep = {s for s in ckpt.complete_checkpoints(out)
@@ -256,13 +333,49 @@ def main(argv=None):
             if wall_up and not done:
                 phase = "segment_end"
                 break
+        complete = phase is None and state["step"] == proto.steps
+        if complete:
+            # the final checkpoint precedes these evaluations; a resumed segment re-runs only them
+            final = evaluator.final(proto.final_bpb_tokens)
+            if rank == 0:
+                atomic_json(out / "bpb_final.json", final)
+            event({"event": "final_bpb", "step": proto.steps, "train": final["train"], "val": final["val"]})
+            if evaluator.has_core and (not args.formal or proto.steps not in budget.core_steps):
+                result = evaluator.core(final=True)
+                if args.formal:
+                    budget.record_eval("core")
+                if rank == 0:
+                    atomic_json(out / "core_final.json", {"step": proto.steps, **result})
+                event({"event": "core", "step": proto.steps, **result})
         if rank == 0:
-            atomic_json(out / "run_status.json", {"phase": phase or ("complete" if state["step"] == stop else "stopped"),
-                                                  **state})
+            budget_state = budget.state_dict()
+            atomic_json(out / "budget.json", {"step": state["step"], **budget_state,
+                                              "dense_flops_per_token": dense_anchor})
+            final_status = budget.final_status(dense_anchor) if args.formal and dense_anchor else None
+            atomic_json(out / "run_status.json", {
+                "phase": phase or ("training_complete" if complete else "stopped"), "final_status": final_status,
+                "evaluation_seconds": evaluator.seconds, **state})
     shutdown()
     if phase == "nonfinite":
         sys.exit(NONFINITE_EXIT)
     return state
+
+
+def _evaluator(args, model, config, train, rank, world, device, micro, stream_rank, stream_world):
+    """The run's evaluator: real-data bits per byte with ``--data bestfit``, CORE with ``--core``."""
+    from nexttransformer_b200.training.evals import RunEvaluator, load_core_bundle
+    tokenizer = tasks = None
+    data_dir = None
+    if args.data == "bestfit" or args.core:
+        from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+        tokenizer = BPETokenizer.from_directory(args.tokenizer or Path(args.resources) / "tokenizer")
+        data_dir = args.data_dir or Path(args.resources) / "base_data_climbmix"
+    if args.core:
+        tasks = load_core_bundle(args.core)
+    return RunEvaluator(model, config, rank=rank, world=world, device=device, micro=micro, data=args.data,
+                        data_dir=data_dir, tokenizer=tokenizer, core_tasks=tasks,
+                        core_max_tokens=args.core_max_tokens, core_max_per_task=args.core_max_per_task,
+                        seed=args.seed, stream_rank=stream_rank, stream_world=stream_world)
 
 
 def _rewind_events(out, step):

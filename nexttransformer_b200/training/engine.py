@@ -8,6 +8,7 @@ update applied by the optimizer, then the mean loss is read back to the host.
 import torch
 
 from nexttransformer_b200.optim.groups import set_schedule
+from nexttransformer_b200.utils.trace import nvtx_range
 
 
 class Trainer:
@@ -38,12 +39,15 @@ class Trainer:
         for j, (x, y) in enumerate(zip(inputs, targets)):
             if st is not None:
                 st.final_micro = j == n - 1    # the last backward may start the gradient reductions
-            loss = self.model(x, y)
-            (loss / self.accumulation).backward()
+            with nvtx_range(f"micro{j}.forward"):
+                loss = self.model(x, y)
+            with nvtx_range(f"micro{j}.backward"):
+                (loss / self.accumulation).backward()
             total += loss.detach().float()
         if st is not None:
             st.final_micro = False
-        self.optimizer.step()
+        with nvtx_range("optimizer.step"):
+            self.optimizer.step()
         if hasattr(self.model, "update_router_bias"):
             self.model.update_router_bias()     # MoE aux-loss-free balancing, once per update
         self.step_index += 1

@@ -45,3 +45,35 @@ def test_attention_forward_backward(B, T, H, Hk, window):
         e = (g[:, sl] - rg[:, sl]).abs().max().item()
         scale = rg[:, sl].abs().max().item()
         assert e <= 2e-2 + 2e-2 * scale, f"{name} max err {e} (scale {scale})"
+
+
+@pytest.mark.parametrize("B,T,H,Hk,window", [(2, 512, 4, 2, -1), (1, 700, 2, 1, 300)])
+def test_deterministic_backward_is_bitwise_reproducible(B, T, H, Hk, window):
+    """Deterministic mode: the same gradients bit for bit on every run, equal to the default mode's
+    within fp32 summation-order noise, and within the fp32 oracle's tolerance."""
+    from nexttransformer_b200.ops import attention as A
+    from nexttransformer_b200.ops._ext import check_errors
+    torch.manual_seed(3)
+    D = 128
+    M = B * T
+    qkv = (torch.randn(M, (H + 2 * Hk) * D, device="cuda") * 0.5).bfloat16()
+    dout = torch.randn(M, H * D, device="cuda").bfloat16()
+
+    def grads():
+        inp = qkv.clone().requires_grad_()
+        A._KernelAttn.apply(inp, B, T, H, Hk, D, window).backward(dout)
+        torch.cuda.synchronize()
+        return inp.grad.clone()
+    try:
+        A.set_deterministic(True)
+        first, second = grads(), grads()
+    finally:
+        A.set_deterministic(False)
+    default = grads()
+    check_errors()
+    assert torch.equal(first, second)
+    assert (first.float() - default.float()).abs().max().item() <= 1e-2 * default.float().abs().max().item()
+    ref_in = qkv.float().requires_grad_()
+    _ref(ref_in, B, T, H, Hk, D, window).backward(dout.float())
+    e = (first.float() - ref_in.grad).abs().max().item()
+    assert e <= 2e-2 + 2e-2 * ref_in.grad.abs().max().item()

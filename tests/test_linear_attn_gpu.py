@@ -47,31 +47,6 @@ def test_gated_rmsnorm(rows, D):
     torch.testing.assert_close(gain.grad, gainr.grad, atol=0.5, rtol=2e-2)
 
 
-@pytest.mark.parametrize("kind", ["gdn", "kda", "deltanet"])
-def test_linear_mixer_cuda_matches_cpu(kind):
-    """The CUDA path of a chunked delta-rule model (conv, chunk scan, gated norm) against the CPU path."""
-    from nexttransformer_b200.models import build_model
-    from nexttransformer_b200.models.config import debug_config
-    c = debug_config(kind, width=256, sequence_len=128)
-    torch.manual_seed(2)
-    tok = torch.randint(0, c.vocab_size, (2, 129))
-    x, y = tok[:, :-1], tok[:, 1:]
-    cpu = build_model(c, "cpu", seed=3)
-    gpu = build_model(c, "cuda", seed=3)
-    gpu.load_state_dict(cpu.state_dict())
-    lc = cpu(x, y)
-    lg = gpu(x.cuda(), y.cuda())
-    lc.backward()
-    lg.backward()
-    assert abs(lc.item() - lg.item()) < 0.05
-    # weight matrices only: scalar gains sum many bf16 terms with cancellation
-    for (n, pc), pg in zip(cpu.named_parameters(), gpu.parameters()):
-        if pc.grad is None or pc.dim() < 2 or pc.grad.norm() == 0:
-            continue
-        rel = (pc.grad - pg.grad.float().cpu()).norm() / pc.grad.norm().clamp_min(1e-12)
-        assert rel < 0.15, (n, rel.item())
-
-
 def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 

@@ -75,3 +75,31 @@ def test_nonfinite_exit(tmp_path, monkeypatch):
     assert e.value.code == train.NONFINITE_EXIT
     events = [json.loads(l) for l in (tmp_path / "metrics.jsonl").read_text().splitlines()]
     assert events[-1]["event"] == "nonfinite"
+
+
+def test_run_records_schedule_budget_and_status(tmp_path, monkeypatch):
+    """Validation follows --val-every, every update logs a device-free step time and grad norm, and
+    the run ends with budget.json and run_status.json."""
+    from nexttransformer_b200 import train
+    for k in ("WORLD_SIZE", "RANK", "LOCAL_RANK"):
+        monkeypatch.delenv(k, raising=False)
+    out = tmp_path / "run"
+    train.main([*ARGS, "--output", str(out), "--steps", "4"])
+    events = [json.loads(l) for l in (out / "metrics.jsonl").read_text().splitlines()]
+    assert [e["step"] for e in events if e["event"] == "validation"] == [3, 4]
+    steps = [e for e in events if e["event"] == "train"]
+    assert all(e["grad_norm"] > 0 and e["step_seconds"] > 0 for e in steps)
+    budget = json.loads((out / "budget.json").read_text())
+    status = json.loads((out / "run_status.json").read_text())
+    assert budget["step"] == 4 and status["step"] == 4 and status["phase"] == "stopped"
+    assert (out / "val_00000003.json").exists()
+
+
+def test_grad_norm_matches_direct_sum():
+    from nexttransformer_b200.train import grad_norm_sq
+    ps = [torch.nn.Parameter(torch.randn(5, 3)), torch.nn.Parameter(torch.randn(7)),
+          torch.nn.Parameter(torch.randn(2, 2, dtype=torch.float64))]
+    for p in ps:
+        p.grad = torch.randn_like(p)
+    want = sum(float(p.grad.double().square().sum()) for p in ps)
+    assert abs(float(grad_norm_sq(ps)) - want) < 1e-5 * want     # fp32 norms per tensor
