@@ -273,26 +273,30 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       tc_fence_after();
       const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
-      // pass 1: row max of the scaled, masked scores
-      float mx = -INFINITY;
+      // pass 1: row max of the scaled, masked scores, 64 keys per tensor-memory wait (two loads in
+      // flight; a whole 128-key row in registers would spill under the 168-register budget)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_s + lane_off + c * 32, v);
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t v[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
-        float xs[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) xs[e] = __uint_as_float(v[e]) * p.scale_log2;
         if (boundary) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int kj = k0 + c * 32 + e;
-            xs[e] = (kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window)) ? xs[e] : -INFINITY;
+          for (int e = 0; e < 64; ++e) {
+            const int kj = k0 + hlf * 64 + e;
+            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
           }
         }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, xs[e]);
+        for (int e = 0; e < 64; e += 2) {
+          mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+          mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+        }
       }
+      // raw scores are scaled after the max (the scale is positive)
+      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
       // lazy rescale: keep the old reference max unless the row grew by more than 2^8
       float m_new = m;
       if (i == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
@@ -305,43 +309,47 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(t_o + lane_off + c * 32, v);
+          uint32_t w[32];
+          tmem_ld32(t_o + lane_off + c * 32, w);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-          tmem_st16(t_o + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-          tmem_st16(t_o + lane_off + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+          for (int e = 0; e < 32; ++e) w[e] = __float_as_uint(__uint_as_float(w[e]) * alpha);
+          tmem_st16(t_o + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&w[0]));
+          tmem_st16(t_o + lane_off + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&w[16]));
         }
         tmem_wait_st();
       }
       m = m_new;
-      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S
-      float sum = 0.f;
+      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S, 64 keys per wait
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_s + lane_off + c * 32, v);
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t v[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
-        uint32_t pk[16];
-        float xs[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) xs[e] = __uint_as_float(v[e]) * p.scale_log2 - mref;
         if (boundary) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int kj = k0 + c * 32 + e;
-            xs[e] = (kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window)) ? xs[e] : -INFINITY;
+          for (int e = 0; e < 64; ++e) {
+            const int kj = k0 + hlf * 64 + e;
+            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
           }
         }
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float e0 = fast_exp2(xs[e]), e1 = fast_exp2(xs[e + 1]);
-          sum += e0 + e1;
-          pk[e / 2] = pack_bf16x2(e0, e1);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float e0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), p.scale_log2, -mref));
+            const float e1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), p.scale_log2, -mref));
+            sum0 += e0;
+            sum1 += e1;
+            pk[e / 2] = pack_bf16x2(e0, e1);
+          }
+          tmem_st16(t_s + lane_off + hlf * 32 + c * 16, pk);
         }
-        tmem_st16(t_s + lane_off + c * 16, pk);
       }
+      const float sum = sum0 + sum1;
       l = l * alpha + sum;
       tmem_wait_st();
       tc_fence_before();
@@ -611,34 +619,40 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (r == 0) stamp(p, 2, it, 1);
       __syncwarp();
       tc_fence_after();
+      // 64 queries per tensor-memory wait: two loads in flight
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tmem_ld32(t_s + lane_off + c * 32, sv);
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t sv[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        if (r == 0 && c == 0) stamp(p, 2, it, 6);
-        uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
-        // the mask is applied in a separate loop so the unrolled exp loop carries no branches
-        float xs[32];
+        if (r == 0 && hlf == 0) stamp(p, 2, it, 6);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
-          xs[i] = __uint_as_float(sv[i]) * p.scale_log2 - l2.x;
-          xs[i + 1] = __uint_as_float(sv[i + 1]) * p.scale_log2 - l2.y;
-        }
-        if (boundary) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hlf + cc;
+          uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
+          // the mask is applied in a separate loop so the unrolled exp loop carries no branches
+          float xs[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int qi = q0 + c * 32 + i;
-            const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
-            xs[i] = valid ? xs[i] : -INFINITY;
+          for (int i = 0; i < 32; i += 2) {
+            const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
+            xs[i] = fmaf(__uint_as_float(sv[cc * 32 + i]), p.scale_log2, -l2.x);
+            xs[i + 1] = fmaf(__uint_as_float(sv[cc * 32 + i + 1]), p.scale_log2, -l2.y);
           }
-        }
+          if (boundary) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) pk[i / 2] = pack_bf16x2(fast_exp2(xs[i]), fast_exp2(xs[i + 1]));
-        // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier chunk
-        tmem_st16(t_s + lane_off + c * 16, pk);
-        if (r == 0 && c == 0) stamp(p, 2, it, 7);
+            for (int i = 0; i < 32; ++i) {
+              const int qi = q0 + c * 32 + i;
+              const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+              xs[i] = valid ? xs[i] : -INFINITY;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) pk[i / 2] = pack_bf16x2(fast_exp2(xs[i]), fast_exp2(xs[i + 1]));
+          // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier half
+          tmem_st16(t_s + lane_off + c * 16, pk);
+        }
+        if (r == 0 && hlf == 0) stamp(p, 2, it, 7);
       }
       tmem_wait_st();
       tc_fence_before();

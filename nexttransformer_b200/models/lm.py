@@ -51,6 +51,8 @@ class LanguageModel(GPTShell):
         self.last_trace, self.last_stats = [], {}
         self.last_aux_loss = self.last_lm_loss = None
         self.row_offset = 0
+        # False keeps CUDA training on the plain PyTorch graph (a bf16 baseline for numerics checks)
+        self.kernel_path = True
         self.plugin = plug.load(c.method) if c.method in PLUGIN_METHODS else None
         for i, blk in enumerate(self.transformer.h):
             kind = c.layer_mixers[i] if c.method in HYBRID else c.method
@@ -415,7 +417,7 @@ class LanguageModel(GPTShell):
             raise NotImplementedError("KV-cache decoding goes through nexttransformer_b200.inference")
         self.last_trace, self.last_stats = [], {}
         if (idx.is_cuda and targets is not None and loss_reduction == "mean" and self.training
-                and self.fused_supported()):
+                and self.kernel_path and self.fused_supported()):
             from nexttransformer_b200.models.fused_dense import fused_forward
             loss, aux = fused_forward(self, idx, targets, "mean")
             aux = loss.new_zeros(()) if aux is None else aux

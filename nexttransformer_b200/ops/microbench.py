@@ -11,7 +11,9 @@ sizes, so no flush is needed between launches.  The same command with small ``--
 
 Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, vocab 65536):
   gemm_qkv, gemm_fc, gemm_proj, gemm_wgrad, gemm_head - the GEMM engine with its epilogues
-  attn_fwd, attn_bwd                                   - flash attention, rows = B*T (T 2048)
+  attn_fwd, attn_bwd                                   - flash attention, rows = B*T (T 2048, or --seq)
+  sdpa_fwd, sdpa_bwd                                   - the same shape through torch SDPA with one backend
+                                                         (--sdpa cudnn | flash | efficient): the library bar
   ce                                                   - soft-capped cross-entropy over 65536 logits
   adamw                                                - AdamW over a [rows, 1280] table
   muon                                                 - the Muon chain on 20 matrices [5120, 1280]
@@ -96,6 +98,32 @@ def case_gemm(kind, rows):
 def _attn_flops(B, causal_pairs, fwd):
     per_pair = 4 * HEAD_DIM * HEADS      # QK^T and PV
     return B * causal_pairs * per_pair * (1 if fwd else 2.5)
+
+
+def case_sdpa(kind, rows, backend):
+    """torch SDPA (one backend forced) on the attention benchmark shape, [B, H, T, D] layout."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    chosen = {"cudnn": SDPBackend.CUDNN_ATTENTION, "flash": SDPBackend.FLASH_ATTENTION,
+              "efficient": SDPBackend.EFFICIENT_ATTENTION}[backend]
+    B = max(1, rows // SEQ)
+    q = _bf16(B, HEADS, SEQ, HEAD_DIM).mul_(0.3).requires_grad_(kind == "sdpa_bwd")
+    k = _bf16(B, KV_HEADS, SEQ, HEAD_DIM).mul_(0.3).requires_grad_(kind == "sdpa_bwd")
+    v = _bf16(B, KV_HEADS, SEQ, HEAD_DIM).mul_(0.3).requires_grad_(kind == "sdpa_bwd")
+    pairs = SEQ * (SEQ + 1) // 2
+
+    def run():
+        with sdpa_kernel([chosen]):
+            return F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+    if kind == "sdpa_fwd":
+        return run, _attn_flops(B, pairs, True)
+    y = run()
+    dy = torch.randn_like(y)
+
+    def bwd():
+        with sdpa_kernel([chosen]):
+            torch.autograd.grad(y, (q, k, v), dy, retain_graph=True)
+    return bwd, _attn_flops(B, pairs, False)
 
 
 def case_attn(kind, rows):
@@ -290,7 +318,12 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--seq", type=int, default=0, help="sequence length of the attention cases (default 2048)")
+    ap.add_argument("--sdpa", choices=("cudnn", "flash", "efficient"), default="cudnn")
     a = ap.parse_args(argv)
+    global SEQ
+    if a.seq:
+        SEQ = a.seq
     torch.manual_seed(0)
     byts = None
     if a.case == "attn_bwd_trace":
@@ -300,6 +333,8 @@ def main(argv=None):
         fn, flops = case_gemm(a.case, a.rows)
     elif a.case.startswith("attn_"):
         fn, flops = case_attn(a.case, a.rows)
+    elif a.case.startswith("sdpa_"):
+        fn, flops = case_sdpa(a.case, a.rows, a.sdpa)
     elif a.case.startswith("delta_scan"):
         fn, flops = case_delta(a.case, a.rows)
     elif a.case.startswith("sparse_"):
@@ -322,7 +357,7 @@ def main(argv=None):
     from nexttransformer_b200.ops._ext import check_errors
     check_errors()
     pk = peaks()
-    out = {"case": a.case, "rows": a.rows, "ms": ms}
+    out = {"case": a.case, "rows": a.rows, "seq": SEQ, "ms": ms, **({"sdpa": a.sdpa} if a.case.startswith("sdpa_") else {})}
     if flops:
         tf = flops / ms / 1e9
         out.update(tflops=tf)

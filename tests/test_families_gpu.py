@@ -6,11 +6,12 @@ engine (``ops.dense.KernelLinear``), RMSNorms on the row kernels, linear mixers 
 conv / gated-norm kernels, sparse mixers on the block-sparse kernels, routed experts as grouped
 GEMMs, the head as the fused soft-capped cross-entropy GEMM.  The oracle is the same model,
 same weights, run eagerly on the CPU in float64.  The loss and every parameter gradient must
-agree elementwise: ``max |g - g_ref| <= tol * max(max |g_ref|, floor)`` per tensor, where tol
-reflects bf16 activations through a few layers (5 % for weight matrices; 15 % for the shell's
-scalar gains, whose gradients sum bf16 products over every token with cancellation) and the floor
-is 1e-4 of the largest gradient of the model (a gradient that is exactly zero in the oracle, like
-the backout gain's when the backout point is the last layer, is bf16 noise on the GPU).
+agree elementwise, per tensor: ``max |g - g_ref|`` within 5 % of the tensor's largest entry (10 %
+for routed experts, whose router may break near-ties differently), or within twice the error of
+the same model run on the plain bf16 PyTorch graph (which calibrates what bf16 activations alone
+cost, e.g. for scalar gains whose gradients sum bf16 products over every token with
+cancellation), plus 1e-4 of the model's largest gradient (a gradient that is exactly zero in the
+oracle, like the backout gain's when the backout point is the last layer, is bf16 noise).
 """
 from contextlib import contextmanager
 from dataclasses import replace
@@ -100,6 +101,17 @@ def test_family_matches_fp64_oracle(method):
         assert not idle, f"registered projections that never ran: {idle}"
     got = _grads(model)
 
+    # bf16 baseline: the same model on the plain PyTorch graph (no kernel state), whose error against
+    # the fp64 oracle calibrates what bf16 activations alone cost
+    eager = build_model(cfg, "cuda", seed=5)
+    eager.kernel_path = False
+    eager.load_state_dict(model.state_dict())
+    if method in ("nsa", "moba"):
+        eager.set_sparse_backend("reference")
+    eager.train()
+    eager(x.cuda(), y.cuda()).backward()
+    base = {n: p.grad.detach().double().cpu() for n, p in eager.named_parameters() if p.grad is not None}
+
     with compute_dtype(torch.float64):
         oracle = build_model(cfg, "cpu", seed=5)
         oracle.load_state_dict({k: v.detach().cpu() for k, v in model.state_dict().items()})
@@ -109,7 +121,7 @@ def test_family_matches_fp64_oracle(method):
     ref = {n: p.grad.detach().double() for n, p in oracle.named_parameters() if p.grad is not None}
 
     assert abs(loss.item() - ref_loss.item()) <= 1e-2 * abs(ref_loss.item()), (loss.item(), ref_loss.item())
-    floor = 1e-4 * max(float(r.abs().max()) for r in ref.values())
+    top = max(float(r.abs().max()) for r in ref.values())
     checked = 0
     for name, r in ref.items():
         scale = float(r.abs().max())
@@ -117,7 +129,10 @@ def test_family_matches_fp64_oracle(method):
             continue
         assert name in got, f"{name}: no gradient on the kernel path"
         err = float((got[name] - r).abs().max())
-        tol = 0.15 if r.ndim <= 1 else 0.1 if ("experts" in name or "router" in name) else 0.05
-        assert err <= tol * max(scale, floor), (name, err, scale)
+        bf16 = float((base[name] - r).abs().max()) if name in base else 0.0
+        # within 5 % of the tensor's largest entry (10 % for routed experts), or at most twice the
+        # bf16 baseline's own error; entries far below the model's largest gradient are bf16 noise
+        tol = 0.1 if ("experts" in name or "router" in name) else 0.05
+        assert err <= max(tol * scale, 2.0 * bf16) + 1e-4 * top, (name, err, scale, bf16)
         checked += 1
     assert checked >= 8
