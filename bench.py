@@ -70,6 +70,9 @@ def parse():
                    help="gradient averaging / parameter gather of our arm on N > 1: NCCL collectives (default) "
                         "or the peer-memory kernels (their standalone checks are exact; the training step "
                         "with them is still being validated)")
+    p.add_argument("--breakdown", action="store_true",
+                   help="also report per-rank CUDA-event phase times (forward+backward, optimizer) of the timed "
+                        "updates")
     p.add_argument("--no-overlap", action="store_true",
                    help="N > 1: reduce gradients after the backward and gather parameters before the next "
                         "forward (default: per-layer reductions during the backward, per-layer gather waits "
@@ -434,6 +437,8 @@ def main():
     barrier()
 
     # ---- device-timed region
+    if args.breakdown and args.impl == "ours":
+        trainer.timing = True
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local == 0)
     with sampler:
@@ -445,6 +450,17 @@ def main():
         end.record()
         barrier()
     ms = start.elapsed_time(end) / args.steps
+    breakdown = None
+    if args.breakdown and args.impl == "ours":
+        trainer.timing = False
+        phases = trainer.phase_times()
+        local = torch.tensor([statistics.median(p[0] for p in phases), statistics.median(p[1] for p in phases), ms],
+                             device=device, dtype=torch.float64)
+        every = [torch.empty_like(local) for _ in range(world)] if world > 1 else [local]
+        if world > 1:
+            dist.all_gather(every, local)
+        breakdown = [{"rank": r, "forward_backward_ms": float(t[0]), "optimizer_ms": float(t[1]),
+                      "step_ms": float(t[2])} for r, t in enumerate(every)]
     if rank == 0:
         print(f"timed region done: {ms:.1f} ms per step", file=sys.stderr, flush=True)
     t = torch.tensor([ms], device=device, dtype=torch.float64)
@@ -518,6 +534,8 @@ def main():
                           else ("none" if world == 1 else "nccl"),
                           "flops_per_token": flops_per_token, "params_equal_across_ranks": params_agree},
                "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "loss": final_loss}
+        if breakdown is not None:
+            out["phase_breakdown"] = breakdown
         if args.impl == "reference":
             out["impl"] = "reference"
             out.pop("gpu_launches")

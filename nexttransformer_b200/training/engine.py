@@ -20,6 +20,10 @@ class Trainer:
         self.schedule = schedule and train_config is not None
         self.step_index = 0
         self.device = model.get_device()
+        # optional per-phase CUDA events of each update (``timing = True``): forward+backward of
+        # all micro-batches, then the optimizer step; read with ``phase_times()`` after a sync
+        self.timing = False
+        self._events = []
 
     def zero_grad(self):
         m = self.model
@@ -32,6 +36,10 @@ class Trainer:
         """One update on device-resident micro-batches ``inputs[i], targets[i]``; returns the loss tensor."""
         if self.schedule:
             set_schedule(self.optimizer, self.step_index, self.train_config)
+        marks = None
+        if self.timing and self.device.type == "cuda":
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            marks[0].record()
         self.zero_grad()
         total = torch.zeros((), device=self.device, dtype=torch.float32)
         st = getattr(self.model, "_fused", None)
@@ -46,12 +54,25 @@ class Trainer:
             total += loss.detach().float()
         if st is not None:
             st.final_micro = False
+        if marks is not None:
+            marks[1].record()
         with nvtx_range("optimizer.step"):
             self.optimizer.step()
+        if marks is not None:
+            marks[2].record()
+            self._events.append(marks)
         if hasattr(self.model, "update_router_bias"):
             self.model.update_router_bias()     # MoE aux-loss-free balancing, once per update
         self.step_index += 1
         return total / self.accumulation
+
+    def phase_times(self, reset=True):
+        """[(forward+backward ms, optimizer ms)] of the updates timed since the last call (the
+        optimizer phase includes waiting for the gradient reductions it needs)."""
+        out = [(a.elapsed_time(b), b.elapsed_time(c)) for a, b, c in self._events]
+        if reset:
+            self._events = []
+        return out
 
     def flush(self):
         """Wait (on the current stream) for the parameter gathers the last update left running

@@ -9,8 +9,9 @@ same weights, run eagerly on the CPU in float64.  The loss and every parameter g
 agree elementwise, per tensor: ``max |g - g_ref|`` within 5 % of the tensor's largest entry (10 %
 for routed experts, whose router may break near-ties differently), or within twice the error of
 the same model run on the plain bf16 PyTorch graph (which calibrates what bf16 activations alone
-cost, e.g. for scalar gains whose gradients sum bf16 products over every token with
-cancellation), plus 1e-4 of the model's largest gradient (a gradient that is exactly zero in the
+cost), plus 1e-4 of the model's largest gradient; the shell's scalar gains, whose gradients are
+one sum of bf16 products over every token with cancellation, get 25 % or four times the baseline's
+error plus 2e-4 of the largest gradient (a gradient that is exactly zero in the
 oracle, like the backout gain's when the backout point is the last layer, is bf16 noise).
 """
 from contextlib import contextmanager
@@ -132,7 +133,10 @@ def test_family_matches_fp64_oracle(method):
         bf16 = float((base[name] - r).abs().max()) if name in base else 0.0
         # within 5 % of the tensor's largest entry (10 % for routed experts), or at most twice the
         # bf16 baseline's own error; entries far below the model's largest gradient are bf16 noise
-        tol = 0.1 if ("experts" in name or "router" in name) else 0.05
-        assert err <= max(tol * scale, 2.0 * bf16) + 1e-4 * top, (name, err, scale, bf16)
+        if r.numel() <= 64:      # scalar gains: one fp32 sum of bf16 products over every token
+            assert err <= max(0.25 * scale, 4.0 * bf16) + 2e-4 * top, (name, err, scale, bf16)
+        else:
+            tol = 0.1 if ("experts" in name or "router" in name) else 0.05
+            assert err <= max(tol * scale, 2.0 * bf16) + 1e-4 * top, (name, err, scale, bf16)
         checked += 1
     assert checked >= 8
