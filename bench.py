@@ -454,11 +454,11 @@ def main():
     if args.breakdown and args.impl == "ours":
         trainer.timing = False
         phases = trainer.phase_times()
-        local = torch.tensor([statistics.median(p[0] for p in phases), statistics.median(p[1] for p in phases), ms],
-                             device=device, dtype=torch.float64)
-        every = [torch.empty_like(local) for _ in range(world)] if world > 1 else [local]
+        mine = torch.tensor([statistics.median(p[0] for p in phases), statistics.median(p[1] for p in phases), ms],
+                            device=device, dtype=torch.float64)
+        every = [torch.empty_like(mine) for _ in range(world)] if world > 1 else [mine]
         if world > 1:
-            dist.all_gather(every, local)
+            dist.all_gather(every, mine)
         breakdown = [{"rank": r, "forward_backward_ms": float(t[0]), "optimizer_ms": float(t[1]),
                       "step_ms": float(t[2])} for r, t in enumerate(every)]
     if rank == 0:

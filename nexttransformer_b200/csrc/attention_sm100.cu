@@ -273,31 +273,26 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       tc_fence_after();
       const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
-      // pass 1: row max of the masked scores.  Tensor-memory loads are software-pipelined in 32-key
-      // chunks: chunk c+1 is requested before chunk c is reduced, so the load latency overlaps the
-      // math (tcgen05.wait::ld waits for every load in flight, and only chunk c+1 is in flight then).
+      // pass 1: row max of the scaled, masked scores, 64 keys per tensor-memory wait (two loads in
+      // flight; a whole 128-key row in registers would spill under the 168-register budget)
       float mx0 = -INFINITY, mx1 = -INFINITY;
-      {
-        uint32_t buf[2][32];
-        tmem_ld32(t_s + lane_off, buf[0]);
+#pragma unroll 1
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t v[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
+        if (boundary) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(t_s + lane_off + (c + 1) * 32, buf[(c + 1) & 1]);
-          uint32_t* v = buf[c & 1];
-          if (boundary) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int kj = k0 + c * 32 + e;
-              if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
-            }
+          for (int e = 0; e < 64; ++e) {
+            const int kj = k0 + hlf * 64 + e;
+            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
           }
+        }
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(v[e]));
-            mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
-          }
-          if (c < 3) tmem_wait_ld();
+        for (int e = 0; e < 64; e += 2) {
+          mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+          mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
         }
       }
       // raw scores are scaled after the max (the scale is positive)
@@ -325,36 +320,33 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_wait_st();
       }
       m = m_new;
-      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S, with the same
-      // software-pipelined 32-key chunks (P of chunk c lands in columns [16c, 16c + 16), which hold
-      // S of chunks already read)
+      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S, 64 keys per wait
       float sum0 = 0.f, sum1 = 0.f;
-      {
-        uint32_t buf[2][32];
-        tmem_ld32(t_s + lane_off, buf[0]);
+#pragma unroll 1
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t v[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
+        if (boundary) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(t_s + lane_off + (c + 1) * 32, buf[(c + 1) & 1]);
-          uint32_t* v = buf[c & 1];
-          if (boundary) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int kj = k0 + c * 32 + e;
-              if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
-            }
+          for (int e = 0; e < 64; ++e) {
+            const int kj = k0 + hlf * 64 + e;
+            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
           }
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(v[e]), p.scale_log2, -mref));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), p.scale_log2, -mref));
+            const float e0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), p.scale_log2, -mref));
+            const float e1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), p.scale_log2, -mref));
             sum0 += e0;
             sum1 += e1;
             pk[e / 2] = pack_bf16x2(e0, e1);
           }
-          if (c < 3) tmem_wait_ld();
-          tmem_st16(t_s + lane_off + c * 16, pk);
+          tmem_st16(t_s + lane_off + hlf * 32 + c * 16, pk);
         }
       }
       const float sum = sum0 + sum1;
@@ -627,25 +619,25 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (r == 0) stamp(p, 2, it, 1);
       __syncwarp();
       tc_fence_after();
-      // software-pipelined 32-query chunks: chunk c+1 is requested before chunk c is turned into P^T,
-      // so the tensor-memory load latency overlaps the math
-      {
-        uint32_t buf[2][32];
-        tmem_ld32(t_s + lane_off, buf[0]);
+      // 64 queries per tensor-memory wait: two loads in flight
+#pragma unroll 1
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint32_t sv[64];
+        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        if (r == 0) stamp(p, 2, it, 6);
+        if (r == 0 && hlf == 0) stamp(p, 2, it, 6);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) tmem_ld32(t_s + lane_off + (c + 1) * 32, buf[(c + 1) & 1]);
-          const uint32_t* sv = buf[c & 1];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hlf + cc;
           uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
           // the mask is applied in a separate loop so the unrolled exp loop carries no branches
           float xs[32];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
-            xs[i] = fmaf(__uint_as_float(sv[i]), p.scale_log2, -l2.x);
-            xs[i + 1] = fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -l2.y);
+            xs[i] = fmaf(__uint_as_float(sv[cc * 32 + i]), p.scale_log2, -l2.x);
+            xs[i + 1] = fmaf(__uint_as_float(sv[cc * 32 + i + 1]), p.scale_log2, -l2.y);
           }
           if (boundary) {
 #pragma unroll
@@ -657,11 +649,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           }
 #pragma unroll
           for (int i = 0; i < 32; i += 2) pk[i / 2] = pack_bf16x2(fast_exp2(xs[i]), fast_exp2(xs[i + 1]));
-          if (c < 3) tmem_wait_ld();
-          // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier chunk
+          // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier half
           tmem_st16(t_s + lane_off + c * 16, pk);
         }
-        if (r == 0) stamp(p, 2, it, 7);
+        if (r == 0 && hlf == 0) stamp(p, 2, it, 7);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -674,33 +665,23 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (r == 0) stamp(p, 2, it, 4);
       __syncwarp();
       tc_fence_after();
-      {
-        // dP^T and P^T (read-only for the dV MMA) of chunk c+1 are requested before chunk c is used
-        uint32_t dvb[2][32], pkb[2][16];
-        tmem_ld32(t_dp + lane_off, dvb[0]);
-        tmem_ld16(t_s + lane_off, pkb[0]);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dv[32], pk[16];
+        tmem_ld32(t_dp + lane_off + c * 32, dv);
+        tmem_ld16(t_s + lane_off + c * 16, pk);  // P^T back from tensor memory (read-only for the dV MMA)
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < 3) {
-            tmem_ld32(t_dp + lane_off + (c + 1) * 32, dvb[(c + 1) & 1]);
-            tmem_ld16(t_s + lane_off + (c + 1) * 16, pkb[(c + 1) & 1]);
-          }
-          const uint32_t* dv = dvb[c & 1];
-          const uint32_t* pk = pkb[c & 1];
+        for (int g = 0; g < 4; ++g) {
+          uint32_t w[4];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 8 * g + 2 * e;
-              const float2 pp = unpack_bf16x2(pk[i / 2]);
-              const float2 dl = *reinterpret_cast<const float2*>(s_del + c * 32 + i);
-              w[e] = pack_bf16x2(pp.x * (__uint_as_float(dv[i]) - dl.x), pp.y * (__uint_as_float(dv[i + 1]) - dl.y));
-            }
-            *reinterpret_cast<uint4*>(dsb + swz_off(r, c * 4 + g)) = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * g + 2 * e;
+            const float2 pp = unpack_bf16x2(pk[i / 2]);
+            const float2 dl = *reinterpret_cast<const float2*>(s_del + c * 32 + i);
+            w[e] = pack_bf16x2(pp.x * (__uint_as_float(dv[i]) - dl.x), pp.y * (__uint_as_float(dv[i + 1]) - dl.y));
           }
-          if (c < 3) tmem_wait_ld();
+          *reinterpret_cast<uint4*>(dsb + swz_off(r, c * 4 + g)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       fence_proxy_async_smem();

@@ -7,6 +7,7 @@
 #include "attention_sm100.h"
 #include "comm.h"
 #include "linear_attn.h"
+#include "delta_prep.h"
 #include "delta_scan.h"
 #include "moe.h"
 #include "sparse_attn.h"
@@ -700,6 +701,77 @@ void check_chunks(const Tensor& t, int64_t cols, const char* name) {
               name, " must be a contiguous bf16 CUDA tensor [BH, N, rows, ", cols, "]");
 }
 
+// Per-chunk delta-rule terms (delta_prep.cu): q, k, v bf16 [B, T, H, 128] contiguous, g fp32 [B, T, H]
+// (gate 1) or [B, T, H, 128] (gate 2), beta fp32 [B, T, H]; chunk-major outputs [B*H, N, 64, ..].
+static DeltaPrepArgs prep_args(const Tensor& q, const Tensor& k, const Tensor& v, const OptT& g, const Tensor& beta,
+                               int64_t gate, double qk_scale) {
+  for (auto* t : {&q, &k, &v}) {
+    check_cuda(*t, "delta operand");
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4 && t->size(-1) == 128,
+                "q / k / v: contiguous bf16 [B, T, H, 128]");
+    TORCH_CHECK(t->sizes() == q.sizes(), "q / k / v shapes differ");
+  }
+  TORCH_CHECK(beta.is_cuda() && beta.scalar_type() == at::kFloat && beta.is_contiguous() && beta.numel() == q.numel() / 128,
+              "beta: contiguous fp32 [B, T, H]");
+  DeltaPrepArgs a;
+  a.B = static_cast<int>(q.size(0)); a.T = static_cast<int>(q.size(1)); a.H = static_cast<int>(q.size(2));
+  a.gate = static_cast<int>(gate);
+  a.qk_scale = static_cast<float>(qk_scale);
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr();
+  a.beta = beta.data_ptr<float>();
+  if (gate != DELTA_NONE) {
+    TORCH_CHECK(g.has_value() && g->defined() && g->is_cuda() && g->scalar_type() == at::kFloat && g->is_contiguous(),
+                "g: contiguous fp32");
+    TORCH_CHECK(g->numel() == (gate == DELTA_FEATURE ? q.numel() : q.numel() / 128), "g shape");
+    a.g = g->data_ptr<float>();
+  }
+  return a;
+}
+
+void delta_prep_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const OptT& g, const Tensor& beta, int64_t gate,
+                    double qk_scale, const Tensor& w, const Tensor& u0, const Tensor& qt, const Tensor& kc,
+                    const Tensor& aqk, const Tensor& carry) {
+  DeltaPrepArgs a = prep_args(q, k, v, g, beta, gate, qk_scale);
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * ((a.T + 63) / 64) * 64;
+  for (auto* t : {&w, &u0, &qt, &kc})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->numel() == rows * 128, "chunk outputs");
+  TORCH_CHECK(aqk.scalar_type() == at::kBFloat16 && aqk.is_contiguous() && aqk.numel() == rows * 64, "aqk");
+  TORCH_CHECK(carry.scalar_type() == at::kFloat && carry.is_contiguous() && carry.numel() == rows * 2, "carry");
+  a.w = w.data_ptr(); a.u0 = u0.data_ptr(); a.qt = qt.data_ptr(); a.kc = kc.data_ptr(); a.aqk = aqk.data_ptr();
+  a.carry = carry.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_delta_prep_fwd(a, stream()), "delta_prep_fwd");
+}
+
+void delta_prep_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const OptT& g, const Tensor& beta, int64_t gate,
+                    double qk_scale, const Tensor& w, const Tensor& u0, const Tensor& dw, const Tensor& du0,
+                    const Tensor& dqt, const Tensor& dkc, const Tensor& daqk, const Tensor& dcarry, const Tensor& dq,
+                    const Tensor& dk, const Tensor& dv, const OptT& dg, const Tensor& dbeta) {
+  DeltaPrepArgs a = prep_args(q, k, v, g, beta, gate, qk_scale);
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * ((a.T + 63) / 64) * 64;
+  for (auto* t : {&w, &u0})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->numel() == rows * 128, "w / u0");
+  for (auto* t : {&dw, &du0, &dqt, &dkc})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == rows * 128, "chunk gradients");
+  TORCH_CHECK(daqk.scalar_type() == at::kFloat && daqk.is_contiguous() && daqk.numel() == rows * 64, "daqk");
+  TORCH_CHECK(dcarry.scalar_type() == at::kFloat && dcarry.is_contiguous() && dcarry.numel() == rows * 2, "dcarry");
+  for (auto* t : {&dq, &dk, &dv})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == q.numel(), "dq / dk / dv");
+  TORCH_CHECK(dbeta.scalar_type() == at::kFloat && dbeta.is_contiguous() && dbeta.numel() == q.numel() / 128, "dbeta");
+  a.w = w.data_ptr(); a.u0 = u0.data_ptr();
+  a.dw = dw.data_ptr<float>(); a.du0 = du0.data_ptr<float>(); a.dqt = dqt.data_ptr<float>();
+  a.dkc = dkc.data_ptr<float>(); a.daqk = daqk.data_ptr<float>(); a.dcarry = dcarry.data_ptr<float>();
+  a.dq = dq.data_ptr<float>(); a.dk = dk.data_ptr<float>(); a.dv = dv.data_ptr<float>();
+  a.dbeta = dbeta.data_ptr<float>();
+  if (gate != DELTA_NONE) {
+    TORCH_CHECK(dg.has_value() && dg->defined() && dg->scalar_type() == at::kFloat && dg->is_contiguous() &&
+                    dg->numel() == g->numel(), "dg");
+    a.dg = dg->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_delta_prep_bwd(a, stream()), "delta_prep_bwd");
+}
+
 void delta_scan_fwd(const Tensor& w, const Tensor& qt, const Tensor& kc, const Tensor& aqk, const Tensor& u0,
                     const Tensor& carry, const Tensor& o, const Tensor& states, const Tensor& u) {
   for (auto* t : {&w, &qt, &kc, &u0, &o, &u}) check_chunks(*t, 128, "delta scan operand");
@@ -807,6 +879,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_pull_rows", &moe_pull_rows);
   m.def("moe_push_rows", &moe_push_rows);
   m.def("delta_scan_fwd", &delta_scan_fwd);
+  m.def("delta_prep_fwd", &delta_prep_fwd, "per-chunk delta-rule terms (WY solve, gates, q/k norm)");
+  m.def("delta_prep_bwd", &delta_prep_bwd, "backward of the per-chunk delta-rule terms");
   m.def("delta_scan_bwd", &delta_scan_bwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);

@@ -5,9 +5,12 @@
   is kept for the backward.
 * ``gated_rms_norm(y, gate, gain)``: ``RMSNorm(y) * gain * SiLU(gate)`` over the head dimension,
   one kernel each way.
-* ``delta_chunk_cuda(...)``: the chunked (gated) delta rule.  It runs the chunk form of
-  ``models/linear.py`` with fp32 matrix products on the GPU (q/k L2 normalisation for GDN first)
-  until the fused chunk kernel replaces it.
+* ``delta_chunk_cuda(...)``: the chunked (gated) delta rule.  With bf16 q / k / v of head size 128
+  and chunk 64 it is two kernels each way: the per-chunk terms (``csrc/delta_prep.cu``: q / k L2
+  normalisation for GDN, cumulative gates, the WY solve, qt / kc / aqk / carry) and the inter-chunk
+  scan (``csrc/delta_scan.cu``); the backward runs the scan's reverse pass, four batched GEMMs for
+  the chain-free products and the terms' backward kernel.  Other shapes keep the fp32 PyTorch chunk
+  form of ``models/linear.py``.
 """
 import torch
 from torch.autograd import Function
@@ -121,6 +124,74 @@ class _DeltaScan(Function):
                 daqk.reshape(*shp, 64), dcarry.reshape(B, H, N, 128))
 
 
+GATE_MODE = {"deltanet": 0, "gdn": 1, "kda": 2}
+# The fused chunk-term kernels; NT_FUSED_DELTA=0 keeps the fp32 PyTorch chunk terms.
+import os as _os
+FUSED_DELTA = _os.environ.get("NT_FUSED_DELTA", "0") == "1"
+
+
+class _DeltaChunk(Function):
+    """Fused chunked delta rule: chunk terms (delta_prep) + inter-chunk scan (delta_scan)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, gate, scale):
+        lib = ext()
+        B, T, H, D = q.shape
+        N = (T + 63) // 64
+        BH = B * H
+        dev = q.device
+        bf = torch.bfloat16
+        w, u0, qt, kc = (torch.empty(BH, N, 64, 128, device=dev, dtype=bf) for _ in range(4))
+        aqk = torch.empty(BH, N, 64, 64, device=dev, dtype=bf)
+        carry = torch.empty(BH, N, 128, device=dev, dtype=torch.float32)
+        lib.delta_prep_fwd(q, k, v, g, beta, gate, scale, w, u0, qt, kc, aqk, carry)
+        o = torch.empty_like(u0)
+        u = torch.empty_like(u0)
+        states = torch.empty(BH, N, 128, 128, device=dev, dtype=bf)
+        lib.delta_scan_fwd(w, qt, kc, aqk, u0, carry, o, states, u)
+        ctx.save_for_backward(q, k, v, g, beta, w, u0, qt, kc, aqk, carry, states, u)
+        ctx.meta = (gate, scale)
+        return o.view(B, H, N * 64, 128)[:, :, :T].transpose(1, 2)
+
+    @staticmethod
+    def backward(ctx, dout):
+        from nexttransformer_b200.ops.gemm import EPI_F32, gemm
+        lib = ext()
+        q, k, v, g, beta, w, u0, qt, kc, aqk, carry, states, u = ctx.saved_tensors
+        gate, scale = ctx.meta
+        B, T, H, D = q.shape
+        N = (T + 63) // 64
+        BH = B * H
+        M = BH * N
+        do = torch.zeros(B, H, N * 64, 128, device=q.device, dtype=torch.bfloat16)
+        do[:, :, :T] = dout.transpose(1, 2)
+        do = do.view(BH, N, 64, 128)
+        ds = torch.empty_like(states)
+        dut = torch.empty(BH, N, 128, 64, device=q.device, dtype=torch.bfloat16)
+        dcarry = torch.empty_like(carry)
+        lib.delta_scan_bwd(do, w, qt, kc, aqk, carry, states, ds, dut, dcarry)
+
+        def f32(rows, cols):
+            return torch.empty(M, rows, cols, device=q.device, dtype=torch.float32)
+        flat = lambda t: t.view(M, *t.shape[2:])
+        dqt = gemm(flat(do), flat(states), f32(64, 128), epi=EPI_F32)                      # do S^T
+        dw = gemm(flat(dut), flat(states), f32(64, 128), a_mn=True, epi=EPI_F32, s_acc=-1.0)  # -du S^T
+        daqk = gemm(flat(do), flat(u), f32(64, 64), epi=EPI_F32)                           # do u^T
+        dkc = gemm(flat(u), flat(ds), f32(64, 128), epi=EPI_F32)                           # u dS^T
+        du0 = dut.transpose(-1, -2).float().contiguous()
+        dq, dk, dv = (torch.empty(q.shape, device=q.device, dtype=torch.float32) for _ in range(3))
+        dbeta = torch.empty_like(beta)
+        dg = torch.empty_like(g) if g is not None else None
+        lib.delta_prep_bwd(q, k, v, g, beta, gate, scale, w, u0, dw, du0, dqt, dkc, daqk, dcarry, dq, dk, dv, dg,
+                           dbeta)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta, None, None
+
+
+def fused_chunk_supported(q, k, v, chunk):
+    return (FUSED_DELTA and q.is_cuda and chunk == 64 and q.shape[-1] == 128 and v.shape[-1] == 128 and
+            q.dtype == k.dtype == v.dtype == torch.bfloat16 and q.shape == k.shape == v.shape)
+
+
 def scan_supported(q, v, chunk):
     return q.is_cuda and chunk == 64 and q.shape[-1] == 128 and v.shape[-1] == 128
 
@@ -130,6 +201,11 @@ def delta_chunk_cuda(q, k, v, *, kind, g=None, beta=None, chunk, qk_l2norm_scale
     KDA [B, T, H, 128]); beta [B, T, H].  The per-chunk WY terms are formed in fp32 with torch
     (triangular solve included), the scan runs on the sm_100a kernels."""
     from nexttransformer_b200.models.linear import _chunked, _delta_scan, _delta_terms
+    if fused_chunk_supported(q, k, v, chunk) and kind in GATE_MODE:
+        gate = GATE_MODE[kind]
+        gf = None if gate == 0 else g.float().contiguous()
+        return _DeltaChunk.apply(q.contiguous(), k.contiguous(), v.contiguous(), gf, beta.float().contiguous(), gate,
+                                 float(qk_l2norm_scale) if qk_l2norm_scale is not None else 1.0)
     dt = q.dtype
     T = q.shape[1]
     q, k, v = q.float(), k.float(), v.float()

@@ -20,6 +20,10 @@ Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, v
   step                                                 - one fused training micro-step (all kernels)
   attn_bwd_trace                                       - clock stamps of the first backward CTA per pair
   delta_scan_fwd, delta_scan_bwd                       - chunked delta-rule scan, B*H = rows/4096*12, T 4096
+  delta_gdn, delta_kda                                 - the fused chunked delta rule (chunk terms + scan),
+                                                         forward + backward, bf16, T 4096, B*H = rows/4096*12
+  fla_gdn, fla_kda                                     - FLA's chunk_kda on the same inputs (the library bar;
+                                                         GDN through chunk_kda with a broadcast gate)
   sparse_fwd, sparse_bwd                               - block-sparse attention (NSA shape: 16 / 1 heads,
                                                          16 selected 64-key blocks per row), T 8192
   moe_fwd, moe_fwd_bwd                                 - grouped experts: 64 x (2048 -> 1024 -> 2048), top-8
@@ -176,6 +180,47 @@ def attn_bwd_trace(rows):
                 rows_.append(ev)
         out[names[role]] = rows_
     return out
+
+
+def case_delta_fused(kind, rows):
+    """Forward + backward of the whole chunked delta rule on [B, 4096, 12, 128] bf16 inputs."""
+    import torch.nn.functional as F
+    T, H, D = 4096, 12, 128
+    B = max(1, rows // T)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, T, H, D, device="cuda", generator=g)
+    k = torch.randn(B, T, H, D, device="cuda", generator=g)
+    v = torch.randn(B, T, H, D, device="cuda", generator=g).bfloat16().requires_grad_()
+    beta = torch.rand(B, T, H, device="cuda", generator=g).requires_grad_()
+    gdn = kind.endswith("gdn")
+    if gdn:
+        gate = (-F.softplus(torch.randn(B, T, H, device="cuda", generator=g)) * 0.3).requires_grad_()
+    else:
+        gate = (-F.softplus(torch.randn(B, T, H, D, device="cuda", generator=g)) * 0.05).requires_grad_()
+        q, k = F.normalize(q, dim=-1) * D ** -.5, F.normalize(k, dim=-1)
+    q, k = q.bfloat16().requires_grad_(), k.bfloat16().requires_grad_()
+    if kind.startswith("fla_"):
+        from fla.ops.kda import chunk_kda
+
+        def run():
+            gk = gate[..., None].expand(-1, -1, -1, D).contiguous() if gdn else gate
+            y, _ = chunk_kda(q, k, v, gk, beta.bfloat16(), scale=D ** -.5 if gdn else 1.0,
+                             use_qk_l2norm_in_kernel=gdn)
+            return y
+    else:
+        from nexttransformer_b200.ops.linear_attention import delta_chunk_cuda
+
+        def run():
+            return delta_chunk_cuda(q, k, v, kind="gdn" if gdn else "kda", g=gate, beta=beta, chunk=64,
+                                    qk_l2norm_scale=D ** -.5 if gdn else None)
+    dy = torch.randn(B, T, H, D, device="cuda").bfloat16()
+
+    def step():
+        y = run()
+        torch.autograd.grad(y, (q, k, v, beta, gate), dy.to(y.dtype))
+    # 4 D^2 per token and head for the WY terms, 4 D^2 for the state products, 2 x for the backward
+    flops = 3 * 8 * D * D * B * T * H
+    return step, flops
 
 
 def case_delta(kind, rows):
@@ -337,6 +382,8 @@ def main(argv=None):
         fn, flops = case_sdpa(a.case, a.rows, a.sdpa)
     elif a.case.startswith("delta_scan"):
         fn, flops = case_delta(a.case, a.rows)
+    elif a.case in ("delta_gdn", "delta_kda", "fla_gdn", "fla_kda"):
+        fn, flops = case_delta_fused(a.case, a.rows)
     elif a.case.startswith("sparse_"):
         fn, flops = case_sparse(a.case, a.rows)
     elif a.case.startswith("moe_"):
