@@ -32,7 +32,9 @@ def _inputs(kind, B, T, H, seed):
 
 @pytest.mark.parametrize("kind,B,T,H", [("gdn", 2, 200, 3), ("kda", 2, 256, 2), ("deltanet", 1, 192, 3),
                                         ("gdn", 1, 1024, 2), ("kda", 1, 700, 1)])
-def test_fused_delta_chunk_matches_fp64(kind, B, T, H):
+def test_fused_delta_chunk_matches_fp64(kind, B, T, H, monkeypatch):
+    import nexttransformer_b200.ops.linear_attention as LA
+    monkeypatch.setattr(LA, "FUSED_DELTA", True)
     from nexttransformer_b200.models.linear import chunk_scan
     from nexttransformer_b200.ops._ext import check_errors
     from nexttransformer_b200.ops.linear_attention import delta_chunk_cuda, fused_chunk_supported
