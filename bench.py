@@ -73,10 +73,10 @@ def parse():
     p.add_argument("--breakdown", action="store_true",
                    help="also report per-rank CUDA-event phase times (forward+backward, optimizer) of the timed "
                         "updates")
-    p.add_argument("--no-overlap", action="store_true",
-                   help="N > 1: reduce gradients after the backward and gather parameters before the next "
-                        "forward (default: per-layer reductions during the backward, per-layer gather waits "
-                        "in the next forward)")
+    p.add_argument("--overlap", action="store_true",
+                   help="N > 1: start each layer's gradient reductions during the last backward and let the next "
+                        "forward wait for each layer's parameter gathers (default: grouped reductions after the "
+                        "backward)")
     p.add_argument("--method", default="dense", choices=("dense", *METHOD_CONFIGS),
                    help="benchmark configuration (default: the dense headline configuration)")
     p.add_argument("--layers", type=int, default=MODEL["n_layer"], help=argparse.SUPPRESS)
@@ -165,13 +165,23 @@ def synthetic_batches(n_micro, rows, T, vocab, seed, device=None, pinned=False):
     return xs, ys
 
 
-def count_own_kernels(step_fn):
-    """Launches of this repository's kernels in one step (torch profiler, outside the timed region)."""
+def count_own_kernels(step_fn, optimizer=None):
+    """Launches of this repository's kernels in one step (torch profiler, outside the timed region).
+    The step runs without the data-parallel overlap: no collective is issued from the autograd thread
+    while the profiler is active."""
     import torch
     from torch.profiler import ProfilerActivity, profile
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        step_fn()
-        torch.cuda.synchronize()
+    saved = None
+    if optimizer is not None and getattr(optimizer, "defer_gathers", False):
+        optimizer.flush()
+        saved = optimizer.overlap_off()
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step_fn()
+            torch.cuda.synchronize()
+    finally:
+        if saved is not None:
+            optimizer.overlap_restore(saved)
     n = 0
     for ev in prof.events():
         name = ev.name or ""
@@ -230,7 +240,7 @@ def bench_method(args, rank, world, local, device):
                 enable_expert_parallel(model)
             shadows = {p: s for p, s in model.fused_state().casts}
             opt = MuonAdamW(protocol_groups(model), shadows=shadows)
-            if world > 1 and not args.no_overlap and model.fused_supported():
+            if world > 1 and args.overlap and model.fused_supported():
                 opt.overlap_with(model)
             trainer = Trainer(model, opt, accumulation=accum)
             step_device, step_e2e = trainer.step_device, trainer.step
@@ -286,7 +296,7 @@ def bench_method(args, rank, world, local, device):
         launches = None
         if args.impl == "ours":
             try:
-                launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush())) * args.steps
+                launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush()), opt) * args.steps
             except Exception:
                 launches = None
     except (ImportError, RuntimeError, NotImplementedError, TypeError) as exc:
@@ -337,7 +347,7 @@ def main():
         sys.path.append(str(ref))
 
     from nexttransformer_b200.runtime.process import initialize, shutdown
-    rank, world, device = initialize(seed=42, timeout_s=900)
+    rank, world, device = initialize(seed=42, timeout_s=300)
     if device.type != "cuda":
         raise SystemExit("bench.py needs a CUDA device")
     if args.method != "dense":
@@ -383,7 +393,7 @@ def main():
                     print(f"peer-memory step: reduce-scatter pad {int(opt.p2p.pads[rank]):#x}, gather pad "
                           f"{int(gather.pads[rank]):#x}, {len(segs)} segments, {opt.p2p.blocks} / {gather.blocks} "
                           f"blocks", file=sys.stderr)
-        overlap = world > 1 and not args.no_overlap
+        overlap = world > 1 and args.overlap
         if overlap:
             opt.overlap_with(model)
         trainer = Trainer(model, opt, accumulation=accum)
@@ -508,7 +518,7 @@ def main():
     if args.impl == "ours":
         barrier()       # every rank enters the profiled step together (its peer-memory kernels wait on peers)
         try:
-            launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush())) * args.steps
+            launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush()), opt) * args.steps
         except Exception as exc:  # profiler unavailable: report as unknown
             launches = None
             if rank == 0:

@@ -104,7 +104,16 @@ struct FwdSmem {
   static constexpr int TOTAL = BAR + NBAR * 8 + 32 + 1024;  // + tmem holder, abort and veto flags
 };
 static_assert(FwdSmem::TOTAL <= 232448, "forward shared memory exceeds the sm_100 limit");
-constexpr int FWD_THREADS = 320;
+// 12 warps in three warpgroups: warpgroup 0 = TMA producer (warp 0), MMA issuer (warp 1) and two
+// idle warps; warpgroups 1 and 2 = the softmax of query tiles A and B.  Launched at 168 registers a
+// thread (the most 384 threads may hold); warpgroup 0 gives registers back so each softmax thread
+// can keep a whole 128-key S row in registers: 128 x FWD_REGS_LOW + 256 x FWD_REGS_HIGH = 384 x 168.
+constexpr int FWD_THREADS = 384;
+constexpr uint32_t FWD_REGS_LAUNCH = 168;
+constexpr uint32_t FWD_REGS_LOW = 56;
+constexpr uint32_t FWD_REGS_HIGH = 224;
+static_assert(128 * FWD_REGS_LOW + 256 * FWD_REGS_HIGH <= FWD_THREADS * FWD_REGS_LAUNCH,
+              "forward register split exceeds the launch budget");
 
 // Key-tile range [lo, hi] of query tile qt (causal, optional left window); empty when qt is past T.
 NT_DEVICE void fwd_kv_range(const Params& p, int qt, int& lo, int& hi) {
@@ -166,8 +175,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
-
-  if (warp == 0) {
+  if (warp < 4) {
+   setmaxnreg_dec<FWD_REGS_LOW>();
+   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -252,9 +262,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       (void)iA;
       (void)iB;
     }
+   }
   } else {
+    setmaxnreg_inc<FWD_REGS_HIGH>();
     // ------------------------------------------------------------ softmax warpgroups
-    const int grp = warp < 6 ? 0 : 1;  // 0: tile A, 1: tile B
+    const int grp = warp < 8 ? 0 : 1;  // 0: tile A, 1: tile B
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qt = grp ? qtB : qtA;
@@ -273,30 +285,30 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       tc_fence_after();
       const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
-      // pass 1: row max of the scaled, masked scores, 64 keys per tensor-memory wait (two loads in
-      // flight; a whole 128-key row in registers would spill under the 168-register budget)
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll 1
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        uint32_t v[64];
-        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_wait_ld();
-        if (boundary) {
+      // the whole S row (128 keys) comes into registers with four loads and one wait; it is read
+      // from tensor memory once, scaled (log2 domain) and masked in place
+      uint32_t v[128];
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const int kj = k0 + hlf * 64 + e;
-            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
-          }
-        }
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+      tmem_wait_ld();
+      if (boundary) {
 #pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          mx0 = fmaxf(mx0, __uint_as_float(v[e]));
-          mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+        for (int e = 0; e < 128; ++e) {
+          const int kj = k0 + e;
+          const bool keep = kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+          if (!keep) v[e] = __float_as_uint(-INFINITY);
         }
       }
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 128; e += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(v[e]));
+        mx1 = fmaxf(mx1, __uint_as_float(v[e + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(v[e + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(v[e + 3]));
+      }
       // raw scores are scaled after the max (the scale is positive)
-      const float mx = fmaxf(mx0, mx1) * p.scale_log2;
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
       // lazy rescale: keep the old reference max unless the row grew by more than 2^8
       float m_new = m;
       if (i == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
@@ -320,34 +332,20 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_wait_st();
       }
       m = m_new;
-      // pass 2: P = exp2(S - m) as bf16 over columns [0, 64) of this tile's S, 64 keys per wait
+      // P = exp2(S scale - m) as bf16 over columns [0, 64) of this tile's S (S is in registers)
       float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll 1
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        uint32_t v[64];
-        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_wait_ld();
-        if (boundary) {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const int kj = k0 + hlf * 64 + e;
-            if (!(kj <= qi && kj < p.T && (p.window < 0 || qi - kj <= p.window))) v[e] = __float_as_uint(-INFINITY);
-          }
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), p.scale_log2, -mref));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), p.scale_log2, -mref));
+          sum0 += e0;
+          sum1 += e1;
+          pk[e / 2] = pack_bf16x2(e0, e1);
         }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), p.scale_log2, -mref));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), p.scale_log2, -mref));
-            sum0 += e0;
-            sum1 += e1;
-            pk[e / 2] = pack_bf16x2(e0, e1);
-          }
-          tmem_st16(t_s + lane_off + hlf * 32 + c * 16, pk);
-        }
+        tmem_st16(t_s + lane_off + c * 16, pk);
       }
       const float sum = sum0 + sum1;
       l = l * alpha + sum;

@@ -381,6 +381,17 @@ NT_DEVICE bool elect_one() {
   return pred != 0;
 }
 
+// Warpgroup register reallocation (every thread of the warpgroup executes it).  The CTA's register
+// file is what it was launched with (threads x registers per thread); a split must fit it.
+template <uint32_t N>
+NT_DEVICE void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+NT_DEVICE void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 NT_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -13,6 +13,12 @@ Distribution (world > 1): each rank owns whole Muon matrices (``ceil(K / world)`
 same-shape group, in group order) and row slices of the large AdamW tensors.  Gradients are
 reduced to their owner (averaged), the owner updates, and updated parameters are sent back
 to every rank - reduce-scatter + all-gather volume, never a full all-reduce of gradients.
+By default each Muon shape group moves as ONE stacked reduce-scatter and ONE all-gather (the
+group's gradients copied into a persistent ``[chunk x world, m, n]`` buffer, the owner's chunk
+reduced into a second one), the reference DistMuon's layout: 12 collectives for the six shape
+groups of a dense model instead of two per matrix, whose per-call latency dominated the
+exposed communication.  The per-matrix path serves the overlap mode, whose reductions start
+layer by layer during the backward.
 
 Gradients are read from ``p.main_grad`` when a fused path produced one, else ``p.grad``.
 
@@ -126,6 +132,9 @@ class MuonAdamW(torch.optim.Optimizer):
         # overlap state: parameter -> forward-use group, early-issued reductions, deferred gathers
         self.use_group = {}
         self.defer_gathers = False
+        self.stack_muon = True       # grouped reduce-scatter / all-gather of Muon matrices
+        self._stacks = {}
+        self._stack_finish = []
         self._early = {}
         self._pending = {}
         self._meta = None
@@ -141,6 +150,22 @@ class MuonAdamW(torch.optim.Optimizer):
         self.use_group = {p: g for g, ps in st.use_groups().items() for p in ps}
         self.defer_gathers = True
         st.optimizer = self
+        self._overlap_state = st
+
+    def overlap_off(self):
+        """Suspend the overlap (returns what ``overlap_restore`` needs)."""
+        state = getattr(self, "_overlap_state", None)
+        saved = (self.defer_gathers, state.optimizer if state is not None else None)
+        self.defer_gathers = False
+        if state is not None:
+            state.optimizer = None
+        return saved
+
+    def overlap_restore(self, saved):
+        self.defer_gathers = saved[0]
+        state = getattr(self, "_overlap_state", None)
+        if state is not None:
+            state.optimizer = saved[1]
 
     def _param_meta(self):
         """parameter -> ('adamw', group) or ('muon', group, index in its group)."""
@@ -270,10 +295,30 @@ class MuonAdamW(torch.optim.Optimizer):
     def _muon_issue(p, owner):
         return dist.reduce(grad_of(p), dst=owner, op=dist.ReduceOp.SUM, async_op=True)
 
+    def _stacked(self, group, world):
+        return (world > 1 and self.stack_muon and not self.defer_gathers and group["params"][0].is_cuda
+                and not any(p in self.p2p_params or p in self.gather_params or p in self._early
+                            for p in group["params"]))
+
+    def _stack(self, group, name, shape, like):
+        key = (id(group), name)
+        buf = self._stacks.get(key)
+        if buf is None or tuple(buf.shape) != tuple(shape):
+            buf = torch.zeros(shape, device=like.device, dtype=torch.float32)
+            self._stacks[key] = buf
+        return buf
+
     def _muon_reduce(self, group, rank, world):
         params, chunk, _ = self._muon_owned(group, rank, world)
         if world == 1:
             return []
+        if self._stacked(group, world):
+            m, n = params[0].shape[-2:]
+            grads = [grad_of(p) for p in params]
+            full = self._stack(group, "grads", (chunk * world, m, n), params[0])
+            mine = self._stack(group, "mine", (chunk, m, n), params[0])
+            torch._foreach_copy_(list(full[:len(params)].unbind(0)), [g.float() for g in grads])
+            return ("stacked", dist.reduce_scatter_tensor(mine, full, op=dist.ReduceOp.SUM, async_op=True), mine)
         works = []
         for i, p in enumerate(params):
             if p in self.p2p_params:
@@ -283,8 +328,13 @@ class MuonAdamW(torch.optim.Optimizer):
         return works
 
     def _muon_apply(self, group, rank, world, works, gathers):
-        for w in works:
-            w.wait()
+        stacked = isinstance(works, tuple) and works and works[0] == "stacked"
+        if stacked:
+            works[1].wait()
+            reduced = works[2]
+        else:
+            for w in works:
+                w.wait()
         params, chunk, owned = self._muon_owned(group, rank, world)
         shape = params[0].shape
         m, n = shape[-2], shape[-1]
@@ -297,14 +347,18 @@ class MuonAdamW(torch.optim.Optimizer):
                     st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.float32)
                     st["second_momentum_buffer"] = torch.zeros((m, 1) if m >= n else (1, n), device=p.device,
                                                                dtype=torch.float32)
-            if world > 1:
+            own_grads = None
+            if stacked:
+                own_grads = list(reduced[:len(mine)].unbind(0))
+                reduced.div_(world)
+            elif world > 1:
                 for p in mine:
                     if p not in self.p2p_params:
                         grad_of(p).div_(world)
             if mine[0].is_cuda and self.gemm_shape_ok(m, n):
-                self._muon_cuda(group, mine, m, n, lr)
+                self._muon_cuda(group, mine, m, n, lr, own_grads)
             else:
-                grads = torch.stack([grad_of(p).float() for p in mine])
+                grads = torch.stack(own_grads if own_grads is not None else [grad_of(p).float() for p in mine])
                 stack = torch.stack([p.data for p in mine])
                 mom = torch.stack([self.state[p]["momentum_buffer"] for p in mine])
                 smb = torch.stack([self.state[p]["second_momentum_buffer"] for p in mine])
@@ -316,6 +370,15 @@ class MuonAdamW(torch.optim.Optimizer):
                     self.state[p]["second_momentum_buffer"].copy_(smb[j])
                     if p in self.shadows:
                         self.shadows[p].copy_(p.data)
+        if stacked:
+            # the owner's updated matrices go out in one all-gather of the group's stack
+            m, n = params[0].shape[-2:]
+            if owned:
+                torch._foreach_copy_(list(reduced[:len(owned)].unbind(0)), [params[i].data for i in owned])
+            full = self._stack(group, "params", (chunk * world, m, n), params[0])
+            work = dist.all_gather_into_tensor(full, reduced, async_op=True)
+            self._stack_finish.append((work, full, params))
+            return
         if world > 1:
             for i, p in enumerate(params):
                 if p in self.gather_params:
@@ -334,7 +397,7 @@ class MuonAdamW(torch.optim.Optimizer):
         return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64).to(tensors[0].device,
                                                                                    non_blocking=True)
 
-    def _muon_cuda(self, group, mine, m, n, lr):
+    def _muon_cuda(self, group, mine, m, n, lr, grads=None):
         from nexttransformer_b200.ops._ext import ext
         from nexttransformer_b200.ops import gemm as G
         lib = ext()
@@ -354,7 +417,8 @@ class MuonAdamW(torch.optim.Optimizer):
                 red=torch.empty(K, L, device=dev, dtype=torch.float32),
                 fscale=torch.empty(K, L, device=dev, dtype=torch.float32))
         w = self._work[key]
-        grads = [grad_of(p) for p in mine]
+        if grads is None:
+            grads = [grad_of(p) for p in mine]
         if any(g.dtype != torch.float32 or not g.is_contiguous() for g in grads):
             grads = [g.float().contiguous() for g in grads]
         g_ptr = self._ptrs(grads)
@@ -416,5 +480,12 @@ class MuonAdamW(torch.optim.Optimizer):
         self._pending = pending
         if not self.defer_gathers:
             self.flush()
+        for work, full, params in self._stack_finish:
+            work.wait()
+            torch._foreach_copy_([p.data for p in params], list(full[:len(params)].unbind(0)))
+            for p in params:
+                if p in self.shadows:
+                    self.shadows[p].copy_(p.data)
+        self._stack_finish = []
         if self.gather is not None and world > 1:
             self.gather()
