@@ -127,7 +127,7 @@ class _DeltaScan(Function):
 GATE_MODE = {"deltanet": 0, "gdn": 1, "kda": 2}
 # The fused chunk-term kernels; NT_FUSED_DELTA=0 keeps the fp32 PyTorch chunk terms.
 import os as _os
-FUSED_DELTA = _os.environ.get("NT_FUSED_DELTA", "0") == "1"
+FUSED_DELTA = _os.environ.get("NT_FUSED_DELTA", "1") == "1"
 
 
 class _DeltaChunk(Function):

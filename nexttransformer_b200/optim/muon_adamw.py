@@ -256,7 +256,31 @@ class MuonAdamW(torch.optim.Optimizer):
         return (p, slice(rank * n, (rank + 1) * n), work, out)
 
     def _adamw_plan(self, group, rank, world):
-        return [self._early.pop(p, None) or self._adamw_issue(p, rank, world) for p in group["params"]]
+        """Plans of a group's parameters; on several ranks the small tensors (updated whole on every
+        rank) share ONE averaging all-reduce of their concatenated gradients."""
+        plans, small = [], []
+        for p in group["params"]:
+            early = self._early.pop(p, None)
+            if early is not None:
+                plans.append(early)
+                continue
+            g = grad_of(p)
+            if (world > 1 and g is not None and p not in self.p2p_params and g.is_cuda
+                    and (p.numel() < 1024 or p.shape[0] % world)):
+                small.append(len(plans))
+                plans.append((p, None, None, g))
+                continue
+            plans.append(self._adamw_issue(p, rank, world))
+        if small:
+            grads = [plans[i][3] for i in small]
+            flat = torch.cat([g.reshape(-1).float() for g in grads])
+            work = dist.all_reduce(flat, op=dist.ReduceOp.AVG, async_op=True)
+            off = 0
+            for i, g in zip(small, grads):
+                n = g.numel()
+                plans[i] = (plans[i][0], None, work, flat[off:off + n].view(g.shape))
+                off += n
+        return plans
 
     def _adamw_apply(self, group, plans, world, gathers):
         b1, b2 = group["betas"]
