@@ -47,6 +47,8 @@ def main(argv=None):
     p.add_argument("--existing-core-resources", type=Path)
     p.add_argument("--max-chars", type=int, default=MAX_CHARS)
     p.add_argument("--vocab-size", type=int, default=VOCAB)
+    p.add_argument("--download-shards", type=int, default=None,
+                   help="fetch this many training shards (-1: all) and the validation shard before verifying")
     a = p.parse_args(argv)
     from nexttransformer_b200.runtime.site import resolve
     resolve(a)
@@ -60,6 +62,11 @@ def main(argv=None):
     out = Path(a.resources)
     out.mkdir(parents=True, exist_ok=True)
     with FileLock(str(out / "prepare.lock")):
+        if a.download_shards is not None:
+            from nexttransformer_b200.runtime.dataset import download
+            failed = [i for i, s in download(a.data_dir, a.download_shards).items() if s.startswith("failed")]
+            if failed:
+                raise SystemExit(f"{len(failed)} shard downloads failed (first: {failed[0]})")
         official = res.load_source_manifest(a.source_manifest)
         expected, val_sha = res.verify_dataset(a.data_dir, official, VALIDATION_SHARD)
         core_root = a.existing_core_resources or out
