@@ -41,6 +41,8 @@ def parse(argv=None):
     p.add_argument("--circle-stage-step", type=int, default=0, help="smoke-only curriculum offset")
     p.add_argument("--global-batch", type=int, default=0, help="smoke-only override of tokens per update")
     p.add_argument("--seed", type=int, default=None)
+    p.add_argument("--core", type=Path, default=None,
+                   help="CORE bundle directory (tasks.json + <label>.jsonl) scored at the configuration's CORE steps")
     a = p.parse_args(argv)
     from nexttransformer_b200.runtime.site import resolve
     resolve(a)
@@ -65,14 +67,42 @@ def plan(mc, tc, world, micro):
             "train_GFLOPs_per_input_token": theoretical_training_flops(mc) / 1e9}
 
 
-def make_stream(args, mc, rank, world, seed):
+def data_dir(args):
+    return args.data_dir or Path(args.resources) / "base_data_climbmix"
+
+
+def load_tokenizer(args):
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    return BPETokenizer.from_directory(Path(args.resources) / "tokenizer")
+
+
+def make_stream(args, mc, rank, world, seed, tok=None):
     from nexttransformer_b200.runtime.data import BestFitStream, SyntheticStream
     if args.data == "synthetic":
         return SyntheticStream(mc.vocab_size, mc.sequence_len, rank, world, seed=seed)
-    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
-    tok = BPETokenizer.from_directory(Path(args.resources) / "tokenizer")
-    return BestFitStream(args.data_dir or Path(args.resources) / "base_data_climbmix", tok, "train", rank, world,
-                         mc.sequence_len)
+    return BestFitStream(data_dir(args), tok or load_tokenizer(args), "train", rank, world, mc.sequence_len)
+
+
+def scheduled_evaluations(args, model, tc, tok, tasks, step, final, micro, rank, world, device):
+    """Counted BPB at the validation steps and CORE at the CORE steps (real data only), and at the
+    end the final train / validation BPB; returns the metric events to log."""
+    from nexttransformer_b200.evaluation.native import evaluate_native_bpb, evaluate_native_core
+    events = []
+    if tok is None:
+        return events
+    if step in tc.validation_steps():
+        res = evaluate_native_bpb(model, tok, data_dir(args), tc.val_tokens, micro, rank, world, device)
+        events.append({"event": "validation", "step": step, **res})
+    if tasks is not None and step in tc.core_steps():
+        res = evaluate_native_core(model, tok, tasks, device, rank, world, tc.core_max_per_task,
+                                   model.config.sequence_len)
+        events.append({"event": "core", "step": step, **res})
+    if final:
+        both = {split: evaluate_native_bpb(model, tok, data_dir(args), tc.final_bpb_tokens, micro, rank, world,
+                                           device, split) for split in ("train", "val")}
+        events.append({"event": "final_bpb", "step": step, "train_bpb": both["train"]["train_bpb"],
+                       "val_bpb": both["val"]["val_bpb"], "train": both["train"], "val": both["val"]})
+    return events
 
 
 def update(model, optimizer, stream, mc, tc, accum, micro, world, device, step):
@@ -136,7 +166,12 @@ def main(argv=None):
     if rank == 0:
         out.mkdir(parents=True, exist_ok=True)
     accum = tc.accumulation(mc, world, micro)
-    stream = make_stream(args, mc, rank, world, seed)
+    tok = load_tokenizer(args) if args.data == "bestfit" else None
+    stream = make_stream(args, mc, rank, world, seed, tok)
+    tasks = None
+    if args.core is not None and tok is not None:
+        from nexttransformer_b200.training.evals import load_core_bundle
+        tasks = load_core_bundle(args.core)
     model = build_model(mc, device, seed=seed)
     # The dense model trains through the fused sm_100a path on CUDA; the optimizer then writes the
     # bf16 shadows that path reads.
@@ -160,6 +195,10 @@ def main(argv=None):
     phase = None
     with start_tracker(out, rank, args.wandb_mode, dict(model=asdict(mc), train=asdict(tc)), device) as tracker:
         model.train()
+        if state["step"] == 0 and not args.smoke_steps:
+            for event in scheduled_evaluations(args, model, tc, tok, tasks, 0, False, micro, rank, world, device):
+                if rank == 0:
+                    tracker.log(event)
         for step in range(state["step"], stop):
             model.set_circle_step(step + args.circle_stage_step)
             mult = set_schedule(optimizer, step, tc)
@@ -190,6 +229,11 @@ def main(argv=None):
                                            seed)
                 if rank == 0:
                     tracker.log({"event": "validation", "step": step + 1, **res})
+            if not args.smoke_steps or args.smoke_val_tokens:
+                for event in scheduled_evaluations(args, model, tc, tok, tasks, step + 1, step + 1 == tc.steps, micro,
+                                                   rank, world, device):
+                    if rank == 0:
+                        tracker.log(event)
             if (every and (step + 1) % every == 0) or step + 1 == stop:
                 ckpt.save_checkpoint(out, model, optimizer, stream, mc, tc, state, rank, world)
         if rank == 0:

@@ -90,3 +90,32 @@ def test_budget_updates_and_depth_law():
     assert out["budget_updates"] == 1
     with pytest.raises(ValueError):
         m.update_route_budget([100, 70, 20], 100, 0)
+
+
+@pytest.mark.parametrize("arch", ["mor", "circle"])
+def test_counted_native_evaluation(tmp_path, arch):
+    """Counted BPB reads exactly its token budget and reports route accounting; CORE through the
+    counted model scores every example."""
+    pa = pytest.importorskip("pyarrow")
+    import pyarrow.parquet as pq
+    from nexttransformer_b200.evaluation.native import evaluate_native_bpb, evaluate_native_core
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    words = ["alpha", "beta", "gamma", "delta", "epsilon", "zeta"]
+    docs = [" ".join(words[(i + j) % 6] for j in range(3 + i % 11)) for i in range(300)]
+    for k, name in enumerate(("shard_00000.parquet", "shard_06542.parquet")):
+        pq.write_table(pa.table({"text": docs[k * 150:(k + 1) * 150]}), tmp_path / name, row_group_size=25)
+    tok = BPETokenizer.train_from_iterator(docs, vocab_size=300)
+    c = NativeModelConfig(**_cfg(arch, vocab_size=320))
+    m = native.build_model(c, "cpu", seed=1)
+    res = evaluate_native_bpb(m, tok, tmp_path, tokens=4 * c.sequence_len, batch=2, rank=0, world=1,
+                              device=torch.device("cpu"))
+    assert res["input_tokens"] == 4 * c.sequence_len and res["val_bpb"] > 0
+    assert len(res["active_ratios"]) == c.routing_steps and res["forward_flops_estimate"] > 0
+    assert ("mean_ring_steps" in res) == (arch == "circle") and m.training
+    with pytest.raises(ValueError):
+        evaluate_native_bpb(m, tok, tmp_path, tokens=3 * c.sequence_len, batch=2, rank=0, world=1,
+                            device=torch.device("cpu"))
+    tasks = [{"label": "lm", "random_baseline": 0.0, "meta": {"task_type": "language_modeling", "num_fewshot": 0},
+              "data": [{"context": "alpha beta", "continuation": " gamma"}] * 2}]
+    core = evaluate_native_core(m, tok, tasks, torch.device("cpu"))
+    assert core["full_core"] and core["entries"] == 1 and core["input_tokens"] > 0 and 0 <= core["core_metric"] <= 1

@@ -71,3 +71,41 @@ def test_preflight_halves_on_oom(tmp_path):
     assert json.loads((tmp_path / "pf.json").read_text())["status"] == "passed"
     with pytest.raises(RuntimeError):
         preflight.main(["--config", str(cfg), "--output", str(tmp_path / "pf2.json")], runner=runner, busy="123")
+
+
+def test_native_full_run_scheduled_evaluations(tmp_path, monkeypatch):
+    """A full (non-smoke) run on real data logs counted validation BPB at every validation step,
+    CORE at the final step and the final train / validation BPB."""
+    pa = pytest.importorskip("pyarrow")
+    import pyarrow.parquet as pq
+    from nexttransformer_b200.native import train
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    words = ["alpha", "beta", "gamma", "delta", "epsilon", "zeta"]
+    docs = [" ".join(words[(i + j) % 6] for j in range(3 + i % 11)) for i in range(300)]
+    data = tmp_path / "data"
+    data.mkdir()
+    for k, name in enumerate(("shard_00000.parquet", "shard_06542.parquet")):
+        pq.write_table(pa.table({"text": docs[k * 150:(k + 1) * 150]}), data / name, row_group_size=25)
+    BPETokenizer.train_from_iterator(docs, vocab_size=300).save(tmp_path / "res" / "tokenizer")
+    bundle = tmp_path / "bundle"
+    bundle.mkdir()
+    (bundle / "tasks.json").write_text(json.dumps([{"label": "lm", "random_baseline": 0.0,
+                                                    "meta": {"task_type": "language_modeling", "num_fewshot": 0}}]))
+    (bundle / "lm.jsonl").write_text(json.dumps({"context": "alpha beta", "continuation": " gamma"}) + "\n")
+    cfg = tmp_path / "mor.json"
+    write_config(cfg, NativeModelConfig(**dict(TINY, architecture="mor", vocab_size=320)),
+                 NativeTrainConfig(total_tokens=64, global_batch_tokens=32, val_tokens=32, final_bpb_tokens=32,
+                                   val_every=1, checkpoint_every=2))
+    state = train.main(["--config", str(cfg), "--output", str(tmp_path / "run"), "--micro-batch", "1",
+                        "--data", "bestfit", "--data-dir", str(data), "--resources", str(tmp_path / "res"),
+                        "--core", str(bundle)])
+    assert state["step"] == 2
+    events = [json.loads(l) for l in (tmp_path / "run" / "metrics.jsonl").read_text().splitlines()]
+    val = [e for e in events if e["event"] == "validation"]
+    assert [e["step"] for e in val] == [0, 1, 2] and all(e["input_tokens"] == 32 and e["val_bpb"] > 0 for e in val)
+    assert "mean_recursions" in val[0]
+    core = [e for e in events if e["event"] == "core"]
+    assert [e["step"] for e in core] == [2] and core[0]["full_core"]
+    final = [e for e in events if e["event"] == "final_bpb"]
+    assert len(final) == 1 and final[0]["train_bpb"] > 0 and final[0]["val_bpb"] > 0
