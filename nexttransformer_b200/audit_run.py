@@ -5,6 +5,7 @@ this package's trainer writes).
     python -m nexttransformer_b200.audit_run RUN_DIR --method gdn [--output audits/gdn.json]
     python -m nexttransformer_b200.audit_run RUN_DIR --method gdn --export results/gdn.json --name "Gated DeltaNet"
     python -m nexttransformer_b200.audit_run --check results/
+    python -m nexttransformer_b200.audit_run RUN_DIR --frozen audits/gdn.json --export results/gdn.json
 
 The audit re-reads everything the trainer wrote and checks it against the protocol: the ledger in
 ``run_status.json`` (all updates and input tokens, the protocol fingerprint, the validation / CORE
@@ -15,9 +16,15 @@ validation events against their ``val_*.json`` files, and the provenance of ever
 batch).  The report records scientific quantities and fingerprints only - no host names, paths,
 devices or timings - and the command exits non-zero when a check fails.  An export refuses a run
 whose audit failed; ``--check`` validates every record of a results directory.
+
+``--frozen AUDIT`` exports an archived run under the accounting its audit was made with, without
+re-auditing it under the current ledger (``nexttransformer/export_frozen.py`` of the reference):
+the run's ``metrics.jsonl`` must still hash to the audit's digest, the audit must have passed, and
+every field of the record must equal the audit's; the record carries the audit's own sha256.
 """
 import argparse
 from datetime import date
+import hashlib
 import json
 import math
 from pathlib import Path
@@ -99,13 +106,15 @@ def audit(run, method, protocol=None, dense_flops_per_token=None):
                              accumulation=p["gradient_accumulation"]))
 
     final_val = [e for e in val if e["step"] == P.steps]
+    digest = hashlib.sha256((run / "metrics.jsonl").read_bytes()).hexdigest()
     report = dict(schema="run-audit-v1", method=method, date=date.today().isoformat(), checks=CHECKS,
                   ok=not problems, problems=problems, optimizer_steps=ledger.get("optimizer_step"),
                   input_tokens=ledger.get("input_tokens"), theory_flops=ledger.get("theory_flops"),
                   dense_flops_per_token=anchor, cumulative_relative_error=cumulative, train_events=len(train),
                   validation_events=len(val), last_loss=train[-1]["lm_loss"] if train else None,
                   final_val=_val_metric(final_val[0]) if final_val else None, segments=segments,
-                  protocol_hash=P.fingerprint, model=first["model"])
+                  protocol_hash=P.fingerprint, model=first["model"], metrics_sha256=digest,
+                  accounting=first.get("accounting", "ledger-v1"))
     return report, problems
 
 
@@ -116,6 +125,31 @@ def export_record(report, name):
     return dict(schema="run-record-v1", method=report["method"], name=name, status="complete",
                 step=report["optimizer_steps"], val=report["final_val"], protocol_hash=report["protocol_hash"],
                 audit={k: report[k] for k in ("date", "cumulative_relative_error", "theory_flops", "segments")})
+
+
+FROZEN_NOTE = "Frozen accounting: the record keeps the cumulative FLOPs and fingerprints of its original audit."
+
+
+def export_frozen(run, audit_path, name=None):
+    """Record of an archived run under its audit's (frozen) accounting; raises on any difference
+    between the run directory, the audit and the record."""
+    run, audit_path = Path(run), Path(audit_path)
+    raw = audit_path.read_bytes()
+    report = json.loads(raw)
+    if hashlib.sha256((run / "metrics.jsonl").read_bytes()).hexdigest() != report.get("metrics_sha256"):
+        raise ValueError("metrics.jsonl differs from the audited archive")
+    events = [json.loads(line) for line in (run / "metrics.jsonl").read_text().splitlines() if line.strip()]
+    train = [e for e in events if e["event"] == "train"]
+    val = [e for e in events if e["event"] == "validation"]
+    record = export_record(report, name or report["method"])
+    observed = {"optimizer_steps": train[-1]["step"] if train else None, "train_events": len(train),
+                "validation_events": len(val), "final_val": _val_metric(val[-1]) if val else None}
+    mismatched = [k for k, v in observed.items() if report.get(k) != v]
+    if mismatched or record["val"] != report["final_val"] or record["step"] != report["optimizer_steps"]:
+        raise ValueError(f"archived run differs from its audit: {mismatched or ['record']}")
+    record.update(accounting=report.get("accounting", "ledger-v1"), comparisonNote=FROZEN_NOTE,
+                  auditSha256=hashlib.sha256(raw).hexdigest(), metrics_sha256=report["metrics_sha256"])
+    return record
 
 
 def check_records(directory, protocol=None):
@@ -144,7 +178,21 @@ def main(argv=None):
     parser.add_argument("--export", type=Path, help="also write the results record here")
     parser.add_argument("--name", help="display name of the exported record")
     parser.add_argument("--check", type=Path, help="validate every record of this results directory")
+    parser.add_argument("--frozen", type=Path, help="export RUN_DIR under this archived audit's accounting")
     args = parser.parse_args(argv)
+    if args.frozen:
+        if args.run_dir is None or args.export is None:
+            parser.error("--frozen needs RUN_DIR and --export")
+        record = export_frozen(args.run_dir, args.frozen, args.name)
+        if args.export.exists():
+            if json.loads(args.export.read_text()) != record:
+                raise SystemExit(f"{args.export}: published frozen record differs")
+            print(f"unchanged {args.export}")
+            return
+        args.export.parent.mkdir(parents=True, exist_ok=True)
+        args.export.write_text(json.dumps(record, indent=1) + "\n")
+        print(f"wrote {args.export}")
+        return
     if args.check:
         problems = check_records(args.check)
         for p in problems:

@@ -62,3 +62,27 @@ def test_audit_finds_problems(tmp_path):
     assert "val_00000002.json" in text and "formal" in text and "cumulative" in text
     with pytest.raises(ValueError):
         export_record(report, "Dense")
+
+
+def test_frozen_export_checks_the_archive(tmp_path):
+    from nexttransformer_b200.audit_run import export_frozen
+    run = _run(tmp_path)
+    report, problems = audit(run, "dense", protocol=P, dense_flops_per_token=ANCHOR)
+    assert not problems
+    path = tmp_path / "audit.json"
+    path.write_text(json.dumps(report))
+    record = export_frozen(run, path, "Dense")
+    assert record["val"] == report["final_val"] and record["metrics_sha256"] == report["metrics_sha256"]
+    assert len(record["auditSha256"]) == 64 and record["accounting"] == "ledger-v1"
+    with open(run / "metrics.jsonl", "a") as f:
+        f.write(json.dumps(dict(event="train", step=5, input_tokens=5 * 4096, lm_loss=1.0)) + "\n")
+    with pytest.raises(ValueError, match="archive"):
+        export_frozen(run, path)
+    bad = dict(report, ok=False, problems=["x"])
+    path.write_text(json.dumps(bad))
+    (tmp_path / "b").mkdir()
+    run2 = _run(tmp_path / "b")
+    bad["metrics_sha256"] = audit(run2, "dense", protocol=P, dense_flops_per_token=ANCHOR)[0]["metrics_sha256"]
+    path.write_text(json.dumps(bad))
+    with pytest.raises(ValueError, match="audit failed"):
+        export_frozen(run2, path)
