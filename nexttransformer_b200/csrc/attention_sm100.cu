@@ -20,6 +20,7 @@
 
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -80,6 +81,48 @@ NT_DEVICE float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pairs (sm_100a f32x2 instructions: one issue slot for two lanes' worth of math).
+NT_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+NT_DEVICE float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe instead of the MUFU unit, which caps the softmax at 16
+// exponentials per clock per SM.  Range reduction to the nearest integer j (adding 1.5 x 2^23
+// rounds x into the low mantissa bits), then 2^f for f in [-1/2, 1/2] by a cubic fitted here for
+// minimum relative error (Lawson-weighted least squares; max relative error 7.5e-5, below bf16's
+// 2^-9 rounding of P), and j added to the exponent field.  The split of a softmax between this and
+// ex2.approx follows the FlashAttention-4 write-up (software exponentials on the FMA units).
+// Inputs are clamped at -125 (2^-125 stands in for 0: far below any row maximum's share).
+NT_DEVICE float2 exp2_fma2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 x 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 r = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = add2(x, make_float2(-r.x, -r.y));
+  float2 q = fma2(make_float2(0.05517166853f, 0.05517166853f), f, make_float2(0.24261112511f, 0.24261112511f));
+  q = fma2(q, f, make_float2(0.69326096773f, 0.69326096773f));
+  q = fma2(q, f, make_float2(0.99992805719f, 0.99992805719f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+// Of every 8 exponential pairs of a softmax row, FWD_EMU go to exp2_fma2 (the rest to MUFU);
+// NT_ATTN_FWD_EMU selects another compiled split (0, 2, 3 or 4) for measurement.
+constexpr int FWD_EMU_DEFAULT = 3;
+
 // ------------------------------------------------------------------------------ forward
 // One CTA per pair of consecutive query tiles (A = 2c, B = 2c + 1) of one (head, batch); 320 threads.
 // The two tiles share every K/V tile load, and their softmax warpgroups alternate with the MMAs:
@@ -123,6 +166,7 @@ NT_DEVICE void fwd_kv_range(const Params& p, int qt, int& lo, int& hi) {
   hi = qt;
 }
 
+template <int FWD_EMU>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
@@ -332,22 +376,25 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_wait_st();
       }
       m = m_new;
-      // P = exp2(S scale - m) as bf16 over columns [0, 64) of this tile's S (S is in registers)
-      float sum0 = 0.f, sum1 = 0.f;
+      // P = exp2(S scale - m) as bf16 over columns [0, 64) of this tile's S (S is in registers);
+      // FWD_EMU of every 8 pairs on the FMA pipe, the others on MUFU
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mref, -mref);
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e]), p.scale_log2, -mref));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(v[c * 32 + e + 1]), p.scale_log2, -mref));
-          sum0 += e0;
-          sum1 += e1;
-          pk[e / 2] = pack_bf16x2(e0, e1);
+          const float2 x = fma2(make_float2(__uint_as_float(v[c * 32 + e]), __uint_as_float(v[c * 32 + e + 1])),
+                                sc2, nm2);
+          const float2 ev = ((e >> 1) & 7) < FWD_EMU ? exp2_fma2(x)
+                                                            : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          acc = add2(acc, ev);
+          pk[e / 2] = pack_bf16x2(ev.x, ev.y);
         }
         tmem_st16(t_s + lane_off + c * 16, pk);
       }
-      const float sum = sum0 + sum1;
+      const float sum = acc.x + acc.y;
       l = l * alpha + sum;
       tmem_wait_st();
       tc_fence_before();
@@ -926,11 +973,23 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
   CUtensorMap to = tile_map(a.o, static_cast<int64_t>(a.H) * HD, a.ldo, a.T, a.B);
   Params p = make_params(a);
-  static std::atomic<uint64_t> smem_set{0};
-  nt::smem_limit(smem_set, attn_fwd_kernel, FwdSmem::TOTAL);
+  static const int emu = [] {
+    const char* e = std::getenv("NT_ATTN_FWD_EMU");
+    return e ? std::atoi(e) : FWD_EMU_DEFAULT;
+  }();
   const int n_qt = (a.T + TILE - 1) / TILE;
   dim3 grid((n_qt + 1) / 2, a.H, a.B);
-  attn_fwd_kernel<<<grid, FWD_THREADS, FwdSmem::TOTAL, s>>>(tq, tk, tv, to, p);
+  auto launch = [&](auto kern, std::atomic<uint64_t>& set) {
+    nt::smem_limit(set, kern, FwdSmem::TOTAL);
+    kern<<<grid, FWD_THREADS, FwdSmem::TOTAL, s>>>(tq, tk, tv, to, p);
+  };
+  static std::atomic<uint64_t> set0{0}, set2{0}, set3{0}, set4{0};
+  switch (emu) {
+    case 0: launch(attn_fwd_kernel<0>, set0); break;
+    case 2: launch(attn_fwd_kernel<2>, set2); break;
+    case 4: launch(attn_fwd_kernel<4>, set4); break;
+    default: launch(attn_fwd_kernel<3>, set3); break;
+  }
   return 0;
 }
 

@@ -10,6 +10,7 @@
 #include "delta_prep.h"
 #include "delta_scan.h"
 #include "moe.h"
+#include "moe_route.h"
 #include "sparse_attn.h"
 #include "residual.h"
 #include "elementwise.h"
@@ -629,6 +630,74 @@ void moe_combine_bwd(const Tensor& dy, const Tensor& rows, const Tensor& row_of,
      "moe_combine_bwd");
 }
 
+// Fused routing: (choice, w, lse, row_of, src_of, grp_m, grp_k, counts, aux_grad, aux[2]) of fp32
+// logits [N, E]; P rows of padded layout.
+std::vector<Tensor> moe_route(const Tensor& logits, const OptT& bias, int64_t k, double aux_coeff, double z_coeff,
+                              const OptT& load) {
+  check_rows(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2, "router logits must be fp32 [N, E]");
+  const int N = static_cast<int>(logits.size(0)), E = static_cast<int>(logits.size(1)), K = static_cast<int>(k);
+  const int nblk = (N + NT_ROUTE_TOKENS - 1) / NT_ROUTE_TOKENS;
+  const int64_t P = (static_cast<int64_t>(N) * K + NT_ROUTE_PAD - 1) / NT_ROUTE_PAD * NT_ROUTE_PAD +
+                    static_cast<int64_t>(NT_ROUTE_PAD) * E;
+  auto i32 = logits.options().dtype(at::kInt);
+  auto f32 = logits.options();
+  Tensor choice = torch::empty({N, K}, i32), w = torch::empty({N, K}, f32), lse = torch::empty({N}, f32);
+  Tensor blk_counts = torch::empty({nblk, E}, i32), blk_offset = torch::empty({nblk, E}, i32);
+  Tensor blk_probs = torch::empty({nblk, E}, f32), blk_z = torch::empty({nblk}, f32);
+  Tensor counts = torch::empty({E}, i32), seg = torch::empty({E}, i32), grp_k = torch::empty({E + 1}, i32);
+  Tensor grp_m = torch::empty({P / NT_ROUTE_PAD}, i32), row_of = torch::empty({static_cast<int64_t>(N) * K}, i32);
+  Tensor src_of = torch::empty({P}, i32), aux_grad = torch::empty({E}, f32), aux = torch::empty({2}, f32);
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == E && bias->is_contiguous(), "bias: fp32 [E]");
+  if (load.has_value() && load->defined())
+    TORCH_CHECK(load->scalar_type() == at::kFloat && load->numel() == E && load->is_contiguous(), "load: fp32 [E]");
+  MoeRouteArgs a;
+  a.N = N;
+  a.E = E;
+  a.k = K;
+  a.P = static_cast<int>(P);
+  a.logits = logits.data_ptr<float>();
+  a.bias = static_cast<const float*>(ptr_or_null(bias));
+  a.aux_coeff = static_cast<float>(aux_coeff);
+  a.z_coeff = static_cast<float>(z_coeff);
+  a.choice = choice.data_ptr<int>();
+  a.w = w.data_ptr<float>();
+  a.lse = lse.data_ptr<float>();
+  a.blk_counts = blk_counts.data_ptr<int>();
+  a.blk_probs = blk_probs.data_ptr<float>();
+  a.blk_z = blk_z.data_ptr<float>();
+  a.counts = counts.data_ptr<int>();
+  a.seg_start = seg.data_ptr<int>();
+  a.blk_offset = blk_offset.data_ptr<int>();
+  a.grp_m = grp_m.data_ptr<int>();
+  a.grp_k = grp_k.data_ptr<int>();
+  a.row_of = row_of.data_ptr<int>();
+  a.src_of = src_of.data_ptr<int>();
+  a.load = static_cast<float*>(mptr_or_null(load));
+  a.aux_grad = aux_grad.data_ptr<float>();
+  a.aux = aux.data_ptr<float>();
+  ok(nt_moe_route(a, stream()), "moe_route");
+  return {choice, w, lse, row_of, src_of, grp_m, grp_k, counts, aux_grad, aux};
+}
+
+Tensor moe_route_bwd(const Tensor& logits, const Tensor& lse, const Tensor& choice, const Tensor& w, const OptT& dw,
+                     const Tensor& aux_grad, const OptT& daux, double z_coeff) {
+  check_rows(logits, "logits");
+  if (dw.has_value() && dw->defined())
+    TORCH_CHECK(dw->scalar_type() == at::kFloat && dw->is_contiguous() && dw->sizes() == w.sizes(), "dw: fp32 like w");
+  if (daux.has_value() && daux->defined())
+    TORCH_CHECK(daux->scalar_type() == at::kFloat && daux->numel() == 1 && daux->is_cuda(), "daux: fp32 device scalar");
+  Tensor d = torch::empty_like(logits);
+  ok(nt_moe_route_bwd(logits.data_ptr<float>(), lse.data_ptr<float>(), choice.data_ptr<int>(), w.data_ptr<float>(),
+                      static_cast<const float*>(ptr_or_null(dw)), aux_grad.data_ptr<float>(),
+                      static_cast<const float*>(ptr_or_null(daux)),
+                      static_cast<float>(z_coeff), d.data_ptr<float>(), static_cast<int>(logits.size(0)),
+                      static_cast<int>(logits.size(1)), static_cast<int>(choice.size(1)), stream()),
+     "moe_route_bwd");
+  return d;
+}
+
 void moe_pull_rows(const Tensor& peers, const Tensor& src_rank, const Tensor& src_row, const Tensor& out) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
   check_i32(src_rank, "src_rank");
@@ -877,6 +946,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("moe_pull_rows", &moe_pull_rows);
+  m.def("moe_route", &moe_route);
+  m.def("moe_route_bwd", &moe_route_bwd);
   m.def("moe_push_rows", &moe_push_rows);
   m.def("delta_scan_fwd", &delta_scan_fwd);
   m.def("delta_prep_fwd", &delta_prep_fwd, "per-chunk delta-rule terms (WY solve, gates, q/k norm)");

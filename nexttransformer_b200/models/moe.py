@@ -55,6 +55,9 @@ class MoEFFN(nn.Module):
         self._w_fc = self._w_proj = self._g_fc = self._g_proj = None
         self.last_aux = None
         self.last_stats = {}
+        # CUDA routing through the fused kernels (ops.moe.fused_route); False: the torch ops below
+        self.fused_route = True
+        self._plan = None
 
     # -------------------------------------------------------------- experts held by this rank
     def local_experts(self):
@@ -73,13 +76,24 @@ class MoEFFN(nn.Module):
 
     # -------------------------------------------------------------- routing
     def route(self, rows):
+        """(choice [T, k], weights [T, k], aux loss or None); on CUDA the fused kernels also leave
+        the grouped-GEMM row plan in ``self._plan`` and add the counts to ``self.load``."""
         logits = F.linear(rows.float(), self.router.weight.float())
+        self._plan = None
+        use_aux = self.training and bool(self.aux_loss_coeff or self.z_loss_coeff)
+        if self.fused_route and rows.is_cuda:
+            from nexttransformer_b200.ops.moe import fused_route, fused_route_supported
+            if fused_route_supported(logits, self.top_k):
+                choice, w, aux, self._plan = fused_route(
+                    logits, self.expert_bias, self.top_k, self.aux_loss_coeff if use_aux else 0.0,
+                    self.z_loss_coeff if use_aux else 0.0, self.load)
+                return choice, w, aux if use_aux else None
         probs = logits.softmax(-1)
         choice = (probs + self.expert_bias).topk(self.top_k, dim=-1).indices
         w = probs.gather(-1, choice)
         w = w / w.sum(-1, keepdim=True)
         aux = None
-        if self.training and (self.aux_loss_coeff or self.z_loss_coeff):
+        if use_aux:
             aux = logits.new_zeros(())
             if self.aux_loss_coeff:
                 # Switch-style balance loss: E * sum_e (fraction of assignments to e) * (mean router prob of e)
@@ -93,23 +107,25 @@ class MoEFFN(nn.Module):
     def forward(self, x):
         rows = x.reshape(-1, x.shape[-1])
         choice, w, self.last_aux = self.route(rows)
-        with torch.no_grad():
-            self.load += torch.bincount(choice.flatten(), minlength=self.num_experts).float()
+        if self._plan is None:
+            with torch.no_grad():
+                self.load += torch.bincount(choice.flatten(), minlength=self.num_experts).float()
         out = self.shared(rows) if self.shared is not None else torch.zeros_like(rows)
         if self.ep_size > 1:
             from nexttransformer_b200.parallel import expert as ep
+            choice = choice.long()
             if ep.peer_exchange_supported(self, rows) and self.ep_exchange == "peer":
                 routed = ep.peer_expert_combine(self, rows, choice, w)
             else:
                 routed = ep.expert_parallel_combine(self, rows, choice, w)
         elif rows.is_cuda and self._w_fc is not None:
             from nexttransformer_b200.ops.moe import grouped_experts_state
-            routed = grouped_experts_state(rows, choice, w, self)
+            routed = grouped_experts_state(rows, choice, w, self, self._plan)
         elif rows.is_cuda and rows.shape[-1] % 64 == 0 and self.expert(0).c_fc.weight.shape[0] % 64 == 0:
             from nexttransformer_b200.ops.moe import grouped_experts
             w_fc = torch.stack([e.c_fc.weight for e in self.local_experts()])
             w_proj = torch.stack([e.c_proj.weight for e in self.local_experts()])
-            routed = grouped_experts(rows, choice, w, w_fc, w_proj)
+            routed = grouped_experts(rows, choice, w, w_fc, w_proj, self._plan)
         else:
             routed = self.run_experts(rows, choice, w)
         out = out + routed

@@ -106,19 +106,56 @@ class _GroupedExperts(Function):
         return dx.to(xd), dw.view(T, -1).to(wd), dwf.to(fd), dwp.to(pd), None, None, None, None, None
 
 
-def grouped_experts(x, choice, w, w_fc, w_proj):
+def fused_route_supported(logits, k):
+    E = logits.shape[-1]
+    return (logits.is_cuda and E % 32 == 0 and 32 <= E <= 256 and 1 <= k <= min(16, E)
+            and getattr(ext(), "moe_route", None) is not None)
+
+
+class _Route(Function):
+    """Router softmax, biased top-k, normalised weights, losses and the row plan (moe_route.cu)."""
+
+    @staticmethod
+    def forward(ctx, logits, bias, k, aux_coeff, z_coeff, load):
+        choice, w, lse, row_of, src_of, grp_m, grp_k, counts, aux_grad, aux = ext().moe_route(
+            logits, bias, k, aux_coeff, z_coeff, load)
+        ctx.save_for_backward(logits, lse, choice, w, aux_grad)
+        ctx.z = z_coeff
+        ctx.mark_non_differentiable(choice, row_of, src_of, grp_m, grp_k, counts)
+        return choice, w, aux.sum(), row_of, src_of, grp_m, grp_k, counts
+
+    @staticmethod
+    def backward(ctx, _choice, dw, daux, *_plan):
+        logits, lse, choice, w, aux_grad = ctx.saved_tensors
+        d = ext().moe_route_bwd(logits, lse, choice, w, None if dw is None else dw.float().contiguous(), aux_grad,
+                                None if daux is None else daux.float().reshape(1), ctx.z)
+        return d, None, None, None, None, None
+
+
+def fused_route(logits, bias, k, aux_coeff=0.0, z_coeff=0.0, load=None):
+    """(choice int32 [T, k], w fp32 [T, k], aux scalar, plan) from fp32 router logits [T, E] in
+    three launches; ``plan`` has the keys of ``plan()``.  ``load`` (fp32 [E]) gains the counts."""
+    choice, w, aux, row_of, src_of, grp_m, grp_k, counts = _Route.apply(
+        logits.contiguous(), None if bias is None else bias.float().contiguous(), k, float(aux_coeff),
+        float(z_coeff), load)
+    return choice, w, aux, dict(row_of=row_of, src_of=src_of, grp_m=grp_m, grp_k=grp_k, P=src_of.numel(),
+                                counts=counts)
+
+
+def grouped_experts(x, choice, w, w_fc, w_proj, pl=None):
     """Routed-expert output sum_s w[t, s] expert_{choice[t, s]}(x[t]) for x [T, d] (CUDA).
 
     w_fc [E, F, d] and w_proj [E, d, F] are the stacked expert weights (any float dtype; the
-    GEMMs run in bf16 with fp32 accumulation, gradients come back in the weights' dtype)."""
-    pl = plan(choice, w_fc.shape[0])
+    GEMMs run in bf16 with fp32 accumulation, gradients come back in the weights' dtype).  ``pl``:
+    a row plan already made by ``fused_route``."""
+    pl = pl or plan(choice, w_fc.shape[0])
     return _GroupedExperts.apply(x, w, w_fc, w_proj, pl["row_of"], pl["src_of"], pl["grp_m"], pl["grp_k"])
 
 
-def grouped_experts_state(x, choice, w, moe):
+def grouped_experts_state(x, choice, w, moe, pl=None):
     """``grouped_experts`` on a layer's kernel state: the stacked bf16 shadows ``moe._w_fc`` /
     ``moe._w_proj`` are the operands and the weight gradients accumulate into the experts'
     ``main_grad`` stacks, so no per-forward stack or cast of the fp32 experts is made."""
-    pl = plan(choice, moe._w_fc.shape[0])
+    pl = pl or plan(choice, moe._w_fc.shape[0])
     return _GroupedExperts.apply(x, w, moe._w_fc, moe._w_proj, pl["row_of"], pl["src_of"], pl["grp_m"], pl["grp_k"],
                                  moe)
