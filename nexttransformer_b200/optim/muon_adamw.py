@@ -132,7 +132,9 @@ class MuonAdamW(torch.optim.Optimizer):
         # overlap state: parameter -> forward-use group, early-issued reductions, deferred gathers
         self.use_group = {}
         self.defer_gathers = False
-        self.stack_muon = True       # grouped reduce-scatter / all-gather of Muon matrices
+        # grouped reduce-scatter / all-gather of Muon matrices: True on CUDA, "always" on any device
+        # (gloo supports both collectives; the CPU tests use it), False: per-matrix reduce / broadcast
+        self.stack_muon = True
         self._stacks = {}
         self._stack_finish = []
         self._early = {}
@@ -320,7 +322,8 @@ class MuonAdamW(torch.optim.Optimizer):
         return dist.reduce(grad_of(p), dst=owner, op=dist.ReduceOp.SUM, async_op=True)
 
     def _stacked(self, group, world):
-        return (world > 1 and self.stack_muon and not self.defer_gathers and group["params"][0].is_cuda
+        return (world > 1 and self.stack_muon and not self.defer_gathers
+                and (group["params"][0].is_cuda or self.stack_muon == "always")
                 and not any(p in self.p2p_params or p in self.gather_params or p in self._early
                             for p in group["params"]))
 

@@ -206,3 +206,53 @@ def test_overlapped_reduce_and_deferred_gathers_match():
         results = m.dict()
         mp.start_processes(_overlap_worker, args=(port, results), nprocs=2, start_method="spawn")
         assert results[0] == 0.0 and results[1] == 0.0, dict(results)
+
+
+def _stacked_worker(rank, world, port, results):
+    """Stacked Muon reduce-scatter / all-gather equals the per-matrix reduce / broadcast at several
+    world sizes, shape groups with fewer matrices than ranks included."""
+    import os
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nexttransformer_b200.optim.muon_adamw import MuonAdamW
+
+    def make():
+        torch.manual_seed(0)
+        ps = [*[torch.nn.Parameter(torch.randn(32, 16)) for _ in range(5)], torch.nn.Parameter(torch.randn(24, 40)),
+              *[torch.nn.Parameter(torch.randn(16, 16)) for _ in range(2)]]
+        return ps, [dict(kind="muon", params=ps[:5], lr=2e-2, momentum=0.95, ns_steps=5, beta2=0.9, weight_decay=0.1),
+                    dict(kind="muon", params=ps[5:6], lr=2e-2, momentum=0.95, ns_steps=5, beta2=0.9, weight_decay=0.1),
+                    dict(kind="muon", params=ps[6:], lr=2e-2, momentum=0.95, ns_steps=5, beta2=0.9, weight_decay=0.1)]
+    ref_p, ref_g = make()
+    st_p, st_g = make()
+    ref, st = MuonAdamW(ref_g), MuonAdamW(st_g)
+    ref.stack_muon, st.stack_muon = False, "always"
+    for step in range(3):
+        g = torch.Generator().manual_seed(100 * step + rank)
+        for a, b in zip(ref_p, st_p):
+            a.grad = torch.randn(a.shape, generator=g)
+            b.grad = a.grad.clone()
+        ref.step()
+        st.step()
+    diff = max(float((a - b).abs().max()) for a, b in zip(ref_p, st_p))
+    gathered = [torch.zeros(1) for _ in range(world)]
+    dist.all_gather(gathered, torch.tensor([float(sum(p.sum() for p in st_p))]))
+    results[rank] = (diff, max(float(x) for x in gathered) - min(float(x) for x in gathered))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [3, 4])
+def test_stacked_muon_matches_per_matrix(world):
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.start_processes(_stacked_worker, args=(world, port, results), nprocs=world, start_method="spawn")
+        for r in range(world):
+            diff, spread = results[r]
+            assert diff < 1e-5 and spread == 0.0, dict(results)
