@@ -2,10 +2,16 @@
 
 Resolution happens before torch is imported by the entry points (cache directories and thread
 counts must be in the environment first), as in the reference's ``runtime/site.py``.
+
+``python -m nexttransformer_b200.runtime.site --shell [options]`` prints the resolved settings as
+shell ``export`` lines (``launch/env.sh`` evaluates them); the site JSON is read as data, and every
+value is shell-quoted, so nothing from it is executed.
 """
 import argparse
 import json
 import os
+import shlex
+import sys
 from pathlib import Path
 
 HOME = Path(os.environ.get("NEXTTRANSFORMER_HOME", Path.home() / ".cache" / "nexttransformer_b200"))
@@ -60,3 +66,25 @@ def bootstrap_runtime(argv=None):
     if r["cache_dir"] is not None:
         Path(r["cache_dir"]).mkdir(parents=True, exist_ok=True)
     return r
+
+
+def shell_exports(argv=None):
+    """``export VAR=value`` lines of every resolved setting (None values are skipped)."""
+    parser = add_runtime_arguments(argparse.ArgumentParser(add_help=False))
+    args, _ = parser.parse_known_args(argv)
+    r = resolve(args)
+    lines = []
+    for name, (env, _) in PATHS.items():
+        if r[name] is not None:
+            lines.append(f"export {env}={shlex.quote(str(r[name]))}")
+    for name, (env, _, _) in VALUES.items():
+        if r[name] is not None:
+            lines.append(f"export {env}={shlex.quote(str(r[name]))}")
+    return "\n".join(lines)
+
+
+if __name__ == "__main__":
+    argv = sys.argv[1:]
+    if "--shell" not in argv:
+        raise SystemExit("usage: python -m nexttransformer_b200.runtime.site --shell [--site-config F] [--runtime-dir D] ...")
+    print(shell_exports([a for a in argv if a != "--shell"]))
