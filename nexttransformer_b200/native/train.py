@@ -34,6 +34,8 @@ def parse(argv=None):
     p.add_argument("--dry-run", action="store_true")
     p.add_argument("--resume", default="never", help="never | auto")
     p.add_argument("--data", choices=("bestfit", "synthetic"), default="synthetic")
+    p.add_argument("--prefetch", type=int, default=2,
+                   help="micro-batches packed ahead on a background thread (real data; 0: pack inline)")
     p.add_argument("--smoke-steps", type=int, default=0)
     p.add_argument("--smoke-val-tokens", type=int, default=0)
     p.add_argument("--log-every", type=int, default=10)
@@ -168,6 +170,9 @@ def main(argv=None):
     accum = tc.accumulation(mc, world, micro)
     tok = load_tokenizer(args) if args.data == "bestfit" else None
     stream = make_stream(args, mc, rank, world, seed, tok)
+    if args.data == "bestfit" and args.prefetch > 0:
+        from nexttransformer_b200.runtime.prefetch import PrefetchStream
+        stream = PrefetchStream(stream, args.prefetch)
     tasks = None
     if args.core is not None and tok is not None:
         from nexttransformer_b200.training.evals import load_core_bundle

@@ -74,11 +74,13 @@ class BestFitStream:
         self.rows += 1
         return row
 
-    def batch(self, batch_size, device):
+    def cpu_batch(self, batch_size, pin=False):
         rows = torch.tensor([self._row() for _ in range(batch_size)], dtype=torch.long)
         x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
-        if torch.device(device).type == "cuda":
-            x, y = x.pin_memory(), y.pin_memory()
+        return (x.pin_memory(), y.pin_memory()) if pin else (x, y)
+
+    def batch(self, batch_size, device):
+        x, y = self.cpu_batch(batch_size, pin=torch.device(device).type == "cuda")
         return x.to(device, non_blocking=True), y.to(device, non_blocking=True)
 
     def batches(self, batch_size, device):
@@ -111,12 +113,14 @@ class SyntheticStream:
         g = torch.Generator().manual_seed((self.seed * 1_000_003 + self.rank) * 1_000_033 + r)
         return torch.randint(0, self.vocab_size, (self.sequence_len + 1,), generator=g)
 
-    def batch(self, batch_size, device):
+    def cpu_batch(self, batch_size, pin=False):
         rows = torch.stack([self._row(self.rows + i) for i in range(batch_size)])
         self.rows += batch_size
         x, y = rows[:, :-1].contiguous(), rows[:, 1:].contiguous()
-        if torch.device(device).type == "cuda":
-            x, y = x.pin_memory(), y.pin_memory()
+        return (x.pin_memory(), y.pin_memory()) if pin else (x, y)
+
+    def batch(self, batch_size, device):
+        x, y = self.cpu_batch(batch_size, pin=torch.device(device).type == "cuda")
         return x.to(device, non_blocking=True), y.to(device, non_blocking=True)
 
     def state_dict(self):

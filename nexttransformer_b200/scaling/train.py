@@ -112,6 +112,8 @@ def parse(argv=None):
     p.add_argument("--resume", default="never", help="never | auto | <step>")
     p.add_argument("--allow-source-change", action="store_true", help="resume with changed source files (recorded)")
     p.add_argument("--data", choices=("bestfit", "synthetic"), default="synthetic")
+    p.add_argument("--prefetch", type=int, default=2,
+                   help="micro-batches packed ahead on a background thread (real data; 0: pack inline)")
     p.add_argument("--smoke-steps", type=int, default=0, help="short test, never a completed pretraining run")
     p.add_argument("--smoke-val-tokens", type=int, default=0, help="0: one distributed evaluation batch")
     p.add_argument("--stop-after", type=int, default=0, help="checkpoint and stop after this many updates")
@@ -200,6 +202,9 @@ def main(argv=None):
     if world > 1:
         dist.barrier()
     stream = make_stream(args, mc, rank, world, tc.seed)
+    if args.data == "bestfit" and args.prefetch > 0:
+        from nexttransformer_b200.runtime.prefetch import PrefetchStream
+        stream = PrefetchStream(stream, args.prefetch)
     described = {"kind": args.data, "vocab": mc.vocab_size, "seq": mc.sequence_len, "seed": tc.seed, "world": world}
     if args.data == "bestfit":
         # every node must hold the same shards and the same tokenizer

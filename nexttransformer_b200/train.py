@@ -49,6 +49,8 @@ def parse(argv=None):
     p.add_argument("--debug-scale", action="store_true", help="tiny debug configuration of --method")
     p.add_argument("--output", type=Path, required=True)
     p.add_argument("--data", choices=("bestfit", "synthetic"), default="synthetic")
+    p.add_argument("--prefetch", type=int, default=2,
+                   help="micro-batches packed ahead on a background thread (real data; 0: pack inline)")
     p.add_argument("--steps", type=int, default=0, help="stop after this update (0: protocol length)")
     p.add_argument("--total-tokens", type=int, default=0, help="research: token budget of the schedule")
     p.add_argument("--global-batch", type=int, default=0, help="research: tokens per update")
@@ -177,6 +179,9 @@ def main(argv=None):
         tok = BPETokenizer.from_directory(Path(args.resources) / "tokenizer")
         stream = BestFitStream(args.data_dir or Path(args.resources) / "base_data_climbmix", tok, "train",
                                stream_rank, stream_world, T)
+        if args.prefetch > 0:
+            from nexttransformer_b200.runtime.prefetch import PrefetchStream
+            stream = PrefetchStream(stream, args.prefetch)
 
     model = build_model(config, device, seed=args.seed)
     model.set_sparse_backend(args.sparse_backend)

@@ -135,3 +135,35 @@ def test_optimizer_state_keeps_fp32_moments_of_bf16_tables():
     for key in ("exp_avg", "exp_avg_sq"):
         assert fresh.state[fresh_table][key].dtype == torch.float32
         assert torch.equal(fresh.state[fresh_table][key], opt.state[table][key])
+
+
+def test_prefetch_stream_is_exact(tmp_path):
+    """Prefetched batches, row counts and checkpoint states equal the plain stream's, across a
+    batch-size change and a resume."""
+    pa = pytest.importorskip("pyarrow")
+    import pyarrow.parquet as pq
+    from nexttransformer_b200.runtime.data import BestFitStream, SyntheticStream
+    from nexttransformer_b200.runtime.prefetch import PrefetchStream
+    from nexttransformer_b200.runtime.tokenizer import BPETokenizer
+    words = ["alpha", "beta", "gamma", "delta", "epsilon", "zeta"]
+    docs = [" ".join(words[(i + j) % 6] for j in range(3 + i % 11)) for i in range(400)]
+    for k, name in enumerate(("shard_00000.parquet", "shard_00001.parquet", "shard_06542.parquet")):
+        pq.write_table(pa.table({"text": docs[k * 100:(k + 1) * 100]}), tmp_path / name, row_group_size=20)
+    tok = BPETokenizer.train_from_iterator(docs, vocab_size=300)
+    cpu = torch.device("cpu")
+    for make in (lambda: BestFitStream(tmp_path, tok, "train", sequence_len=16, buffer_size=8, tokenizer_batch_size=4),
+                 lambda: SyntheticStream(300, 16, seed=3)):
+        plain, pre = make(), PrefetchStream(make(), depth=3)
+        for size in (3, 3, 2, 3):
+            a, b = plain.batch(size, cpu), pre.batch(size, cpu)
+            assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+            assert plain.rows == pre.rows
+        assert pre.state_dict() == plain.state_dict()
+        state = pre.state_dict()
+        nxt = plain.batch(2, cpu)
+        resumed = PrefetchStream(make(), depth=2)
+        resumed.load_state_dict(state)
+        got = resumed.batch(2, cpu)
+        assert torch.equal(nxt[0], got[0])
+        pre.close()
+        resumed.close()
