@@ -12,6 +12,7 @@
 #include "moe.h"
 #include "moe_route.h"
 #include "sparse_attn.h"
+#include "sparse_teacher.h"
 #include "residual.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
@@ -698,6 +699,45 @@ Tensor moe_route_bwd(const Tensor& logits, const Tensor& lse, const Tensor& choi
   return d;
 }
 
+// Head-mean teacher [B, Q, T] fp32 of q [B, H, Q, 128] and k [B, Hk, T, 128] (bf16, any strides with a
+// unit feature stride); mask [B, Q, T] bool / uint8 or None (causal only).
+Tensor sparse_teacher(const Tensor& q, const Tensor& k, const OptT& mask, int64_t q_start, double scale) {
+  check_cuda(q, "q");
+  check_cuda(k, "k");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16, "teacher: bf16 q and k");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && q.stride(3) == 1 && k.stride(3) == 1, "teacher: [B, H, L, D] views");
+  TeacherArgs a;
+  a.B = static_cast<int>(q.size(0));
+  a.H = static_cast<int>(q.size(1));
+  a.Q = static_cast<int>(q.size(2));
+  a.D = static_cast<int>(q.size(3));
+  a.Hk = static_cast<int>(k.size(1));
+  a.T = static_cast<int>(k.size(2));
+  a.q_start = static_cast<int>(q_start);
+  a.scale = static_cast<float>(scale);
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.sqb = q.stride(0);
+  a.sqh = q.stride(1);
+  a.sqt = q.stride(2);
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.skb = k.stride(0);
+  a.skh = k.stride(1);
+  a.skt = k.stride(2);
+  Tensor m;
+  if (mask.has_value() && mask->defined()) {
+    TORCH_CHECK(mask->dim() == 3 && mask->size(0) == a.B && mask->size(1) == a.Q && mask->size(2) == a.T,
+                "teacher: mask [B, Q, T]");
+    m = mask->to(at::kByte).contiguous();
+    a.mask = m.data_ptr<uint8_t>();
+  }
+  Tensor lse = torch::empty({a.B, a.H, a.Q}, q.options().dtype(at::kFloat));
+  Tensor out = torch::zeros({a.B, a.Q, a.T}, q.options().dtype(at::kFloat));
+  a.lse = lse.data_ptr<float>();
+  a.out = out.data_ptr<float>();
+  ok(nt_sparse_teacher(a, stream()), "sparse_teacher");
+  return out;
+}
+
 void moe_pull_rows(const Tensor& peers, const Tensor& src_rank, const Tensor& src_row, const Tensor& out) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
   check_i32(src_rank, "src_rank");
@@ -947,6 +987,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("moe_pull_rows", &moe_pull_rows);
   m.def("moe_route", &moe_route);
+  m.def("sparse_teacher", &sparse_teacher);
   m.def("moe_route_bwd", &moe_route_bwd);
   m.def("moe_push_rows", &moe_push_rows);
   m.def("delta_scan_fwd", &delta_scan_fwd);

@@ -37,6 +37,31 @@ constexpr int NT = 256;    // threads per CTA
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
+// 16 bytes at p (16-byte aligned) as floats: 8 bf16 or 4 fp32 elements.
+template <typename TIn>
+__device__ __forceinline__ void load_vec(const TIn* p, float (&out)[16 / sizeof(TIn)]);
+template <>
+__device__ __forceinline__ void load_vec<__nv_bfloat16>(const __nv_bfloat16* p, float (&out)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  // a bf16 is the upper half of the fp32 with the same value: widen by shifting
+  out[0] = __uint_as_float(raw.x << 16);
+  out[1] = __uint_as_float(raw.x & 0xffff0000u);
+  out[2] = __uint_as_float(raw.y << 16);
+  out[3] = __uint_as_float(raw.y & 0xffff0000u);
+  out[4] = __uint_as_float(raw.z << 16);
+  out[5] = __uint_as_float(raw.z & 0xffff0000u);
+  out[6] = __uint_as_float(raw.w << 16);
+  out[7] = __uint_as_float(raw.w & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void load_vec<float>(const float* p, float (&out)[4]) {
+  const float4 f = __ldg(reinterpret_cast<const float4*>(p));
+  out[0] = f.x;
+  out[1] = f.y;
+  out[2] = f.z;
+  out[3] = f.w;
+}
+
 __device__ __forceinline__ float sum16(float v) {  // sum over 16 consecutive lanes
   v += __shfl_xor_sync(0xffffffffu, v, 8);
   v += __shfl_xor_sync(0xffffffffu, v, 4);
@@ -87,25 +112,54 @@ __device__ void load_chunk(const DeltaPrepArgs& a, float* sm, int n, int h, int 
   const TIn* q = reinterpret_cast<const TIn*>(a.q) + base;
   const TIn* k = reinterpret_cast<const TIn*>(a.k) + base;
   const TIn* v = reinterpret_cast<const TIn*>(a.v) + base;
-  for (int e = tid; e < C * D; e += NT) {
-    const int i = e / D, d = e % D;
-    const int t = t0 + i;
-    float qv = 0.f, kv = 0.f, vv = 0.f;
-    if (t < a.T) {
-      qv = to_f(q[t * rs + d]);
-      kv = to_f(k[t * rs + d]);
-      vv = to_f(v[t * rs + d]);
+  // 16-byte vector loads, every pass's loads issued before any is used (one memory latency, not one
+  // per element): VEC elements per load, LPR lanes per 128-feature row, RPP rows per pass
+  {
+    constexpr int VEC = 16 / static_cast<int>(sizeof(TIn));
+    constexpr int LPR = D / VEC, RPP = NT / LPR, PASSES = C / RPP;
+    const int d0 = (tid % LPR) * VEC, i0 = tid / LPR;
+    float qv[PASSES][VEC], kv[PASSES][VEC], vv[PASSES][VEC];
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const int t = t0 + i0 + ps * RPP;
+      if (t < a.T) {
+        load_vec<TIn>(q + t * rs + d0, qv[ps]);
+        load_vec<TIn>(k + t * rs + d0, kv[ps]);
+        load_vec<TIn>(v + t * rs + d0, vv[ps]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) qv[ps][u] = kv[ps][u] = vv[ps][u] = 0.f;
+      }
     }
-    sq[i * LDF + d] = qv;
-    sk[i * LDF + d] = kv;
-    sv[i * D + d] = __float2bfloat16_rn(vv);
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const int i = i0 + ps * RPP;
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) {
+        sq[i * LDF + d0 + u] = qv[ps][u];
+        sk[i * LDF + d0 + u] = kv[ps][u];
+        sv[i * D + d0 + u] = __float2bfloat16_rn(vv[ps][u]);
+      }
+    }
   }
   if (GATE == DELTA_FEATURE) {
-    for (int e = tid; e < C * D; e += NT) {
-      const int i = e / D, d = e % D;
-      const int t = t0 + i;
-      sb[i * LDF + d] = t < a.T ? a.g[((static_cast<int64_t>(b) * a.T + t) * a.H + h) * D + d] : 0.f;
+    constexpr int LPR = D / 4, RPP = NT / LPR, PASSES = C / RPP;
+    const int d0 = (tid % LPR) * 4, i0 = tid / LPR;
+    float gv[PASSES][4];
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const int t = t0 + i0 + ps * RPP;
+      if (t < a.T) {
+        load_vec<float>(a.g + ((static_cast<int64_t>(b) * a.T + t) * a.H + h) * D + d0, gv[ps]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) gv[ps][u] = 0.f;
+      }
     }
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sb[(i0 + ps * RPP) * LDF + d0 + u] = gv[ps][u];
   } else if (GATE == DELTA_SCALAR) {
     if (tid < C) {
       const int t = t0 + tid;
@@ -317,8 +371,10 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
   // from the forward's bf16 outputs in the stages below (the scan consumed the same values).
   float y[C];
 #pragma unroll
+  for (int i = 0; i < C; ++i) y[i] = __ldg(dX + i * D);  // all 64 loads in flight before the solve
+#pragma unroll
   for (int i = C - 1; i >= 0; --i) {
-    float s = dX[i * D];
+    float s = y[i];
 #pragma unroll
     for (int k = C - 1; k > i; --k) s = fmaf(-sA[k * LDA + i], y[k], s);
     y[i] = s;
@@ -348,11 +404,20 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
       for (int i = 0; i < C; ++i) sY[i * LDA + cc] = y[i];
     }
     {
+      // X columns [c0, c0 + 64) of this stage: two 16-byte loads per thread, both in flight
       const __nv_bfloat16* src = st < 2 ? xw : xu;
       const int c0 = 64 * (st & 1);
-      for (int e = tid; e < C * 64; e += NT) {
-        const int i = e >> 6, cc = e & 63;
-        sX[i * LDA + cc] = __bfloat162float(src[i * D + c0 + cc]);
+      float xv[2][8];
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+        const int e = tid + ps * NT, i = e >> 3, cc = (e & 7) * 8;
+        load_vec<__nv_bfloat16>(src + i * D + c0 + cc, xv[ps]);
+      }
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+        const int e = tid + ps * NT, i = e >> 3, cc = (e & 7) * 8;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sX[i * LDA + cc + u] = xv[ps][u];
       }
     }
     __syncthreads();
@@ -407,6 +472,11 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
   float* sGq = sX;    // stage buffers are free now
   float* sM = sY;
   const float* daqk = a.daqk + row0 * C;
+  float dqv[4][4];  // this thread's daqk entries, loaded together
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) dqv[r][c] = __ldg(daqk + (4 * ti + r) * C + tj + 16 * c);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int i = 4 * ti + r;
@@ -419,7 +489,7 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
       const float akk_ungated = sK2[i * LDA + j];
       dbeta_p[r] = fmaf(dAij, akk_ungated * p, dbeta_p[r]);
       const float dakk = be * dAij;
-      const float dq_ = j <= i ? daqk[i * C + j] : 0.f;
+      const float dq_ = j <= i ? dqv[r][c] : 0.f;
       sA[i * LDA + j] = dakk * p;       // Gk
       sGq[i * LDA + j] = dq_ * p;       // Gq
       if (GATE == DELTA_SCALAR) sM[i * LDA + j] = (dakk * akk_ungated + dq_ * sQ2[i * LDA + j]) * p;
@@ -481,10 +551,16 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int i = 4 * ti + r;
+    float gqv[8], gkv[8];  // the row's incoming gradients, loaded together
+#pragma unroll
+    for (int oc = 0; oc < 8; ++oc) {
+      gqv[oc] = __ldg(dqt + i * D + tj + 16 * oc);
+      gkv[oc] = __ldg(dkc + i * D + tj + 16 * oc);
+    }
 #pragma unroll
     for (int oc = 0; oc < 8; ++oc) {
       const int d = tj + 16 * oc;
-      const float gq_in = dqt[i * D + d], gkc = dkc[i * D + d];
+      const float gq_in = gqv[oc], gkc = gkv[oc];
       if (GATE == DELTA_SCALAR) {
         const float eb = __expf(sb[i]), el = __expf(sb[C - 1] - sb[i]);
         const float qh = sm[S::Q + i * LDF + d], kh = sm[S::K + i * LDF + d];
@@ -665,8 +741,14 @@ static_assert(Smem<DELTA_SCALAR>::BYTES <= 232448, "GDN chunk terms exceed the s
 }  // namespace dprep
 }  // namespace nt
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The chunk loads are 16-byte vectors: q / k / v, the per-feature gate and the forward's w / u0
+// must start on 16-byte boundaries (rows are 128 features, so every row then does too).
 static bool prep_args_ok(const DeltaPrepArgs& a) {
-  return a.B > 0 && a.T > 0 && a.H > 0 && a.q && a.k && a.v && a.beta && (a.gate == DELTA_NONE || a.g);
+  return a.B > 0 && a.T > 0 && a.H > 0 && a.q && a.k && a.v && a.beta && (a.gate == DELTA_NONE || a.g) &&
+         aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && (a.gate != DELTA_FEATURE || aligned16(a.g)) &&
+         (!a.w || aligned16(a.w)) && (!a.u0 || aligned16(a.u0));
 }
 
 int nt_delta_prep_fwd(const DeltaPrepArgs& a, cudaStream_t s) {

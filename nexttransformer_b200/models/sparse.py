@@ -282,8 +282,14 @@ class SparseMixer(nn.Module):
                             sel = torch.zeros_like(domain, dtype=torch.int32)
                             sel.scatter_add_(-1, idx, valid.to(torch.int32))
                             domain = sel > 0
-                        raw = torch.matmul(qq.float(), k.float().transpose(-2, -1)) * c.head_dim ** -.5
-                        teacher = safe_softmax(raw, domain).mean(1)
+                        from nexttransformer_b200.ops.sparse_teacher import head_mean_teacher, kernel_supported
+                        if kernel_supported(qq, k):
+                            # two-pass kernel: no [B, H, Q, T] scores; the domain is shared by the heads
+                            teacher = head_mean_teacher(qq, k, None if burnin else domain[:, 0], start,
+                                                        c.head_dim ** -.5)
+                        else:
+                            raw = torch.matmul(qq.float(), k.float().transpose(-2, -1)) * c.head_dim ** -.5
+                            teacher = safe_softmax(raw, domain).mean(1)
                         student_dom = complete[None].expand(B, -1, -1)
                         if size > 1:
                             teacher = pool_teacher(teacher, size, ik.shape[2], self.kind)
