@@ -13,6 +13,7 @@
 #include "moe_route.h"
 #include "sparse_attn.h"
 #include "sparse_teacher.h"
+#include "nsa_compress.h"
 #include "residual.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
@@ -738,6 +739,66 @@ Tensor sparse_teacher(const Tensor& q, const Tensor& k, const OptT& mask, int64_
   return out;
 }
 
+// NSA compressed branch: q [B, T, H, 128], ck / cv [B, Nc, Hk, 128] bf16 contiguous.
+static NsaArgs nsa_args(const Tensor& q, const Tensor& ck, const Tensor& cv, int64_t cstride, int64_t csize,
+                        int64_t ssize, int64_t topk, double scale) {
+  for (const Tensor* t : {&q, &ck, &cv}) {
+    check_rows(*t, "nsa operand");
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4, "nsa operands: bf16 [B, L, heads, 128]");
+  }
+  NsaArgs a;
+  a.B = static_cast<int>(q.size(0));
+  a.T = static_cast<int>(q.size(1));
+  a.H = static_cast<int>(q.size(2));
+  a.D = static_cast<int>(q.size(3));
+  a.Nc = static_cast<int>(ck.size(1));
+  a.Hk = static_cast<int>(ck.size(2));
+  a.cstride = static_cast<int>(cstride);
+  a.csize = static_cast<int>(csize);
+  a.ssize = static_cast<int>(ssize);
+  a.topk = static_cast<int>(topk);
+  a.scale = static_cast<float>(scale);
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(ck.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(cv.data_ptr());
+  return a;
+}
+
+std::vector<Tensor> nsa_compressed_fwd(const Tensor& q, const Tensor& ck, const Tensor& cv, int64_t cstride,
+                                       int64_t csize, int64_t ssize, int64_t topk, double scale) {
+  NsaArgs a = nsa_args(q, ck, cv, cstride, csize, ssize, topk, scale);
+  const int64_t nsel = (a.T + a.ssize - 1) / a.ssize;
+  Tensor o = torch::empty_like(q);
+  Tensor lse = torch::empty({a.B, a.H, a.T}, q.options().dtype(at::kFloat));
+  Tensor sel = torch::empty({a.B, a.H, a.T, nsel}, q.options().dtype(at::kByte));
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.sel = sel.data_ptr<uint8_t>();
+  ok(nt_nsa_compressed_fwd(a, stream()), "nsa_compressed_fwd");
+  return {o, lse, sel};
+}
+
+std::vector<Tensor> nsa_compressed_bwd(const Tensor& q, const Tensor& ck, const Tensor& cv, const Tensor& lse,
+                                       const Tensor& dout, const Tensor& delta, int64_t cstride, int64_t csize,
+                                       double scale) {
+  NsaArgs a = nsa_args(q, ck, cv, cstride, csize, 64, 0, scale);
+  check_rows(dout, "dout");
+  TORCH_CHECK(dout.sizes() == q.sizes() && dout.scalar_type() == at::kBFloat16, "dout like q");
+  TORCH_CHECK(lse.is_contiguous() && delta.is_contiguous() && lse.scalar_type() == at::kFloat &&
+              delta.scalar_type() == at::kFloat, "lse / delta: fp32 [B, H, T]");
+  Tensor dq = torch::zeros(q.sizes(), q.options().dtype(at::kFloat));
+  Tensor dk = torch::zeros(ck.sizes(), ck.options().dtype(at::kFloat));
+  Tensor dv = torch::zeros(cv.sizes(), cv.options().dtype(at::kFloat));
+  a.lse = const_cast<float*>(lse.data_ptr<float>());
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.delta = delta.data_ptr<float>();
+  a.dq_acc = dq.data_ptr<float>();
+  a.dk_acc = dk.data_ptr<float>();
+  a.dv_acc = dv.data_ptr<float>();
+  ok(nt_nsa_compressed_bwd(a, stream()), "nsa_compressed_bwd");
+  return {dq, dk, dv};
+}
+
 void moe_pull_rows(const Tensor& peers, const Tensor& src_rank, const Tensor& src_row, const Tensor& out) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
   check_i32(src_rank, "src_rank");
@@ -988,6 +1049,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_pull_rows", &moe_pull_rows);
   m.def("moe_route", &moe_route);
   m.def("sparse_teacher", &sparse_teacher);
+  m.def("nsa_compressed_fwd", &nsa_compressed_fwd);
+  m.def("nsa_compressed_bwd", &nsa_compressed_bwd);
   m.def("moe_route_bwd", &moe_route_bwd);
   m.def("moe_push_rows", &moe_push_rows);
   m.def("delta_scan_fwd", &delta_scan_fwd);

@@ -403,7 +403,19 @@ class SparseMixer(nn.Module):
             size = c.block_size if c.compression_stride else c.compression_size
             topk = max(1, c.sparse_topk // size)
         nsel = (T + size - 1) // size
-        for start in range(0, T, rows_per_pass):
+        fused = False
+        if self.kind == "nsa" and x.is_cuda:
+            from nexttransformer_b200.ops.nsa_compress import nsa_compressed, supported
+            qt, ckk, cvk = q.transpose(1, 2), ck[:, ::rep].transpose(1, 2), cv[:, ::rep].transpose(1, 2)
+            if supported(qt, ckk) and nsel <= 256:
+                # compressed attention, block importance and the top-k choice in two kernels: no
+                # [B, H, T, Nc] scores, probabilities or importance in memory
+                comp, mem = nsa_compressed(qt, ckk, cvk, c.compression_stride or c.compression_size,
+                                           c.compression_size, size, topk, c.head_dim ** -.5)
+                compressed, mems, fused = [comp.transpose(1, 2)], [mem], True
+                pos = torch.arange(T, device=dev)
+                edges += (int(mem.sum()) - B * H * T) * size + B * H * int(((pos % size) + 1).sum())
+        for start in range(0, T if not fused else 0, rows_per_pass):
             stop = min(start + rows_per_pass, T)
             pos = torch.arange(start, stop, device=dev)
             qq = q[:, :, start:stop]
