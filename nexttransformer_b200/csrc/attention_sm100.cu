@@ -446,43 +446,51 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------ backward
-// One CTA per (key tile of 128, KV head, batch); 320 threads.  Key tiles are the fastest-varying
+// One CTA per (key tile of 128, KV head, batch); 512 threads in four warpgroups (the first one
+// gives registers back to the dQ drain).  Key tiles are the fastest-varying
 // block index: CTAs running at the same time then share one (batch, KV head), so the fp32 dQ rows
-// they all add into stay resident in L2 (ordering heavy key tiles first across all heads instead
-// quadrupled the DRAM write traffic of dQ).
-//   warp 0      TMA: K and V once, then (Q, dO) tiles of every (query head, query tile) pair into
-//               a 2-stage ring.
+// they all add into stay resident in L2.
+//   warp 0      TMA: K and V once, then Q tiles of every (query head, query tile) pair into a
+//               2-stage ring and the dO tiles into one buffer (refilled once dV of the pair is done).
 //   warp 1      TMEM owner and MMA issuer, per pair i:
-//                 S^T = K Q^T -> tS;  dP^T = V dO^T -> tDP (after dQ of pair i-1 left tDP);
+//                 dP^T = V dO^T -> tDP (after dQ of pair i-1 left tDP);
 //                 dV += P^T dO with P^T read from tensor memory (tS, bf16);
+//                 S^T of pair i+1 = K Q^T -> tS at once (MMAs from one thread run in order, and the
+//                 softmax keeps P^T in registers, so nothing reads tS after the dV product);
 //                 dK += dS^T Q;  dQ = dS K -> tDP.
-//   warps 2..5  one key row per thread: P^T = exp2(S^T scale - lse) written back over tS as
-//               bf16, then dS^T = P^T (dP^T - delta) into shared memory (128B-swizzled).
-//   warps 6..9  drain dQ: tcgen05.ld of the 128 x 128 fp32 tile in two halves of 64 columns,
-//               release tDP, stage each half in the dS^T buffer (free once dK and dQ are done) and
-//               add it to the fp32 dQ buffer with one bulk tensor reduction (performed in L2), while
-//               the MMAs of the next pair go on; the softmax warps write the next dS^T once the
-//               last reduction has read the buffer.
-// Tensor-memory columns: tS [0,128) | tDP [128,256) | dV [256,384) | dK [384,512).
-// MMAs issued by one thread execute in order, so S^T of pair i+1 may be issued while the dV MMA
-// of pair i still reads P^T from the same columns.
+//   warps 4..11 two warpgroups, one key row per thread, warpgroup g on queries [64 g, 64 g + 64):
+//               P^T = exp2(S^T scale - lse) written back as bf16 into the group's own S^T columns
+//               (queries 64 g .. go to columns [64 g, 64 g + 32)) and kept in registers, then
+//               dS^T = P^T (dP^T - delta) into shared memory (128B-swizzled) once dK and dQ of the
+//               previous pair have read it.  Each pair's lse / delta are loaded a pair ahead.
+//   warps 12..15 drain dQ: tcgen05.ld of the 128 x 128 fp32 tile, release tDP, stage it in
+//               quarters of 32 columns through a two-slot ring and add each quarter to the fp32 dQ
+//               buffer with a bulk tensor reduction (performed in L2); two reductions in flight.
+// Tensor-memory columns: tS [0,128) | tDP [128,256) | dV [256,384) | dK [384,512); P^T of queries
+// [64 g, 64 g + 64) in bf16 pairs at columns [64 g, 64 g + 32) of tS.
 struct BwdSmem {
   static constexpr int K = 0;
   static constexpr int V = K + TILE_BYTES;
   static constexpr int Q = V + TILE_BYTES;        // 2 stages
-  static constexpr int DO = Q + 2 * TILE_BYTES;   // 2 stages
-  static constexpr int DST = DO + 2 * TILE_BYTES; // dS^T [keys x queries]
-  static constexpr int STAT = DST + TILE_BYTES;   // lse * log2(e) [128], delta [128] of the current pair
+  static constexpr int DO = Q + 2 * TILE_BYTES;   // 1 stage
+  static constexpr int DST = DO + TILE_BYTES;     // dS^T [keys x queries]
+  static constexpr int STG = DST + TILE_BYTES;    // dQ staging: 2 slots of [128 rows x 32 fp32]
+  static constexpr int STAT = STG + TILE_BYTES;   // lse * log2(e) [128], delta [128] of the current pair
   static constexpr int BAR = STAT + 1024;
-  // kv_full, qd_full[2], qd_empty[2], s_full, p_full, dp_full, ds_full, dq_full, dq_free,
-  // stg_full, stg_free, stg_done (the dS^T buffer doubles as the fp32 staging tile of the dQ
-  // reduction; stg_free completes per staged half, stg_done once per pair), stat_ready, stat_free
-  static constexpr int NBAR = 16;
+  // kv_full, q_full[2], q_empty[2], do_full, do_empty, s_full, p_full, dp_full, ds_full, dq_full,
+  // dq_free, stg_full, stg_free[2], stat_ready, stat_free
+  static constexpr int NBAR = 18;
   static constexpr int TOTAL = BAR + NBAR * 8 + 16 + 1024;
 };
 static_assert(BwdSmem::TOTAL <= 232448, "backward shared memory exceeds the sm_100 limit");
 
-constexpr int BWD_THREADS = 320;
+constexpr int BWD_THREADS = 512;
+constexpr uint32_t BWD_REGS_LAUNCH = 128;  // the two softmax warpgroups keep the launch count
+constexpr uint32_t BWD_REGS_LOW = 72;      // TMA / MMA warpgroup
+constexpr uint32_t BWD_REGS_DRAIN = 184;   // dQ drain (a whole fp32 dQ row in registers)
+static_assert(128 * BWD_REGS_LOW + 256 * BWD_REGS_LAUNCH + 128 * BWD_REGS_DRAIN <= BWD_THREADS * BWD_REGS_LAUNCH,
+              "backward register split exceeds the launch budget");
+constexpr int STG_SLOT = 16384;
 
 NT_DEVICE void bwd_q_range(const Params& p, int k0, int& i_lo, int& i_hi) {
   const int n_qt = (p.T + TILE - 1) / TILE;
@@ -499,19 +507,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BwdSmem::BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* dp_full = bars + 7;
-  uint64_t* ds_full = bars + 8;
-  uint64_t* dq_full = bars + 9;
-  uint64_t* dq_free = bars + 10;
-  uint64_t* stg_full = bars + 11;
-  uint64_t* stg_free = bars + 12;
-  uint64_t* stg_done = bars + 13;
-  uint64_t* stat_ready = bars + 14;
-  uint64_t* stat_free = bars + 15;
+  uint64_t* q_full = bars + 1;    // [2]
+  uint64_t* q_empty = bars + 3;   // [2]
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* p_full = bars + 8;
+  uint64_t* dp_full = bars + 9;
+  uint64_t* ds_full = bars + 10;
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;
+  uint64_t* stg_full = bars + 13;
+  uint64_t* stg_free = bars + 14;  // [2]
+  uint64_t* stat_ready = bars + 16;
+  uint64_t* stat_free = bars + 17;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + BwdSmem::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -527,20 +536,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&qd_full[i], 1);
-      mbar_init(&qd_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&stg_free[i], 1);
     }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(dp_full, 1);
-    mbar_init(ds_full, 128);
+    mbar_init(ds_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
     mbar_init(stg_full, 128);
-    mbar_init(stg_free, 1);
-    mbar_init(stg_done, 1);
-    mbar_init(stat_ready, 128);
-    mbar_init(stat_free, 128);
+    mbar_init(stat_ready, 256);
+    mbar_init(stat_free, 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -557,7 +567,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const uint32_t t_dv = tbase + 256;
   const uint32_t t_dk = tbase + 384;
 
-  if (warp == 0) {
+  if (warp < 4) {
+   setmaxnreg_dec<BWD_REGS_LOW>();
+   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmDO);
@@ -566,25 +578,31 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tma_load_3d(sm + BwdSmem::K + BOX_BYTES, &tmK, kv_full, hk * HD + 64, k0, b);
       tma_load_3d(sm + BwdSmem::V, &tmV, kv_full, hk * HD, k0, b);
       tma_load_3d(sm + BwdSmem::V + BOX_BYTES, &tmV, kv_full, hk * HD + 64, k0, b);
-      int issued = 0;
+      int q_issued = 0, do_issued = 0;
       for (int it = 0; it < n_it; ++it) {
         const int st = it & 1;
         const int h = hk * group + it / n_q;
         const int q0 = (i_lo + it % n_q) * TILE;
-        if (!mbar_wait(&qd_empty[st], ((it >> 1) & 1) ^ 1u, 0x50u + st, abort_flag)) break;
+        if (!mbar_wait(&q_empty[st], ((it >> 1) & 1) ^ 1u, 0x50u + st, abort_flag)) break;
         stamp(p, 0, it, 0);
         uint8_t* qs = sm + BwdSmem::Q + st * TILE_BYTES;
-        uint8_t* ds = sm + BwdSmem::DO + st * TILE_BYTES;
-        mbar_expect_tx(&qd_full[st], 2 * TILE_BYTES);
-        tma_load_3d(qs, &tmQ, &qd_full[st], h * HD, q0, b);
-        tma_load_3d(qs + BOX_BYTES, &tmQ, &qd_full[st], h * HD + 64, q0, b);
-        tma_load_3d(ds, &tmDO, &qd_full[st], h * HD, q0, b);
-        tma_load_3d(ds + BOX_BYTES, &tmDO, &qd_full[st], h * HD + 64, q0, b);
-        ++issued;
+        mbar_expect_tx(&q_full[st], TILE_BYTES);
+        tma_load_3d(qs, &tmQ, &q_full[st], h * HD, q0, b);
+        tma_load_3d(qs + BOX_BYTES, &tmQ, &q_full[st], h * HD + 64, q0, b);
+        ++q_issued;
+        // dO of this pair once the dV product of the previous pair has read the buffer
+        if (!mbar_wait(do_empty, (it & 1) ^ 1u, 0x52u, abort_flag)) break;
+        stamp(p, 0, it, 1);
+        uint8_t* ds = sm + BwdSmem::DO;
+        mbar_expect_tx(do_full, TILE_BYTES);
+        tma_load_3d(ds, &tmDO, do_full, h * HD, q0, b);
+        tma_load_3d(ds + BOX_BYTES, &tmDO, do_full, h * HD + 64, q0, b);
+        ++do_issued;
       }
       // no copy may still be in flight when the CTA exits
       mbar_wait(kv_full, 0, 0x5Eu, nullptr);
-      for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait(&qd_full[it & 1], (it >> 1) & 1, 0x5Fu, nullptr);
+      for (int it = max(0, q_issued - 2); it < q_issued; ++it) mbar_wait(&q_full[it & 1], (it >> 1) & 1, 0x5Fu, nullptr);
+      if (do_issued > 0) mbar_wait(do_full, (do_issued - 1) & 1, 0x5Du, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -592,20 +610,24 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       constexpr uint32_t id_kv = idesc_bf16_f32(TILE, HD, 0, 1);    // dV += P^T dO ; dK += dS^T Q
       constexpr uint32_t id_q = idesc_bf16_f32(TILE, HD, 1, 1);     // dQ = dS K  (A = dS^T read M-major)
       const uint32_t k_addr = smem_u32(sm + BwdSmem::K), v_addr = smem_u32(sm + BwdSmem::V);
-      const uint32_t ds_addr = smem_u32(sm + BwdSmem::DST);
-      bool ok = mbar_wait(kv_full, 0, 0x60u, abort_flag);
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int st = it & 1;
-        const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + st * TILE_BYTES);
-        const uint32_t do_addr = smem_u32(sm + BwdSmem::DO + st * TILE_BYTES);
-        if (!mbar_wait(&qd_full[st], (it >> 1) & 1, 0x61u, abort_flag)) break;
-        stamp(p, 1, it, 0);
+      const uint32_t ds_addr = smem_u32(sm + BwdSmem::DST), do_addr = smem_u32(sm + BwdSmem::DO);
+      // S^T of pair `it` into tS (Q of the pair must have landed)
+      auto issue_s = [&](int it) -> bool {
+        if (!mbar_wait(&q_full[it & 1], (it >> 1) & 1, 0x61u, abort_flag)) return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + (it & 1) * TILE_BYTES);
         // loops are kept rolled: fully unrolled, the descriptors of every k-step of every operand
         // would be hoisted into registers that the other warp roles need
 #pragma unroll 1
         for (int j = 0; j < HD / 16; ++j) umma_bf16(t_s, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
         umma_commit(s_full);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, 0x60u, abort_flag) && (n_it == 0 || issue_s(0));
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it & 1;
+        const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + st * TILE_BYTES);
+        if (!mbar_wait(do_full, it & 1, 0x66u, abort_flag)) break;
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x62u, abort_flag)) break;  // dQ of it-1 left tDP
         stamp(p, 1, it, 1);
         tc_fence_after();
@@ -618,7 +640,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tc_fence_after();
 #pragma unroll 1
         for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16_tmem_a(t_dv, t_s + j * 8, mnmajor_desc(do_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
+          umma_bf16_tmem_a(t_dv, t_s + (j >> 2) * 64 + (j & 3) * 8, mnmajor_desc(do_addr, j), id_kv,
+                           (it > 0 || j > 0) ? 1u : 0u);
+        umma_commit(do_empty);
+        if (it + 1 < n_it && !issue_s(it + 1)) break;
         if (!mbar_wait(ds_full, it & 1, 0x64u, abort_flag)) break;
         stamp(p, 1, it, 3);
         tc_fence_after();
@@ -629,92 +654,93 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int j = 0; j < TILE / 16; ++j)
           umma_bf16(t_dp, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
         umma_commit(dq_full);
-        umma_commit(&qd_empty[st]);
+        umma_commit(&q_empty[st]);
         stamp(p, 1, it, 4);
       }
     }
-  } else if (warp < 6) {
+   }
+  } else if (warp < 12) {
     // ------------------------------------------------------------ P^T and dS^T (one key row each)
+    const int grp = (warp - 4) >> 2;   // queries [64 grp, 64 grp + 64)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int kj = k0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t t_sg = t_s + grp * 64;
     uint8_t* dsb = sm + BwdSmem::DST;
-    for (int it = 0; it < n_it; ++it) {
+    float* s_lse = reinterpret_cast<float*>(sm + BwdSmem::STAT);
+    float* s_del = s_lse + 128;
+    // lse (group 0) or delta (group 1) of query row r of a pair, read a pair ahead
+    auto stat_of = [&](int it) -> float {
       const int h = hk * group + it / n_q;
+      const int qi = (i_lo + it % n_q) * TILE + r;
+      const int64_t o = (static_cast<int64_t>(b) * p.H + h) * p.T + min(qi, p.T - 1);
+      return grp ? p.delta[o] : p.lse[o] * LOG2E;
+    };
+    float stat_next = n_it > 0 ? stat_of(0) : 0.f;
+    for (int it = 0; it < n_it; ++it) {
       const int q0 = (i_lo + it % n_q) * TILE;
-      // per-query statistics of this pair into shared memory: every row reads all 128 of them.
-      // stat_free (all rows done with the previous pair) and stat_ready are mbarriers, so a row that
-      // leaves the loop after a timed-out wait cannot strand the others.
-      float* s_lse = reinterpret_cast<float*>(sm + BwdSmem::STAT);
-      float* s_del = s_lse + 128;
+      const float stat_cur = stat_next;
+      if (it + 1 < n_it) stat_next = stat_of(it + 1);
+      // statistics of this pair into shared memory once every row is done with the previous pair's.
+      // stat_free and stat_ready are mbarriers, so a row that leaves the loop after a timed-out wait
+      // cannot strand the others.
       if (it > 0 && !mbar_wait(stat_free, (it - 1) & 1, 0x74u, abort_flag)) break;
-      {
-        const int qi = q0 + r;
-        const int64_t o = (static_cast<int64_t>(b) * p.H + h) * p.T + min(qi, p.T - 1);
-        s_lse[r] = p.lse[o] * LOG2E;
-        s_del[r] = p.delta[o];
-      }
+      (grp ? s_del : s_lse)[r] = stat_cur;
       mbar_arrive(stat_ready);
       if (!mbar_wait(stat_ready, it & 1, 0x75u, abort_flag)) break;
-      if (r == 0) stamp(p, 2, it, 0);
+      if (r == 0 && grp == 0) stamp(p, 2, it, 0);
       const bool boundary = (k0 + TILE - 1 > q0) || (q0 + TILE > p.T) || (k0 + TILE > p.T) ||
                             (p.window >= 0 && q0 + TILE - 1 - k0 > p.window);
       if (!mbar_wait(s_full, it & 1, 0x70u, abort_flag)) break;
-      if (r == 0) stamp(p, 2, it, 1);
+      if (r == 0 && grp == 0) stamp(p, 2, it, 1);
       __syncwarp();
       tc_fence_after();
-      // 64 queries per tensor-memory wait: two loads in flight
-#pragma unroll 1
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        uint32_t sv[64];
-        tmem_ld32(t_s + lane_off + hlf * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(t_s + lane_off + hlf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      // P^T of this key row over the group's 64 queries, bf16 pairs: written to tS for the dV
+      // product and kept here for dS^T (tS takes the next pair's S^T right after the dV product)
+      uint32_t pk[32];
+      {
+        uint32_t sv[64];  // the group's 64 S^T columns, two loads in flight
+        tmem_ld32(t_sg + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(t_sg + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        if (r == 0 && hlf == 0) stamp(p, 2, it, 6);
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * hlf + cc;
-          uint32_t pk[16];  // 32 entries of this P^T row, bf16 pairs
-          // the mask is applied in a separate loop so the unrolled exp loop carries no branches
-          float xs[32];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float2 l2 = *reinterpret_cast<const float2*>(s_lse + c * 32 + i);
-            xs[i] = fmaf(__uint_as_float(sv[cc * 32 + i]), p.scale_log2, -l2.x);
-            xs[i + 1] = fmaf(__uint_as_float(sv[cc * 32 + i + 1]), p.scale_log2, -l2.y);
-          }
-          if (boundary) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int qi = q0 + c * 32 + i;
-              const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
-              xs[i] = valid ? xs[i] : -INFINITY;
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) pk[i / 2] = pack_bf16x2(fast_exp2(xs[i]), fast_exp2(xs[i + 1]));
-          // columns [16c, 16c+16) of tS: S^T there was read in this or an earlier half
-          tmem_st16(t_s + lane_off + c * 16, pk);
+        for (int i = 0; i < 64; i += 2) {
+          const float2 l2 = *reinterpret_cast<const float2*>(s_lse + grp * 64 + i);
+          sv[i] = __float_as_uint(fmaf(__uint_as_float(sv[i]), p.scale_log2, -l2.x));
+          sv[i + 1] = __float_as_uint(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, -l2.y));
         }
-        if (r == 0 && hlf == 0) stamp(p, 2, it, 7);
+        // the mask is applied in a separate loop so the unrolled exp loop carries no branches
+        if (boundary) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const int qi = q0 + grp * 64 + i;
+            const bool valid = kj <= qi && qi < p.T && kj < p.T && (p.window < 0 || qi - kj <= p.window);
+            if (!valid) sv[i] = __float_as_uint(-INFINITY);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 64; i += 2)
+          pk[i / 2] = pack_bf16x2(fast_exp2(__uint_as_float(sv[i])), fast_exp2(__uint_as_float(sv[i + 1])));
       }
+      // columns [64 grp, 64 grp + 32): this group's own S^T, already read above
+      tmem_st16(t_sg + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+      tmem_st16(t_sg + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
-      if (r == 0) stamp(p, 2, it, 2);
+      if (r == 0 && grp == 0) stamp(p, 2, it, 2);
       if (!mbar_wait(dp_full, it & 1, 0x71u, abort_flag)) break;
-      if (r == 0) stamp(p, 2, it, 3);
-      // the dS^T buffer served as dQ staging for the previous pair: its second reduction read it last
-      if (it > 0 && !mbar_wait(stg_done, (it - 1) & 1, 0x73u, abort_flag)) break;
-      if (r == 0) stamp(p, 2, it, 4);
+      if (r == 0 && grp == 0) stamp(p, 2, it, 3);
+      // dS^T buffer: the dK and dQ products of the previous pair read it last
+      if (it > 0 && !mbar_wait(dq_full, (it - 1) & 1, 0x73u, abort_flag)) break;
+      if (r == 0 && grp == 0) stamp(p, 2, it, 4);
       __syncwarp();
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t dv[32], pk[16];
-        tmem_ld32(t_dp + lane_off + c * 32, dv);
-        tmem_ld16(t_s + lane_off + c * 16, pk);  // P^T back from tensor memory (read-only for the dV MMA)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dv[32];
+        tmem_ld32(t_dp + lane_off + grp * 64 + c * 32, dv);
         tmem_wait_ld();
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
@@ -722,28 +748,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int i = 8 * g + 2 * e;
-            const float2 pp = unpack_bf16x2(pk[i / 2]);
-            const float2 dl = *reinterpret_cast<const float2*>(s_del + c * 32 + i);
+            const float2 pp = unpack_bf16x2(pk[c * 16 + i / 2]);
+            const float2 dl = *reinterpret_cast<const float2*>(s_del + grp * 64 + c * 32 + i);
             w[e] = pack_bf16x2(pp.x * (__uint_as_float(dv[i]) - dl.x), pp.y * (__uint_as_float(dv[i + 1]) - dl.y));
           }
-          *reinterpret_cast<uint4*>(dsb + swz_off(r, c * 4 + g)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(dsb + swz_off(r, grp * 8 + c * 4 + g)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
       mbar_arrive(stat_free);
-      if (r == 0) stamp(p, 2, it, 5);
+      if (r == 0 && grp == 0) stamp(p, 2, it, 5);
     }
-    // dK of this key tile once every MMA has completed (the last dq_full)
-    if (!*abort_flag && mbar_wait(dq_full, (n_it - 1) & 1, 0x72u, abort_flag)) {
+    // dK of this key tile (columns [64 grp, 64 grp + 64)) once every MMA has completed
+    if (!*abort_flag && n_it > 0 && mbar_wait(dq_full, (n_it - 1) & 1, 0x72u, abort_flag)) {
       __syncwarp();
       tc_fence_after();
       // every lane takes part in the aligned TMEM loads; only rows inside the sequence store
       const bool live = kj < p.T;
       __nv_bfloat16* dkr = p.dk + (static_cast<int64_t>(b) * p.T + (live ? kj : 0)) * p.lddk + hk * HD;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * grp; c < 2 * grp + 2; ++c) {
         uint32_t k[32];
         tmem_ld32(t_dk + lane_off + c * 32, k);
         tmem_wait_ld();
@@ -762,19 +788,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
   } else {
+    setmaxnreg_inc<BWD_REGS_DRAIN>();
     // ------------------------------------------------------------ dQ drain (one query row each)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const bool leader = threadIdx.x == 384;  // warp 12, lane 0: issues the bulk reductions
+    int n_q4 = 0;                            // quarters staged so far
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * group + it / n_q;
       const int q0 = (i_lo + it % n_q) * TILE;
       if (!mbar_wait(dq_full, it & 1, 0x78u, abort_flag)) break;
-      if (threadIdx.x == 192) stamp(p, 3, it, 0);
+      if (leader) stamp(p, 3, it, 0);
       __syncwarp();
       tc_fence_after();
-      const bool leader = threadIdx.x == 192;  // warp 6, lane 0: issues the bulk reductions
-      uint8_t* stg = sm + BwdSmem::DST;
       // the whole dQ row comes into registers first, so tDP is released for the next dP^T at once
       uint32_t vq[128];
 #pragma unroll
@@ -782,53 +809,53 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_free);  // tDP may take the next dP^T
+      bool fine = true;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t* v = vq + half * 64;
-        // staging must be free: read by the previous reduction (none before the first half of pair 0)
-        const int k = 2 * it + half - 1;
-        if (k >= 0 && !mbar_wait(stg_free, k & 1, 0x7Au, abort_flag)) { it = n_it; break; }
-        if (threadIdx.x == 192) stamp(p, 3, it, 1 + 2 * half);
+      for (int qq = 0; qq < 4; ++qq) {
+        const int n = n_q4 + qq;
+        const int slot = n & 1;
+        uint8_t* stg = sm + BwdSmem::STG + slot * STG_SLOT;
+        // the slot's previous reduction (quarter n - 2) must have read it
+        if (n >= 2 && !mbar_wait(&stg_free[slot], ((n - 2) >> 1) & 1, 0x7Au, abort_flag)) { fine = false; break; }
+        if (leader && qq == 0) stamp(p, 3, it, 1);
         __syncwarp();
-        // two boxes of [128 rows x 32 fp32], 128-byte rows, 128-byte swizzle
+        // one box of [128 rows x 32 fp32], 128-byte rows, 128-byte swizzle
 #pragma unroll
-        for (int bx = 0; bx < 2; ++bx) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int i = bx * 32 + c * 4;
-            float4 w = make_float4(__uint_as_float(v[i]) * p.scale, __uint_as_float(v[i + 1]) * p.scale,
-                                   __uint_as_float(v[i + 2]) * p.scale, __uint_as_float(v[i + 3]) * p.scale);
-            *reinterpret_cast<float4*>(stg + bx * 16384 + r * 128 + ((c ^ (r & 7)) << 4)) = w;
-          }
+        for (int c = 0; c < 8; ++c) {
+          const int i = qq * 32 + c * 4;
+          float4 w = make_float4(__uint_as_float(vq[i]) * p.scale, __uint_as_float(vq[i + 1]) * p.scale,
+                                 __uint_as_float(vq[i + 2]) * p.scale, __uint_as_float(vq[i + 3]) * p.scale);
+          *reinterpret_cast<float4*>(stg + r * 128 + ((c ^ (r & 7)) << 4)) = w;
         }
         fence_proxy_async_smem();
         mbar_arrive(stg_full);
         if (leader) {
-          if (mbar_wait(stg_full, (2 * it + half) & 1, 0x7Bu, abort_flag)) {
+          if (mbar_wait(stg_full, n & 1, 0x7Bu, abort_flag)) {
             if (p.dq_slices) {
               // deterministic mode: this key tile's contribution goes to its own slice (plain stores);
               // the convert kernel sums the slices in key-tile order
-              const int z = kt * p.B + b;
-              tma_store_3d(&tmDQ, stg, h * HD + half * 64, q0, z);
-              tma_store_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, z);
+              tma_store_3d(&tmDQ, stg, h * HD + qq * 32, q0, kt * p.B + b);
             } else {
-              tma_reduce_add_3d(&tmDQ, stg, h * HD + half * 64, q0, b);
-              tma_reduce_add_3d(&tmDQ, stg + 16384, h * HD + half * 64 + 32, q0, b);
+              tma_reduce_add_3d(&tmDQ, stg, h * HD + qq * 32, q0, b);
             }
             tma_store_commit();
-            tma_store_wait_read0();
-            stamp(p, 3, it, 2 + 2 * half);
+            // the reduction before this one has read its slot: release that slot
+            tma_store_wait_read1();
+            if (n >= 1) mbar_arrive(&stg_free[(n - 1) & 1]);
+            if (qq == 3) stamp(p, 3, it, 2);
+          } else {
+            fine = false;
           }
-          mbar_arrive(stg_free);
-          if (half == 1) mbar_arrive(stg_done);
         }
         __syncwarp();
       }
+      n_q4 += 4;
+      if (!fine) break;
     }
-    if (threadIdx.x == 192) tma_store_wait0();  // every reduction has landed before the CTA retires
+    if (leader) tma_store_wait0();  // every reduction has landed before the CTA retires
     // dV of this key tile (every MMA has completed once the last dq_full fired)
     const int kj = k0 + r;
-    if (!*abort_flag && mbar_wait(dq_full, (n_it - 1) & 1, 0x79u, abort_flag)) {
+    if (!*abort_flag && n_it > 0 && mbar_wait(dq_full, (n_it - 1) & 1, 0x79u, abort_flag)) {
       __syncwarp();
       tc_fence_after();
       const bool live = kj < p.T;
