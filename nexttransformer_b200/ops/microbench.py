@@ -169,8 +169,8 @@ def attn_bwd_trace(rows):
     torch.cuda.synchronize()
     t = trace.cpu()
     base = int(t[t > 0].min())
-    names = {0: "producer: qd_empty", 1: "mma: qd_full dq_free p_full ds_full issued",
-             2: "softmax: stat s_full p_arrive dp_full stg_done ds_arrive", 3: "drain: dq_full free0 read0 free1 read1"}
+    names = {0: "producer: q_empty do_empty", 1: "mma: - dP_issued p_full ds_full dq_issued",
+             2: "softmax: stat s_full p_arrive dp_full prev_dq_full ds_arrive", 3: "drain: dq_full staged0 issued3"}
     out = {}
     for role in range(4):
         rows_ = []
