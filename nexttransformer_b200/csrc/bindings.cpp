@@ -14,6 +14,7 @@
 #include "sparse_attn.h"
 #include "sparse_teacher.h"
 #include "nsa_compress.h"
+#include "msar.h"
 #include "residual.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
@@ -799,6 +800,96 @@ std::vector<Tensor> nsa_compressed_bwd(const Tensor& q, const Tensor& ck, const 
   return {dq, dk, dv};
 }
 
+// MSAR temporal augmentation: x [B, T, C] (bf16 / fp32), taps fp32 [C, 24] -> y [B, T, 4, C]
+Tensor msar_temporal_fwd(const Tensor& x, const Tensor& taps) {
+  check_rows(x, "x");
+  TORCH_CHECK(x.dim() == 3 && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat), "x: [B, T, C]");
+  TORCH_CHECK(taps.scalar_type() == at::kFloat && taps.is_contiguous() && taps.size(0) == x.size(2) &&
+              taps.size(1) == 24, "taps: fp32 [C, 24]");
+  MsarTemporalArgs a;
+  a.B = static_cast<int>(x.size(0));
+  a.T = static_cast<int>(x.size(1));
+  a.C = static_cast<int>(x.size(2));
+  a.bf16 = x.scalar_type() == at::kBFloat16;
+  Tensor y = torch::empty({a.B, a.T, 4, a.C}, x.options());
+  a.x = x.data_ptr();
+  a.taps = taps.data_ptr<float>();
+  a.y = y.data_ptr();
+  ok(nt_msar_temporal_fwd(a, stream()), "msar_temporal_fwd");
+  return y;
+}
+
+std::vector<Tensor> msar_temporal_bwd(const Tensor& x, const Tensor& taps, const Tensor& dy) {
+  check_rows(x, "x");
+  check_rows(dy, "dy");
+  TORCH_CHECK(dy.scalar_type() == x.scalar_type() && dy.dim() == 4 && dy.size(2) == 4, "dy like y");
+  MsarTemporalArgs a;
+  a.B = static_cast<int>(x.size(0));
+  a.T = static_cast<int>(x.size(1));
+  a.C = static_cast<int>(x.size(2));
+  a.bf16 = x.scalar_type() == at::kBFloat16;
+  Tensor dx = torch::empty_like(x);
+  Tensor part = torch::empty({nt_msar_temporal_part_floats(a.B, a.T, a.C)}, x.options().dtype(at::kFloat));
+  Tensor dtaps = torch::empty({a.C, 24}, x.options().dtype(at::kFloat));
+  a.x = x.data_ptr();
+  a.taps = taps.data_ptr<float>();
+  a.dy = dy.data_ptr();
+  a.dx = dx.data_ptr();
+  a.part = part.data_ptr<float>();
+  a.dtaps = dtaps.data_ptr<float>();
+  ok(nt_msar_temporal_bwd(a, stream()), "msar_temporal_bwd");
+  return {dx, dtaps};
+}
+
+// MSAR depth-read gate: s [N, 4, C], P fp32 [4C, 4], alpha fp32 [1], bias fp32 [4] -> (out [N, C], zr [N, 5])
+std::vector<Tensor> msar_gate_fwd(const Tensor& s, const Tensor& P, const Tensor& alpha, const Tensor& bias) {
+  check_rows(s, "s");
+  TORCH_CHECK(s.dim() == 3 && s.size(1) == 4, "s: [N, 4, C]");
+  TORCH_CHECK(P.scalar_type() == at::kFloat && P.is_contiguous() && P.size(0) == 4 * s.size(2) && P.size(1) == 4,
+              "P: fp32 [4C, 4]");
+  MsarGateArgs a;
+  a.N = static_cast<int>(s.size(0));
+  a.C = static_cast<int>(s.size(2));
+  a.bf16 = s.scalar_type() == at::kBFloat16;
+  Tensor out = torch::empty({a.N, a.C}, s.options());
+  Tensor zr = torch::empty({a.N, 5}, s.options().dtype(at::kFloat));
+  a.s = s.data_ptr();
+  a.P = P.data_ptr<float>();
+  a.alpha = alpha.data_ptr<float>();
+  a.bias = bias.data_ptr<float>();
+  a.out = out.data_ptr();
+  a.zr = zr.data_ptr<float>();
+  ok(nt_msar_gate_fwd(a, stream()), "msar_gate_fwd");
+  return {out, zr};
+}
+
+// -> (ds [N, 4, C], dP [4C, 4], dalpha [1], dbias [4]); the token reductions are fixed-order sums
+std::vector<Tensor> msar_gate_bwd(const Tensor& s, const Tensor& P, const Tensor& alpha, const Tensor& bias,
+                                  const Tensor& zr, const Tensor& dout) {
+  check_rows(s, "s");
+  check_rows(dout, "dout");
+  MsarGateArgs a;
+  a.N = static_cast<int>(s.size(0));
+  a.C = static_cast<int>(s.size(2));
+  a.bf16 = s.scalar_type() == at::kBFloat16;
+  auto f32 = s.options().dtype(at::kFloat);
+  Tensor ds = torch::empty_like(s), y = torch::empty({a.N, 4}, f32), ab = torch::empty({a.N, 5}, f32);
+  Tensor pp = torch::empty({nt_msar_gate_proj_slices(a.N), 4 * a.C, 4}, f32);
+  a.s = s.data_ptr();
+  a.P = P.data_ptr<float>();
+  a.alpha = alpha.data_ptr<float>();
+  a.bias = bias.data_ptr<float>();
+  a.zr = const_cast<float*>(zr.data_ptr<float>());
+  a.dout = dout.data_ptr();
+  a.ds = ds.data_ptr();
+  a.y = y.data_ptr<float>();
+  a.ab_part = ab.data_ptr<float>();
+  a.p_part = pp.data_ptr<float>();
+  ok(nt_msar_gate_bwd(a, stream()), "msar_gate_bwd");
+  Tensor sums = ab.sum(0);
+  return {ds, pp.sum(0), sums.narrow(0, 0, 1), sums.narrow(0, 1, 4)};
+}
+
 void moe_pull_rows(const Tensor& peers, const Tensor& src_rank, const Tensor& src_row, const Tensor& out) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong, "peers: int64 CUDA pointer table");
   check_i32(src_rank, "src_rank");
@@ -1051,6 +1142,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_teacher", &sparse_teacher);
   m.def("nsa_compressed_fwd", &nsa_compressed_fwd);
   m.def("nsa_compressed_bwd", &nsa_compressed_bwd);
+  m.def("msar_temporal_fwd", &msar_temporal_fwd);
+  m.def("msar_temporal_bwd", &msar_temporal_bwd);
+  m.def("msar_gate_fwd", &msar_gate_fwd);
+  m.def("msar_gate_bwd", &msar_gate_bwd);
   m.def("moe_route_bwd", &moe_route_bwd);
   m.def("moe_push_rows", &moe_push_rows);
   m.def("delta_scan_fwd", &delta_scan_fwd);

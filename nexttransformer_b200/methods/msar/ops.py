@@ -35,6 +35,9 @@ class TemporalAugmentation(nn.Module):
             nn.init.zeros_(t)
 
     def forward(self, raw):
+        from nexttransformer_b200.ops import msar as K
+        if K.supported(raw) and raw.dim() == 3:
+            return K.temporal(raw, tuple(self.taps))   # one kernel per direction (csrc/msar.cu)
         ch = raw.transpose(1, 2)
         out = [raw]
         for t in self.taps:
@@ -60,6 +63,9 @@ class DepthRead(nn.Module):
         nn.init.zeros_(self.bias_pre)
 
     def forward(self, streams):
+        from nexttransformer_b200.ops import msar as K
+        if K.supported(streams) and streams.shape[-2] == 4:
+            return K.gate(streams, self.proj_pre, self.alpha_pre, self.bias_pre)
         flat = streams.flatten(-2)
         ms = flat.square().mean(-1, keepdim=True)
         ms = torch.where(ms > 0, ms, torch.ones_like(ms))   # before rsqrt: no inf/NaN gradient at zero
