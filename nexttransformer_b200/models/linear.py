@@ -196,6 +196,11 @@ def _scalar_decay_chunks(q, k, v, g, C):
     return out + torch.stack(inter, 2)
 
 
+def _gla_kernel_ok(q, v):
+    from nexttransformer_b200.ops.linear_attention import gla_supported
+    return gla_supported(q, v)
+
+
 def chunk_scan(q, k, v, *, kind, g=None, beta=None, chunk):
     """Chunked training form; g is a log decay (KDA [B,T,H,D], GDN/RetNet [B,T,H], None otherwise)."""
     T = q.shape[1]
@@ -390,6 +395,10 @@ class LinearMixer(nn.Module):
         if chunked:
             y = chunk_attention(q, k, v, kind=self.kind, g=decay, beta=beta, chunk=CHUNK_BACKENDS[c.backend],
                                 qk_l2norm_scale=D ** -.5 if self.kind == "gdn" else None)
+        elif self.kind == "gla" and x.is_cuda and _gla_kernel_ok(q, v):
+            # the same recurrence in the chunk form on the scan kernels (log decay, not its exp)
+            from nexttransformer_b200.ops.linear_attention import gla_chunk_cuda
+            y = gla_chunk_cuda(q, k, v, F.logsigmoid(gate.float()) / 16)
         else:
             y, _ = recurrent_scan(q, k, v, kind=self.kind, decay=decay, beta=beta)
         gated = self.kind in ("gdn", "kda") and chunked and y.is_cuda

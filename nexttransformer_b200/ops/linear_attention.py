@@ -254,3 +254,27 @@ def scalar_chunk_cuda(q, k, v, g, chunk):
     w = torch.zeros_like(qt)
     out = _DeltaScan.apply(w, vc, qt, kc, aqk, carry)
     return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)
+
+
+def gla_supported(q, v):
+    return q.is_cuda and q.shape[-1] == 128 and v.shape[-1] == 128
+
+
+def gla_chunk_cuda(q, k, v, log_decay, chunk=64):
+    """GLA, S <- diag(e^{g_t}) S + k_t v_t^T and o_t = q_t S_t with a per-feature log decay
+    g [B, T, H, 128], in the chunk form on the scan kernels: the delta-rule scan with w = 0 and
+    u0 = v, qt = q e^{b}, kc = k e^{b_last - b}, aqk = tril(qt (k e^{-b})^T) and carry e^{b_last}
+    (b the within-chunk cumulative log decay), so the recurrence over T tokens becomes one scan over
+    T / 64 chunks."""
+    from nexttransformer_b200.models.linear import _chunked, _tril
+    dt, T = q.dtype, q.shape[1]
+    qc, kc_, vc = (_chunked(x.float(), chunk) for x in (q, k, v))
+    b = _chunked(log_decay.float(), chunk).cumsum(-2)
+    causal = _tril(chunk, q.device)
+    qt = qc * b.exp()
+    aqk = (qt @ (kc_ * (-b).exp()).transpose(-1, -2)).masked_fill(~causal, 0)
+    last = b[..., -1:, :]
+    kc = kc_ * (last - b).exp()
+    carry = last.squeeze(-2).exp().contiguous()
+    out = _DeltaScan.apply(torch.zeros_like(qt), vc, qt, kc, aqk, carry)
+    return out.movedim(1, 3).flatten(1, 2)[:, :T].to(dt)

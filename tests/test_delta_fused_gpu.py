@@ -64,3 +64,27 @@ def test_fused_delta_chunk_matches_fp64(kind, B, T, H, monkeypatch):
         assert err < 3e-2, (name, err)
         worst = (a.grad.double() - b.grad).abs().max().item()
         assert worst <= 5e-2 * b.grad.abs().max().item(), (name, worst)
+
+
+def test_gla_chunk_kernels_match_recurrence():
+    """GLA through the chunk form on the scan kernels equals the token recurrence (fp64 oracle)."""
+    import torch.nn.functional as F
+    from nexttransformer_b200.models.linear import recurrent_scan
+    from nexttransformer_b200.ops.linear_attention import gla_chunk_cuda
+    g = torch.Generator(device="cuda").manual_seed(3)
+    B, T, H, D = 2, 200, 3, 128
+    q = (torch.randn(B, T, H, D, device="cuda", generator=g) * D ** -.5).requires_grad_()
+    k = torch.randn(B, T, H, D, device="cuda", generator=g).requires_grad_()
+    v = torch.randn(B, T, H, D, device="cuda", generator=g).requires_grad_()
+    gate = torch.randn(B, T, H, D, device="cuda", generator=g).requires_grad_()
+    logd = F.logsigmoid(gate) / 16
+    y = gla_chunk_cuda(q, k, v, logd)
+    dy = torch.randn_like(y)
+    grads = torch.autograd.grad(y, (q, k, v, gate), dy)
+    leaves = [x.detach().double().requires_grad_() for x in (q, k, v, gate)]
+    ref, _ = recurrent_scan(leaves[0], leaves[1], leaves[2], kind="gla",
+                            decay=(F.logsigmoid(leaves[3]) / 16).exp())
+    rgrads = torch.autograd.grad(ref, leaves, dy.double())
+    assert ((y.double() - ref).norm() / ref.norm()) < 1e-2
+    for a, r in zip(grads, rgrads):
+        assert ((a.double() - r).norm() / r.norm()) < 3e-2
