@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 #pragma unroll 1
         for (int q = 0; q < HD / 16; ++q) umma_bf16(tsx, kmajor_desc(qx, q), kmajor_desc(k_addr, q), idesc_s, q > 0);
         umma_commit(&s_full[X]);
+        stamp(p, 1, t, X);
         if (X) ++iB; else ++iA;
         return true;
       };
@@ -286,6 +287,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         for (int q = 0; q < TILE / 16; ++q)
           umma_bf16_tmem_a(tox, tsx + q * 8, mnmajor_desc(v_addr, q), idesc_pv, (u > 0 || q > 0) ? 1u : 0u);
         umma_commit(&o_done[X]);
+        stamp(p, 1, t, 2 + X);
         ++u;
         return true;
       };
@@ -325,6 +327,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     for (int i = 0; i < n; ++i) {
       const int k0 = (lo + i) * TILE;
       if (!mbar_wait(&s_full[grp], i & 1, 0x30u, abort_flag)) { ok = false; break; }
+      if (r == 0) stamp(p, 2 + grp, i, 0);
       __syncwarp();
       tc_fence_after();
       const bool boundary = (k0 + TILE - 1 > q0) || (k0 + TILE > p.T) ||
@@ -335,6 +338,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(t_s + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
       tmem_wait_ld();
+      if (r == 0) stamp(p, 2 + grp, i, 1);
       if (boundary) {
 #pragma unroll
         for (int e = 0; e < 128; ++e) {
@@ -358,6 +362,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       if (i == 0 || mx > m + 8.f) m_new = fmaxf(m, mx);
       const float alpha = (i == 0 || m_new == m) ? 1.f : fast_exp2(m - m_new);
       const float mref = (m_new == -INFINITY) ? 0.f : m_new;
+      if (r == 0) stamp(p, 2 + grp, i, 2);
       if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O holds every earlier product: wait for the last one, then scale O in place
         if (!mbar_wait(&o_done[grp], (i - 1) & 1, 0x31u, abort_flag)) { ok = false; break; }
@@ -376,6 +381,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_wait_st();
       }
       m = m_new;
+      if (r == 0) stamp(p, 2 + grp, i, 3);
       // P = exp2(S scale - m) as bf16 over columns [0, 64) of this tile's S (S is in registers);
       // FWD_EMU of every 8 pairs on the FMA pipe, the others on MUFU
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-mref, -mref);
@@ -399,6 +405,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[grp]);
+      if (r == 0) stamp(p, 2 + grp, i, 4);
     }
     // epilogue: O / l -> this tile's Q buffer (its last reader, S of the last key tile, is done once
     // the last PV product is) -> bulk tensor store; lse per row.  Every thread of the group reaches
@@ -1000,6 +1007,7 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tv = tile_map(a.v, static_cast<int64_t>(a.Hk) * HD, a.ldv, a.T, a.B);
   CUtensorMap to = tile_map(a.o, static_cast<int64_t>(a.H) * HD, a.ldo, a.T, a.B);
   Params p = make_params(a);
+  p.trace = a.trace;
   static const int emu = [] {
     const char* e = std::getenv("NT_ATTN_FWD_EMU");
     return e ? std::atoi(e) : FWD_EMU_DEFAULT;

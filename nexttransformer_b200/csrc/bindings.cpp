@@ -289,6 +289,16 @@ void attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o
   ok(nt_attention_fwd(a, stream()), "attention_fwd");
 }
 
+// the forward with the pipeline stamps of its first CTA in `trace` (int64 [4][64][8], zero-filled)
+void attn_fwd_trace(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse, int64_t B,
+                    int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window, double scale, const Tensor& trace) {
+  AttnArgs a = attn_args(q, k, v, o, lse, B, T, H, Hk, D, window, scale);
+  TORCH_CHECK(trace.scalar_type() == at::kLong && trace.numel() >= 4 * 64 * 8, "trace: int64 [4, 64, 8]");
+  a.trace = reinterpret_cast<long long*>(trace.data_ptr<int64_t>());
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_attention_fwd(a, stream()), "attention_fwd");
+}
+
 void attn_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
               const Tensor& dout, const Tensor& dq, const Tensor& dk, const Tensor& dv, const Tensor& dq_acc,
               const Tensor& delta, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window,
@@ -1117,6 +1127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_normalize", &muon_normalize);
   m.def("muon_finish", &muon_finish);
   m.def("attn_fwd", &attn_fwd);
+  m.def("attn_fwd_trace", &attn_fwd_trace);
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("dq_acc"), py::arg("delta"), py::arg("B"),
         py::arg("T"), py::arg("H"), py::arg("Hk"), py::arg("D"), py::arg("window"), py::arg("scale"),

@@ -182,6 +182,31 @@ def attn_bwd_trace(rows):
     return out
 
 
+def attn_fwd_trace(rows):
+    """Pipeline stamps of the first forward CTA: per (role, key tile) the SM-clock offsets of its events."""
+    from nexttransformer_b200.ops._ext import ext
+    B = max(1, rows // SEQ)
+    M, H, Hk, D = B * SEQ, HEADS, KV_HEADS, HEAD_DIM
+    qkv = _bf16(M, (H + 2 * Hk) * D).mul_(0.3)
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:(H + Hk) * D], qkv[:, (H + Hk) * D:]
+    o = torch.empty(M, H * D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, H, SEQ, device="cuda")
+    trace = torch.zeros(4, 64, 8, dtype=torch.int64, device="cuda")
+    for _ in range(2):
+        trace.zero_()
+        ext().attn_fwd_trace(q, k, v, o, lse, B, SEQ, H, Hk, D, -1, 1.0 / math.sqrt(D), trace)
+    torch.cuda.synchronize()
+    t = trace.cpu()
+    base = int(t[t > 0].min())
+    names = {1: "mma: S_A S_B PV_A PV_B", 2: "softmax A: s_full loaded max rescaled p_arrive",
+             3: "softmax B: s_full loaded max rescaled p_arrive"}
+    out = {}
+    for role, name in names.items():
+        out[name] = [[int(x) - base if int(x) else None for x in t[role, it][:5]] for it in range(16)
+                     if (t[role, it] > 0).any()]
+    return out
+
+
 def case_delta_fused(kind, rows):
     """Forward + backward of the whole chunked delta rule on [B, 4096, 12, 128] bf16 inputs."""
     import torch.nn.functional as F
@@ -373,6 +398,9 @@ def main(argv=None):
     byts = None
     if a.case == "attn_bwd_trace":
         print(json.dumps(attn_bwd_trace(a.rows)), flush=True)
+        return
+    if a.case == "attn_fwd_trace":
+        print(json.dumps(attn_fwd_trace(a.rows)), flush=True)
         return
     if a.case.startswith("gemm_"):
         fn, flops = case_gemm(a.case, a.rows)
