@@ -25,6 +25,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <atomic>
 
 namespace nt {
@@ -114,7 +115,9 @@ struct FwdSmem {
   static constexpr int K = Q + TQ * LDS * 2;
   static constexpr int VT = K + TK * LDS * 2;
   static constexpr int IMP = VT + HD * LDT * 2;
-  static constexpr int BYTES = IMP + TQ * MAX_SEL * 4;
+  // the importance rows take TQ x nsel floats: sized per launch, so short sequences fit two CTAs / SM
+  static int bytes(int nsel) { return IMP + TQ * nsel * 4; }
+  static constexpr int MAX_BYTES = IMP + TQ * MAX_SEL * 4;
 };
 
 __global__ void __launch_bounds__(THREADS) fwd_kernel(const NsaArgs a) {
@@ -284,7 +287,10 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(const NsaArgs a) {
   __nv_bfloat16* sds = reinterpret_cast<__nv_bfloat16*>(smem + BwdSmem::DS);   // dS [query][key]
   float* slse = reinterpret_cast<float*>(smem + BwdSmem::STAT);
   float* sdel = slse + TQ;
-  const int c0 = blockIdx.x * TK, h = blockIdx.y, b = blockIdx.z, hk = h / (a.H / a.Hk);
+  // the query tiles of a key tile are split round-robin over `splits` CTAs (dK / dV are added atomically)
+  const int splits = a.bwd_splits > 0 ? a.bwd_splits : 1;
+  const int c0 = (blockIdx.x / splits) * TK, part = blockIdx.x % splits;
+  const int h = blockIdx.y, b = blockIdx.z, hk = h / (a.H / a.Hk);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
   const int first = a.cstride * c0 + a.csize - 1;  // first query that sees key c0
   if (first >= a.T) return;
@@ -299,7 +305,7 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(const NsaArgs a) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) dk[n][e] = dv[n][e] = 0.f;
   const int key[2] = {c0 + 16 * warp + g, c0 + 16 * warp + g + 8};
-  for (int q0 = (first / TQ) * TQ; q0 < a.T; q0 += TQ) {
+  for (int q0 = (first / TQ + part) * TQ; q0 < a.T; q0 += splits * TQ) {
     __syncthreads();
     load_tile(sq, sqT, qb, ldq, q0, a.T);
     load_tile(sdo, sdoT, dob, ldq, q0, a.T);
@@ -408,8 +414,9 @@ int nt_nsa_compressed_fwd(const NsaArgs& a, cudaStream_t s) {
   using namespace nt::nsa;
   if (!nsa_ok(a) || !a.o || !a.lse || !a.sel) return -1;
   static std::atomic<uint64_t> set{0};
-  if (smem_once(set, fwd_kernel, FwdSmem::BYTES) != cudaSuccess) return -1;
-  fwd_kernel<<<dim3((a.T + TQ - 1) / TQ, a.H, a.B), THREADS, FwdSmem::BYTES, s>>>(a);
+  if (smem_once(set, fwd_kernel, FwdSmem::MAX_BYTES) != cudaSuccess) return -1;
+  const int nsel = (a.T + a.ssize - 1) / a.ssize;
+  fwd_kernel<<<dim3((a.T + TQ - 1) / TQ, a.H, a.B), THREADS, FwdSmem::bytes(nsel), s>>>(a);
   return 0;
 }
 
@@ -418,6 +425,10 @@ int nt_nsa_compressed_bwd(const NsaArgs& a, cudaStream_t s) {
   if (!nsa_ok(a) || !a.dout || !a.lse || !a.delta || !a.dq_acc || !a.dk_acc || !a.dv_acc || !al16(a.dout)) return -1;
   static std::atomic<uint64_t> set{0};
   if (smem_once(set, bwd_kernel, BwdSmem::BYTES) != cudaSuccess) return -1;
-  bwd_kernel<<<dim3((a.Nc + TK - 1) / TK, a.H, a.B), THREADS, BwdSmem::BYTES, s>>>(a);
+  NsaArgs b = a;
+  // enough CTAs to cover the SMs twice: split each key tile's query tiles over CTAs
+  const int base = ((a.Nc + TK - 1) / TK) * a.H * a.B;
+  b.bwd_splits = std::max(1, std::min((2 * 148 + base - 1) / base, (a.T + TQ - 1) / TQ));
+  bwd_kernel<<<dim3(((a.Nc + TK - 1) / TK) * b.bwd_splits, a.H, a.B), THREADS, BwdSmem::BYTES, s>>>(b);
   return 0;
 }

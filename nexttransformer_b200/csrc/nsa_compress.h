@@ -23,6 +23,7 @@ struct NsaArgs {
   float* dq_acc = nullptr;              // fp32 [B, T, H, D], zeroed
   float* dk_acc = nullptr;              // fp32 [B, Nc, Hk, D], zeroed
   float* dv_acc = nullptr;              // fp32 [B, Nc, Hk, D], zeroed
+  int bwd_splits = 0;                   // set by the launcher: CTAs sharing one key tile's query tiles
 };
 
 // Return 0, -1 for unsupported shapes (D 128, nsel <= 256, 16-byte aligned rows).
