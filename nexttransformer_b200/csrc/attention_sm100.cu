@@ -52,6 +52,8 @@ struct Params {
   const float* delta;
   long long* trace;
   int dq_slices;  // 0: dQ added into one fp32 buffer (bulk reductions); else one slice per key tile
+  int dq_direct;  // 1: the drain adds dQ rows from registers with vector reductions (no shared staging)
+  float* dq_base; // dq_acc (row stride H * 128) for the direct drain
 };
 
 // Clock stamp of (role, pair, event) for the first CTA when a trace buffer is given.
@@ -816,6 +818,29 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_free);  // tDP may take the next dP^T
+      if (p.dq_direct) {
+        // each thread adds its query row from registers: 32 vector reductions of 4 fp32 (plain vector
+        // stores into the key tile's slice in deterministic mode); no shared staging, no bulk copies
+        const int qi = q0 + r;
+        if (qi < p.T) {
+          float* dst = p.dq_base +
+                       ((p.dq_slices ? static_cast<int64_t>(kt) * p.B * p.T : 0) + static_cast<int64_t>(b) * p.T + qi) *
+                           (static_cast<int64_t>(p.H) * HD) + h * HD;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float a0 = __uint_as_float(vq[4 * j]) * p.scale, a1 = __uint_as_float(vq[4 * j + 1]) * p.scale;
+            const float a2 = __uint_as_float(vq[4 * j + 2]) * p.scale, a3 = __uint_as_float(vq[4 * j + 3]) * p.scale;
+            if (p.dq_slices)
+              *reinterpret_cast<float4*>(dst + 4 * j) = make_float4(a0, a1, a2, a3);
+            else
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j), "f"(a0), "f"(a1),
+                           "f"(a2), "f"(a3)
+                           : "memory");
+          }
+        }
+        if (leader) stamp(p, 3, it, 2);
+        continue;
+      }
       bool fine = true;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq) {
@@ -1055,6 +1080,14 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   p.dq_acc = a.dq_acc;
   p.delta = a.delta;
   p.trace = a.trace;
+  // NT_ATTN_DQ_DIRECT=1: the drain adds dQ with vector reductions from registers instead of staging it
+  // through shared memory for bulk reductions (selectable for measurement)
+  static const int direct = [] {
+    const char* e = std::getenv("NT_ATTN_DQ_DIRECT");
+    return e ? std::atoi(e) : 0;
+  }();
+  p.dq_direct = direct;
+  p.dq_base = a.dq_acc;
   static std::atomic<uint64_t> smem_set{0};
   nt::smem_limit(smem_set, attn_bwd_kernel, BwdSmem::TOTAL);
   dim3 grid((a.T + TILE - 1) / TILE, a.Hk, a.B);
