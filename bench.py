@@ -258,7 +258,14 @@ def bench_method(args, rank, world, local, device):
             config = replace(rc.candidate_config(raw["method"]),
                              **{k: v for k, v in raw.items() if k not in ("method", "scale")}, scale="debug")
             model = ref_build(config, device)
-            opt = model.setup_optimizer() if hasattr(model, "setup_optimizer") else None
+            try:
+                # the optimizer of the reference's own trainer (train.py): method-auxiliary and
+                # non-matrix parameters to AdamW, matrices by shape to Muon
+                from nexttransformer.training.optimizer import build_optimizer as ref_optimizer
+                from nexttransformer.models.native.config import NativeTrainConfig
+                opt = ref_optimizer(model, NativeTrainConfig())
+            except ImportError:
+                opt = model.setup_optimizer() if hasattr(model, "setup_optimizer") else None
             if opt is None:
                 raise RuntimeError("the reference model exposes no optimizer setup")
 
@@ -299,13 +306,14 @@ def bench_method(args, rank, world, local, device):
                 launches = count_own_kernels(lambda: (step_device(dev_x, dev_y), flush()), opt) * args.steps
             except Exception:
                 launches = None
-    except (ImportError, RuntimeError, NotImplementedError, TypeError) as exc:
-        if args.impl == "reference" and rank == 0:
+    except Exception as exc:
+        if args.impl != "reference":
+            raise
+        if rank == 0:
             print(json.dumps({"impl": "reference", "method": args.method,
                               "unavailable": f"{type(exc).__name__}: {exc}"[:300]}), flush=True)
-            shutdown()
-            return
-        raise
+        shutdown()
+        return
     value = global_batch / (ms / 1000.0)
     gpus = [int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(world))).split(",")
             if x.strip().isdigit()] or list(range(world))

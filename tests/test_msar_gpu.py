@@ -15,7 +15,8 @@ def _both(module, x, monkeypatch, dout):
         xi = x.detach().clone().requires_grad_()
         y = module(xi)
         y.backward(dout)
-        outs.append((y.detach().float(), xi.grad.float(), [p.grad.float().clone() for p in module.parameters()]))
+        outs.append((y.detach().float(), xi.grad.float(), [p.grad.float().clone() if p.grad is not None else torch.zeros_like(p, dtype=torch.float32)
+                                                            for p in module.parameters()]))
     return outs
 
 
