@@ -18,6 +18,8 @@
 #include "attention_sm100.h"
 #include "common.cuh"
 
+#include <type_traits>
+
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <cstdlib>
@@ -69,6 +71,48 @@ NT_DEVICE uint64_t kmajor_desc(uint32_t base, int j) {
 // MN-major operand: rows are the reduction index (128 rows), two 64-wide MN boxes.
 NT_DEVICE uint64_t mnmajor_desc(uint32_t base, int j) {
   return smem_desc(base + j * 2048, BOX_BYTES, 1024);
+}
+
+// Byte offsets of k-step j from step 0 in the two operand forms above.  An MMA loop builds the step-0
+// descriptor once and adds offset >> 4 to its start-address field (address >> 4 in 14 bits; every tile
+// lies below 256 KB, so the sum never carries out of the field): fully unrolled, the issuing thread
+// spends no instructions on descriptors between MMAs.
+__host__ __device__ constexpr uint32_t kmajor_step(int j) { return ((j >> 2) * BOX_BYTES + (j & 3) * 32) >> 4; }
+__host__ __device__ constexpr uint32_t mnmajor_step(int j) { return (j * 2048) >> 4; }
+
+// The MMAs of one k-step loop: step-0 descriptors plus immediate steps, added inside the asm statement
+// so that the compiler neither keeps every step's descriptor live across the loop nor spends
+// registers of the issuing warp (which runs with few after its register split) on them.
+template <uint32_t SA, uint32_t SB>
+NT_DEVICE void umma_step(uint32_t tmem_d, uint64_t a0, uint64_t b0, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "add.s64 da, %1, %5;\n\t"
+      "add.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a0), "l"(b0), "r"(idesc), "r"(accumulate), "n"(static_cast<uint64_t>(SA)), "n"(static_cast<uint64_t>(SB))
+      : "memory");
+}
+// The same with A read from tensor memory at column offset TA.
+template <uint32_t TA, uint32_t SB>
+NT_DEVICE void umma_step_tmem_a(uint32_t tmem_d, uint32_t tmem_a0, uint64_t b0, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "add.u32 ta, %1, %5;\n\t"
+      "add.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a0), "l"(b0), "r"(idesc), "r"(accumulate), "n"(TA), "n"(static_cast<uint64_t>(SB))
+      : "memory");
+}
+// Eight k-steps (K = 128) of one operand-form pair, unrolled at compile time.
+template <int J = 0, class F>
+NT_DEVICE void for_steps(F&& f) {
+  if constexpr (J < 8) {
+    f(std::integral_constant<int, J>{});
+    for_steps<J + 1>(f);
+  }
 }
 
 // Byte offset of 16-byte chunk `c` (0..15) of row `r` in a two-box 128B-swizzled tile.
@@ -269,11 +313,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       auto issue_s = [&](int X, int t) -> bool {
         const int st = t & 1;
         if (!mbar_wait(&kv_full[st], (t >> 1) & 1, 0x21u, abort_flag)) return false;
+        stamp(p, 1, t, 4 + X);
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm + FwdSmem::K0 + st * TILE_BYTES);
         const uint32_t qx = X ? qb_addr : qa_addr, tsx = X ? t_sB : t_sA;
-#pragma unroll 1
-        for (int q = 0; q < HD / 16; ++q) umma_bf16(tsx, kmajor_desc(qx, q), kmajor_desc(k_addr, q), idesc_s, q > 0);
+        const uint64_t da = kmajor_desc(qx, 0), db = kmajor_desc(k_addr, 0);
+        for_steps([&](auto q) {
+          constexpr int Q = decltype(q)::value;
+          umma_step<kmajor_step(Q), kmajor_step(Q)>(tsx, da, db, idesc_s, Q > 0);
+        });
         umma_commit(&s_full[X]);
         stamp(p, 1, t, X);
         if (X) ++iB; else ++iA;
@@ -282,12 +330,16 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       auto issue_pv = [&](int X, int t) -> bool {
         int& u = X ? uB : uA;
         if (!mbar_wait(&p_full[X], u & 1, 0x23u + X, abort_flag)) return false;
+        stamp(p, 1, t, 6 + X);
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sm + FwdSmem::V0 + (t & 1) * TILE_BYTES);
         const uint32_t tox = X ? t_oB : t_oA, tsx = X ? t_sB : t_sA;
-#pragma unroll 1
-        for (int q = 0; q < TILE / 16; ++q)
-          umma_bf16_tmem_a(tox, tsx + q * 8, mnmajor_desc(v_addr, q), idesc_pv, (u > 0 || q > 0) ? 1u : 0u);
+        const uint64_t dv = mnmajor_desc(v_addr, 0);
+        const uint32_t acc0 = u > 0 ? 1u : 0u;
+        for_steps([&](auto q) {
+          constexpr int Q = decltype(q)::value;
+          umma_step_tmem_a<Q * 8, mnmajor_step(Q)>(tox, tsx, dv, idesc_pv, Q > 0 ? 1u : acc0);
+        });
         umma_commit(&o_done[X]);
         stamp(p, 1, t, 2 + X);
         ++u;
@@ -625,10 +677,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (!mbar_wait(&q_full[it & 1], (it >> 1) & 1, 0x61u, abort_flag)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sm + BwdSmem::Q + (it & 1) * TILE_BYTES);
-        // loops are kept rolled: fully unrolled, the descriptors of every k-step of every operand
-        // would be hoisted into registers that the other warp roles need
-#pragma unroll 1
-        for (int j = 0; j < HD / 16; ++j) umma_bf16(t_s, kmajor_desc(k_addr, j), kmajor_desc(q_addr, j), id_s, j > 0);
+        // unrolled over k-steps from two step-0 descriptors (the steps are immediates)
+        const uint64_t dk = kmajor_desc(k_addr, 0), dq = kmajor_desc(q_addr, 0);
+        for_steps([&](auto j) {
+          constexpr int J = decltype(j)::value;
+          umma_step<kmajor_step(J), kmajor_step(J)>(t_s, dk, dq, id_s, J > 0);
+        });
         umma_commit(s_full);
         return true;
       };
@@ -640,28 +694,36 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x62u, abort_flag)) break;  // dQ of it-1 left tDP
         stamp(p, 1, it, 1);
         tc_fence_after();
-#pragma unroll 1
-        for (int j = 0; j < HD / 16; ++j)
-          umma_bf16(t_dp, kmajor_desc(v_addr, j), kmajor_desc(do_addr, j), id_s, j > 0);
+        const uint64_t dvk = kmajor_desc(v_addr, 0), ddo = kmajor_desc(do_addr, 0);
+        for_steps([&](auto j) {
+          constexpr int J = decltype(j)::value;
+          umma_step<kmajor_step(J), kmajor_step(J)>(t_dp, dvk, ddo, id_s, J > 0);
+        });
         umma_commit(dp_full);
         if (!mbar_wait(p_full, it & 1, 0x63u, abort_flag)) break;
         stamp(p, 1, it, 2);
         tc_fence_after();
-#pragma unroll 1
-        for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16_tmem_a(t_dv, t_s + (j >> 2) * 64 + (j & 3) * 8, mnmajor_desc(do_addr, j), id_kv,
-                           (it > 0 || j > 0) ? 1u : 0u);
+        const uint64_t ddo_mn = mnmajor_desc(do_addr, 0);
+        const uint32_t acc_kv = it > 0 ? 1u : 0u;
+        for_steps([&](auto j) {
+          constexpr int J = decltype(j)::value;
+          umma_step_tmem_a<(J >> 2) * 64 + (J & 3) * 8, mnmajor_step(J)>(t_dv, t_s, ddo_mn, id_kv, J > 0 ? 1u : acc_kv);
+        });
         umma_commit(do_empty);
         if (it + 1 < n_it && !issue_s(it + 1)) break;
         if (!mbar_wait(ds_full, it & 1, 0x64u, abort_flag)) break;
         stamp(p, 1, it, 3);
         tc_fence_after();
-#pragma unroll 1
-        for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16(t_dk, kmajor_desc(ds_addr, j), mnmajor_desc(q_addr, j), id_kv, (it > 0 || j > 0) ? 1u : 0u);
-#pragma unroll 1
-        for (int j = 0; j < TILE / 16; ++j)
-          umma_bf16(t_dp, mnmajor_desc(ds_addr, j), mnmajor_desc(k_addr, j), id_q, j > 0);
+        const uint64_t dds = kmajor_desc(ds_addr, 0), dq_mn = mnmajor_desc(q_addr, 0);
+        const uint64_t dds_mn = mnmajor_desc(ds_addr, 0), dk_mn = mnmajor_desc(k_addr, 0);
+        for_steps([&](auto j) {
+          constexpr int J = decltype(j)::value;
+          umma_step<kmajor_step(J), mnmajor_step(J)>(t_dk, dds, dq_mn, id_kv, J > 0 ? 1u : acc_kv);
+        });
+        for_steps([&](auto j) {
+          constexpr int J = decltype(j)::value;
+          umma_step<mnmajor_step(J), mnmajor_step(J)>(t_dp, dds_mn, dk_mn, id_q, J > 0);
+        });
         umma_commit(dq_full);
         umma_commit(&q_empty[st]);
         stamp(p, 1, it, 4);

@@ -198,11 +198,14 @@ def attn_fwd_trace(rows):
     torch.cuda.synchronize()
     t = trace.cpu()
     base = int(t[t > 0].min())
-    names = {1: "mma: S_A S_B PV_A PV_B", 2: "softmax A: s_full loaded max rescaled p_arrive",
+    # MMA role: the four issues (stamped after their commit), then the four wait exits before them
+    names = {1: "mma: S_A S_B PV_A PV_B issued, then ready S_A S_B PV_A PV_B",
+             2: "softmax A: s_full loaded max rescaled p_arrive",
              3: "softmax B: s_full loaded max rescaled p_arrive"}
     out = {}
     for role, name in names.items():
-        out[name] = [[int(x) - base if int(x) else None for x in t[role, it][:5]] for it in range(16)
+        width = 8 if role == 1 else 5
+        out[name] = [[int(x) - base if int(x) else None for x in t[role, it][:width]] for it in range(16)
                      if (t[role, it] > 0).any()]
     return out
 
