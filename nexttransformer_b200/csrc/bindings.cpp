@@ -960,8 +960,10 @@ void gated_rmsnorm_bwd(const Tensor& x, const Tensor& g, const Tensor& gain, con
   for (auto* t : {&x, &g, &dy, &dx, &dg}) check_rows(*t, "gated norm operand");
   const int D = static_cast<int>(gain.numel());
   const c10::cuda::CUDAGuard guard(x.device());
+  auto work = at::empty({NT_GATED_NORM_PARTS, D}, x.options().dtype(at::kFloat));
   ok(nt_gated_rmsnorm_bwd(x.data_ptr(), g.data_ptr(), gain.data_ptr<float>(), rstd.data_ptr<float>(), dy.data_ptr(),
-                          dx.data_ptr(), dg.data_ptr(), dgain.data_ptr<float>(), x.numel() / D, D, stream()),
+                          dx.data_ptr(), dg.data_ptr(), dgain.data_ptr<float>(), work.data_ptr<float>(), x.numel() / D,
+                          D, stream()),
      "gated_rmsnorm_bwd");
 }
 
@@ -1012,6 +1014,74 @@ void delta_prep_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Opt
   a.carry = carry.data_ptr<float>();
   const c10::cuda::CUDAGuard guard(q.device());
   ok(nt_delta_prep_fwd(a, stream()), "delta_prep_fwd");
+}
+
+// KDA with the gate from its pre-activation and (qk_norm) the q / k L2 normalisation in the kernel:
+// g_raw bf16 [B, T, H, 128], g_log / g_bias fp32 [H, 128].
+static DeltaPrepArgs kda_args(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& g_raw,
+                              const Tensor& g_log, const Tensor& g_bias, const Tensor& beta, double qk_scale,
+                              bool qk_norm) {
+  DeltaPrepArgs a = prep_args(q, k, v, c10::nullopt, beta, DELTA_NONE, qk_scale);
+  check_cuda(g_raw, "g_raw");
+  TORCH_CHECK(g_raw.scalar_type() == at::kBFloat16 && g_raw.is_contiguous() && g_raw.sizes() == q.sizes(),
+              "g_raw: contiguous bf16 [B, T, H, 128]");
+  for (auto* t : {&g_log, &g_bias})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == q.size(2) * 128,
+                "g_log / g_bias: contiguous fp32 [H, 128]");
+  a.gate = DELTA_FEATURE;
+  a.qk_norm = qk_norm ? 1 : 0;
+  a.g_raw = reinterpret_cast<const __nv_bfloat16*>(g_raw.data_ptr());
+  a.g_log = g_log.data_ptr<float>();
+  a.g_bias = g_bias.data_ptr<float>();
+  return a;
+}
+
+void delta_prep_kda_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& g_raw, const Tensor& g_log,
+                        const Tensor& g_bias, const Tensor& beta, double qk_scale, bool qk_norm, const Tensor& w,
+                        const Tensor& u0, const Tensor& qt, const Tensor& kc, const Tensor& aqk, const Tensor& carry) {
+  DeltaPrepArgs a = kda_args(q, k, v, g_raw, g_log, g_bias, beta, qk_scale, qk_norm);
+  const int64_t rows = static_cast<int64_t>(a.B) * a.H * ((a.T + 63) / 64) * 64;
+  for (auto* t : {&w, &u0, &qt, &kc})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->numel() == rows * 128, "chunk outputs");
+  TORCH_CHECK(aqk.scalar_type() == at::kBFloat16 && aqk.is_contiguous() && aqk.numel() == rows * 64, "aqk");
+  TORCH_CHECK(carry.scalar_type() == at::kFloat && carry.is_contiguous() && carry.numel() == rows * 2, "carry");
+  a.w = w.data_ptr(); a.u0 = u0.data_ptr(); a.qt = qt.data_ptr(); a.kc = kc.data_ptr(); a.aqk = aqk.data_ptr();
+  a.carry = carry.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_delta_prep_fwd(a, stream()), "delta_prep_kda_fwd");
+}
+
+void delta_prep_kda_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& g_raw, const Tensor& g_log,
+                        const Tensor& g_bias, const Tensor& beta, double qk_scale, bool qk_norm, const Tensor& w,
+                        const Tensor& u0, const Tensor& dw, const Tensor& du0, const Tensor& dqt, const Tensor& dkc,
+                        const Tensor& daqk, const Tensor& dcarry, const Tensor& dq, const Tensor& dk, const Tensor& dv,
+                        const Tensor& dg_raw, const Tensor& dg_log_part, const Tensor& dg_bias_part,
+                        const Tensor& dbeta) {
+  DeltaPrepArgs a = kda_args(q, k, v, g_raw, g_log, g_bias, beta, qk_scale, qk_norm);
+  const int64_t N = (a.T + 63) / 64, rows = static_cast<int64_t>(a.B) * a.H * N * 64;
+  for (auto* t : {&w, &u0})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->numel() == rows * 128, "w / u0");
+  for (auto* t : {&dw, &du0, &dqt, &dkc})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == rows * 128, "chunk gradients");
+  TORCH_CHECK(daqk.scalar_type() == at::kFloat && daqk.is_contiguous() && daqk.numel() == rows * 64, "daqk");
+  TORCH_CHECK(dcarry.scalar_type() == at::kFloat && dcarry.is_contiguous() && dcarry.numel() == rows * 2, "dcarry");
+  for (auto* t : {&dq, &dk, &dv})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == q.numel(), "dq / dk / dv");
+  TORCH_CHECK(dbeta.scalar_type() == at::kFloat && dbeta.is_contiguous() && dbeta.numel() == q.numel() / 128, "dbeta");
+  TORCH_CHECK(dg_raw.scalar_type() == at::kBFloat16 && dg_raw.is_contiguous() && dg_raw.sizes() == q.sizes(), "dg_raw");
+  for (auto* t : {&dg_log_part, &dg_bias_part})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == a.B * N * a.H * 128,
+                "g_log / g_bias partials: fp32 [B, N, H, 128]");
+  a.w = w.data_ptr(); a.u0 = u0.data_ptr();
+  a.dw = dw.data_ptr<float>(); a.du0 = du0.data_ptr<float>(); a.dqt = dqt.data_ptr<float>();
+  a.dkc = dkc.data_ptr<float>(); a.daqk = daqk.data_ptr<float>(); a.dcarry = dcarry.data_ptr<float>();
+  a.dq = dq.data_ptr<float>(); a.dk = dk.data_ptr<float>(); a.dv = dv.data_ptr<float>();
+  a.dbeta = dbeta.data_ptr<float>();
+  a.dg_raw = reinterpret_cast<__nv_bfloat16*>(dg_raw.data_ptr());
+  a.dg_log_part = dg_log_part.data_ptr<float>();
+  a.dg_bias_part = dg_bias_part.data_ptr<float>();
+  const c10::cuda::CUDAGuard guard(q.device());
+  ok(nt_delta_prep_bwd(a, stream()), "delta_prep_kda_bwd");
 }
 
 void delta_prep_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const OptT& g, const Tensor& beta, int64_t gate,
@@ -1162,6 +1232,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("delta_scan_fwd", &delta_scan_fwd);
   m.def("delta_prep_fwd", &delta_prep_fwd, "per-chunk delta-rule terms (WY solve, gates, q/k norm)");
   m.def("delta_prep_bwd", &delta_prep_bwd, "backward of the per-chunk delta-rule terms");
+  m.def("delta_prep_kda_fwd", &delta_prep_kda_fwd, "KDA chunk terms with the gate from its pre-activation");
+  m.def("delta_prep_kda_bwd", &delta_prep_kda_bwd, "backward of delta_prep_kda_fwd");
   m.def("delta_scan_bwd", &delta_scan_bwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);

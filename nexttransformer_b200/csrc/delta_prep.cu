@@ -62,6 +62,10 @@ __device__ __forceinline__ void load_vec<float>(const float* p, float (&out)[4])
   out[3] = f.w;
 }
 
+// torch's softplus (beta 1, threshold 20) and the logistic function, for the KDA gate
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
 __device__ __forceinline__ float sum16(float v) {  // sum over 16 consecutive lanes
   v += __shfl_xor_sync(0xffffffffu, v, 8);
   v += __shfl_xor_sync(0xffffffffu, v, 4);
@@ -142,7 +146,35 @@ __device__ void load_chunk(const DeltaPrepArgs& a, float* sm, int n, int h, int 
       }
     }
   }
-  if (GATE == DELTA_FEATURE) {
+  if (GATE == DELTA_FEATURE && a.g_raw) {
+    // g = -exp(g_log) softplus(g_raw + g_bias) per feature (0 past the end of the sequence)
+    constexpr int LPR = D / 8, RPP = NT / LPR, PASSES = C / RPP;
+    const int d0 = (tid % LPR) * 8, i0 = tid / LPR;
+    float rv[PASSES][8];
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const int t = t0 + i0 + ps * RPP;
+      if (t < a.T) {
+        load_vec<__nv_bfloat16>(a.g_raw + ((static_cast<int64_t>(b) * a.T + t) * a.H + h) * D + d0, rv[ps]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rv[ps][u] = 0.f;
+      }
+    }
+    float ea[8], bias[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      ea[u] = expf(a.g_log[h * D + d0 + u]);
+      bias[u] = a.g_bias[h * D + d0 + u];
+    }
+#pragma unroll
+    for (int ps = 0; ps < PASSES; ++ps) {
+      const bool live = t0 + i0 + ps * RPP < a.T;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        sb[(i0 + ps * RPP) * LDF + d0 + u] = live ? -ea[u] * softplus_f(rv[ps][u] + bias[u]) : 0.f;
+    }
+  } else if (GATE == DELTA_FEATURE) {
     constexpr int LPR = D / 4, RPP = NT / LPR, PASSES = C / RPP;
     const int d0 = (tid % LPR) * 4, i0 = tid / LPR;
     float gv[PASSES][4];
@@ -171,7 +203,7 @@ __device__ void load_chunk(const DeltaPrepArgs& a, float* sm, int n, int h, int 
     sm[S::BETA + tid] = t < a.T ? a.beta[(static_cast<int64_t>(b) * a.T + t) * a.H + h] : 0.f;
   }
   __syncthreads();
-  if (GATE == DELTA_SCALAR) {
+  if (GATE == DELTA_SCALAR || (GATE == DELTA_FEATURE && a.qk_norm)) {
     // L2 normalisation of every q and k row (one warp per row; F.normalize's eps of 1e-12)
     const int warp = tid >> 5, lane = tid & 31;
     for (int i = warp; i < C; i += NT / 32) {
@@ -192,6 +224,8 @@ __device__ void load_chunk(const DeltaPrepArgs& a, float* sm, int n, int h, int 
         sm[S::NK + i] = nk;
       }
     }
+  }
+  if (GATE == DELTA_SCALAR) {
     if (tid == 0) {
       float s = 0.f;
       for (int i = 0; i < C; ++i) {
@@ -587,6 +621,38 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
     }
   }
 
+  // ---- KDA with the normalisation in this kernel: dQ / dK are gradients of q^ = s q / |q| and
+  // k^ = k / |k|; back through the normalisation with the raw rows re-read from global memory
+  if (GATE == DELTA_FEATURE && a.qk_norm) {
+    const float s = a.qk_scale;
+    const TIn* qraw = reinterpret_cast<const TIn*>(a.q);
+    const TIn* kraw = reinterpret_cast<const TIn*>(a.k);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = 4 * ti + r;
+      const bool live = n * C + i < a.T;
+      const int64_t o = (tok_base + static_cast<int64_t>(i) * a.H) * D;
+      const float nq = sm[S::NQ + i], nk = sm[S::NK + i];
+      float qh[8], kh[8], pq = 0.f, pk = 0.f;
+#pragma unroll
+      for (int oc = 0; oc < 8; ++oc) {
+        const int d = tj + 16 * oc;
+        qh[oc] = live ? s * to_f(qraw[o + d]) / nq : 0.f;
+        kh[oc] = live ? to_f(kraw[o + d]) / nk : 0.f;
+        pq = fmaf(qh[oc], dQ[r][oc], pq);
+        pk = fmaf(kh[oc], dK[r][oc], pk);
+      }
+      pq = sum16(pq);
+      pk = sum16(pk);
+      const bool liveq = nq > 1e-12f, livek = nk > 1e-12f;
+#pragma unroll
+      for (int oc = 0; oc < 8; ++oc) {
+        dQ[r][oc] = liveq ? (s / nq) * (dQ[r][oc] - qh[oc] * pq / (s * s)) : (s / nq) * dQ[r][oc];
+        dK[r][oc] = livek ? (dK[r][oc] - kh[oc] * pk) / nk : dK[r][oc] / nk;
+      }
+    }
+  }
+
   // ---- reductions (deterministic): dbeta and the GDN per-token db over the 16 lanes of a row
   float* sDB = sm + S::DB;
   float* sDBETA = sm + S::DBETA;
@@ -655,9 +721,29 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
       for (int i = 0; i < C; ++i) last += sLast[i * LDF + d];
       last = fmaf(dcar[d], __expf(sb[(C - 1) * LDF + d]), last);
       float acc = 0.f;
-      for (int i = C - 1; i >= 0; --i) {
-        acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
-        if (n * C + i < a.T) a.dg[(tok_base + static_cast<int64_t>(i) * a.H) * D + d] = acc;
+      if (a.g_raw) {
+        // g = -e^{A} softplus(z), z = g_raw + bias:  dz = -dg e^{A} sigmoid(z),  dA = dg g
+        const float ea = expf(a.g_log[h * D + d]), bias = a.g_bias[h * D + d];
+        float pa = 0.f, pb = 0.f;
+        for (int i = C - 1; i >= 0; --i) {
+          acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
+          if (n * C + i < a.T) {
+            const int64_t o = (tok_base + static_cast<int64_t>(i) * a.H) * D + d;
+            const float z = __bfloat162float(a.g_raw[o]) + bias;
+            const float dz = -acc * ea * sigmoid_f(z);
+            a.dg_raw[o] = __float2bfloat16_rn(dz);
+            pb += dz;
+            pa = fmaf(acc, -ea * softplus_f(z), pa);
+          }
+        }
+        const int64_t part = ((static_cast<int64_t>(b) * N + n) * a.H + h) * D + d;
+        a.dg_log_part[part] = pa;
+        a.dg_bias_part[part] = pb;
+      } else {
+        for (int i = C - 1; i >= 0; --i) {
+          acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
+          if (n * C + i < a.T) a.dg[(tok_base + static_cast<int64_t>(i) * a.H) * D + d] = acc;
+        }
       }
     }
   }
@@ -746,8 +832,11 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // The chunk loads are 16-byte vectors: q / k / v, the per-feature gate and the forward's w / u0
 // must start on 16-byte boundaries (rows are 128 features, so every row then does too).
 static bool prep_args_ok(const DeltaPrepArgs& a) {
-  return a.B > 0 && a.T > 0 && a.H > 0 && a.q && a.k && a.v && a.beta && (a.gate == DELTA_NONE || a.g) &&
-         aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && (a.gate != DELTA_FEATURE || aligned16(a.g)) &&
+  const bool raw = a.gate == DELTA_FEATURE && a.g_raw;
+  if (a.g_raw && (a.gate != DELTA_FEATURE || !a.g_log || !a.g_bias || !aligned16(a.g_raw))) return false;
+  if (a.qk_norm && a.gate != DELTA_FEATURE) return false;
+  return a.B > 0 && a.T > 0 && a.H > 0 && a.q && a.k && a.v && a.beta && (a.gate == DELTA_NONE || a.g || raw) &&
+         aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && (a.gate != DELTA_FEATURE || raw || aligned16(a.g)) &&
          (!a.w || aligned16(a.w)) && (!a.u0 || aligned16(a.u0));
 }
 
@@ -761,7 +850,8 @@ int nt_delta_prep_bwd(const DeltaPrepArgs& a, cudaStream_t s) {
   nt::current_context();
   if (!prep_args_ok(a) || !a.w || !a.u0 || !a.dw || !a.du0 || !a.dqt || !a.dkc || !a.daqk || !a.dcarry || !a.dq ||
       !a.dk || !a.dv ||
-      !a.dbeta || (a.gate != DELTA_NONE && !a.dg))
+      !a.dbeta)
     return -1;
+  if (a.g_raw ? (!a.dg_raw || !a.dg_log_part || !a.dg_bias_part) : (a.gate != DELTA_NONE && !a.dg)) return -1;
   return a.in_bf16 ? nt::dprep::dispatch<__nv_bfloat16>(a, s, true) : nt::dprep::dispatch<float>(a, s, true);
 }

@@ -1,5 +1,6 @@
 // Per-chunk terms of the chunked (gated) delta rule, forward and backward (delta_prep.cu).
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime_api.h>
 #include <stdint.h>
 
@@ -38,6 +39,18 @@ struct DeltaPrepArgs {
   float* dv = nullptr;
   float* dg = nullptr;
   float* dbeta = nullptr;
+  // DELTA_FEATURE options.  qk_norm: q <- qk_scale q / |q| and k <- k / |k| here, as DELTA_SCALAR
+  // always does.  g_raw: the gate from its pre-activation instead of g,
+  //   g = -exp(g_log[h, d]) softplus(g_raw + g_bias[h, d])   (g_raw bf16 [B, T, H, 128]; g_log, g_bias fp32 [H, 128]);
+  // its backward writes dg_raw (bf16, the layout of g_raw) and per-chunk partial sums of the g_log / g_bias
+  // gradients, fp32 [B, N, H, 128], that the caller sums over (B, N); dg is then not written.
+  int qk_norm = 0;
+  const __nv_bfloat16* g_raw = nullptr;
+  const float* g_log = nullptr;
+  const float* g_bias = nullptr;
+  __nv_bfloat16* dg_raw = nullptr;
+  float* dg_log_part = nullptr;
+  float* dg_bias_part = nullptr;
 };
 
 // Return 0 on success, -1 for an unsupported shape.

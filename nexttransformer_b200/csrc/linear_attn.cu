@@ -13,6 +13,8 @@
 #include "common.cuh"
 #include "linear_attn.h"
 
+#include <algorithm>
+
 namespace nt {
 namespace lin {
 
@@ -172,32 +174,59 @@ __global__ void gated_rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, co
   }
 }
 
-// dx, dg and per-block dgain partials of the gated RMSNorm (dgain reduced with fp32 atomics)
+// dx and dg of the gated RMSNorm, one warp per row with the warps striding over the rows; each warp
+// keeps its dgain terms in registers and every block writes one partial row (fixed order, no
+// atomics), summed by gated_rmsnorm_dgain_kernel.
 template <int E>
-__global__ void gated_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ g,
-                                         const float* __restrict__ gain, const float* __restrict__ rstd,
-                                         const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dx,
-                                         __nv_bfloat16* __restrict__ dg, float* __restrict__ dgain, int64_t rows) {
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
-  const int64_t base = r * 32 * E + lane * E;
-  const float rs = rstd[r];
-  float n[E], a[E], dot = 0.f;
+__global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ g, const float* __restrict__ gain,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dx,
+    __nv_bfloat16* __restrict__ dg, float* __restrict__ part, int64_t rows) {
+  __shared__ float red[8][32 * E];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float gn[E], acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const float xv = bf2f(x[base + e]), gv = bf2f(g[base + e]), d = bf2f(dy[base + e]);
-    const float sg = 1.f / (1.f + __expf(-gv));
-    const float s = gv * sg;
-    n[e] = xv * rs;
-    dg[base + e] = f2bf(d * n[e] * gain[lane * E + e] * sg * (1.f + gv * (1.f - sg)));
-    atomicAdd(&dgain[lane * E + e], d * n[e] * s);
-    a[e] = d * gain[lane * E + e] * s;  // dL/dn
-    dot += a[e] * n[e];
+    gn[e] = gain[lane * E + e];
+    acc[e] = 0.f;
   }
-  dot = warp_sum(dot) / (32 * E);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp; r < rows; r += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t base = r * 32 * E + lane * E;
+    const float rs = rstd[r];
+    float n[E], a[E], dot = 0.f;
 #pragma unroll
-  for (int e = 0; e < E; ++e) dx[base + e] = f2bf(rs * (a[e] - n[e] * dot));
+    for (int e = 0; e < E; ++e) {
+      const float xv = bf2f(x[base + e]), gv = bf2f(g[base + e]), d = bf2f(dy[base + e]);
+      const float sg = 1.f / (1.f + __expf(-gv));
+      const float sl = gv * sg;
+      n[e] = xv * rs;
+      dg[base + e] = f2bf(d * n[e] * gn[e] * sg * (1.f + gv * (1.f - sg)));
+      acc[e] = fmaf(d * n[e], sl, acc[e]);
+      a[e] = d * gn[e] * sl;  // dL/dn
+      dot += a[e] * n[e];
+    }
+    dot = warp_sum(dot) / (32 * E);
+#pragma unroll
+    for (int e = 0; e < E; ++e) dx[base + e] = f2bf(rs * (a[e] - n[e] * dot));
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) red[warp][lane * E + e] = acc[e];
+  __syncthreads();
+  for (int c = threadIdx.x; c < 32 * E; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][c];
+    part[static_cast<int64_t>(blockIdx.x) * 32 * E + c] = t;
+  }
+}
+
+// dgain[c] += sum over the blocks' partial rows, in block order
+__global__ void gated_rmsnorm_dgain_kernel(const float* __restrict__ part, float* __restrict__ dgain, int parts, int D) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= D) return;
+  float t = 0.f;
+  for (int p = 0; p < parts; ++p) t += part[static_cast<int64_t>(p) * D + c];
+  dgain[c] += t;
 }
 
 }  // namespace lin
@@ -251,15 +280,17 @@ int nt_gated_rmsnorm_fwd(const void* x, const void* g, const float* gain, void* 
 }
 
 int nt_gated_rmsnorm_bwd(const void* x, const void* g, const float* gain, const float* rstd, const void* dy, void* dx,
-                         void* dg, float* dgain, int64_t rows, int D, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+                         void* dg, float* dgain, float* work, int64_t rows, int D, cudaStream_t s) {
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((rows + 7) / 8, NT_GATED_NORM_PARTS));
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto G = static_cast<const __nv_bfloat16*>(g);
   auto DY = static_cast<const __nv_bfloat16*>(dy);
   auto DX = static_cast<__nv_bfloat16*>(dx);
   auto DG = static_cast<__nv_bfloat16*>(dg);
-  if (D == 128) gated_rmsnorm_bwd_kernel<4><<<blocks, 256, 0, s>>>(X, G, gain, rstd, DY, DX, DG, dgain, rows);
-  else if (D == 64) gated_rmsnorm_bwd_kernel<2><<<blocks, 256, 0, s>>>(X, G, gain, rstd, DY, DX, DG, dgain, rows);
+  if (rows <= 0) return 0;
+  if (D == 128) gated_rmsnorm_bwd_kernel<4><<<blocks, 256, 0, s>>>(X, G, gain, rstd, DY, DX, DG, work, rows);
+  else if (D == 64) gated_rmsnorm_bwd_kernel<2><<<blocks, 256, 0, s>>>(X, G, gain, rstd, DY, DX, DG, work, rows);
   else return -1;
+  gated_rmsnorm_dgain_kernel<<<1, 128, 0, s>>>(work, dgain, static_cast<int>(blocks), D);
   return 0;
 }

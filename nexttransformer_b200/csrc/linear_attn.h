@@ -13,6 +13,8 @@ int nt_causal_conv_silu_bwd(const void* x, const void* pre, const void* dy, cons
 // rows of D (64 or 128) channels; gain fp32 [D]; rstd fp32 [rows] saved for the backward.
 int nt_gated_rmsnorm_fwd(const void* x, const void* g, const float* gain, void* y, float* rstd, int64_t rows, int D,
                          cudaStream_t s);
-// dgain (fp32 [D]) is accumulated into (zero it first).
+// dgain (fp32 [D]) is accumulated into (zero it first); work: fp32 [NT_GATED_NORM_PARTS, D] scratch for
+// the per-block partial sums (deterministic: no atomics).
+constexpr int NT_GATED_NORM_PARTS = 592;
 int nt_gated_rmsnorm_bwd(const void* x, const void* g, const float* gain, const float* rstd, const void* dy, void* dx,
-                         void* dg, float* dgain, int64_t rows, int D, cudaStream_t s);
+                         void* dg, float* dgain, float* work, int64_t rows, int D, cudaStream_t s);

@@ -196,6 +196,14 @@ def _scalar_decay_chunks(q, k, v, g, C):
     return out + torch.stack(inter, 2)
 
 
+def _kda_kernel_ok(q, k, v):
+    """The fused KDA chunk kernels take these operands (CUDA, bf16, head size 128, chunk 64)."""
+    if not q.is_cuda:
+        return False
+    from nexttransformer_b200.ops.linear_attention import fused_chunk_supported
+    return fused_chunk_supported(q, k, v, 64)
+
+
 def _gla_kernel_ok(q, v):
     from nexttransformer_b200.ops.linear_attention import gla_supported
     return gla_supported(q, v)
@@ -364,12 +372,14 @@ class LinearMixer(nn.Module):
         if ve is not None and self.ve_gate is not None:
             v = v + (3 * torch.sigmoid(self.ve_gate(x[..., :12]))).unsqueeze(-1) * ve.reshape_as(v)
         beta = decay = None
+        # KDA on the fused kernels: the gate and the q / k normalisation are formed inside them
+        kda_fused = self.kind == "kda" and chunked and x.dtype == torch.bfloat16 and _kda_kernel_ok(q, k, v)
         if self.kind in ("elu_linear", "elu_norm", "elu_qknorm"):
             if self.kind == "elu_qknorm":
                 q, k = (norm(z.to(acc_dtype(z))) * ELU_QK_TEMPERATURE for z in (q, k))
             q, k = elu_feature_map(q), elu_feature_map(k)
         elif self.kind in ("deltanet", "kda", "gdn"):
-            if not (self.kind == "gdn" and chunked):
+            if not (self.kind == "gdn" and chunked) and not kda_fused:
                 q, k = F.normalize(q, dim=-1), F.normalize(k, dim=-1)
                 q = q * D ** -.5
             beta = torch.sigmoid(self.beta_proj(x))
@@ -384,7 +394,7 @@ class LinearMixer(nn.Module):
             gate = self.gate_up(self.gate_down(x)).reshape(B, T, H, D)
             if self.kind == "gla":
                 decay = (F.logsigmoid(gate.float()) / 16).exp()
-            else:
+            elif not kda_fused:
                 decay = -self.log_decay.exp() * F.softplus(gate.float() + self.dt_bias)
                 if not chunked:
                     decay = decay.exp()
@@ -392,7 +402,10 @@ class LinearMixer(nn.Module):
             decay = -self.log_decay.exp() * F.softplus(self.decay_proj(x).float() + self.dt_bias)
             if not chunked:
                 decay = decay.exp().unsqueeze(-1)
-        if chunked:
+        if kda_fused:
+            from nexttransformer_b200.ops.linear_attention import kda_chunk_cuda
+            y = kda_chunk_cuda(q, k, v, gate, self.log_decay, self.dt_bias, beta, qk_l2norm_scale=D ** -.5)
+        elif chunked:
             y = chunk_attention(q, k, v, kind=self.kind, g=decay, beta=beta, chunk=CHUNK_BACKENDS[c.backend],
                                 qk_l2norm_scale=D ** -.5 if self.kind == "gdn" else None)
         elif self.kind == "gla" and x.is_cuda and _gla_kernel_ok(q, v):
@@ -408,7 +421,9 @@ class LinearMixer(nn.Module):
         elif self.kind == "elu_linear":
             y = y.to(x.dtype)
         elif gated:
-            y = gated_rms_norm(y, self.output_gate(x).reshape(B, T, H, D), self.output_gain)
+            # one kernel each way (ops.linear_attention), the fp32 torch expression elsewhere
+            from nexttransformer_b200.ops.linear_attention import gated_rms_norm as gated_rms_norm_cuda
+            y = gated_rms_norm_cuda(y, self.output_gate(x).reshape(B, T, H, D), self.output_gain)
         else:
             y = norm(y) * self.output_gain.to(y.dtype)
         y = y.reshape(B, T, d)

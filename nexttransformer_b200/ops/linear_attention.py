@@ -130,61 +130,125 @@ import os as _os
 FUSED_DELTA = _os.environ.get("NT_FUSED_DELTA", "1") == "1"
 
 
+def _chunk_scan_forward(prep, q):
+    """Chunk terms (``prep`` fills w, u0, qt, kc, aqk, carry) and the inter-chunk scan; returns the
+    output [B, T, H, 128] (a view of the chunk-major result) and the tensors the backward needs."""
+    lib = ext()
+    B, T, H, D = q.shape
+    N = (T + 63) // 64
+    BH = B * H
+    dev = q.device
+    bf = torch.bfloat16
+    w, u0, qt, kc = (torch.empty(BH, N, 64, 128, device=dev, dtype=bf) for _ in range(4))
+    aqk = torch.empty(BH, N, 64, 64, device=dev, dtype=bf)
+    carry = torch.empty(BH, N, 128, device=dev, dtype=torch.float32)
+    prep(w, u0, qt, kc, aqk, carry)
+    o = torch.empty_like(u0)
+    u = torch.empty_like(u0)
+    states = torch.empty(BH, N, 128, 128, device=dev, dtype=bf)
+    lib.delta_scan_fwd(w, qt, kc, aqk, u0, carry, o, states, u)
+    return o.view(B, H, N * 64, 128)[:, :, :T].transpose(1, 2), (w, u0, qt, kc, aqk, carry, states, u)
+
+
+def _chunk_scan_backward(dout, saved, shape):
+    """The scan's reverse pass and the four chain-free products: dw, du0, dqt, dkc, daqk, dcarry."""
+    from nexttransformer_b200.ops.gemm import EPI_F32, gemm
+    lib = ext()
+    w, u0, qt, kc, aqk, carry, states, u = saved
+    B, T, H = shape
+    N = (T + 63) // 64
+    BH = B * H
+    M = BH * N
+    dev = dout.device
+    do = torch.zeros(B, H, N * 64, 128, device=dev, dtype=torch.bfloat16)
+    do[:, :, :T] = dout.transpose(1, 2)
+    do = do.view(BH, N, 64, 128)
+    ds = torch.empty_like(states)
+    dut = torch.empty(BH, N, 128, 64, device=dev, dtype=torch.bfloat16)
+    dcarry = torch.empty_like(carry)
+    lib.delta_scan_bwd(do, w, qt, kc, aqk, carry, states, ds, dut, dcarry)
+
+    def f32(rows, cols):
+        return torch.empty(M, rows, cols, device=dev, dtype=torch.float32)
+    flat = lambda t: t.view(M, *t.shape[2:])
+    dqt = gemm(flat(do), flat(states), f32(64, 128), epi=EPI_F32)                      # do S^T
+    dw = gemm(flat(dut), flat(states), f32(64, 128), a_mn=True, epi=EPI_F32, s_acc=-1.0)  # -du S^T
+    daqk = gemm(flat(do), flat(u), f32(64, 64), epi=EPI_F32)                           # do u^T
+    dkc = gemm(flat(u), flat(ds), f32(64, 128), epi=EPI_F32)                           # u dS^T
+    du0 = dut.transpose(-1, -2).float().contiguous()
+    return dw, du0, dqt, dkc, daqk, dcarry
+
+
 class _DeltaChunk(Function):
     """Fused chunked delta rule: chunk terms (delta_prep) + inter-chunk scan (delta_scan)."""
 
     @staticmethod
     def forward(ctx, q, k, v, g, beta, gate, scale):
         lib = ext()
-        B, T, H, D = q.shape
-        N = (T + 63) // 64
-        BH = B * H
-        dev = q.device
-        bf = torch.bfloat16
-        w, u0, qt, kc = (torch.empty(BH, N, 64, 128, device=dev, dtype=bf) for _ in range(4))
-        aqk = torch.empty(BH, N, 64, 64, device=dev, dtype=bf)
-        carry = torch.empty(BH, N, 128, device=dev, dtype=torch.float32)
-        lib.delta_prep_fwd(q, k, v, g, beta, gate, scale, w, u0, qt, kc, aqk, carry)
-        o = torch.empty_like(u0)
-        u = torch.empty_like(u0)
-        states = torch.empty(BH, N, 128, 128, device=dev, dtype=bf)
-        lib.delta_scan_fwd(w, qt, kc, aqk, u0, carry, o, states, u)
-        ctx.save_for_backward(q, k, v, g, beta, w, u0, qt, kc, aqk, carry, states, u)
+        out, saved = _chunk_scan_forward(
+            lambda *o: lib.delta_prep_fwd(q, k, v, g, beta, gate, scale, *o), q)
+        ctx.save_for_backward(q, k, v, g, beta, *saved)
         ctx.meta = (gate, scale)
-        return o.view(B, H, N * 64, 128)[:, :, :T].transpose(1, 2)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
-        from nexttransformer_b200.ops.gemm import EPI_F32, gemm
         lib = ext()
-        q, k, v, g, beta, w, u0, qt, kc, aqk, carry, states, u = ctx.saved_tensors
+        q, k, v, g, beta, *saved = ctx.saved_tensors
         gate, scale = ctx.meta
         B, T, H, D = q.shape
-        N = (T + 63) // 64
-        BH = B * H
-        M = BH * N
-        do = torch.zeros(B, H, N * 64, 128, device=q.device, dtype=torch.bfloat16)
-        do[:, :, :T] = dout.transpose(1, 2)
-        do = do.view(BH, N, 64, 128)
-        ds = torch.empty_like(states)
-        dut = torch.empty(BH, N, 128, 64, device=q.device, dtype=torch.bfloat16)
-        dcarry = torch.empty_like(carry)
-        lib.delta_scan_bwd(do, w, qt, kc, aqk, carry, states, ds, dut, dcarry)
-
-        def f32(rows, cols):
-            return torch.empty(M, rows, cols, device=q.device, dtype=torch.float32)
-        flat = lambda t: t.view(M, *t.shape[2:])
-        dqt = gemm(flat(do), flat(states), f32(64, 128), epi=EPI_F32)                      # do S^T
-        dw = gemm(flat(dut), flat(states), f32(64, 128), a_mn=True, epi=EPI_F32, s_acc=-1.0)  # -du S^T
-        daqk = gemm(flat(do), flat(u), f32(64, 64), epi=EPI_F32)                           # do u^T
-        dkc = gemm(flat(u), flat(ds), f32(64, 128), epi=EPI_F32)                           # u dS^T
-        du0 = dut.transpose(-1, -2).float().contiguous()
+        w, u0 = saved[0], saved[1]
+        dw, du0, dqt, dkc, daqk, dcarry = _chunk_scan_backward(dout, saved, (B, T, H))
         dq, dk, dv = (torch.empty(q.shape, device=q.device, dtype=torch.float32) for _ in range(3))
         dbeta = torch.empty_like(beta)
         dg = torch.empty_like(g) if g is not None else None
         lib.delta_prep_bwd(q, k, v, g, beta, gate, scale, w, u0, dw, du0, dqt, dkc, daqk, dcarry, dq, dk, dv, dg,
                            dbeta)
         return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta, None, None
+
+
+class _KdaChunk(Function):
+    """KDA with the per-feature gate formed in the chunk-term kernel from its pre-activation,
+    g = -exp(g_log) softplus(g_raw + g_bias), and (qk_norm) the q / k L2 normalisation there too:
+    the fp32 [B, T, H, 128] gate and the normalised q / k never reach global memory."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g_raw, g_log, g_bias, beta, scale, qk_norm):
+        lib = ext()
+        gl, gb = g_log.float().contiguous(), g_bias.float().contiguous()
+        out, saved = _chunk_scan_forward(
+            lambda *o: lib.delta_prep_kda_fwd(q, k, v, g_raw, gl, gb, beta, scale, qk_norm, *o), q)
+        ctx.save_for_backward(q, k, v, g_raw, gl, gb, beta, *saved)
+        ctx.meta = (scale, qk_norm, g_log.dtype, g_bias.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        lib = ext()
+        q, k, v, g_raw, gl, gb, beta, *saved = ctx.saved_tensors
+        scale, qk_norm, log_dt, bias_dt = ctx.meta
+        B, T, H, D = q.shape
+        N = (T + 63) // 64
+        w, u0 = saved[0], saved[1]
+        dw, du0, dqt, dkc, daqk, dcarry = _chunk_scan_backward(dout, saved, (B, T, H))
+        dq, dk, dv = (torch.empty(q.shape, device=q.device, dtype=torch.float32) for _ in range(3))
+        dbeta = torch.empty_like(beta)
+        dg_raw = torch.empty_like(g_raw)
+        parts = torch.empty(2, B, N, H, 128, device=q.device, dtype=torch.float32)
+        lib.delta_prep_kda_bwd(q, k, v, g_raw, gl, gb, beta, scale, qk_norm, w, u0, dw, du0, dqt, dkc, daqk, dcarry,
+                               dq, dk, dv, dg_raw, parts[0], parts[1], dbeta)
+        sums = parts.sum((1, 2))
+        return (dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg_raw, sums[0].to(log_dt), sums[1].to(bias_dt),
+                dbeta, None, None)
+
+
+def kda_chunk_cuda(q, k, v, g_raw, g_log, g_bias, beta, *, qk_l2norm_scale=None):
+    """KDA on the fused kernels from the gate's pre-activation (bf16 [B, T, H, 128]) and its per-head,
+    per-feature parameters g_log / g_bias [H, 128]; q / k raw when ``qk_l2norm_scale`` is given (the
+    kernel normalises them: q <- s q / |q|, k <- k / |k|), else already normalised."""
+    norm = qk_l2norm_scale is not None
+    return _KdaChunk.apply(q.contiguous(), k.contiguous(), v.contiguous(), g_raw.contiguous(), g_log, g_bias,
+                           beta.float().contiguous(), float(qk_l2norm_scale) if norm else 1.0, norm)
 
 
 def fused_chunk_supported(q, k, v, chunk):

@@ -88,3 +88,45 @@ def test_gla_chunk_kernels_match_recurrence():
     assert ((y.double() - ref).norm() / ref.norm()) < 1e-2
     for a, r in zip(grads, rgrads):
         assert ((a.double() - r).norm() / r.norm()) < 3e-2
+
+
+@pytest.mark.parametrize("B,T,H,norm", [(2, 256, 2, True), (1, 700, 3, True), (1, 320, 2, False)])
+def test_kda_gate_from_preactivation_matches_fp64(B, T, H, norm):
+    """KDA with the gate formed in the kernel, g = -exp(g_log) softplus(g_raw + g_bias), and the q / k
+    normalisation there too, against the fp64 chunk form of the same expression."""
+    from nexttransformer_b200.models.linear import chunk_scan
+    from nexttransformer_b200.ops._ext import check_errors
+    from nexttransformer_b200.ops.linear_attention import kda_chunk_cuda
+    D = 128
+    g = torch.Generator(device="cuda").manual_seed(T + H)
+    q = torch.randn(B, T, H, D, device="cuda", generator=g)
+    k = torch.randn(B, T, H, D, device="cuda", generator=g)
+    if not norm:
+        q, k = F.normalize(q, dim=-1) * D ** -.5, F.normalize(k, dim=-1)
+    v = torch.randn(B, T, H, D, device="cuda", generator=g)
+    raw = torch.randn(B, T, H, D, device="cuda", generator=g)
+    beta = torch.rand(B, T, H, device="cuda", generator=g)
+    g_log = (torch.randn(H, D, device="cuda", generator=g) * 0.5 - 1.0)
+    g_bias = torch.full((H, D), -3.0, device="cuda") + torch.randn(H, D, device="cuda", generator=g)
+    q, k, v, raw = (t.bfloat16() for t in (q, k, v, raw))
+    leaves = [t.clone().requires_grad_() for t in (q, k, v, raw, g_log, g_bias, beta)]
+    y = kda_chunk_cuda(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], leaves[5], leaves[6],
+                       qk_l2norm_scale=D ** -.5 if norm else None)
+    assert "KdaChunk" in type(y.grad_fn).__name__
+    dy = torch.randn_like(y.float())
+    y.float().backward(dy)
+    torch.cuda.synchronize()
+    check_errors()
+    ref = [t.detach().double().requires_grad_() for t in (q, k, v, raw, g_log, g_bias, beta)]
+    qr, kr = ref[0], ref[1]
+    if norm:
+        qr, kr = F.normalize(qr, dim=-1) * D ** -.5, F.normalize(kr, dim=-1)
+    decay = -ref[4].exp() * F.softplus(ref[3] + ref[5])
+    yr = chunk_scan(qr, kr, ref[2], kind="kda", g=decay, beta=ref[6], chunk=64)
+    yr.backward(dy.double())
+    assert _rel(y, yr) < 1e-2, _rel(y, yr)
+    for name, a, b in zip(("q", "k", "v", "g_raw", "g_log", "g_bias", "beta"), leaves, ref):
+        err = _rel(a.grad, b.grad)
+        assert err < 3e-2, (name, err)
+        worst = (a.grad.double() - b.grad).abs().max().item()
+        assert worst <= 5e-2 * b.grad.abs().max().item(), (name, worst)
