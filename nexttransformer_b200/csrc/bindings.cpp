@@ -15,6 +15,7 @@
 #include "sparse_teacher.h"
 #include "nsa_compress.h"
 #include "msar.h"
+#include "probe_sm100.h"
 #include "residual.h"
 #include "elementwise.h"
 #include "gemm_sm100.h"
@@ -1179,6 +1180,16 @@ std::vector<int64_t> read_errors() {
 
 }  // namespace
 
+// tcgen05 issue-rate probe (microbenchmark): out int64 [ctas, 3]
+void mma_rate(int64_t variant, int64_t groups, const Tensor& out) {
+  check_cuda(out, "out");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.dim() == 2 && out.size(1) == 3, "out: int64 [ctas, 3]");
+  const c10::cuda::CUDAGuard guard(out.device());
+  ok(nt_mma_rate(static_cast<int>(variant), static_cast<int>(groups), static_cast<int>(out.size(0)),
+                 reinterpret_cast<long long*>(out.data_ptr<int64_t>()), stream()),
+     "mma_rate");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nexttransformer_b200 sm_100a kernels";
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM with fused epilogue");
@@ -1234,6 +1245,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("delta_prep_bwd", &delta_prep_bwd, "backward of the per-chunk delta-rule terms");
   m.def("delta_prep_kda_fwd", &delta_prep_kda_fwd, "KDA chunk terms with the gate from its pre-activation");
   m.def("delta_prep_kda_bwd", &delta_prep_kda_bwd, "backward of delta_prep_kda_fwd");
+  m.def("mma_rate", &mma_rate, "tcgen05.mma issue-rate probe");
   m.def("delta_scan_bwd", &delta_scan_bwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);

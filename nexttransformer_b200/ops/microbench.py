@@ -18,7 +18,9 @@ Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, v
   adamw                                                - AdamW over a [rows, 1280] table
   muon                                                 - the Muon chain on 20 matrices [5120, 1280]
   step                                                 - one fused training micro-step (all kernels)
-  attn_bwd_trace                                       - clock stamps of the first backward CTA per pair
+  attn_bwd_trace, attn_fwd_trace                       - clock stamps of the first backward / forward CTA
+  mma_rate                                             - tcgen05.mma issue rate of one thread per SM (probe
+                                                         kernel): rolled vs unrolled k-steps, N 128 / 256, TS
   delta_scan_fwd, delta_scan_bwd                       - chunked delta-rule scan, B*H = rows/4096*12, T 4096
   delta_gdn, delta_kda                                 - the fused chunked delta rule (chunk terms + scan),
                                                          forward + backward, bf16, T 4096, B*H = rows/4096*12
@@ -208,6 +210,33 @@ def attn_fwd_trace(rows):
         out[name] = [[int(x) - base if int(x) else None for x in t[role, it][:width]] for it in range(16)
                      if (t[role, it] > 0).any()]
     return out
+
+
+def mma_rate(groups=4096):
+    """tcgen05 issue rate: per probe variant, SM clocks per MMA of the issue loop and to completion (median
+    over one CTA per SM) and the aggregate TFLOP/s from CUDA events."""
+    from nexttransformer_b200.ops._ext import ext
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    variants = {0: ("rolled loop, run-time descriptors, SS 128x128x16", 128),
+                1: ("unrolled, SS 128x128x16", 128), 2: ("unrolled, SS 128x256x16", 256),
+                3: ("unrolled, TS (A from TMEM) 128x128x16", 128)}
+    res = {}
+    for v, (name, n) in variants.items():
+        out = torch.zeros(sms, 3, dtype=torch.int64, device="cuda")
+        ext().mma_rate(v, groups, out)              # warm-up
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        ext().mma_rate(v, groups, out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        o = out.cpu()
+        mmas = groups * 8
+        res[name] = {"issue_clk_per_mma": float(o[:, 0].median()) / mmas,
+                     "total_clk_per_mma": float(o[:, 1].median()) / mmas, "waits_ok": int(o[:, 2].sum()),
+                     "tflops": sms * mmas * 2 * 128 * n * 16 / (ms * 1e-3) / 1e12}
+    return res
 
 
 def case_delta_fused(kind, rows):
@@ -401,6 +430,9 @@ def main(argv=None):
     byts = None
     if a.case == "attn_bwd_trace":
         print(json.dumps(attn_bwd_trace(a.rows)), flush=True)
+        return
+    if a.case == "mma_rate":
+        print(json.dumps(mma_rate()), flush=True)
         return
     if a.case == "attn_fwd_trace":
         print(json.dumps(attn_fwd_trace(a.rows)), flush=True)
