@@ -5,7 +5,8 @@
         python -m nexttransformer_b200.ops.step_profile METHOD LAYERS MICRO
 
 METHOD is one of ``bench.py``'s method configurations (``gdn_hybrid_swa``, ``kda_hybrid``, ``nsa``,
-``moba``, ``moe``) at LAYERS layers (default 4) and one micro-batch of MICRO rows (default 8).  The
+``moba``, ``moe``) or ``dense`` (the headline shell, d20 by default) at LAYERS layers (default 4) and
+one micro-batch of MICRO rows (default 8).  The
 model is built with ``models.build_model``, its kernel state and a ``training.Trainer``; two updates
 warm up, then one update runs between ``torch.cuda.profiler.start()`` and ``stop()``, so a capture
 with ``--profile-from-start off`` holds exactly one update's launches.
@@ -31,17 +32,26 @@ def main(argv=None):
     from nexttransformer_b200.optim.groups import protocol_groups
     from nexttransformer_b200.optim.muon_adamw import MuonAdamW
     from nexttransformer_b200.training.engine import Trainer
-    raw, _ = bench.METHOD_CONFIGS[method]
-    fields = {k: v for k, v in raw.items() if k != "method"}
-    fields.update(layers=layers)
-    cfg = replace(candidate_config(raw["method"]), **fields)
-    model = build_model(cfg, "cuda", seed=42)
-    if raw["method"] in ("nsa", "moba"):
-        model.set_sparse_backend("kernel")
-    state = model.fused_state()
-    trainer = Trainer(model, MuonAdamW(protocol_groups(model), shadows={p: s for p, s in state.casts}))
-    x = torch.randint(0, cfg.vocab_size, (micro, cfg.sequence_len), device="cuda")
-    y = torch.randint(0, cfg.vocab_size, (micro, cfg.sequence_len), device="cuda")
+    if method == "dense":
+        from nexttransformer_b200.models.shell import ShellConfig, build_shell
+        from nexttransformer_b200.optim.groups import shell_groups
+        model = build_shell(ShellConfig(**dict(bench.MODEL, n_layer=layers)), "cuda", seed=42)
+        state = model.fused_state()
+        trainer = Trainer(model, MuonAdamW(shell_groups(model), shadows={p: s for p, s in state.casts}))
+        vocab, seq = bench.MODEL["vocab_size"], bench.MODEL["sequence_len"]
+    else:
+        raw, _ = bench.METHOD_CONFIGS[method]
+        fields = {k: v for k, v in raw.items() if k != "method"}
+        fields.update(layers=layers)
+        cfg = replace(candidate_config(raw["method"]), **fields)
+        model = build_model(cfg, "cuda", seed=42)
+        if raw["method"] in ("nsa", "moba"):
+            model.set_sparse_backend("kernel")
+        state = model.fused_state()
+        trainer = Trainer(model, MuonAdamW(protocol_groups(model), shadows={p: s for p, s in state.casts}))
+        vocab, seq = cfg.vocab_size, cfg.sequence_len
+    x = torch.randint(0, vocab, (micro, seq), device="cuda")
+    y = torch.randint(0, vocab, (micro, seq), device="cuda")
     for _ in range(2):
         trainer.step_device([x], [y])
     torch.cuda.synchronize()
@@ -49,7 +59,7 @@ def main(argv=None):
     trainer.step_device([x], [y])
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
-    print(f"profiled one update: {method}, {layers} layers, micro-batch {micro} x {cfg.sequence_len}")
+    print(f"profiled one update: {method}, {layers} layers, micro-batch {micro} x {seq}")
 
 
 if __name__ == "__main__":
