@@ -62,9 +62,8 @@ __device__ __forceinline__ void load_vec<float>(const float* p, float (&out)[4])
   out[3] = f.w;
 }
 
-// torch's softplus (beta 1, threshold 20) and the logistic function, for the KDA gate
+// torch's softplus (beta 1, threshold 20), for the KDA gate
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
 __device__ __forceinline__ float sum16(float v) {  // sum over 16 consecutive lanes
   v += __shfl_xor_sync(0xffffffffu, v, 8);
@@ -622,33 +621,61 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
   }
 
   // ---- KDA with the normalisation in this kernel: dQ / dK are gradients of q^ = s q / |q| and
-  // k^ = k / |k|; back through the normalisation with the raw rows re-read from global memory
+  // k^ = k / |k|.  The raw rows come back with 16-byte loads into the KI and A..SY regions (free once
+  // the products and direct terms above are done), then through the normalisation per thread.
   if (GATE == DELTA_FEATURE && a.qk_norm) {
+    __syncthreads();  // every thread is done reading KI, A, K2 and the stage buffers
+    float* sqr = sm + S::KI;
+    float* skr = sm + S::A;  // 64 x LDF floats spill over K2 and SX, both free here
+    {
+      constexpr int VEC = 16 / static_cast<int>(sizeof(TIn));
+      constexpr int LPR = D / VEC, RPP = NT / LPR, PASSES = C / RPP;
+      const int d0 = (tid % LPR) * VEC, i0 = tid / LPR;
+      const int64_t rs = static_cast<int64_t>(a.H) * D;
+      const TIn* qg = reinterpret_cast<const TIn*>(a.q) + (static_cast<int64_t>(b) * a.T * a.H + h) * D;
+      const TIn* kg = reinterpret_cast<const TIn*>(a.k) + (static_cast<int64_t>(b) * a.T * a.H + h) * D;
+      float qv[PASSES][VEC], kv[PASSES][VEC];
+#pragma unroll
+      for (int ps = 0; ps < PASSES; ++ps) {
+        const int t = n * C + i0 + ps * RPP;
+        if (t < a.T) {
+          load_vec<TIn>(qg + t * rs + d0, qv[ps]);
+          load_vec<TIn>(kg + t * rs + d0, kv[ps]);
+        } else {
+#pragma unroll
+          for (int u = 0; u < VEC; ++u) qv[ps][u] = kv[ps][u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int ps = 0; ps < PASSES; ++ps)
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) {
+          sqr[(i0 + ps * RPP) * LDF + d0 + u] = qv[ps][u];
+          skr[(i0 + ps * RPP) * LDF + d0 + u] = kv[ps][u];
+        }
+    }
+    __syncthreads();
     const float s = a.qk_scale;
-    const TIn* qraw = reinterpret_cast<const TIn*>(a.q);
-    const TIn* kraw = reinterpret_cast<const TIn*>(a.k);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = 4 * ti + r;
-      const bool live = n * C + i < a.T;
-      const int64_t o = (tok_base + static_cast<int64_t>(i) * a.H) * D;
       const float nq = sm[S::NQ + i], nk = sm[S::NK + i];
-      float qh[8], kh[8], pq = 0.f, pk = 0.f;
+      float pq = 0.f, pk = 0.f;
 #pragma unroll
       for (int oc = 0; oc < 8; ++oc) {
         const int d = tj + 16 * oc;
-        qh[oc] = live ? s * to_f(qraw[o + d]) / nq : 0.f;
-        kh[oc] = live ? to_f(kraw[o + d]) / nk : 0.f;
-        pq = fmaf(qh[oc], dQ[r][oc], pq);
-        pk = fmaf(kh[oc], dK[r][oc], pk);
+        pq = fmaf(s * sqr[i * LDF + d] / nq, dQ[r][oc], pq);
+        pk = fmaf(skr[i * LDF + d] / nk, dK[r][oc], pk);
       }
       pq = sum16(pq);
       pk = sum16(pk);
       const bool liveq = nq > 1e-12f, livek = nk > 1e-12f;
 #pragma unroll
       for (int oc = 0; oc < 8; ++oc) {
-        dQ[r][oc] = liveq ? (s / nq) * (dQ[r][oc] - qh[oc] * pq / (s * s)) : (s / nq) * dQ[r][oc];
-        dK[r][oc] = livek ? (dK[r][oc] - kh[oc] * pk) / nk : dK[r][oc] / nk;
+        const int d = tj + 16 * oc;
+        const float qh = s * sqr[i * LDF + d] / nq, kh = skr[i * LDF + d] / nk;
+        dQ[r][oc] = liveq ? (s / nq) * (dQ[r][oc] - qh * pq / (s * s)) : (s / nq) * dQ[r][oc];
+        dK[r][oc] = livek ? (dK[r][oc] - kh * pk) / nk : dK[r][oc] / nk;
       }
     }
   }
@@ -715,35 +742,71 @@ __global__ void __launch_bounds__(NT, 1) prep_bwd_kernel(const DeltaPrepArgs a) 
         sLast[(4 * ti + r) * LDF + tj + 16 * oc] = dKI[r][oc];
       }
     __syncthreads();
+    if (a.g_raw) {
+      // the gate's pre-activation tile comes in with 16-byte loads (KI is free: the normalisation
+      // above has read its rows before the reductions' barrier)
+      float* sraw = sm + S::KI;
+      constexpr int LPR = D / 8, RPP = NT / LPR, PASSES = C / RPP;
+      const int d0 = (tid % LPR) * 8, i0 = tid / LPR;
+      float rv[PASSES][8];
+#pragma unroll
+      for (int ps = 0; ps < PASSES; ++ps) {
+        const int t = n * C + i0 + ps * RPP;
+        if (t < a.T) {
+          load_vec<__nv_bfloat16>(a.g_raw + ((static_cast<int64_t>(b) * a.T + t) * a.H + h) * D + d0, rv[ps]);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) rv[ps][u] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int ps = 0; ps < PASSES; ++ps)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sraw[(i0 + ps * RPP) * LDF + d0 + u] = rv[ps][u];
+    }
+    __syncthreads();
     if (tid < D) {
+      // reverse cumulative sum per feature: dg_t = sum_{s >= t} db_s (+ d b_last at the last token)
       const int d = tid;
       float last = 0.f;
       for (int i = 0; i < C; ++i) last += sLast[i * LDF + d];
       last = fmaf(dcar[d], __expf(sb[(C - 1) * LDF + d]), last);
       float acc = 0.f;
-      if (a.g_raw) {
-        // g = -e^{A} softplus(z), z = g_raw + bias:  dz = -dg e^{A} sigmoid(z),  dA = dg g
-        const float ea = expf(a.g_log[h * D + d]), bias = a.g_bias[h * D + d];
-        float pa = 0.f, pb = 0.f;
-        for (int i = C - 1; i >= 0; --i) {
-          acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
-          if (n * C + i < a.T) {
-            const int64_t o = (tok_base + static_cast<int64_t>(i) * a.H) * D + d;
-            const float z = __bfloat162float(a.g_raw[o]) + bias;
-            const float dz = -acc * ea * sigmoid_f(z);
-            a.dg_raw[o] = __float2bfloat16_rn(dz);
-            pb += dz;
-            pa = fmaf(acc, -ea * softplus_f(z), pa);
-          }
-        }
-        const int64_t part = ((static_cast<int64_t>(b) * N + n) * a.H + h) * D + d;
-        a.dg_log_part[part] = pa;
-        a.dg_bias_part[part] = pb;
-      } else {
-        for (int i = C - 1; i >= 0; --i) {
-          acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
-          if (n * C + i < a.T) a.dg[(tok_base + static_cast<int64_t>(i) * a.H) * D + d] = acc;
-        }
+      for (int i = C - 1; i >= 0; --i) {
+        acc += sDBT[i * LDF + d] + (i == C - 1 ? last : 0.f);
+        if (a.g_raw) sDBT[i * LDF + d] = acc;
+        else if (n * C + i < a.T) a.dg[(tok_base + static_cast<int64_t>(i) * a.H) * D + d] = acc;
+      }
+    }
+    if (a.g_raw) {
+      // g = -e^{A} softplus(z), z = g_raw + bias:  dz = -dg e^{A} sigmoid(z),  d A = dg g.  Every
+      // thread takes one feature (tid mod 128) and every other token; the two partial sums of a
+      // feature are added in a fixed order.
+      __syncthreads();
+      const int d = tid & (D - 1), half = tid >> 7;
+      const float ea = expf(a.g_log[h * D + d]), bias = a.g_bias[h * D + d];
+      const float* sraw = sm + S::KI;
+      float pa = 0.f, pb = 0.f;
+      for (int i = half; i < C; i += 2) {
+        if (n * C + i >= a.T) break;
+        const float z = sraw[i * LDF + d] + bias, dg = sDBT[i * LDF + d];
+        const float ez = expf(z);
+        const float sp = z > 20.f ? z : log1pf(ez);
+        const float sg = z > 20.f ? 1.f : ez / (1.f + ez);
+        const float dz = -dg * ea * sg;
+        a.dg_raw[(tok_base + static_cast<int64_t>(i) * a.H) * D + d] = __float2bfloat16_rn(dz);
+        pb += dz;
+        pa = fmaf(dg, -ea * sp, pa);
+      }
+      float* red = sm + S::K;  // sLast is read
+      __syncthreads();
+      red[tid] = pa;
+      red[NT + tid] = pb;
+      __syncthreads();
+      if (tid < D) {
+        const int64_t part = ((static_cast<int64_t>(b) * N + n) * a.H + h) * D + tid;
+        a.dg_log_part[part] = red[tid] + red[tid + D];
+        a.dg_bias_part[part] = red[NT + tid] + red[NT + tid + D];
       }
     }
   }

@@ -11,6 +11,7 @@ sizes, so no flush is needed between launches.  The same command with small ``--
 
 Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, vocab 65536):
   gemm_qkv, gemm_fc, gemm_proj, gemm_wgrad, gemm_head - the GEMM engine with its epilogues
+  gemm_head_ce                                         - the LM head with the soft-capped CE epilogue
   attn_fwd, attn_bwd                                   - flash attention, rows = B*T (T 2048, or --seq)
   sdpa_fwd, sdpa_bwd                                   - the same shape through torch SDPA with one backend
                                                          (--sdpa cudnn | flash | efficient): the library bar
@@ -98,6 +99,16 @@ def case_gemm(kind, rows):
         a, w = _bf16(rows, WIDTH), _bf16(VOCAB, WIDTH)
         out = torch.empty(rows, VOCAB, device="cuda", dtype=torch.bfloat16)
         return (lambda: G.gemm(a, w, out)), 2 * rows * VOCAB * WIDTH
+    if kind == "gemm_head_ce":
+        # the LM head with the soft-capped cross-entropy in its epilogue (the training path)
+        from nexttransformer_b200.ops._ext import ext
+        a, w = _bf16(rows, WIDTH), _bf16(VOCAB, WIDTH).mul_(0.2)
+        out = torch.empty(rows, VOCAB, device="cuda", dtype=torch.bfloat16)
+        tgt = torch.randint(0, VOCAB, (rows,), device="cuda")
+        part = torch.empty(rows, (VOCAB + 127) // 128, device="cuda")
+        ztgt, loss, rscale, rcorr = (torch.empty(rows, device="cuda") for _ in range(4))
+        return (lambda: ext().gemm_ce_fwd(a, w, out, tgt, part, ztgt, loss, rscale, rcorr, VOCAB, 15.0)), \
+            2 * rows * VOCAB * WIDTH
     raise ValueError(kind)
 
 
