@@ -127,24 +127,6 @@ NT_DEVICE float fast_exp2(float x) {
   return y;
 }
 
-// Packed fp32 pairs (sm_100a f32x2 instructions: one issue slot for two lanes' worth of math).
-NT_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-NT_DEVICE float2 add2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-
 // 2^x for a pair on the FMA pipe instead of the MUFU unit, which caps the softmax at 16
 // exponentials per clock per SM.  Range reduction to the nearest integer j (adding 1.5 x 2^23
 // rounds x into the low mantissa bits), then 2^f for f in [-1/2, 1/2] by a cubic fitted here for

@@ -148,6 +148,51 @@ NT_DEVICE void ce_terms(float x, const CeConst& k, float& e, float& g, float& z)
   z = k.cap * fmaf(-2.f, r, 1.f);
 }
 
+NT_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+NT_DEVICE float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// A row chunk of 32 live logits without branches, in packed fp32 pairs: out = bf16 e (1 - t^2),
+// returns the chunk's sum of e.
+NT_DEVICE float ce_chunk32(const uint32_t (&acc)[32], const CeConst& k, uint32_t (&out)[16]) {
+  const float2 kin = make_float2(k.k_in, k.k_in), kout = make_float2(k.k_out, k.k_out);
+  const float2 one = make_float2(1.f, 1.f), four = make_float2(4.f, 4.f);
+  float2 se = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 y = mul2(make_float2(__uint_as_float(acc[2 * i]), __uint_as_float(acc[2 * i + 1])), kin);
+    const float2 big = add2(make_float2(ex2_approx(y.x), ex2_approx(y.y)), one);
+    const float2 r = make_float2(rcp_approx(big.x), rcp_approx(big.y));
+    const float2 w = mul2(r, kout);
+    const float2 ex = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+    se = add2(se, ex);
+    const float2 q = fma2(make_float2(-r.x, -r.y), r, r);  // r (1 - r)
+    const float2 g = mul2(mul2(ex, four), q);
+    out[i] = pack_bf16x2(g.x, g.y);
+  }
+  return se.x + se.y;
+}
+
+// z of the target column when it falls in this chunk (one thread in 2048 chunks per row)
+NT_DEVICE void ce_target(const CeArgs& ce, const CeConst& k, int64_t tgt, int row, int col0, int lim,
+                         const uint32_t (&acc)[32]) {
+  if (tgt < col0 || tgt >= col0 + lim) return;
+  const int j = static_cast<int>(tgt - col0);
+  float x = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x = i == j ? __uint_as_float(acc[i]) : x;
+  float e, g, z;
+  ce_terms(x, k, e, g, z);
+  ce.ztgt[row] = z;
+}
+
 NT_DEVICE float ce_fwd32(const Params& p, int row, int col0, const uint32_t (&acc)[32]) {
   const CeArgs& ce = p.ce;
   const CeConst k = ce_const(ce.cap);
@@ -155,6 +200,11 @@ NT_DEVICE float ce_fwd32(const Params& p, int row, int col0, const uint32_t (&ac
   const int ncols = min(32, p.N - col0);
   float se = 0.f;
   uint32_t out[16];
+  const int lim = min(ncols, ce.vocab - col0);
+  if (lim >= 32) {
+    se = ce_chunk32(acc, k, out);
+    ce_target(ce, k, tgt, row, col0, lim, acc);
+  } else {
 #pragma unroll
   for (int i = 0; i < 32; i += 2) {
     float g[2];
@@ -171,6 +221,7 @@ NT_DEVICE float ce_fwd32(const Params& p, int row, int col0, const uint32_t (&ac
       }
     }
     out[i / 2] = pack_bf16x2(g[0], g[1]);
+  }
   }
   __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + col0;
   if (ncols == 32 && (reinterpret_cast<uintptr_t>(c) & 15) == 0) {
@@ -235,6 +286,12 @@ NT_DEVICE void epi_pack(const Params& p, float sacc, int b, int row, int col0, c
     const CeArgs& ce = p.ce;
     const CeConst k = ce_const(ce.cap);
     const int64_t tgt = live ? ce.tgt[row] : -1;
+    const int lim = min(ncols, ce.vocab - col0);
+    if (lim >= 32) {
+      se += ce_chunk32(acc, k, out);
+      ce_target(ce, k, tgt, row, col0, lim, acc);
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
       float g[2];
