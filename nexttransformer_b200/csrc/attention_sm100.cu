@@ -22,6 +22,7 @@
 
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <stdexcept>
@@ -54,8 +55,9 @@ struct Params {
   const float* delta;
   long long* trace;
   int dq_slices;  // 0: dQ added into one fp32 buffer (bulk reductions); else one slice per key tile
-  int dq_direct;  // 1: the drain adds dQ rows from registers with vector reductions (no shared staging)
+  int dq_direct;  // drain: 0 staged bulk reductions, 1 register reductions only, 2 half and half
   float* dq_base; // dq_acc (row stride H * 128) for the direct drain
+  int order_window;  // CTA order: 0 = (batch, head)-major; W > 0 = longest first within W (batch, head) groups
 };
 
 // Clock stamp of (role, pair, event) for the first CTA when a trace buffer is given.
@@ -116,6 +118,23 @@ NT_DEVICE void for_steps(F&& f) {
 }
 
 // Byte offset of 16-byte chunk `c` (0..15) of row `r` in a two-box 128B-swizzled tile.
+// Work unit of flat block index x for `units` work units per (batch, head) group, `groups` groups,
+// unit 0 the longest.  Window 0: group-major (a group's units run together, so their shared tiles stay
+// in L2).  Window W: longest first within each run of W groups, which keeps long CTAs out of the
+// grid's tail while W groups' tiles share L2.
+NT_DEVICE void work_unit(int x, int units, int groups, int window, int& unit, int& group) {
+  if (window <= 0) {
+    unit = x % units;
+    group = x / units;
+    return;
+  }
+  const int span = window * units;
+  const int w = x / span, local = x - w * span;
+  const int wl = min(window, groups - w * window);
+  unit = local / wl;
+  group = w * window + local % wl;
+}
+
 NT_DEVICE uint32_t swz_off(int r, int c) {
   return (c >> 3) * BOX_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
@@ -213,8 +232,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + TILE - 1) / TILE;
   const int n_pairs = (n_qt + 1) / 2;
-  const int pair = n_pairs - 1 - blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
+  int unit, bh;  // unit 0 = the last (longest) query-tile pair
+  work_unit(static_cast<int>(blockIdx.x), n_pairs, p.H * p.B, p.order_window, unit, bh);
+  const int pair = n_pairs - 1 - unit;
+  const int h = bh % p.H, b = bh / p.H;
   const int hk = h / (p.H / p.Hk);
   const int qtA = 2 * pair, qtB = 2 * pair + 1;
   const bool hasB = qtB < n_qt;
@@ -568,7 +589,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  int kt, bk;  // causal: key tile 0 has the most query tiles
+  work_unit(static_cast<int>(blockIdx.x), (p.T + TILE - 1) / TILE, p.Hk * p.B, p.order_window, kt, bk);
+  const int hk = bk % p.Hk, b = bk / p.Hk;
   const int group = p.H / p.Hk;
   const int k0 = kt * TILE;
   int i_lo, i_hi;
@@ -862,32 +885,39 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(dq_free);  // tDP may take the next dP^T
-      if (p.dq_direct) {
-        // each thread adds its query row from registers: 32 vector reductions of 4 fp32 (plain vector
-        // stores into the key tile's slice in deterministic mode); no shared staging, no bulk copies
+      // columns [4 j0, 4 j1) of this thread's query row added from registers: vector reductions of 4
+      // fp32 (plain vector stores into the key tile's slice in deterministic mode)
+      auto add_direct = [&](int j0, int j1) {
         const int qi = q0 + r;
-        if (qi < p.T) {
-          float* dst = p.dq_base +
-                       ((p.dq_slices ? static_cast<int64_t>(kt) * p.B * p.T : 0) + static_cast<int64_t>(b) * p.T + qi) *
-                           (static_cast<int64_t>(p.H) * HD) + h * HD;
+        if (qi >= p.T) return;
+        float* dst = p.dq_base +
+                     ((p.dq_slices ? static_cast<int64_t>(kt) * p.B * p.T : 0) + static_cast<int64_t>(b) * p.T + qi) *
+                         (static_cast<int64_t>(p.H) * HD) + h * HD;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a0 = __uint_as_float(vq[4 * j]) * p.scale, a1 = __uint_as_float(vq[4 * j + 1]) * p.scale;
-            const float a2 = __uint_as_float(vq[4 * j + 2]) * p.scale, a3 = __uint_as_float(vq[4 * j + 3]) * p.scale;
-            if (p.dq_slices)
-              *reinterpret_cast<float4*>(dst + 4 * j) = make_float4(a0, a1, a2, a3);
-            else
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j), "f"(a0), "f"(a1),
-                           "f"(a2), "f"(a3)
-                           : "memory");
-          }
+        for (int j = 0; j < 32; ++j) {
+          if (j < j0 || j >= j1) continue;
+          const float a0 = __uint_as_float(vq[4 * j]) * p.scale, a1 = __uint_as_float(vq[4 * j + 1]) * p.scale;
+          const float a2 = __uint_as_float(vq[4 * j + 2]) * p.scale, a3 = __uint_as_float(vq[4 * j + 3]) * p.scale;
+          if (p.dq_slices)
+            *reinterpret_cast<float4*>(dst + 4 * j) = make_float4(a0, a1, a2, a3);
+          else
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 4 * j), "f"(a0), "f"(a1),
+                         "f"(a2), "f"(a3)
+                         : "memory");
         }
+      };
+      if (p.dq_direct == 1) {
+        add_direct(0, 32);
         if (leader) stamp(p, 3, it, 2);
         continue;
       }
+      // staged quarters: all four, or (dq_direct 2) the first two while the last two go out directly,
+      // so bulk reductions and register reductions are in flight together
+      const int nst = p.dq_direct == 2 ? 2 : 4;
       bool fine = true;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq) {
+        if (qq >= nst) break;
         const int n = n_q4 + qq;
         const int slot = n & 1;
         uint8_t* stg = sm + BwdSmem::STG + slot * STG_SLOT;
@@ -918,15 +948,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             // the reduction before this one has read its slot: release that slot
             tma_store_wait_read1();
             if (n >= 1) mbar_arrive(&stg_free[(n - 1) & 1]);
-            if (qq == 3) stamp(p, 3, it, 2);
+            if (qq == nst - 1) stamp(p, 3, it, 2);
           } else {
             fine = false;
           }
         }
         __syncwarp();
       }
-      n_q4 += 4;
+      n_q4 += nst;
       if (!fine) break;
+      if (nst < 4) add_direct(8 * nst, 32);
     }
     if (leader) tma_store_wait0();  // every reduction has landed before the CTA retires
     // dV of this key tile (every MMA has completed once the last dq_full fired)
@@ -1064,6 +1095,19 @@ static Params make_params(const AttnArgs& a) {
 
 using namespace nt::attn;
 
+// CTA order: longest first within runs of W (batch, head) groups.  At the benchmark shape (B 32,
+// T 2048, 10 / 5 heads) W = 16 measured 1.66 ms backward / 0.488 ms forward against 1.90 / 0.510 for
+// the plain group-major order (W = 0) and 1.72 / 0.505 for W = 8; a global longest-first order (every
+// group in one run) was slower than both, since concurrent CTAs then share no K / V tiles in L2.
+// NT_ATTN_ORDER overrides W (0: group-major).
+static int order_window() {
+  static const int w = [] {
+    const char* e = std::getenv("NT_ATTN_ORDER");
+    return e ? std::max(0, std::atoi(e)) : 16;
+  }();
+  return w;
+}
+
 static bool supported(const AttnArgs& a) {
   return a.D == HD && a.B > 0 && a.T > 0 && a.H > 0 && a.Hk > 0 && a.H % a.Hk == 0;
 }
@@ -1082,7 +1126,8 @@ int nt_attention_fwd(const AttnArgs& a, cudaStream_t s) {
     return e ? std::atoi(e) : FWD_EMU_DEFAULT;
   }();
   const int n_qt = (a.T + TILE - 1) / TILE;
-  dim3 grid((n_qt + 1) / 2, a.H, a.B);
+  dim3 grid(static_cast<unsigned>((n_qt + 1) / 2) * a.H * a.B);
+  p.order_window = order_window();
   auto launch = [&](auto kern, std::atomic<uint64_t>& set) {
     nt::smem_limit(set, kern, FwdSmem::TOTAL);
     kern<<<grid, FWD_THREADS, FwdSmem::TOTAL, s>>>(tq, tk, tv, to, p);
@@ -1125,7 +1170,7 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   p.delta = a.delta;
   p.trace = a.trace;
   // NT_ATTN_DQ_DIRECT=1: the drain adds dQ with vector reductions from registers instead of staging it
-  // through shared memory for bulk reductions (selectable for measurement)
+  // through shared memory for bulk reductions; 2: half of each row each way (selectable for measurement)
   static const int direct = [] {
     const char* e = std::getenv("NT_ATTN_DQ_DIRECT");
     return e ? std::atoi(e) : 0;
@@ -1134,7 +1179,8 @@ int nt_attention_bwd(const AttnArgs& a, cudaStream_t s) {
   p.dq_base = a.dq_acc;
   static std::atomic<uint64_t> smem_set{0};
   nt::smem_limit(smem_set, attn_bwd_kernel, BwdSmem::TOTAL);
-  dim3 grid((a.T + TILE - 1) / TILE, a.Hk, a.B);
+  p.order_window = order_window();
+  dim3 grid(static_cast<unsigned>((a.T + TILE - 1) / TILE) * a.Hk * a.B);
   attn_bwd_kernel<<<grid, BWD_THREADS, BwdSmem::TOTAL, s>>>(tq, tk, tv, tdo, tdq, p);
   const int cols = a.H * HD;
   const int64_t n = rows * cols;

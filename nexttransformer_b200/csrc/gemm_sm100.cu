@@ -1068,17 +1068,42 @@ static void dispatch_major(const GemmArgs& g, cudaStream_t s) {
 namespace {
 // Split-K pays when an fp32-output problem has a long reduction but too few 128x256 tiles to fill
 // the machine (weight gradients reduce over all tokens).  Returns the slice count (1 = none).
+// The persistent grid gives each CTA ceil(tiles * split / SMs) tiles, so the slice count is picked
+// by a cost model: rounds of tiles x the time of one tile's share of K, plus writing and reading the
+// fp32 partial products (s x M x N x 8 bytes).  Per-SM tensor rate and memory bandwidth are nominal
+// (about 11 TFLOP/s per SM, 6 TB/s); only their ratio matters.
 int choose_split(const GemmArgs& g) {
   if (g.epi != EPI_F32 && g.epi != EPI_F32_ACC) return 1;
   if (g.batch != 1 || g.N < 256 || g.M % 4 || g.N % 4 || g.ldc % 4) return 1;
   const long tiles = static_cast<long>((g.M + 127) / 128) * ((g.N + 255) / 256);
-  const long want = 2L * g.num_sms;
-  if (tiles >= want) return 1;
+  const int sms = g.num_sms > 0 ? g.num_sms : 148;
+  // NT_GEMM_SPLIT_MODEL=0 selects the plain rule (enough slices for two tiles per SM; measurement only)
+  static const bool plain = [] {
+    const char* e = std::getenv("NT_GEMM_SPLIT_MODEL");
+    return e && e[0] == '0';
+  }();
+  if (plain) {
+    if (tiles >= 2L * sms) return 1;
+    const int kb = (g.K + 63) / 64;
+    int split = static_cast<int>((2L * sms + tiles - 1) / tiles);
+    split = split > 16 ? 16 : split;
+    while (split > 1 && kb / split < 16) --split;
+    return split;
+  }
+  if (tiles >= 4L * sms) return 1;
   const int num_kb = (g.K + 63) / 64;
-  int split = static_cast<int>((want + tiles - 1) / tiles);
-  split = split > 16 ? 16 : split;
-  while (split > 1 && num_kb / split < 16) --split;  // keep >= 16 k-blocks per slice
-  return split;
+  const double tile_s = 2.0 * 128 * 256 * static_cast<double>(g.K) / 11e12;
+  const double slice_s = 8.0 * static_cast<double>(g.M) * g.N / 6e12;
+  int best = 1;
+  double best_t = static_cast<double>((tiles + sms - 1) / sms) * tile_s;
+  for (int s = 2; s <= 16 && num_kb / s >= 16; ++s) {  // >= 16 k-blocks per slice
+    const double t = static_cast<double>((tiles * s + sms - 1) / sms) * tile_s / s + s * slice_s;
+    if (t < 0.98 * best_t) {
+      best = s;
+      best_t = t;
+    }
+  }
+  return best;
 }
 }  // namespace
 

@@ -12,6 +12,7 @@ sizes, so no flush is needed between launches.  The same command with small ``--
 Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, vocab 65536):
   gemm_qkv, gemm_fc, gemm_proj, gemm_wgrad, gemm_head - the GEMM engine with its epilogues
   gemm_head_ce                                         - the LM head with the soft-capped CE epilogue
+  gemm_wgrad_qkv, gemm_wgrad_o                         - weight gradients of the QKV / output projections
   attn_fwd, attn_bwd                                   - flash attention, rows = B*T (T 2048, or --seq)
   sdpa_fwd, sdpa_bwd                                   - the same shape through torch SDPA with one backend
                                                          (--sdpa cudnn | flash | efficient): the library bar
@@ -91,10 +92,12 @@ def case_gemm(kind, rows):
         a, w, r = _bf16(rows, FFN), _bf16(WIDTH, FFN), _bf16(rows, WIDTH)
         out = torch.empty(rows, WIDTH, device="cuda", dtype=torch.bfloat16)
         return (lambda: G.gemm(a, w, out, epi=G.EPI_BF16_AXPBY, r=r)), 2 * rows * WIDTH * FFN
-    if kind == "gemm_wgrad":
-        dy, x = _bf16(rows, FFN), _bf16(rows, WIDTH)
-        grad = torch.zeros(FFN, WIDTH, device="cuda")
-        return (lambda: G.wgrad(dy, x, grad, accumulate=True)), 2 * rows * FFN * WIDTH
+    if kind in ("gemm_wgrad", "gemm_wgrad_qkv", "gemm_wgrad_o"):
+        # weight gradients of the MLP up-projection, the QKV projection and the output projection
+        out_f = {"gemm_wgrad": FFN, "gemm_wgrad_qkv": (HEADS + 2 * KV_HEADS) * HEAD_DIM, "gemm_wgrad_o": WIDTH}[kind]
+        dy, x = _bf16(rows, out_f), _bf16(rows, WIDTH)
+        grad = torch.zeros(out_f, WIDTH, device="cuda")
+        return (lambda: G.wgrad(dy, x, grad, accumulate=True)), 2 * rows * out_f * WIDTH
     if kind == "gemm_head":
         a, w = _bf16(rows, WIDTH), _bf16(VOCAB, WIDTH)
         out = torch.empty(rows, VOCAB, device="cuda", dtype=torch.bfloat16)

@@ -70,15 +70,22 @@ def test_matches_allocating_entry_point(lib, T, N, K, accumulate):
 
 
 def _split(M, N, K, sms):
-    """The split-K factor the GEMM launcher picks for an fp32 weight-gradient problem."""
+    """The split-K factor the GEMM launcher picks for an fp32 weight-gradient problem (its cost model:
+    rounds of tiles times one slice's share of K, plus the fp32 partial products written and read)."""
     tiles = -(-M // 128) * -(-N // 256)
-    want = 2 * sms
-    if N < 256 or tiles >= want:
+    if N < 256 or M % 4 or N % 4 or tiles >= 4 * sms:
         return 1
-    split = min(16, -(-want // tiles))
-    while split > 1 and (-(-K // 64)) // split < 16:
-        split -= 1
-    return split
+    num_kb = -(-K // 64)
+    tile_s = 2.0 * 128 * 256 * K / 11e12
+    slice_s = 8.0 * M * N / 6e12
+    best, best_t = 1, -(-tiles // sms) * tile_s
+    s = 2
+    while s <= 16 and num_kb // s >= 16:
+        t = -(-(tiles * s) // sms) * tile_s / s + s * slice_s
+        if t < 0.98 * best_t:
+            best, best_t = s, t
+        s += 1
+    return best
 
 
 def _oversize_shape(sms, cap, K=16384):
