@@ -14,7 +14,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 SOURCES = ["bindings.cpp", "gemm_sm100.cu", "gemm_noalloc.cu", "elementwise.cu", "optim.cu", "attention_sm100.cu",
-           "comm.cu", "linear_attn.cu", "delta_scan.cu", "delta_prep.cu", "moe.cu", "moe_route.cu", "sparse_attn.cu", "sparse_teacher.cu", "nsa_compress.cu", "msar.cu", "residual.cu", "probe_sm100.cu"]
+           "comm.cu", "linear_attn.cu", "delta_scan.cu", "delta_prep.cu", "moe.cu", "moe_route.cu", "sparse_attn.cu", "sparse_teacher.cu", "nsa_compress.cu", "msar.cu", "residual.cu", "probe_sm100.cu", "plugin_ops.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",

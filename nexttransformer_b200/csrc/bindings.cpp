@@ -15,6 +15,7 @@
 #include "sparse_teacher.h"
 #include "nsa_compress.h"
 #include "msar.h"
+#include "plugin_ops.h"
 #include "probe_sm100.h"
 #include "residual.h"
 #include "elementwise.h"
@@ -947,6 +948,65 @@ void conv_silu_bwd(const Tensor& x, const Tensor& pre, const Tensor& dy, const T
      "conv_silu_bwd");
 }
 
+void canon_conv_fwd(const Tensor& x, const Tensor& w, const Tensor& y) {
+  check_rows(x, "x");
+  check_rows(y, "y");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "canon weight must be contiguous fp32 [C, K]");
+  const int B = static_cast<int>(x.size(0)), T = static_cast<int>(x.size(1)), C = static_cast<int>(x.size(2));
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_canon_conv_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), B, T, C, static_cast<int>(w.size(-1)),
+                       stream()),
+     "canon_conv_fwd");
+}
+
+void canon_conv_bwd(const Tensor& x, const Tensor& dy, const Tensor& w, const Tensor& dx, const Tensor& dw) {
+  for (auto* t : {&x, &dy, &dx}) check_rows(*t, "canon operand");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && dw.scalar_type() == at::kFloat, "canon weights are fp32");
+  const int B = static_cast<int>(x.size(0)), T = static_cast<int>(x.size(1)), C = static_cast<int>(x.size(2));
+  const c10::cuda::CUDAGuard guard(x.device());
+  ok(nt_canon_conv_bwd(x.data_ptr(), dy.data_ptr(), w.data_ptr<float>(), dx.data_ptr(), dw.data_ptr<float>(), B, T, C,
+                       static_cast<int>(w.size(-1)), stream()),
+     "canon_conv_bwd");
+}
+
+// gated attention / XSA heads: y [rows, H, 128] bf16; g [rows, H, G]; v [rows, Hk, 128]
+void gate_mul_fwd(const Tensor& y, const Tensor& g, const Tensor& z) {
+  for (auto* t : {&y, &g, &z}) check_rows(*t, "gate operand");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16 && y.dim() == 3 && y.size(2) == 128,
+              "gate_mul: bf16 y [rows, H, 128]");
+  const c10::cuda::CUDAGuard guard(y.device());
+  ok(nt_gate_mul_fwd(y.data_ptr(), g.data_ptr(), z.data_ptr(), y.size(0), static_cast<int>(y.size(1)),
+                     static_cast<int>(g.size(-1)), stream()),
+     "gate_mul_fwd");
+}
+
+void gate_mul_bwd(const Tensor& y, const Tensor& g, const Tensor& dz, const Tensor& dy, const Tensor& dg) {
+  for (auto* t : {&y, &g, &dz, &dy, &dg}) check_rows(*t, "gate operand");
+  const c10::cuda::CUDAGuard guard(y.device());
+  ok(nt_gate_mul_bwd(y.data_ptr(), g.data_ptr(), dz.data_ptr(), dy.data_ptr(), dg.data_ptr(), y.size(0),
+                     static_cast<int>(y.size(1)), static_cast<int>(g.size(-1)), stream()),
+     "gate_mul_bwd");
+}
+
+void xsa_fwd(const Tensor& y, const Tensor& v, const Tensor& z) {
+  for (auto* t : {&y, &v, &z}) check_rows(*t, "xsa operand");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 && y.dim() == 3 && v.dim() == 3 &&
+                  y.size(2) == 128 && v.size(2) == 128 && y.size(0) == v.size(0),
+              "xsa: bf16 y [rows, H, 128], v [rows, Hk, 128]");
+  const c10::cuda::CUDAGuard guard(y.device());
+  ok(nt_xsa_fwd(y.data_ptr(), v.data_ptr(), z.data_ptr(), y.size(0), static_cast<int>(y.size(1)),
+                static_cast<int>(v.size(1)), stream()),
+     "xsa_fwd");
+}
+
+void xsa_bwd(const Tensor& y, const Tensor& v, const Tensor& dz, const Tensor& dy, const Tensor& dv) {
+  for (auto* t : {&y, &v, &dz, &dy, &dv}) check_rows(*t, "xsa operand");
+  const c10::cuda::CUDAGuard guard(y.device());
+  ok(nt_xsa_bwd(y.data_ptr(), v.data_ptr(), dz.data_ptr(), dy.data_ptr(), dv.data_ptr(), y.size(0),
+                static_cast<int>(y.size(1)), static_cast<int>(v.size(1)), stream()),
+     "xsa_bwd");
+}
+
 void gated_rmsnorm_fwd(const Tensor& x, const Tensor& g, const Tensor& gain, const Tensor& y, const Tensor& rstd) {
   for (auto* t : {&x, &g, &y}) check_rows(*t, "gated norm operand");
   const int D = static_cast<int>(gain.numel());
@@ -1248,6 +1308,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mma_rate", &mma_rate, "tcgen05.mma issue-rate probe");
   m.def("delta_scan_bwd", &delta_scan_bwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
+  m.def("canon_conv_fwd", &canon_conv_fwd);
+  m.def("canon_conv_bwd", &canon_conv_bwd);
+  m.def("gate_mul_fwd", &gate_mul_fwd);
+  m.def("gate_mul_bwd", &gate_mul_bwd);
+  m.def("xsa_fwd", &xsa_fwd);
+  m.def("xsa_bwd", &xsa_bwd);
   m.def("gated_rmsnorm_fwd", &gated_rmsnorm_fwd);
   m.def("gated_rmsnorm_bwd", &gated_rmsnorm_bwd);
   m.def("read_comm_errors", &read_comm_errors);

@@ -33,7 +33,8 @@ NT_DEVICE void store8(__nv_bfloat16* p, const float (&v)[8]) {
 NT_DEVICE float silu(float z) { return z / (1.f + __expf(-z)); }
 
 // grid: (ceil(C/8 / 32), ceil(T / TSTEP), B); block 32 threads along channel groups
-template <int K>
+// CANON: y = x + conv(x) (the Canon layer of the AttnRes-Canon plugins) instead of SiLU(conv(x)).
+template <int K, bool CANON = false>
 __global__ void conv_silu_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                                      __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ pre, int T, int C) {
   const int cg = blockIdx.x * blockDim.x + threadIdx.x;
@@ -64,10 +65,10 @@ __global__ void conv_silu_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
 #pragma unroll
       for (int i = 0; i < K - 1; ++i) s += wk[j][i] * hist[i][j];
       z[j] = s;
-      o[j] = silu(s);
+      o[j] = CANON ? cur[j] + s : silu(s);
     }
     store8(y + row, o);
-    if (pre) store8(pre + row, z);
+    if (!CANON && pre) store8(pre + row, z);
 #pragma unroll
     for (int i = 0; i < K - 2; ++i)
 #pragma unroll
@@ -78,7 +79,7 @@ __global__ void conv_silu_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
 }
 
 // dz = dy * SiLU'(z);  dx[t] = sum_i w[i] dz[t + K - 1 - i];  dw partial sums per block (fp32 atomics)
-template <int K>
+template <int K, bool CANON = false>
 __global__ void conv_silu_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ pre,
                                      const __nv_bfloat16* __restrict__ dy, const float* __restrict__ w,
                                      __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int T, int C) {
@@ -102,8 +103,14 @@ __global__ void conv_silu_bwd_kernel(const __nv_bfloat16* __restrict__ x, const 
       return;
     }
     const int64_t row = (static_cast<int64_t>(b) * T + t) * C + c0;
-    float g[8], z[8];
+    float g[8];
     load8(dy + row, g);
+    if (CANON) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = g[j];
+      return;
+    }
+    float z[8];
     load8(pre + row, z);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -120,7 +127,7 @@ __global__ void conv_silu_bwd_kernel(const __nv_bfloat16* __restrict__ x, const 
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float s = 0.f;
+      float s = CANON ? fut[0][j] : 0.f;  // the residual path of the Canon layer
 #pragma unroll
       for (int i = 0; i < K; ++i) s += wk[j][K - 1 - i] * fut[i][j];
       o[j] = s;
@@ -234,24 +241,25 @@ __global__ void gated_rmsnorm_dgain_kernel(const float* __restrict__ part, float
 
 using namespace nt::lin;
 
-int nt_causal_conv_silu_fwd(const void* x, const float* w, void* y, void* pre, int B, int T, int C, int K,
-                            cudaStream_t s) {
-  if (C % 8 || K < 2 || K > KMAX) return -1;
+template <bool CANON>
+static int conv_fwd(const void* x, const float* w, void* y, void* pre, int B, int T, int C, int K, cudaStream_t s) {
+  if (C % 8 || K < 2 || K > 4) return -1;
   dim3 grid((C / 8 + 31) / 32, (T + TSTEP - 1) / TSTEP, B);
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto Y = static_cast<__nv_bfloat16*>(y);
   auto P = static_cast<__nv_bfloat16*>(pre);
   switch (K) {
-    case 2: conv_silu_fwd_kernel<2><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
-    case 3: conv_silu_fwd_kernel<3><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
-    case 4: conv_silu_fwd_kernel<4><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
+    case 2: conv_silu_fwd_kernel<2, CANON><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
+    case 3: conv_silu_fwd_kernel<3, CANON><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
+    case 4: conv_silu_fwd_kernel<4, CANON><<<grid, 32, 0, s>>>(X, w, Y, P, T, C); break;
     default: return -1;
   }
   return 0;
 }
 
-int nt_causal_conv_silu_bwd(const void* x, const void* pre, const void* dy, const float* w, void* dx, float* dw,
-                            int B, int T, int C, int K, cudaStream_t s) {
+template <bool CANON>
+static int conv_bwd(const void* x, const void* pre, const void* dy, const float* w, void* dx, float* dw, int B, int T,
+                    int C, int K, cudaStream_t s) {
   if (C % 8 || K < 2 || K > 4) return -1;
   dim3 grid((C / 8 + 31) / 32, (T + TSTEP - 1) / TSTEP, B);
   auto X = static_cast<const __nv_bfloat16*>(x);
@@ -259,12 +267,31 @@ int nt_causal_conv_silu_bwd(const void* x, const void* pre, const void* dy, cons
   auto DY = static_cast<const __nv_bfloat16*>(dy);
   auto DX = static_cast<__nv_bfloat16*>(dx);
   switch (K) {
-    case 2: conv_silu_bwd_kernel<2><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
-    case 3: conv_silu_bwd_kernel<3><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
-    case 4: conv_silu_bwd_kernel<4><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
+    case 2: conv_silu_bwd_kernel<2, CANON><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
+    case 3: conv_silu_bwd_kernel<3, CANON><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
+    case 4: conv_silu_bwd_kernel<4, CANON><<<grid, 32, 0, s>>>(X, P, DY, w, DX, dw, T, C); break;
     default: return -1;
   }
   return 0;
+}
+
+int nt_causal_conv_silu_fwd(const void* x, const float* w, void* y, void* pre, int B, int T, int C, int K,
+                            cudaStream_t s) {
+  return conv_fwd<false>(x, w, y, pre, B, T, C, K, s);
+}
+
+int nt_causal_conv_silu_bwd(const void* x, const void* pre, const void* dy, const float* w, void* dx, float* dw,
+                            int B, int T, int C, int K, cudaStream_t s) {
+  return conv_bwd<false>(x, pre, dy, w, dx, dw, B, T, C, K, s);
+}
+
+int nt_canon_conv_fwd(const void* x, const float* w, void* y, int B, int T, int C, int K, cudaStream_t s) {
+  return conv_fwd<true>(x, w, y, nullptr, B, T, C, K, s);
+}
+
+int nt_canon_conv_bwd(const void* x, const void* dy, const float* w, void* dx, float* dw, int B, int T, int C, int K,
+                      cudaStream_t s) {
+  return conv_bwd<true>(x, nullptr, dy, w, dx, dw, B, T, C, K, s);
 }
 
 int nt_gated_rmsnorm_fwd(const void* x, const void* g, const float* gain, void* y, float* rstd, int64_t rows, int D,

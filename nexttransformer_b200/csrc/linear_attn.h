@@ -10,6 +10,10 @@ int nt_causal_conv_silu_fwd(const void* x, const float* w, void* y, void* pre, i
 // dw (fp32 [C, K]) is accumulated into (zero it first).
 int nt_causal_conv_silu_bwd(const void* x, const void* pre, const void* dy, const float* w, void* dx, float* dw,
                             int B, int T, int C, int K, cudaStream_t s);
+// Canon layer: y = x + causal depthwise conv(x) (no activation); dw accumulated as above.
+int nt_canon_conv_fwd(const void* x, const float* w, void* y, int B, int T, int C, int K, cudaStream_t s);
+int nt_canon_conv_bwd(const void* x, const void* dy, const float* w, void* dx, float* dw, int B, int T, int C, int K,
+                      cudaStream_t s);
 // rows of D (64 or 128) channels; gain fp32 [D]; rstd fp32 [rows] saved for the backward.
 int nt_gated_rmsnorm_fwd(const void* x, const void* g, const float* gain, void* y, float* rstd, int64_t rows, int D,
                          cudaStream_t s);

@@ -21,6 +21,7 @@ import torch.nn.functional as F
 
 from nexttransformer_b200.models.lm import LanguageModel, shell_config
 from nexttransformer_b200.models.shell import MLP, CausalSelfAttention
+from nexttransformer_b200.ops import plugins as plugin_ops
 
 
 class Canon(nn.Module):
@@ -32,6 +33,8 @@ class Canon(nn.Module):
         self.weight = nn.Parameter(torch.empty(width, 1, size))
 
     def forward(self, x):
+        if plugin_ops.supported(x, head=False) and x.shape[-1] % 8 == 0 and self.size <= 4:
+            return plugin_ops.canon(x, self.weight)  # one kernel each way, fp32 taps
         channels_first = F.pad(x.transpose(1, 2), (self.size - 1, 0))
         return x + F.conv1d(channels_first, self.weight.to(x.dtype), groups=x.shape[-1]).transpose(1, 2)
 

@@ -11,6 +11,7 @@ import torch
 from torch import nn
 
 from nexttransformer_b200.models import shell
+from nexttransformer_b200.ops import plugins as plugin_ops
 from nexttransformer_b200.models.shell import CausalSelfAttention, Linear
 
 GRANULARITY = ("elementwise", "headwise")
@@ -29,8 +30,10 @@ class GatedAttention(CausalSelfAttention):
         B, T, _ = x.shape
         q, k, v = self.project(x, ve, cos_sin)
         y = shell.sdpa(q, k, v, window_size[0])
-        gate = torch.sigmoid(self.output_gate(x)).view(B, T, self.n_head, self.gate_channels)
-        return self.c_proj((y * gate).reshape(B, T, -1))
+        pre = self.output_gate(x).view(B, T, self.n_head, self.gate_channels)
+        if plugin_ops.supported(y, pre):
+            return self.c_proj(plugin_ops.gate_mul(y, pre).reshape(B, T, -1))  # one kernel each way
+        return self.c_proj((y * torch.sigmoid(pre)).reshape(B, T, -1))
 
 
 def mixer(config, layer):

@@ -8,6 +8,7 @@ import torch
 import torch.nn.functional as F
 
 from nexttransformer_b200.models import shell
+from nexttransformer_b200.ops import plugins as plugin_ops
 from nexttransformer_b200.models.shell import CausalSelfAttention
 
 
@@ -26,6 +27,9 @@ class ExclusiveSelfAttention(CausalSelfAttention):
         B, T, _ = x.shape
         q, k, v = self.project(x, ve, cos_sin)
         y = shell.sdpa(q, k, v, window_size[0])
+        if plugin_ops.supported(y, v):
+            # one kernel each way; the KV head of each query head is read in place (no repeat)
+            return self.c_proj(plugin_ops.exclusive_projection(y, v).reshape(B, T, -1))
         if self.n_head != self.n_kv_head:
             v = v.repeat_interleave(self.n_head // self.n_kv_head, dim=2)
         return self.c_proj(exclusive_projection(y, v).reshape(B, T, -1))

@@ -17,6 +17,7 @@ Cases (shapes of the benchmark model: width 1280, 10/5 heads of 128, FFN 5120, v
   sdpa_fwd, sdpa_bwd                                   - the same shape through torch SDPA with one backend
                                                          (--sdpa cudnn | flash | efficient): the library bar
   ce                                                   - soft-capped cross-entropy over 65536 logits
+  mix_norm_fwd/bwd, rope_norm_fwd/bwd                  - the shell's row kernels (bytes they must move)
   adamw                                                - AdamW over a [rows, 1280] table
   muon                                                 - the Muon chain on 20 matrices [5120, 1280]
   step                                                 - one fused training micro-step (all kernels)
@@ -385,6 +386,41 @@ def case_ce(rows):
     return run, None, 3 * logits.numel() * 2
 
 
+def case_norm(kind, rows):
+    """The shell's memory-bound row kernels on [rows, 1280] / the QKV rows (bytes: what each must move)."""
+    from nexttransformer_b200.ops._ext import ext
+    if kind == "mix_norm_fwd":
+        x, x0 = _bf16(rows, WIDTH), _bf16(rows, WIDTH)
+        ab = torch.tensor([0.9, 0.1], device="cuda")
+        xm, h = torch.empty_like(x), torch.empty_like(x)
+        return (lambda: ext().mix_norm_fwd(x, x0, ab, xm, h, None, 1.0)), None, 4 * x.numel() * 2
+    if kind == "mix_norm_bwd":
+        x, x0, xm, dh, dres = (_bf16(rows, WIDTH) for _ in range(5))
+        ab = torch.tensor([0.9, 0.1], device="cuda")
+        dx = torch.empty_like(x)
+        dx0 = torch.zeros(rows, WIDTH, device="cuda")
+        part = torch.empty(rows, 2, device="cuda")
+        # reads x, x0, xm, dh, dres (bf16) and dx0 (fp32), writes dx (bf16) and dx0 (fp32)
+        return (lambda: ext().mix_norm_bwd(x, x0, xm, dh, dres, ab, dx, dx0, part)), None, \
+            x.numel() * (6 * 2 + 2 * 4)
+    if kind in ("rope_norm_fwd", "rope_norm_bwd"):
+        cols = (HEADS + 2 * KV_HEADS) * HEAD_DIM
+        qkv = _bf16(rows, cols)
+        ang = torch.arange(SEQ, device="cuda")[:, None] * torch.rand(HEAD_DIM // 2, device="cuda")[None]
+        cosb, sinb = ang.cos().bfloat16().contiguous(), ang.sin().bfloat16().contiguous()
+        rstd = torch.empty(rows * (HEADS + KV_HEADS), device="cuda")
+        ext().rope_norm_fwd(qkv, cosb, sinb, rstd, SEQ, HEADS, KV_HEADS, HEAD_DIM, 1.2, None, None, None, None, None)
+        qk = rows * (HEADS + KV_HEADS) * HEAD_DIM
+        if kind == "rope_norm_fwd":
+            # q / k rows read and written in place (v untouched without value embeddings)
+            return (lambda: ext().rope_norm_fwd(qkv, cosb, sinb, rstd, SEQ, HEADS, KV_HEADS, HEAD_DIM, 1.2, None, None,
+                                                None, None, None)), None, 2 * qk * 2
+        dqkv = _bf16(rows, cols)
+        return (lambda: ext().rope_norm_bwd(dqkv, qkv, cosb, sinb, rstd, SEQ, HEADS, KV_HEADS, HEAD_DIM, 1.2, None,
+                                            None, None, None, None)), None, 3 * qk * 2
+    raise ValueError(kind)
+
+
 def case_adamw(rows):
     from nexttransformer_b200.ops._ext import ext
     p = torch.randn(rows, WIDTH, device="cuda")
@@ -469,6 +505,8 @@ def main(argv=None):
         fn, flops, byts = case_sinkhorn(a.rows)
     elif a.case == "ce":
         fn, flops, byts = case_ce(a.rows)
+    elif a.case in ("mix_norm_fwd", "mix_norm_bwd", "rope_norm_fwd", "rope_norm_bwd"):
+        fn, flops, byts = case_norm(a.case, a.rows)
     elif a.case == "adamw":
         fn, flops, byts = case_adamw(a.rows)
     elif a.case == "muon":
