@@ -16,6 +16,8 @@
 #include "common.cuh"
 #include "elementwise.h"
 
+#include <cstdlib>
+
 namespace nt {
 namespace ew {
 
@@ -228,14 +230,14 @@ __global__ void rope_norm_fwd_kernel(__nv_bfloat16* __restrict__ qkv, const __nv
                                      int H, int Hk, float scale, const __nv_bfloat16* __restrict__ ve_table,
                                      const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ hrow,
                                      int ldh, const __nv_bfloat16* __restrict__ wg, int G,
-                                     float* __restrict__ gate_out) {
+                                     float* __restrict__ gate_out, int head0) {
   constexpr int D = P * 64;
-  const int nheads = H + 2 * Hk;
+  const int nheads = H + 2 * Hk, nsub = nheads - head0;  // heads [head0, nheads) of every row
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (gw >= static_cast<int64_t>(M) * nheads) return;
-  const int row = static_cast<int>(gw / nheads);
-  const int head = static_cast<int>(gw - static_cast<int64_t>(row) * nheads);
+  if (gw >= static_cast<int64_t>(M) * nsub) return;
+  const int row = static_cast<int>(gw / nsub);
+  const int head = head0 + static_cast<int>(gw - static_cast<int64_t>(row) * nsub);
   const int ld = nheads * D;
   __nv_bfloat16* base = qkv + static_cast<int64_t>(row) * ld + head * D;
   if (head < H + Hk) {
@@ -303,14 +305,14 @@ __global__ void rope_norm_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __n
                                      const float* __restrict__ rstd, int M, int T, int H, int Hk, float scale,
                                      const __nv_bfloat16* __restrict__ ve_table, const int64_t* __restrict__ idx,
                                      const float* __restrict__ gate_in, float* __restrict__ dz,
-                                     float* __restrict__ ve_grad) {
+                                     float* __restrict__ ve_grad, int head0) {
   constexpr int D = P * 64;
-  const int nheads = H + 2 * Hk;
+  const int nheads = H + 2 * Hk, nsub = nheads - head0;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (gw >= static_cast<int64_t>(M) * nheads) return;
-  const int row = static_cast<int>(gw / nheads);
-  const int head = static_cast<int>(gw - static_cast<int64_t>(row) * nheads);
+  if (gw >= static_cast<int64_t>(M) * nsub) return;
+  const int row = static_cast<int>(gw / nsub);
+  const int head = head0 + static_cast<int>(gw - static_cast<int64_t>(row) * nsub);
   const int ld = nheads * D;
   const int64_t o = static_cast<int64_t>(row) * ld + head * D;
   if (head < H + Hk) {
@@ -362,6 +364,77 @@ __global__ void rope_norm_bwd_kernel(__nv_bfloat16* __restrict__ dqkv, const __n
     dg = warp_sum(dg);
     // gate = 3 sigmoid(z): dgate/dz = gate * (1 - gate / 3)
     if (lane == 0) dz[static_cast<int64_t>(row) * Hk + hk] = dg * gate * (1.f - gate / 3.f);
+  }
+}
+
+// rope_norm backward for heads of 128 with 16 lanes each (two half-warps per warp, U heads per
+// half-warp, every load issued before the math) and 16-byte accesses: lane l of a head holds elements
+// [8 l, 8 l + 8), so lanes l and l ^ 8 hold the two halves of the same rotation pairs and swap them with
+// one shuffle.  Same arithmetic as rope_norm_bwd_kernel; q / k heads only (value heads take the
+// per-warp kernel when value embeddings are mixed in).  The same layout for the forward measured no
+// faster than the per-warp forward (0.257 vs 0.252 ms at 65536 rows), which stays.
+// Backward in place on dqkv (q / k heads): undo the scale and the norm, then the rotation with the
+// partner lane's half: dx1 = d1 c - d2 s, dx2 = d1 s + d2 c.
+template <int U>
+__global__ void rope_norm_bwd_wide_kernel(__nv_bfloat16* __restrict__ dqkv, const __nv_bfloat16* __restrict__ qkv,
+                                          const __nv_bfloat16* __restrict__ cosb,
+                                          const __nv_bfloat16* __restrict__ sinb, const float* __restrict__ rstd,
+                                          int M, int T, int H, int Hk, float scale) {
+  constexpr int D = 128;
+  const int nqk = H + Hk, ld = (H + 2 * Hk) * D;
+  const int lane = threadIdx.x & 31, hl = lane & 15, sub = lane >> 4;
+  const int units = M * nqk;
+  const int g0 = ((blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + sub) * U;
+  if (g0 >= units) return;
+  const unsigned mask = 0xFFFFu << (16 * sub);
+  const int k = 8 * (hl & 7);
+  const bool first = hl < 8;
+  uint4 nraw[U], graw[U];
+  int row[U], head[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int gu = min(g0 + u, units - 1);
+    row[u] = gu / nqk;
+    head[u] = gu - row[u] * nqk;
+    const int64_t o = static_cast<int64_t>(row[u]) * ld + head[u] * D + 8 * hl;
+    nraw[u] = *reinterpret_cast<const uint4*>(qkv + o);
+    graw[u] = *reinterpret_cast<const uint4*>(dqkv + o);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (g0 + u >= units) break;
+    auto unpack = [](const uint4& q, float (&v)[8]) {
+      const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), cc = unpack_bf16x2(q.z), d = unpack_bf16x2(q.w);
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = cc.x; v[5] = cc.y; v[6] = d.x; v[7] = d.y;
+    };
+    float n[8], g[8], c[8], sn[8];
+    unpack(nraw[u], n);
+    unpack(graw[u], g);
+    const int t = row[u] % T;
+    load8(cosb + static_cast<int64_t>(t) * (D / 2) + k, c);
+    load8(sinb + static_cast<int64_t>(t) * (D / 2) + k, sn);
+    const float r = rstd[static_cast<int64_t>(row[u]) * nqk + head[u]];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      n[j] /= scale;
+      g[j] *= scale;
+      dot += g[j] * n[j];
+    }
+#pragma unroll
+    for (int of = 8; of > 0; of >>= 1) dot += __shfl_xor_sync(mask, dot, of);
+    dot /= D;
+    float d[8], dp[8], out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = r * (g[j] - n[j] * dot);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dp[j] = __shfl_xor_sync(mask, d[j], 8);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d1 = first ? d[j] : dp[j], d2 = first ? dp[j] : d[j];
+      out[j] = first ? d1 * c[j] - d2 * sn[j] : d1 * sn[j] + d2 * c[j];
+    }
+    store8(dqkv + static_cast<int64_t>(row[u]) * ld + head[u] * D + 8 * hl, out);
   }
 }
 
@@ -610,16 +683,17 @@ int nt_mix_norm_bwd(const void* x, const void* x0, const void* xm, const void* d
 int nt_rope_norm_fwd(void* qkv, const void* cosb, const void* sinb, float* rstd, int M, int T, int H, int Hk, int D,
                      float scale, const void* ve_table, const int64_t* idx, const void* hrow, int ldh,
                      const void* wg, int G, float* gate_out, cudaStream_t s) {
-  const int64_t warps = static_cast<int64_t>(M) * (H + 2 * Hk);
   const int wpb = 8;
-  const unsigned blocks = static_cast<unsigned>((warps + wpb - 1) / wpb);
   if (G > 32) return -1;
+  const int head0 = 0;
+  const int64_t warps = static_cast<int64_t>(M) * (H + 2 * Hk - head0);
+  const unsigned blocks = static_cast<unsigned>((warps + wpb - 1) / wpb);
 #define NT_RN(P)                                                                                                 \
   rope_norm_fwd_kernel<P><<<blocks, wpb * 32, 0, s>>>((__nv_bfloat16*)qkv, (const __nv_bfloat16*)cosb,          \
                                                       (const __nv_bfloat16*)sinb, rstd, M, T, H, Hk, scale,     \
                                                       (const __nv_bfloat16*)ve_table, idx,                      \
                                                       (const __nv_bfloat16*)hrow, ldh, (const __nv_bfloat16*)wg, \
-                                                      G, gate_out)
+                                                      G, gate_out, head0)
   switch (D) {
     case 64: NT_RN(1); break;
     case 128: NT_RN(2); break;
@@ -633,14 +707,25 @@ int nt_rope_norm_fwd(void* qkv, const void* cosb, const void* sinb, float* rstd,
 int nt_rope_norm_bwd(void* dqkv, const void* qkv, const void* cosb, const void* sinb, const float* rstd, int M,
                      int T, int H, int Hk, int D, float scale, const void* ve_table, const int64_t* idx,
                      const float* gate, float* dz, float* ve_grad, cudaStream_t s) {
-  const int64_t warps = static_cast<int64_t>(M) * (H + 2 * Hk);
   const int wpb = 8;
+  // heads of 128: q / k heads by the wide kernel, value heads (only with value embeddings) per warp
+  int head0 = 0;
+  constexpr int U = 2;
+  if (D == 128 && static_cast<int64_t>(M) * (H + Hk) < (int64_t(1) << 30)) {
+    const int64_t halves = (static_cast<int64_t>(M) * (H + Hk) + U - 1) / U;
+    rope_norm_bwd_wide_kernel<U><<<static_cast<unsigned>((halves + 2 * wpb - 1) / (2 * wpb)), wpb * 32, 0, s>>>(
+        (__nv_bfloat16*)dqkv, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)cosb, (const __nv_bfloat16*)sinb, rstd,
+        M, T, H, Hk, scale);
+    if (!ve_table) return 0;
+    head0 = H + Hk;
+  }
+  const int64_t warps = static_cast<int64_t>(M) * (H + 2 * Hk - head0);
   const unsigned blocks = static_cast<unsigned>((warps + wpb - 1) / wpb);
 #define NT_RNB(P)                                                                                                  \
   rope_norm_bwd_kernel<P><<<blocks, wpb * 32, 0, s>>>((__nv_bfloat16*)dqkv, (const __nv_bfloat16*)qkv,            \
                                                       (const __nv_bfloat16*)cosb, (const __nv_bfloat16*)sinb,     \
                                                       rstd, M, T, H, Hk, scale, (const __nv_bfloat16*)ve_table,   \
-                                                      idx, gate, dz, ve_grad)
+                                                      idx, gate, dz, ve_grad, head0)
   switch (D) {
     case 64: NT_RNB(1); break;
     case 128: NT_RNB(2); break;

@@ -23,11 +23,17 @@ from nexttransformer_b200.models.native.conditioning import LoopConditioner
 from nexttransformer_b200.models.native.depth import depth_reference
 from nexttransformer_b200.models.native.halter import DeltaDepthHalter
 from nexttransformer_b200.models.shell import GPTShell, ShellConfig, apply_rotary_emb, norm
+from nexttransformer_b200.models import shell
 from nexttransformer_b200.utils.dtype import COMPUTE_DTYPE
 
 
 def uses_value_embeddings(config):
     return getattr(config, "value_embeddings", True)
+
+
+def _causal_route(x, w, n):
+    """Compacted attention through the causal kernel: on CUDA when the window covers the sequence."""
+    return x.is_cuda and w[0] >= n - 1
 
 
 def window(config, virtual):
@@ -177,10 +183,16 @@ class NativeExperiment(SparseCircleMixin, GPTShell):
         cos, sin = self.cos[0, pos], self.sin[0, pos]
         q = norm(apply_rotary_emb(q, cos, sin)) * 1.2
         k = norm(apply_rotary_emb(k, cos, sin)) * 1.2
-        lag = pos[:, :, None] - pos[:, None, :]
-        visible = (lag >= 0) & (lag <= w[0]) & valid[:, :, None] & valid[:, None, :]
-        y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                           attn_mask=visible[:, None]).transpose(1, 2).reshape(b, width, d)
+        if _causal_route(x, w, n):
+            # full window: rows are sorted by position and padding rows follow every valid row, so the
+            # mask below is plain causal in the compacted order for every valid query; the causal
+            # attention kernel takes it (padding queries' outputs are discarded by `valid`)
+            y = shell.sdpa(q, k, v, -1).reshape(b, width, d)
+        else:
+            lag = pos[:, :, None] - pos[:, None, :]
+            visible = (lag >= 0) & (lag <= w[0]) & valid[:, :, None] & valid[:, None, :]
+            y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               attn_mask=visible[:, None]).transpose(1, 2).reshape(b, width, d)
         out = mixed + a.c_proj(y)
         out = out + blk.mlp(norm(out))
         update = (out - x.gather(1, rows)) * valid[:, :, None].to(x.dtype)
