@@ -219,9 +219,11 @@ def test_muon_kernels_match_reference(shape):
                    0.02 * max(1.0, m / n) ** 0.5, 0.1, 0.9, 5)
     upd = torch.stack([p.detach() for p in ps]) - torch.stack(ref)
     rupd = stack - torch.stack(ref)
-    cos = F.cosine_similarity(upd.flatten(), rupd.flatten(), dim=0).item()
-    assert cos > 0.99, cos
-    assert abs(upd.norm().item() / rupd.norm().item() - 1) < 0.05
+    # the kernels run Newton-Schulz in bf16 against the fp32 reference: about 4 % in norm and 6 % of the
+    # largest entry on these shapes
+    rel = ((upd - rupd).norm() / rupd.norm()).item()
+    worst = ((upd - rupd).abs().max() / rupd.abs().max()).item()
+    assert rel < 0.08 and worst < 0.12, (rel, worst)
 
 
 def test_fused_model_matches_eager():
@@ -249,14 +251,20 @@ def test_fused_model_matches_eager():
     loss_f = model(idx, tgt)
     loss_f.backward()
     torch.cuda.synchronize()
-    assert abs(loss_f.item() - loss_e.item()) < 2e-2 * abs(loss_e.item())
+    # same bf16 math in a different kernel order: the losses agree to about 1e-7 and the weight gradients
+    # to about 1 % in norm; the few scalars (residual / smear lambdas) sum many bf16 terms
+    assert abs(loss_f.item() - loss_e.item()) < 1e-3 * abs(loss_e.item())
     for n, p in model.named_parameters():
-        g = p.main_grad
+        g = p.main_grad.float()
         e = eager[n]
         if e.abs().max() == 0:
             continue
-        cos = F.cosine_similarity(g.flatten().float(), e.flatten(), dim=0).item()
-        assert cos > 0.97, (n, cos)
+        rel = ((g - e).norm() / e.norm()).item()
+        if e.numel() > 64:
+            worst = ((g - e).abs().max() / e.abs().max()).item()
+            assert rel < 0.03 and worst < 0.1, (n, rel, worst)
+        else:
+            assert rel < 0.3, (n, rel)
 
 
 @pytest.mark.parametrize("M,V,d", [(512, 4096, 256), (1000, 8192 + 64, 128), (256, 65536, 1280)])
