@@ -412,6 +412,10 @@ class LinearMixer(nn.Module):
             # the same recurrence in the chunk form on the scan kernels (log decay, not its exp)
             from nexttransformer_b200.ops.linear_attention import gla_chunk_cuda
             y = gla_chunk_cuda(q, k, v, F.logsigmoid(gate.float()) / 16)
+        elif self.kind == "retnet" and x.is_cuda and _gla_kernel_ok(q, v):
+            # the retention recurrence in the chunk form on the scan kernels (per-head log decay)
+            from nexttransformer_b200.ops.linear_attention import scalar_chunk_cuda
+            y = scalar_chunk_cuda(q, k, v, gamma.log()[None, None].expand(B, T, -1), 64)
         else:
             y, _ = recurrent_scan(q, k, v, kind=self.kind, decay=decay, beta=beta)
         gated = self.kind in ("gdn", "kda") and chunked and y.is_cuda

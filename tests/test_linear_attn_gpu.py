@@ -110,3 +110,30 @@ def test_retnet_chunk_scan_matches_fp32(T):
     assert _rel(y, yr) < 2e-2
     for a, b in zip(leaves, ref):
         assert _rel(a.grad, b.grad) < 5e-2
+
+
+@pytest.mark.parametrize("method", ["retnet", "gla"])
+def test_scan_kernel_mixers_match_recurrence(method, monkeypatch):
+    """RetNet and GLA models on CUDA: the chunk form on the scan kernels against the token recurrence
+    of the same mixer (both bf16 activations), loss and every gradient."""
+    import nexttransformer_b200.models.linear as L
+    from nexttransformer_b200.models.config import debug_config
+    from nexttransformer_b200.models.lm import build_model
+    cfg = debug_config(method, width=256, sequence_len=128)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randint(0, cfg.vocab_size, (2, cfg.sequence_len), device="cuda", generator=g)
+    y = torch.randint(0, cfg.vocab_size, (2, cfg.sequence_len), device="cuda", generator=g)
+    res = []
+    for kernels in (True, False):
+        if not kernels:
+            monkeypatch.setattr(L, "_gla_kernel_ok", lambda q, v: False)
+        model = build_model(cfg, "cuda", seed=5)
+        loss = model(x, y)
+        loss.backward()
+        res.append((loss.detach().float(), {n: p.grad.float().clone() for n, p in model.named_parameters()
+                                             if p.grad is not None}))
+    (l1, g1), (l2, g2) = res
+    assert abs(l1.item() - l2.item()) <= 1e-2 * abs(l2.item()), (l1.item(), l2.item())
+    for n in g2:
+        if g2[n].norm() > 0:
+            assert _rel(g1[n], g2[n]) < 5e-2, (n, _rel(g1[n], g2[n]))
