@@ -7,6 +7,12 @@ all-reduce.  ``MLPTP`` pairs them (column fc -> ReLU^2 -> row proj), the standar
 with one collective per direction.  The collectives are NCCL (gloo on CPU) calls around the GEMMs:
 this is the baseline form; the all-gather -> GEMM and GEMM -> reduce-scatter pairs are not yet fused
 into peer-memory kernels.
+
+``enable_tensor_parallel(model, group)`` puts a model's plain ReLU^2 MLPs on the group: every rank keeps
+the rest of the block replicated, takes its slice of the block's rows into ``MLPTP`` and gathers the
+rows back, so replicated parameters see the same gradient on every rank and each rank holds and
+updates only its slices of the MLP matrices (an optimizer then sees the shards: Muon orthogonalises
+each shard on its own, which is not the full matrix's update).
 """
 import torch
 import torch.distributed as dist
@@ -84,3 +90,72 @@ class MLPTP(nn.Module):
         h = F.relu(F.linear(x, self.c_fc.weight.to(x.dtype))).square()
         y = F.linear(h, self.c_proj.weight.to(x.dtype))
         return reduce_scatter_rows(y, self.group)                      # GEMM -> reduce-scatter
+
+
+class _ScatterToRanks(torch.autograd.Function):
+    """Forward: this rank's slice of the rows (no communication).  Backward: the rows' gradients of
+    every rank gathered, so the replicated computation upstream sees the full gradient everywhere."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        size, rank = dist.get_world_size(group), dist.get_rank(group)
+        n = x.shape[0] // size
+        return x[rank * n:(rank + 1) * n].contiguous()
+
+    @staticmethod
+    def backward(ctx, g):
+        return all_gather_rows_plain(g, ctx.group), None
+
+
+class _GatherFromRanks(torch.autograd.Function):
+    """Forward: every rank's rows gathered.  Backward: the (replicated, hence equal) gradient's slice of
+    this rank's rows; no sum, which would count the replicated gradient once per rank."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return all_gather_rows_plain(x, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        size, rank = dist.get_world_size(ctx.group), dist.get_rank(ctx.group)
+        n = g.shape[0] // size
+        return g[rank * n:(rank + 1) * n].contiguous(), None
+
+
+def all_gather_rows_plain(x, group=None):
+    size = dist.get_world_size(group)
+    out = x.new_empty((x.shape[0] * size, *x.shape[1:]))
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+class TensorParallelMLP(nn.Module):
+    """A block's MLP on a tensor-parallel group: [B, T, d] in and out, replicated on every rank."""
+
+    def __init__(self, mlp, group=None):
+        super().__init__()
+        self.group = group
+        self.tp = MLPTP.from_dense(mlp, group)
+
+    def forward(self, x):
+        rows = x.reshape(-1, x.shape[-1])
+        if rows.shape[0] % dist.get_world_size(self.group):
+            raise ValueError("tokens per micro-batch must divide over the tensor-parallel group")
+        y = _GatherFromRanks.apply(self.tp(_ScatterToRanks.apply(rows, self.group)), self.group)
+        return y.view_as(x)
+
+
+def enable_tensor_parallel(model, group=None):
+    """Replace every plain shell ``MLP`` under ``model`` by its tensor-parallel form on ``group``
+    (weights sliced from the current ones).  Returns the number of MLPs replaced.  Variants that
+    transform the hidden layer (a ``hidden`` override) stay replicated."""
+    from nexttransformer_b200.models.shell import MLP
+    replaced = 0
+    for module in list(model.modules()):
+        for name, child in list(module.named_children()):
+            if type(child) is MLP:
+                setattr(module, name, TensorParallelMLP(child, group))
+                replaced += 1
+    return replaced

@@ -67,12 +67,50 @@ def _tp_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("worker", ["ep", "tp"])
+def _tp_model_worker(rank, world, port, q):
+    dist = _init(rank, world, port)
+    import copy
+    from nexttransformer_b200.models.shell import ShellConfig, build_shell
+    from nexttransformer_b200.parallel.tensor import enable_tensor_parallel
+    cfg = ShellConfig(sequence_len=16, vocab_size=64, n_layer=2, n_head=2, n_kv_head=2, n_embd=32, mlp_width=64)
+    dense = build_shell(cfg, "cpu", seed=3)
+    with torch.no_grad():  # signal through the zero-initialised output projections
+        for blk in dense.transformer.h:
+            blk.attn.c_proj.weight.normal_(0, 0.1)
+            blk.mlp.c_proj.weight.normal_(0, 0.1)
+    tp = copy.deepcopy(dense)
+    assert enable_tensor_parallel(tp) == cfg.n_layer
+    g = torch.Generator().manual_seed(5)
+    idx = torch.randint(0, 64, (2, 16), generator=g)
+    tgt = torch.randint(0, 64, (2, 16), generator=g)
+    ld, lt = dense(idx, tgt), tp(idx, tgt)
+    ld.backward()
+    lt.backward()
+    err = abs(ld.item() - lt.item())
+    dg = dict(dense.named_parameters())
+    size = dist.get_world_size()
+    for name, p in tp.named_parameters():
+        if ".mlp.tp." in name:
+            full = dg[name.replace(".mlp.tp.", ".mlp.")].grad
+            if name.endswith("c_fc.weight"):
+                n = full.shape[0] // size
+                ref = full[rank * n:(rank + 1) * n]
+            else:
+                n = full.shape[1] // size
+                ref = full[:, rank * n:(rank + 1) * n]
+        else:
+            ref = dg[name].grad
+        err = max(err, (p.grad - ref).abs().max().item())
+    q.put((rank, err))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", ["ep", "tp", "tp_model"])
 def test_parallel_matches_reference(worker):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    fn = _ep_worker if worker == "ep" else _tp_worker
+    fn = {"ep": _ep_worker, "tp": _tp_worker, "tp_model": _tp_model_worker}[worker]
     procs = [ctx.Process(target=fn, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
