@@ -125,3 +125,17 @@ def test_native_and_benchmark_launchers_dry_run():
     out = subprocess.run([str(ROOT / "launch/scaling/benchmark.sh"), "c.json"], env=dict(env, GPUS="4", STEPS="3"),
                          capture_output=True, text=True, check=True).stdout
     assert "--nproc-per-node 4" in out and "--benchmark 3" in out
+
+
+def test_setup_environment_records_packages(tmp_path):
+    """The set-up script resolves the site settings and records the package set; installing and
+    building are skipped here (no index and no GPU needed)."""
+    rt = tmp_path / "runtime"
+    out = subprocess.run(["bash", str(ROOT / "launch/setup_environment.sh"), "--skip-install", "--no-build",
+                          "--runtime-dir", str(rt)], capture_output=True, text=True, check=True).stdout
+    assert "nexttransformer_b200 with torch" in out
+    lock = (rt / "environment.lock.txt").read_text()
+    assert "torch" in lock
+    usage = subprocess.run(["bash", str(ROOT / "launch/setup_environment.sh"), "--help"], capture_output=True,
+                           text=True, check=True).stdout
+    assert "--wheelhouse" in usage
