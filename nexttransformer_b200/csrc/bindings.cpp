@@ -4,6 +4,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <atomic>
+
 #include "attention_sm100.h"
 #include "comm.h"
 #include "linear_attn.h"
@@ -42,10 +44,16 @@ void* mptr_or_null(const OptT& t) { return t.has_value() && t->defined() ? t->da
 void ok(int rc, const char* what) { TORCH_CHECK(rc == 0, what, ": unsupported shape"); }
 
 int num_sms(const Tensor& t) {
-  static int cached[64] = {0};
+  // cached per device for ids 0..63 (relaxed atomics: concurrent callers store the same value)
+  static std::atomic<int> cached[64] = {};
   const int dev = t.get_device();
-  if (!cached[dev]) cached[dev] = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
-  return cached[dev];
+  if (dev < 0 || dev >= 64) return at::cuda::getDeviceProperties(dev)->multiProcessorCount;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (!v) {
+    v = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
+    cached[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
 }
 
 // ------------------------------------------------------------------ GEMM
